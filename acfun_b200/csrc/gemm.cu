@@ -1,0 +1,382 @@
+// gemm.cu — GEMM-family entry points and the tcgen05 GEMM launcher.
+//
+// Entry points (reference behaviour in brackets, hit-droid/Acfun paths):
+//   acfun_gemm / acfun_gemm_epi   fp32, 3xTF32 on kind::tf32  [gemm.cpp:90-99,138-148]
+//   acfun_gemm_bf16               bf16 RNE operands, f32 acc   [gemm_bf16_avx512.cpp:171-232]
+//   acfun_gemm_int8               u8 x s8 -> s32, exact        [gemm_int8.cpp:45-50]
+//   acfun_gemm_int8_epi           + (float)acc*alpha + beta    [gemm_int8.cpp:69-75]
+//   acfun_gemm_s8_requant         s8 x s8 -> requantised s8    [no counterpart]
+#include <stdio.h>
+
+#include "api_export.cuh"
+#include "gemm.cuh"
+
+namespace acf {
+
+// ------------------------------------------------------------------ operand preparation
+Operand tma_operand(Call& c, const void* src, int rows, int cols, int elem) {
+  Operand o;
+  if (!c.ok()) return o;
+  const size_t pitch = (size_t)cols * elem;
+  const bool dev = ptr_kind(src) == PtrKind::Device;
+  if (dev && aligned16(src) && pitch % 16 == 0) {
+    o.p = src;
+    o.ld = cols;
+    return o;
+  }
+  const size_t ldp = align_up(pitch, 16);
+  void* d = c.scratch((size_t)rows * ldp);
+  if (!d) return o;
+  if (!ACF_CUDA_OK(cudaMemcpy2DAsync(d, ldp, src, pitch, pitch, rows, cudaMemcpyDefault,
+                                     c.stream()))) {
+    c.fail();
+    return o;
+  }
+  if (!dev) c.note_host();
+  o.p = d;
+  o.ld = (long long)(ldp / elem);
+  return o;
+}
+
+__device__ __forceinline__ uint16_t bf16_bits_ref(float f) {
+  // gemm_bf16_avx512.cpp:37-44: add 0x7fff + lsb(bit 16), keep the top half (wrapping)
+  const uint32_t x = __float_as_uint(f);
+  return (uint16_t)((x + 0x7fffu + ((x >> 16) & 1u)) >> 16);
+}
+
+__device__ __forceinline__ float tf32_rne(float x) {
+  uint32_t u = __float_as_uint(x);
+  if ((u & 0x7f800000u) == 0x7f800000u) return x;
+  u += 0xfffu + ((u >> 13) & 1u);
+  return __uint_as_float(u & 0xffffe000u);
+}
+
+__global__ void k_to_bf16(const float* __restrict__ src, long long lds, int rows, int cols,
+                          uint16_t* __restrict__ dst, long long ldp) {
+  const long long groups = ldp / 8;
+  const long long total = (long long)rows * groups;
+  for (long long g = blockIdx.x * (long long)blockDim.x + threadIdx.x; g < total;
+       g += (long long)gridDim.x * blockDim.x) {
+    const long long r = g / groups;
+    const int j = (int)(g - r * groups) * 8;
+    const float* s = src + r * lds;
+    uint32_t w[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const int j0 = j + 2 * t, j1 = j0 + 1;
+      const uint16_t lo = j0 < cols ? bf16_bits_ref(s[j0]) : 0;
+      const uint16_t hi = j1 < cols ? bf16_bits_ref(s[j1]) : 0;
+      w[t] = (uint32_t)lo | ((uint32_t)hi << 16);
+    }
+    *reinterpret_cast<uint4*>(dst + r * ldp + j) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+__global__ void k_to_tf32x2(const float* __restrict__ src, long long lds, int rows, int cols,
+                            float* __restrict__ dst, long long ldp, long long op_stride) {
+  const long long groups = ldp / 4;
+  const long long total = (long long)rows * groups;
+  for (long long g = blockIdx.x * (long long)blockDim.x + threadIdx.x; g < total;
+       g += (long long)gridDim.x * blockDim.x) {
+    const long long r = g / groups;
+    const int j = (int)(g - r * groups) * 4;
+    const float* s = src + r * lds;
+    float hi[4], lo[4];
+    if (j + 4 <= cols && ((reinterpret_cast<uintptr_t>(s + j) & 15) == 0)) {
+      const float4 v = *reinterpret_cast<const float4*>(s + j);
+      const float x[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        hi[t] = tf32_rne(x[t]);
+        lo[t] = tf32_rne(x[t] - hi[t]);
+      }
+    } else {
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const float x = (j + t < cols) ? s[j + t] : 0.0f;
+        hi[t] = tf32_rne(x);
+        lo[t] = tf32_rne(x - hi[t]);
+      }
+    }
+    float* d = dst + r * ldp + j;
+    *reinterpret_cast<float4*>(d) = make_float4(hi[0], hi[1], hi[2], hi[3]);
+    *reinterpret_cast<float4*>(d + op_stride) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+  }
+}
+
+static int ew_grid(Call& c, long long work) {
+  long long b = (work + 255) / 256;
+  long long cap = (long long)c.sm_count() * 8;
+  if (b > cap) b = cap;
+  if (b < 1) b = 1;
+  return (int)b;
+}
+
+Operand to_bf16(Call& c, const float* src, int rows, int cols, long long lds) {
+  Operand o;
+  if (!c.ok()) return o;
+  const long long ldp = (long long)align_up((size_t)cols, 8);
+  uint16_t* d = (uint16_t*)c.scratch((size_t)rows * ldp * 2);
+  if (!d) return o;
+  k_to_bf16<<<ew_grid(c, rows * (ldp / 8)), 256, 0, c.stream()>>>(src, lds, rows, cols, d, ldp);
+  if (!c.launched("k_to_bf16")) return o;
+  o.p = d;
+  o.ld = ldp;
+  return o;
+}
+
+Operand to_tf32x2(Call& c, const float* src, int rows, int cols, long long lds) {
+  Operand o;
+  if (!c.ok()) return o;
+  const long long ldp = (long long)align_up((size_t)cols, 4);
+  float* d = (float*)c.scratch((size_t)2 * rows * ldp * 4);
+  if (!d) return o;
+  k_to_tf32x2<<<ew_grid(c, rows * (ldp / 4)), 256, 0, c.stream()>>>(src, lds, rows, cols, d, ldp,
+                                                                      (long long)rows * ldp);
+  if (!c.launched("k_to_tf32x2")) return o;
+  o.p = d;
+  o.ld = ldp;
+  o.op_stride = (long long)rows * ldp;
+  return o;
+}
+
+// ------------------------------------------------------------------ launcher
+template <dev::MmaKind KIND, int BN, int STAGES, int NPASS, Epi EPI, bool AS>
+static bool launch_one(Call& c, const Operand& A, const Operand& B, int M, int N, int K,
+                       const EpiParams& ep) {
+  using S = GemmShape<KIND, BN, STAGES, NPASS>;
+  static_assert(S::SMEM <= 232448, "shared memory budget");
+  const CUtensorMapDataType dt = (KIND == dev::MmaKind::I8) ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                 : (KIND == dev::MmaKind::F16) ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                               : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  CUtensorMap ta, tb;
+  const uint64_t E = S::ELEM;
+  if (NPASS == 1) {
+    const uint64_t dA[2] = {(uint64_t)K, (uint64_t)M}, sA[1] = {(uint64_t)A.ld * E};
+    const uint32_t bA[2] = {(uint32_t)S::BKE, 128u};
+    const uint64_t dB[2] = {(uint64_t)N, (uint64_t)K}, sB[1] = {(uint64_t)B.ld * E};
+    const uint32_t bB[2] = {(uint32_t)(128 / S::ELEM), (uint32_t)S::BKE};
+    if (!encode_tmap(&ta, dt, 2, A.p, dA, sA, bA, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_tmap(&tb, dt, 2, B.p, dB, sB, bB, CU_TENSOR_MAP_SWIZZLE_128B)) {
+      c.fail();
+      return false;
+    }
+  } else {
+    const uint64_t dA[3] = {(uint64_t)K, (uint64_t)M, 2};
+    const uint64_t sA[2] = {(uint64_t)A.ld * E, (uint64_t)A.op_stride * E};
+    const uint32_t bA[3] = {(uint32_t)S::BKE, 128u, 1u};
+    const uint64_t dB[3] = {(uint64_t)N, (uint64_t)K, 2};
+    const uint64_t sB[2] = {(uint64_t)B.ld * E, (uint64_t)B.op_stride * E};
+    const uint32_t bB[3] = {(uint32_t)(128 / S::ELEM), (uint32_t)S::BKE, 1u};
+    if (!encode_tmap(&ta, dt, 3, A.p, dA, sA, bA, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_tmap(&tb, dt, 3, B.p, dB, sB, bB, CU_TENSOR_MAP_SWIZZLE_128B)) {
+      c.fail();
+      return false;
+    }
+  }
+  auto kern = gemm_tc_kernel<KIND, BN, STAGES, NPASS, EPI, AS>;
+  static bool attr_done[64] = {false};
+  const int dv = current_device();
+  if (dv >= 0 && dv < 64 && !attr_done[dv]) {
+    if (!ACF_CUDA_OK(
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM))) {
+      c.fail();
+      return false;
+    }
+    attr_done[dv] = true;
+  }
+  const dim3 grid((M + 127) / 128, (N + BN - 1) / BN);
+  if (grid.y > 65535u) {
+    set_error(kInvalid, "%s: N=%d too large", c.name(), N);
+    c.fail();
+    return false;
+  }
+  kern<<<grid, 192, S::SMEM, c.stream()>>>(ta, tb, ep, M, N, K, c.err());
+  return c.launched("gemm_tc_kernel");
+}
+
+static long long tiles(int M, int N, int bn) {
+  return (long long)((M + 127) / 128) * ((N + bn - 1) / bn);
+}
+
+bool gemm_launch(Call& c, GemmKind kind, Epi epi, const Operand& A, const Operand& B, int M,
+                 int N, int K, const EpiParams& ep) {
+  if (!c.ok() || !A.p || !B.p) {
+    c.fail();
+    return false;
+  }
+  const int sms = c.sm_count();
+  using MK = dev::MmaKind;
+  switch (kind) {
+    case GemmKind::I8U: {
+      const bool wide = N > 128 && tiles(M, N, 256) >= sms;
+      switch (epi) {
+        case Epi::S32:
+          return wide ? launch_one<MK::I8, 256, 4, 1, Epi::S32, false>(c, A, B, M, N, K, ep)
+                      : launch_one<MK::I8, 128, 6, 1, Epi::S32, false>(c, A, B, M, N, K, ep);
+        case Epi::F32_AB:
+          return wide ? launch_one<MK::I8, 256, 4, 1, Epi::F32_AB, false>(c, A, B, M, N, K, ep)
+                      : launch_one<MK::I8, 128, 6, 1, Epi::F32_AB, false>(c, A, B, M, N, K, ep);
+        case Epi::I8_WINO:
+          return wide ? launch_one<MK::I8, 256, 4, 1, Epi::I8_WINO, false>(c, A, B, M, N, K, ep)
+                      : launch_one<MK::I8, 128, 6, 1, Epi::I8_WINO, false>(c, A, B, M, N, K, ep);
+        default:
+          break;
+      }
+      break;
+    }
+    case GemmKind::I8S: {
+      const bool wide = N > 128 && tiles(M, N, 256) >= sms;
+      if (epi == Epi::S8_REQ)
+        return wide ? launch_one<MK::I8, 256, 4, 1, Epi::S8_REQ, true>(c, A, B, M, N, K, ep)
+                    : launch_one<MK::I8, 128, 6, 1, Epi::S8_REQ, true>(c, A, B, M, N, K, ep);
+      break;
+    }
+    case GemmKind::BF16: {
+      if (epi != Epi::F32_BIAS) break;
+      if (N > 128 && tiles(M, N, 256) >= sms)
+        return launch_one<MK::F16, 256, 4, 1, Epi::F32_BIAS, false>(c, A, B, M, N, K, ep);
+      if (N > 64 && tiles(M, N, 128) >= sms)
+        return launch_one<MK::F16, 128, 6, 1, Epi::F32_BIAS, false>(c, A, B, M, N, K, ep);
+      return launch_one<MK::F16, 64, 8, 1, Epi::F32_BIAS, false>(c, A, B, M, N, K, ep);
+    }
+    case GemmKind::TF32X3: {
+      if (epi != Epi::F32_BIAS) break;
+      if (N > 64 && tiles(M, N, 128) >= sms)
+        return launch_one<MK::TF32, 128, 3, 3, Epi::F32_BIAS, false>(c, A, B, M, N, K, ep);
+      if (N > 32)
+        return launch_one<MK::TF32, 64, 4, 3, Epi::F32_BIAS, false>(c, A, B, M, N, K, ep);
+      return launch_one<MK::TF32, 32, 5, 3, Epi::F32_BIAS, false>(c, A, B, M, N, K, ep);
+    }
+  }
+  set_error(kInvalid, "%s: unsupported GEMM kind/epilogue combination", c.name());
+  c.fail();
+  return false;
+}
+
+// fp32 GEMM (+bias, +ReLU) on device operands, used by GEMM, FC and conv routes.
+bool gemm_f32(Call& c, const float* dA, long long lda, const float* dB, long long ldb, int M,
+              int N, int K, float* dC, long long ldc, const float* dbias, int act) {
+  Operand a = to_tf32x2(c, dA, M, K, lda);
+  Operand b = to_tf32x2(c, dB, K, N, ldb);
+  EpiParams ep{};
+  ep.C = dC;
+  ep.ldc = ldc;
+  ep.f0 = dbias;
+  ep.act = act;
+  return gemm_launch(c, GemmKind::TF32X3, Epi::F32_BIAS, a, b, M, N, K, ep);
+}
+
+}  // namespace acf
+
+using namespace acf;
+
+static bool bad_ptrs(const char* fn, const void* a, const void* b, const void* c) {
+  if (!a || !b || !c) {
+    set_error(kInvalid, "%s: NULL tensor argument", fn);
+    return true;
+  }
+  return false;
+}
+
+extern "C" void acfun_gemm_epi(int M, int N, int K, const float* A, const float* B, float* C,
+                               const float* bias, int act) {
+  if (M <= 0 || N <= 0 || K <= 0 || bad_ptrs("acfun_gemm_epi", A, B, C)) return;
+  Call c("acfun_gemm_epi");
+  if (!c.ok()) return;
+  const float* dA = (const float*)c.in(A, (size_t)M * K * 4);
+  const float* dB = (const float*)c.in(B, (size_t)K * N * 4);
+  const float* db = bias ? (const float*)c.in(bias, (size_t)N * 4) : nullptr;
+  float* dC = (float*)c.out(C, (size_t)M * N * 4);
+  if (!c.ok()) return;
+  gemm_f32(c, dA, K, dB, N, M, N, K, dC, N, db, act ? 1 : 0);
+  c.finish();
+}
+
+extern "C" void acfun_gemm(int M, int N, int K, const float* A, const float* B, float* C) {
+  acfun_gemm_epi(M, N, K, A, B, C, nullptr, 0);
+}
+
+extern "C" void acfun_gemm_bf16(int M, int N, int K, const float* A, const float* B, float* C) {
+  if (M <= 0 || N <= 0 || K <= 0 || bad_ptrs("acfun_gemm_bf16", A, B, C)) return;
+  Call c("acfun_gemm_bf16");
+  if (!c.ok()) return;
+  const float* dA = (const float*)c.in(A, (size_t)M * K * 4);
+  const float* dB = (const float*)c.in(B, (size_t)K * N * 4);
+  float* dC = (float*)c.out(C, (size_t)M * N * 4);
+  if (!c.ok()) return;
+  Operand a = to_bf16(c, dA, M, K, K);
+  Operand b = to_bf16(c, dB, K, N, N);
+  EpiParams ep{};
+  ep.C = dC;
+  ep.ldc = N;
+  gemm_launch(c, GemmKind::BF16, Epi::F32_BIAS, a, b, M, N, K, ep);
+  c.finish();
+}
+
+extern "C" void acfun_gemm_int8(int M, int N, int K, const uint8_t* A, const int8_t* B,
+                                int32_t* C) {
+  if (M <= 0 || N <= 0 || K <= 0 || bad_ptrs("acfun_gemm_int8", A, B, C)) return;
+  Call c("acfun_gemm_int8");
+  if (!c.ok()) return;
+  Operand a = tma_operand(c, A, M, K, 1);
+  Operand b = tma_operand(c, B, K, N, 1);
+  int32_t* dC = (int32_t*)c.out(C, (size_t)M * N * 4);
+  if (!c.ok()) return;
+  EpiParams ep{};
+  ep.C = dC;
+  ep.ldc = N;
+  gemm_launch(c, GemmKind::I8U, Epi::S32, a, b, M, N, K, ep);
+  c.finish();
+}
+
+extern "C" void acfun_gemm_int8_epi(int M, int N, int K, const uint8_t* A, const int8_t* B,
+                                    float* C, const float* alpha, const float* beta, int act) {
+  if (M <= 0 || N <= 0 || K <= 0 || bad_ptrs("acfun_gemm_int8_epi", A, B, C)) return;
+  if (!alpha || !beta) {
+    set_error(kInvalid, "acfun_gemm_int8_epi: alpha/beta must not be NULL");
+    return;
+  }
+  Call c("acfun_gemm_int8_epi");
+  if (!c.ok()) return;
+  Operand a = tma_operand(c, A, M, K, 1);
+  Operand b = tma_operand(c, B, K, N, 1);
+  const float* da = (const float*)c.in(alpha, (size_t)N * 4);
+  const float* db = (const float*)c.in(beta, (size_t)N * 4);
+  float* dC = (float*)c.out(C, (size_t)M * N * 4);
+  if (!c.ok()) return;
+  EpiParams ep{};
+  ep.C = dC;
+  ep.ldc = N;
+  ep.f0 = da;
+  ep.f1 = db;
+  ep.act = act ? 1 : 0;
+  gemm_launch(c, GemmKind::I8U, Epi::F32_AB, a, b, M, N, K, ep);
+  c.finish();
+}
+
+extern "C" void acfun_gemm_s8_requant(int M, int N, int K, const int8_t* A, const int8_t* B,
+                                      const int32_t* bias, const float* scale, int8_t* C,
+                                      int act) {
+  if (M <= 0 || N <= 0 || K <= 0 || bad_ptrs("acfun_gemm_s8_requant", A, B, C)) return;
+  if (!scale) {
+    set_error(kInvalid, "acfun_gemm_s8_requant: scale must not be NULL");
+    return;
+  }
+  Call c("acfun_gemm_s8_requant");
+  if (!c.ok()) return;
+  Operand a = tma_operand(c, A, M, K, 1);
+  Operand b = tma_operand(c, B, K, N, 1);
+  const int32_t* dbias = bias ? (const int32_t*)c.in(bias, (size_t)N * 4) : nullptr;
+  const float* dscale = (const float*)c.in(scale, (size_t)N * 4);
+  int8_t* dC = (int8_t*)c.out(C, (size_t)M * N);
+  if (!c.ok()) return;
+  EpiParams ep{};
+  ep.C = dC;
+  ep.ldc = N;
+  ep.f0 = dscale;
+  ep.i0 = dbias;
+  ep.act = act ? 1 : 0;
+  gemm_launch(c, GemmKind::I8S, Epi::S8_REQ, a, b, M, N, K, ep);
+  c.finish();
+}

@@ -1,0 +1,33 @@
+// gemm.cuh — host-side launch helpers around gemm_tc_kernel, shared by the GEMM, FC and
+// convolution entry points.
+#pragma once
+#include "gemm_tc.cuh"
+#include "runtime.cuh"
+
+namespace acf {
+
+// A device-resident GEMM operand: `rows x cols` elements with row stride `ld` (elements);
+// for 3xTF32 operands a second (lo) copy lives `op_stride` elements after the first.
+struct Operand {
+  const void* p = nullptr;
+  long long ld = 0;
+  long long op_stride = 0;
+};
+
+// Make a byte / 16-bit / 32-bit matrix TMA-addressable: returns `src` when it is device
+// memory with a 16-byte aligned base and a row pitch that is a multiple of 16 bytes,
+// otherwise a zero-padded scratch copy (one 2D copy, host or device source).
+Operand tma_operand(Call& c, const void* src, int rows, int cols, int elem);
+
+// fp32 [rows][cols] (row stride lds) -> bf16 [rows][ldp], RNE as gemm_bf16_avx512.cpp:37-44.
+Operand to_bf16(Call& c, const float* src_dev, int rows, int cols, long long lds);
+// fp32 -> [2][rows][ldp] (hi = tf32-rounded, lo = tf32-rounded residual) for 3xTF32.
+Operand to_tf32x2(Call& c, const float* src_dev, int rows, int cols, long long lds);
+
+enum class GemmKind { I8U, I8S, BF16, TF32X3 };
+
+// C-tile launch: chooses the tile width from the problem size and the SM count.
+bool gemm_launch(Call& c, GemmKind kind, Epi epi, const Operand& A, const Operand& B, int M,
+                 int N, int K, const EpiParams& ep);
+
+}  // namespace acf

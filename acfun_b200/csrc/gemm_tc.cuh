@@ -1,0 +1,316 @@
+// gemm_tc.cuh — tcgen05 (5th-gen tensor core) GEMM for sm_100a.
+//
+// One CTA computes a 128 x BN tile of C = A[M,K] * B[K,N]:
+//   warp 0        TMA producer: per 128-byte K block, A tile (128 rows, K-major, SW128)
+//                 and B tile (K rows x BN, MN-major, SW128, split in 128-byte N chunks)
+//                 into a STAGES-deep shared-memory ring guarded by full/empty mbarriers;
+//   warp 1        TMEM owner + single-thread UMMA issuer (cta_group::1, M=128, N=BN),
+//                 4 K-steps of 32 bytes per block; tcgen05.commit frees a stage as soon
+//                 as its MMAs retire and finally signals the epilogue;
+//   warps 2..5    epilogue: tcgen05.ld 32 columns at a time from their TMEM lane quadrant,
+//                 fused epilogue (int32 store / dequant mul+add / requant to s8 / bias +
+//                 ReLU / int8-Winograd dequant fma), vectorised global stores.
+// 3xTF32 (NPASS = 3): A and B arrive as [2][rows][cols] (hi, lo) pairs; each K-step issues
+// lo*hi + hi*lo + hi*hi into the same fp32 accumulator.
+//
+// Rows of C may be remapped (implicit convolution over a padded NHWC tensor): GEMM row r
+// is output pixel r when remap is off; otherwise r indexes the padded grid and only rows
+// that land on a real output pixel are stored.
+#pragma once
+#include "ptx.cuh"
+
+namespace acf {
+
+enum class Epi : int { S32 = 0, F32_AB = 1, S8_REQ = 2, F32_BIAS = 3, I8_WINO = 4 };
+
+struct EpiParams {
+  void* C;               // output base
+  long long ldc;         // output row stride in elements
+  const float* f0;       // F32_AB alpha | S8_REQ scale | I8_WINO wso | F32_BIAS bias
+  const float* f1;       // F32_AB beta  | I8_WINO bias
+  const int32_t* i0;     // S8_REQ int32 bias | I8_WINO column sums of the u8-zp weights
+  int act;
+  // implicit-convolution row remap (remap != 0): GEMM row r -> image n = r / img_rows,
+  // q = r % img_rows, oh = q / Wp, ow = q % Wp; stored iff oh < OH && ow < OW at
+  // output row (n*OH + oh)*OW + ow.
+  int remap;
+  int img_rows, Wp, OH, OW;
+};
+
+template <dev::MmaKind KIND>
+struct KindTraits;
+template <>
+struct KindTraits<dev::MmaKind::I8> {
+  static constexpr int ELEM = 1;
+};
+template <>
+struct KindTraits<dev::MmaKind::F16> {
+  static constexpr int ELEM = 2;
+};
+template <>
+struct KindTraits<dev::MmaKind::TF32> {
+  static constexpr int ELEM = 4;
+};
+
+template <dev::MmaKind KIND, int BN, int STAGES, int NPASS>
+struct GemmShape {
+  static constexpr int ELEM = KindTraits<KIND>::ELEM;
+  static constexpr int BM = 128;
+  static constexpr int BKB = 128;                      // K bytes per block
+  static constexpr int BKE = BKB / ELEM;               // K elements per block
+  static constexpr int NOPS = (NPASS == 3) ? 2 : 1;    // hi/lo operand copies
+  static constexpr int A_TILE = BM * BKB;              // 16 KB
+  static constexpr int NCHUNK = BN * ELEM / 128;       // 128-byte N chunks of B
+  static constexpr int CHUNK_B = BKE * 128;            // bytes per N chunk
+  static constexpr int B_TILE = NCHUNK * CHUNK_B;
+  static constexpr int STAGE = NOPS * (A_TILE + B_TILE);
+  static constexpr int KSTEP_B = (32 / ELEM) * 128;    // B descriptor advance per MMA K-step
+  static constexpr int SMEM = STAGES * STAGE + 1024 + 256;
+  static constexpr int TMEM_COLS = BN;
+  static_assert(BN * ELEM % 128 == 0, "B tile must be whole 128-byte chunks");
+  static_assert(BN == 32 || BN == 64 || BN == 128 || BN == 256, "TMEM columns");
+};
+
+__device__ __forceinline__ float relu_max(float v) { return v > 0.0f ? v : 0.0f; }
+
+template <Epi EPI>
+__device__ __forceinline__ void epi_store32(const EpiParams& ep, long long orow, int j0, int N,
+                                            const uint32_t (&r)[32]) {
+  // compute 32 outputs for columns j0..j0+31 of output row `orow`
+  const bool full = (j0 + 32 <= N);
+  if constexpr (EPI == Epi::S32) {
+    int32_t* dst = reinterpret_cast<int32_t*>(ep.C) + orow * ep.ldc + j0;
+    if (full && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+#pragma unroll
+      for (int i = 0; i < 32; i += 4)
+        *reinterpret_cast<uint4*>(dst + i) = make_uint4(r[i], r[i + 1], r[i + 2], r[i + 3]);
+    } else {
+      for (int i = 0; i < 32; ++i)
+        if (j0 + i < N) dst[i] = (int32_t)r[i];
+    }
+  } else if constexpr (EPI == Epi::S8_REQ) {
+    uint32_t packed[8];
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+      uint32_t w = 0;
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const int j = j0 + i + t;
+        int q = 0;
+        if (j < N) {
+          int32_t s = (int32_t)((uint32_t)r[i + t] + (uint32_t)(ep.i0 ? ep.i0[j] : 0));
+          float v = __fmul_rn(__int2float_rn(s), ep.f0[j]);
+          if (ep.act) v = relu_max(v);
+          q = __float2int_rn(v);
+          q = q > 127 ? 127 : (q < -128 ? -128 : q);
+        }
+        w |= (uint32_t)(q & 0xFF) << (8 * t);
+      }
+      packed[i / 4] = w;
+    }
+    int8_t* dst = reinterpret_cast<int8_t*>(ep.C) + orow * ep.ldc + j0;
+    if (full && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+      *reinterpret_cast<uint4*>(dst) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+      *reinterpret_cast<uint4*>(dst + 16) = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+    } else {
+      for (int i = 0; i < 32; ++i)
+        if (j0 + i < N) dst[i] = (int8_t)((packed[i / 4] >> (8 * (i % 4))) & 0xFF);
+    }
+  } else {
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int j = j0 + i;
+      const int jj = j < N ? j : 0;
+      float x;
+      if constexpr (EPI == Epi::F32_AB) {
+        x = __fadd_rn(__fmul_rn(__int2float_rn((int32_t)r[i]), ep.f0[jj]), ep.f1[jj]);
+      } else if constexpr (EPI == Epi::F32_BIAS) {
+        x = __uint_as_float(r[i]);
+        if (ep.f0) x = __fadd_rn(x, ep.f0[jj]);
+      } else {  // I8_WINO
+        int32_t c = (int32_t)r[i] - 128 * ep.i0[jj];
+        x = __fmaf_rn(__fmul_rn(4.0f, __int2float_rn(c)), ep.f0[jj], ep.f1 ? ep.f1[jj] : 0.0f);
+      }
+      if (ep.act) x = relu_max(x);
+      v[i] = x;
+    }
+    float* dst = reinterpret_cast<float*>(ep.C) + orow * ep.ldc + j0;
+    if (full && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+#pragma unroll
+      for (int i = 0; i < 32; i += 4)
+        *reinterpret_cast<float4*>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+    } else {
+      for (int i = 0; i < 32; ++i)
+        if (j0 + i < N) dst[i] = v[i];
+    }
+  }
+}
+
+template <dev::MmaKind KIND, int BN, int STAGES, int NPASS, Epi EPI, bool A_SIGNED>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   EpiParams ep, int M, int N, int K, unsigned* err) {
+  using S = GemmShape<KIND, BN, STAGES, NPASS>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * S::STAGE);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* done_bar = empty_bar + STAGES;   // accumulator complete
+  uint64_t* drain_bar = done_bar + 1;        // error-path MMA drain
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * S::BM;
+  const int n0 = blockIdx.y * BN;
+  const int nkb = (K + S::BKE - 1) / S::BKE;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      dev::mbar_init(&full_bar[s], 1);
+      dev::mbar_init(&empty_bar[s], 1);
+    }
+    dev::mbar_init(done_bar, 1);
+    dev::mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    dev::fence_mbar_init();
+    dev::tma_prefetch_desc(&tmA);
+    dev::tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    dev::tmem_alloc(tmem_slot, S::TMEM_COLS);
+    dev::tmem_relinquish();
+  }
+  dev::tc_fence_before();
+  __syncthreads();
+  dev::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer
+    int issued = 0;
+    for (int kb = 0; kb < nkb; ++kb) {
+      const int s = kb % STAGES;
+      const uint32_t ph = (kb / STAGES) & 1;
+      if (*abort_flag) break;
+      if (!dev::mbar_wait(&empty_bar[s], ph ^ 1, err)) {
+        *abort_flag = 1;
+        break;
+      }
+      uint8_t* st = smem + s * S::STAGE;
+      dev::mbar_arrive_expect_tx(&full_bar[s], S::STAGE);
+      const int kx = kb * S::BKE;
+#pragma unroll
+      for (int op = 0; op < S::NOPS; ++op) {
+        uint8_t* a_dst = st + op * S::A_TILE;
+        uint8_t* b_dst = st + S::NOPS * S::A_TILE + op * S::B_TILE;
+        if constexpr (S::NOPS == 1) {
+          dev::tma_load_2d(a_dst, &tmA, &full_bar[s], kx, m0);
+#pragma unroll
+          for (int c = 0; c < S::NCHUNK; ++c)
+            dev::tma_load_2d(b_dst + c * S::CHUNK_B, &tmB, &full_bar[s], n0 + c * (128 / S::ELEM),
+                             kx);
+        } else {
+          dev::tma_load_3d(a_dst, &tmA, &full_bar[s], kx, m0, op);
+#pragma unroll
+          for (int c = 0; c < S::NCHUNK; ++c)
+            dev::tma_load_3d(b_dst + c * S::CHUNK_B, &tmB, &full_bar[s], n0 + c * (128 / S::ELEM),
+                             kx, op);
+        }
+      }
+      ++issued;
+    }
+    if (*abort_flag) {
+      // drain copies that may still be in flight before the CTA releases its smem
+      const int first = issued > STAGES ? issued - STAGES : 0;
+      for (int kb = first; kb < issued; ++kb)
+        dev::mbar_wait(&full_bar[kb % STAGES], (kb / STAGES) & 1, nullptr, 200000000ull);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- UMMA issuer
+    constexpr uint32_t c_fmt = (KIND == dev::MmaKind::I8) ? 2u : 1u;
+    constexpr uint32_t a_fmt = (KIND == dev::MmaKind::I8) ? (A_SIGNED ? 1u : 0u)
+                               : (KIND == dev::MmaKind::F16) ? 1u : 2u;
+    constexpr uint32_t b_fmt = (KIND == dev::MmaKind::I8) ? 1u
+                               : (KIND == dev::MmaKind::F16) ? 1u : 2u;
+    constexpr uint32_t idesc = dev::umma_idesc(c_fmt, a_fmt, b_fmt, 0u, 1u, 128u, (uint32_t)BN);
+    const uint32_t smem_base = dev::smem_u32(smem);
+    bool ok = true;
+    for (int kb = 0; kb < nkb; ++kb) {
+      const int s = kb % STAGES;
+      const uint32_t ph = (kb / STAGES) & 1;
+      if (*abort_flag || !dev::mbar_wait(&full_bar[s], ph, err)) {
+        *abort_flag = 1;
+        ok = false;
+        break;
+      }
+      dev::tc_fence_after();
+      const uint32_t a_base = smem_base + s * S::STAGE;
+      const uint32_t b_base = a_base + S::NOPS * S::A_TILE;
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        if constexpr (NPASS == 1) {
+          const uint64_t ad = dev::umma_sdesc(a_base + ks * 32, 16, 1024, dev::UMMA_SW128);
+          const uint64_t bd = dev::umma_sdesc(b_base + ks * S::KSTEP_B, S::CHUNK_B, 1024,
+                                              dev::UMMA_SW128);
+          dev::umma<KIND>(tmem, ad, bd, idesc, (kb | ks) != 0);
+        } else {
+          // (a_op, b_op): lo*hi, hi*lo, hi*hi
+          const int aop[3] = {1, 0, 0}, bop[3] = {0, 1, 0};
+#pragma unroll
+          for (int p = 0; p < 3; ++p) {
+            const uint64_t ad = dev::umma_sdesc(a_base + aop[p] * S::A_TILE + ks * 32, 16, 1024,
+                                                dev::UMMA_SW128);
+            const uint64_t bd = dev::umma_sdesc(b_base + bop[p] * S::B_TILE + ks * S::KSTEP_B,
+                                                S::CHUNK_B, 1024, dev::UMMA_SW128);
+            dev::umma<KIND>(tmem, ad, bd, idesc, (kb | ks | p) != 0);
+          }
+        }
+      }
+      dev::umma_commit(&empty_bar[s]);
+    }
+    if (ok) {
+      dev::umma_commit(done_bar);
+    } else {
+      dev::umma_commit(drain_bar);
+      dev::mbar_wait(drain_bar, 0, nullptr, 200000000ull);
+      dev::mbar_arrive(done_bar);  // release the epilogue warps (they see abort_flag)
+    }
+  } else if (warp >= 2) {
+    // ---------------- epilogue
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const bool ok = dev::mbar_wait(done_bar, 0, err);
+    dev::tc_fence_after();
+    if (ok && !*abort_flag) {
+      const int r = m0 + q * 32 + lane;
+      long long orow = r;
+      bool store = r < M;
+      if (ep.remap && store) {
+        const int n = r / ep.img_rows, qq = r - n * ep.img_rows;
+        const int oh = qq / ep.Wp, ow = qq - oh * ep.Wp;
+        store = (oh < ep.OH) && (ow < ep.OW);
+        orow = ((long long)n * ep.OH + oh) * ep.OW + ow;
+      }
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        if (n0 + c0 >= N) break;  // warp-uniform
+        uint32_t v[32];
+        dev::tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
+        dev::tmem_ld_wait();
+        if (store) epi_store32<EPI>(ep, orow, n0 + c0, N, v);
+      }
+    }
+  }
+
+  dev::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    dev::tc_fence_after();
+    dev::tmem_dealloc(tmem, S::TMEM_COLS);
+  }
+}
+
+}  // namespace acf

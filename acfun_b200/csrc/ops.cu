@@ -1,0 +1,504 @@
+// ops.cu — bandwidth-bound NHWC kernels: ReLU / ReLU6, max-pool (+ReLU), softmax,
+// batch-norm, u8 activation quantisation, depthwise and grouped direct convolution.
+//
+// Each kernel reproduces the rounding sequence of the reference's routed AVX path so that
+// results are bit-identical where the reference is deterministic:
+//   depthwise   acc = bias; acc = fma(x_or_0, w, acc) over kh, kw   (dw_avx512.cpp:99-124)
+//   grouped     acc = bias; acc = fma(x, w, acc) over kh, kw, ic    (group_conv_avx2.cpp:241-258)
+//               (mul-then-add when Cout_per < 8: the scalar kernel, group_conv.cpp:16-55)
+//   batch-norm  (x - mean) * (gamma / sqrtf(var + eps)) + beta      (layers.cpp:285-296)
+//   quantize    clamp(cvt_rne(x * inv_s) + zp, 0, 255)               (int8_quantize_avx512.cpp:8-35)
+//   max-pool    vector lanes: acc = acc > v ? acc : v (vmaxps);       (maxpool_avx512.cpp:15-66)
+//               scalar tail lanes: if (v > mx) mx = v
+#include <float.h>
+
+#include "api_export.cuh"
+#include "ops.cuh"
+#include "runtime.cuh"
+
+namespace acf {
+
+static inline int grid_for(Call& c, long long work, int block = 256) {
+  long long b = (work + block - 1) / block;
+  long long cap = (long long)c.sm_count() * 16;
+  if (b > cap) b = cap;
+  if (b < 1) b = 1;
+  return (int)b;
+}
+
+#define GRID_STRIDE(i, n)                                                               \
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < (n); \
+       i += (long long)gridDim.x * blockDim.x)
+
+// ------------------------------------------------------------------ relu / relu6
+__global__ void k_relu(float* d, long long n, int six) {
+  GRID_STRIDE(i, n) {
+    float v = d[i];
+    if (v < 0.0f) v = 0.0f;
+    else if (six && v > 6.0f) v = 6.0f;
+    d[i] = v;
+  }
+}
+
+bool relu_dev(Call& c, float* d, long long n, int six) {
+  if (n <= 0) return true;
+  k_relu<<<grid_for(c, n), 256, 0, c.stream()>>>(d, n, six);
+  return c.launched("k_relu");
+}
+
+// ------------------------------------------------------------------ max pool
+__global__ void k_maxpool(const float* __restrict__ in, int N, int H, int W, int C, int pool,
+                          int stride, int pad, int OH, int OW, int cfull, float* __restrict__ out,
+                          int post_relu) {
+  const long long total = (long long)N * OH * OW * C;
+  GRID_STRIDE(idx, total) {
+    const int c = (int)(idx % C);
+    long long p = idx / C;
+    const int ow = (int)(p % OW);
+    p /= OW;
+    const int oh = (int)(p % OH);
+    const int n = (int)(p / OH);
+    const bool vec = c < cfull;
+    float mx = -1e30f;
+    for (int ph = 0; ph < pool; ++ph) {
+      const int ih = oh * stride - pad + ph;
+      if (ih < 0 || ih >= H) continue;
+      for (int pw = 0; pw < pool; ++pw) {
+        const int iw = ow * stride - pad + pw;
+        if (iw < 0 || iw >= W) continue;
+        const float v = in[(((long long)n * H + ih) * W + iw) * C + c];
+        if (vec) mx = (mx > v) ? mx : v;
+        else if (v > mx) mx = v;
+      }
+    }
+    if (post_relu) {
+      if (vec) mx = (mx > 0.0f) ? mx : 0.0f;
+      else if (mx < 0.0f) mx = 0.0f;
+    }
+    out[idx] = mx;
+  }
+}
+
+// float4 variant for whole vector-lane channel groups (C % 4 == 0, all lanes vectorised).
+__global__ void k_maxpool4(const float4* __restrict__ in, int N, int H, int W, int C4, int pool,
+                           int stride, int pad, int OH, int OW, float4* __restrict__ out,
+                           int post_relu) {
+  const long long total = (long long)N * OH * OW * C4;
+  GRID_STRIDE(idx, total) {
+    const int c = (int)(idx % C4);
+    long long p = idx / C4;
+    const int ow = (int)(p % OW);
+    p /= OW;
+    const int oh = (int)(p % OH);
+    const int n = (int)(p / OH);
+    float4 m = make_float4(-1e30f, -1e30f, -1e30f, -1e30f);
+    for (int ph = 0; ph < pool; ++ph) {
+      const int ih = oh * stride - pad + ph;
+      if (ih < 0 || ih >= H) continue;
+      for (int pw = 0; pw < pool; ++pw) {
+        const int iw = ow * stride - pad + pw;
+        if (iw < 0 || iw >= W) continue;
+        const float4 v = in[(((long long)n * H + ih) * W + iw) * C4 + c];
+        m.x = m.x > v.x ? m.x : v.x;
+        m.y = m.y > v.y ? m.y : v.y;
+        m.z = m.z > v.z ? m.z : v.z;
+        m.w = m.w > v.w ? m.w : v.w;
+      }
+    }
+    if (post_relu) {
+      m.x = m.x > 0.f ? m.x : 0.f;
+      m.y = m.y > 0.f ? m.y : 0.f;
+      m.z = m.z > 0.f ? m.z : 0.f;
+      m.w = m.w > 0.f ? m.w : 0.f;
+    }
+    out[idx] = m;
+  }
+}
+
+bool maxpool_dev(Call& c, const float* in, int N, int H, int W, int C, int pool, int stride,
+                 int pad, float* out, int post_relu) {
+  const int OH = (H + 2 * pad - pool) / stride + 1, OW = (W + 2 * pad - pool) / stride + 1;
+  if (OH <= 0 || OW <= 0 || N <= 0 || C <= 0) return true;
+  // lanes handled by the reference's vector kernels (maxpool_impl, layers.cpp:250-258)
+  const int cfull = C >= 16 ? (C & ~15) : (C >= 8 ? (C & ~7) : 0);
+  if (cfull == C && C % 4 == 0 && aligned16(in) && aligned16(out)) {
+    const long long total = (long long)N * OH * OW * (C / 4);
+    k_maxpool4<<<grid_for(c, total), 256, 0, c.stream()>>>(
+        (const float4*)in, N, H, W, C / 4, pool, stride, pad, OH, OW, (float4*)out, post_relu);
+    return c.launched("k_maxpool4");
+  }
+  const long long total = (long long)N * OH * OW * C;
+  k_maxpool<<<grid_for(c, total), 256, 0, c.stream()>>>(in, N, H, W, C, pool, stride, pad, OH,
+                                                        OW, cfull, out, post_relu);
+  return c.launched("k_maxpool");
+}
+
+// ------------------------------------------------------------------ softmax
+__device__ __forceinline__ float block_reduce(float v, bool is_max, float* sh) {
+  for (int o = 16; o > 0; o >>= 1) {
+    const float u = __shfl_xor_sync(0xffffffffu, v, o);
+    v = is_max ? fmaxf(v, u) : v + u;
+  }
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) sh[w] = v;
+  __syncthreads();
+  const int nw = blockDim.x >> 5;
+  v = (threadIdx.x < nw) ? sh[threadIdx.x] : (is_max ? -FLT_MAX : 0.0f);
+  if (w == 0) {
+    for (int o = 16; o > 0; o >>= 1) {
+      const float u = __shfl_xor_sync(0xffffffffu, v, o);
+      v = is_max ? fmaxf(v, u) : v + u;
+    }
+    if (l == 0) sh[0] = v;
+  }
+  __syncthreads();
+  return sh[0];
+}
+
+// layers.cpp:272-283: one block per row; max, e = expf(x - max), sum, out = e * (1/sum).
+__global__ void k_softmax(const float* __restrict__ in, int cols, float* __restrict__ out) {
+  __shared__ float sh[32];
+  const float* ri = in + (long long)blockIdx.x * cols;
+  float* ro = out + (long long)blockIdx.x * cols;
+  float m = -FLT_MAX;
+  for (int j = threadIdx.x; j < cols; j += blockDim.x) m = fmaxf(m, ri[j]);
+  m = block_reduce(m, true, sh);
+  float s = 0.0f;
+  for (int j = threadIdx.x; j < cols; j += blockDim.x) {
+    const float e = expf(ri[j] - m);
+    ro[j] = e;
+    s += e;
+  }
+  s = block_reduce(s, false, sh);
+  const float inv = 1.0f / s;
+  for (int j = threadIdx.x; j < cols; j += blockDim.x) ro[j] = ro[j] * inv;
+}
+
+bool softmax_dev(Call& c, const float* in, int rows, int cols, float* out) {
+  if (rows <= 0 || cols <= 0) return true;
+  k_softmax<<<rows, 256, 0, c.stream()>>>(in, cols, out);
+  return c.launched("k_softmax");
+}
+
+// ------------------------------------------------------------------ batch norm
+__global__ void k_batchnorm(float* d, long long n, int channels, const float* mean,
+                            const float* var, const float* gamma, const float* beta, float eps) {
+  GRID_STRIDE(i, n) {
+    const int c = (int)(i % channels);
+    const float scale = gamma ? gamma[c] : 1.0f;
+    const float shift = beta ? beta[c] : 0.0f;
+    const float inv = __fdiv_rn(scale, __fsqrt_rn(__fadd_rn(var[c], eps)));
+    d[i] = __fadd_rn(__fmul_rn(__fsub_rn(d[i], mean[c]), inv), shift);
+  }
+}
+
+bool batchnorm_dev(Call& c, float* d, int size, int channels, const float* mean,
+                   const float* var, const float* gamma, const float* beta, float eps) {
+  if (channels <= 0 || size <= 0) return true;
+  const long long n = (long long)(size / channels) * channels;  // the reference's `spatial` floor
+  if (n <= 0) return true;
+  k_batchnorm<<<grid_for(c, n), 256, 0, c.stream()>>>(d, n, channels, mean, var, gamma, beta, eps);
+  return c.launched("k_batchnorm");
+}
+
+// ------------------------------------------------------------------ u8 quantisation
+__device__ __forceinline__ uint8_t quant_rne(float x, float inv_s, int zp) {
+  const float t = __fmul_rn(x, inv_s);
+  // cvtps2dq: |t| >= 2^31 or NaN gives the integer indefinite 0x80000000
+  const int q = (fabsf(t) < 2147483648.0f) ? __float2int_rn(t) : (int)0x80000000;
+  const int v = (int)((unsigned)q + (unsigned)zp);
+  return (uint8_t)(v < 0 ? 0 : (v > 255 ? 255 : v));
+}
+
+__global__ void k_quantize_u8(const float* __restrict__ in, uint8_t* __restrict__ out, long long n,
+                              float inv_s, int zp) {
+  const long long n4 = n / 4;
+  GRID_STRIDE(i, n4) {
+    const float4 v = reinterpret_cast<const float4*>(in)[i];
+    uchar4 q;
+    q.x = quant_rne(v.x, inv_s, zp);
+    q.y = quant_rne(v.y, inv_s, zp);
+    q.z = quant_rne(v.z, inv_s, zp);
+    q.w = quant_rne(v.w, inv_s, zp);
+    reinterpret_cast<uchar4*>(out)[i] = q;
+  }
+  if (blockIdx.x == 0 && threadIdx.x < (n & 3)) {
+    const long long i = n4 * 4 + threadIdx.x;
+    out[i] = quant_rne(in[i], inv_s, zp);
+  }
+}
+
+__global__ void k_quantize_u8_scalar(const float* __restrict__ in, uint8_t* __restrict__ out,
+                                     long long n, float inv_s, int zp) {
+  GRID_STRIDE(i, n) out[i] = quant_rne(in[i], inv_s, zp);
+}
+
+bool quantize_u8_dev(Call& c, const float* in, uint8_t* out, long long n, float inv_s, int zp) {
+  if (n <= 0) return true;
+  if (aligned16(in) && (reinterpret_cast<uintptr_t>(out) & 3) == 0) {
+    k_quantize_u8<<<grid_for(c, n / 4 + 1), 256, 0, c.stream()>>>(in, out, n, inv_s, zp);
+  } else {
+    k_quantize_u8_scalar<<<grid_for(c, n), 256, 0, c.stream()>>>(in, out, n, inv_s, zp);
+  }
+  return c.launched("k_quantize_u8");
+}
+
+// ------------------------------------------------------------------ depthwise conv
+// One thread per (output pixel, 4 channels): coalesced NHWC float4 reads / writes.
+__global__ void k_dw4(const float* __restrict__ in, int N, int H, int W, int C,
+                      const float* __restrict__ w, const float* __restrict__ bias, int KH, int KW,
+                      int stride, int pad, int OH, int OW, float* __restrict__ out, int act) {
+  const int C4 = C / 4;
+  const long long total = (long long)N * OH * OW * C4;
+  const int K = KH * KW;
+  GRID_STRIDE(idx, total) {
+    const int c4 = (int)(idx % C4);
+    long long p = idx / C4;
+    const int ow = (int)(p % OW);
+    p /= OW;
+    const int oh = (int)(p % OH);
+    const int n = (int)(p / OH);
+    const int c = c4 * 4;
+    float4 acc = bias ? *reinterpret_cast<const float4*>(bias + c) : make_float4(0, 0, 0, 0);
+    const float* w0 = w + (long long)c * K;
+    for (int kh = 0; kh < KH; ++kh) {
+      const int ih = oh * stride - pad + kh;
+      for (int kw = 0; kw < KW; ++kw) {
+        const int iw = ow * stride - pad + kw;
+        const int k = kh * KW + kw;
+        float4 x = make_float4(0, 0, 0, 0);
+        if (ih >= 0 && ih < H && iw >= 0 && iw < W)
+          x = *reinterpret_cast<const float4*>(in + (((long long)n * H + ih) * W + iw) * C + c);
+        acc.x = __fmaf_rn(x.x, __ldg(w0 + k), acc.x);
+        acc.y = __fmaf_rn(x.y, __ldg(w0 + K + k), acc.y);
+        acc.z = __fmaf_rn(x.z, __ldg(w0 + 2 * K + k), acc.z);
+        acc.w = __fmaf_rn(x.w, __ldg(w0 + 3 * K + k), acc.w);
+      }
+    }
+    if (act == 1) {
+      acc.x = acc.x > 0.f ? acc.x : 0.f;
+      acc.y = acc.y > 0.f ? acc.y : 0.f;
+      acc.z = acc.z > 0.f ? acc.z : 0.f;
+      acc.w = acc.w > 0.f ? acc.w : 0.f;
+    }
+    *reinterpret_cast<float4*>(out + (((long long)n * OH + oh) * OW + ow) * C + c) = acc;
+  }
+}
+
+__global__ void k_dw1(const float* __restrict__ in, int N, int H, int W, int C,
+                      const float* __restrict__ w, const float* __restrict__ bias, int KH, int KW,
+                      int stride, int pad, int OH, int OW, float* __restrict__ out, int act) {
+  const long long total = (long long)N * OH * OW * C;
+  const int K = KH * KW;
+  GRID_STRIDE(idx, total) {
+    const int c = (int)(idx % C);
+    long long p = idx / C;
+    const int ow = (int)(p % OW);
+    p /= OW;
+    const int oh = (int)(p % OH);
+    const int n = (int)(p / OH);
+    float acc = bias ? bias[c] : 0.0f;
+    for (int kh = 0; kh < KH; ++kh) {
+      const int ih = oh * stride - pad + kh;
+      for (int kw = 0; kw < KW; ++kw) {
+        const int iw = ow * stride - pad + kw;
+        float x = 0.0f;
+        if (ih >= 0 && ih < H && iw >= 0 && iw < W) x = in[(((long long)n * H + ih) * W + iw) * C + c];
+        acc = __fmaf_rn(x, w[(long long)c * K + kh * KW + kw], acc);
+      }
+    }
+    if (act == 1) acc = acc > 0.f ? acc : 0.f;
+    out[idx] = acc;
+  }
+}
+
+bool dw_dev(Call& c, const float* in, int N, int H, int W, int C, const float* w,
+            const float* bias, int KH, int KW, int stride, int pad, float* out, int act) {
+  const int OH = (H + 2 * pad - KH) / stride + 1, OW = (W + 2 * pad - KW) / stride + 1;
+  if (OH <= 0 || OW <= 0 || N <= 0 || C <= 0) return true;
+  if (C % 4 == 0 && aligned16(in) && aligned16(out) && (!bias || aligned16(bias))) {
+    const long long total = (long long)N * OH * OW * (C / 4);
+    k_dw4<<<grid_for(c, total), 256, 0, c.stream()>>>(in, N, H, W, C, w, bias, KH, KW, stride, pad,
+                                                      OH, OW, out, act);
+    return c.launched("k_dw4");
+  }
+  const long long total = (long long)N * OH * OW * C;
+  k_dw1<<<grid_for(c, total), 256, 0, c.stream()>>>(in, N, H, W, C, w, bias, KH, KW, stride, pad,
+                                                    OH, OW, out, act);
+  return c.launched("k_dw1");
+}
+
+// ------------------------------------------------------------------ grouped conv
+__global__ void k_group(const float* __restrict__ in, int N, int H, int W, int Cin,
+                        const float* __restrict__ w, const float* __restrict__ bias, int KH,
+                        int KW, int Cout, int stride, int pad, int groups, int OH, int OW,
+                        float* __restrict__ out, int act, int fma_chain) {
+  const int Cin_p = Cin / groups, Cout_p = Cout / groups;
+  const long long total = (long long)N * OH * OW * Cout;
+  const long long wg_stride = (long long)Cout_p * KH * KW * Cin_p;
+  GRID_STRIDE(idx, total) {
+    const int oc_g = (int)(idx % Cout);
+    long long p = idx / Cout;
+    const int ow = (int)(p % OW);
+    p /= OW;
+    const int oh = (int)(p % OH);
+    const int n = (int)(p / OH);
+    const int g = oc_g / Cout_p, oc = oc_g - g * Cout_p;
+    const float* wg = w + g * wg_stride + oc;
+    float s = bias ? bias[oc_g] : 0.0f;
+    for (int kh = 0; kh < KH; ++kh) {
+      const int ih = oh * stride - pad + kh;
+      if (ih < 0 || ih >= H) continue;
+      for (int kw = 0; kw < KW; ++kw) {
+        const int iw = ow * stride - pad + kw;
+        if (iw < 0 || iw >= W) continue;
+        const float* ip = in + (((long long)n * H + ih) * W + iw) * Cin + (long long)g * Cin_p;
+        const float* wp = wg + (long long)((kh * KW + kw) * Cin_p) * Cout_p;
+        for (int ic = 0; ic < Cin_p; ++ic) {
+          const float x = ip[ic], wv = __ldg(wp + (long long)ic * Cout_p);
+          s = fma_chain ? __fmaf_rn(x, wv, s) : __fadd_rn(s, __fmul_rn(x, wv));
+        }
+      }
+    }
+    if (act == 1) s = fma_chain ? (s > 0.f ? s : 0.f) : (s < 0.f ? 0.f : s);
+    out[idx] = s;
+  }
+}
+
+bool group_dev(Call& c, const float* in, int N, int H, int W, int Cin, const float* w,
+               const float* bias, int KH, int KW, int Cout, int stride, int pad, int groups,
+               float* out, int act) {
+  const int OH = (H + 2 * pad - KH) / stride + 1, OW = (W + 2 * pad - KW) / stride + 1;
+  if (OH <= 0 || OW <= 0 || N <= 0) return true;
+  const int Cout_p = Cout / groups;
+  const long long total = (long long)N * OH * OW * Cout;
+  k_group<<<grid_for(c, total), 256, 0, c.stream()>>>(in, N, H, W, Cin, w, bias, KH, KW, Cout,
+                                                      stride, pad, groups, OH, OW, out, act,
+                                                      Cout_p >= 8 ? 1 : 0);
+  return c.launched("k_group");
+}
+
+}  // namespace acf
+
+using namespace acf;
+
+// ============================================================== C API wrappers
+static void relu_api(const char* name, float* d, size_t len, int six) {
+  if (!d || len == 0) return;
+  Call c(name);
+  if (!c.ok()) return;
+  float* dd = (float*)c.inout(d, len * 4);
+  if (!c.ok()) return;
+  relu_dev(c, dd, (long long)len, six);
+  c.finish();
+}
+extern "C" void acfun_relu(float* data, size_t len) { relu_api("acfun_relu", data, len, 0); }
+extern "C" void acfun_relu6(float* data, size_t len) { relu_api("acfun_relu6", data, len, 1); }
+
+static void maxpool_api(const char* name, const float* in, int N, int H, int W, int C, int pool,
+                        int stride, int pad, float* out, int post) {
+  if (N <= 0 || C <= 0 || pool <= 0 || stride <= 0 || !in || !out) return;
+  const int OH = (H + 2 * pad - pool) / stride + 1, OW = (W + 2 * pad - pool) / stride + 1;
+  if (OH <= 0 || OW <= 0) return;
+  Call c(name);
+  if (!c.ok()) return;
+  const float* di = (const float*)c.in(in, (size_t)N * H * W * C * 4);
+  float* dout = (float*)c.out(out, (size_t)N * OH * OW * C * 4);
+  if (!c.ok()) return;
+  maxpool_dev(c, di, N, H, W, C, pool, stride, pad, dout, post);
+  c.finish();
+}
+extern "C" void acfun_maxpool(const float* in, int N, int H, int W, int C, int pool, int stride,
+                              int pad, float* out) {
+  maxpool_api("acfun_maxpool", in, N, H, W, C, pool, stride, pad, out, 0);
+}
+extern "C" void acfun_maxpool_relu(const float* in, int N, int H, int W, int C, int pool,
+                                   int stride, int pad, float* out) {
+  maxpool_api("acfun_maxpool_relu", in, N, H, W, C, pool, stride, pad, out, 1);
+}
+
+extern "C" void acfun_softmax(const float* in, int rows, int cols, float* out) {
+  if (rows <= 0 || cols <= 0 || !in || !out) return;
+  Call c("acfun_softmax");
+  if (!c.ok()) return;
+  const size_t bytes = (size_t)rows * cols * 4;
+  const float* di;
+  float* dout;
+  if (in == out) {  // in-place use (model.cpp:335)
+    dout = (float*)c.inout(out, bytes);
+    di = dout;
+  } else {
+    di = (const float*)c.in(in, bytes);
+    dout = (float*)c.out(out, bytes);
+  }
+  if (!c.ok()) return;
+  softmax_dev(c, di, rows, cols, dout);
+  c.finish();
+}
+
+extern "C" void acfun_batchnorm(float* d, int size, int channels, const float* mean,
+                                const float* var, const float* gamma, const float* beta,
+                                float eps) {
+  if (!d || size <= 0 || channels <= 0 || !mean || !var) return;
+  Call c("acfun_batchnorm");
+  if (!c.ok()) return;
+  float* dd = (float*)c.inout(d, (size_t)size * 4);
+  const float* dm = (const float*)c.in(mean, (size_t)channels * 4);
+  const float* dv = (const float*)c.in(var, (size_t)channels * 4);
+  const float* dg = gamma ? (const float*)c.in(gamma, (size_t)channels * 4) : nullptr;
+  const float* db = beta ? (const float*)c.in(beta, (size_t)channels * 4) : nullptr;
+  if (!c.ok()) return;
+  batchnorm_dev(c, dd, size, channels, dm, dv, dg, db, eps);
+  c.finish();
+}
+
+extern "C" void acfun_quantize_u8(const float* in, uint8_t* out, size_t n, float inv_s, int zp) {
+  if (!in || !out || n == 0) return;
+  Call c("acfun_quantize_u8");
+  if (!c.ok()) return;
+  const float* di = (const float*)c.in(in, n * 4);
+  uint8_t* dout = (uint8_t*)c.out(out, n);
+  if (!c.ok()) return;
+  quantize_u8_dev(c, di, dout, (long long)n, inv_s, zp);
+  c.finish();
+}
+
+extern "C" void acfun_conv2d_dw(const float* input, int N, int H, int W, int C,
+                                const float* weight, const float* bias, int KH, int KW, int stride,
+                                int pad, float* output, int act) {
+  if (KH <= 0 || KW <= 0 || N <= 0 || C <= 0 || stride <= 0 || !input || !weight || !output)
+    return;
+  const int OH = (H + 2 * pad - KH) / stride + 1, OW = (W + 2 * pad - KW) / stride + 1;
+  if (OH <= 0 || OW <= 0) return;
+  Call c("acfun_conv2d_dw");
+  if (!c.ok()) return;
+  const float* di = (const float*)c.in(input, (size_t)N * H * W * C * 4);
+  const float* dw = (const float*)c.in(weight, (size_t)C * KH * KW * 4);
+  const float* db = bias ? (const float*)c.in(bias, (size_t)C * 4) : nullptr;
+  float* dout = (float*)c.out(output, (size_t)N * OH * OW * C * 4);
+  if (!c.ok()) return;
+  dw_dev(c, di, N, H, W, C, dw, db, KH, KW, stride, pad, dout, act);
+  c.finish();
+}
+
+extern "C" void acfun_conv2d_grouped(const float* input, int N, int H, int W, int Cin,
+                                     const float* weight, const float* bias, int KH, int KW,
+                                     int Cout, int stride, int pad, int groups, float* output,
+                                     int act) {
+  if (groups <= 1 || KH <= 0 || KW <= 0 || N <= 0 || stride <= 0 || !input || !weight || !output)
+    return;
+  const int OH = (H + 2 * pad - KH) / stride + 1, OW = (W + 2 * pad - KW) / stride + 1;
+  if (OH <= 0 || OW <= 0) return;
+  Call c("acfun_conv2d_grouped");
+  if (!c.ok()) return;
+  const int Cin_p = Cin / groups, Cout_p = Cout / groups;
+  const float* di = (const float*)c.in(input, (size_t)N * H * W * Cin * 4);
+  const float* dw =
+      (const float*)c.in(weight, (size_t)groups * Cout_p * KH * KW * Cin_p * 4);
+  const float* db = bias ? (const float*)c.in(bias, (size_t)Cout * 4) : nullptr;
+  float* dout = (float*)c.out(output, (size_t)N * OH * OW * Cout * 4);
+  if (!c.ok()) return;
+  group_dev(c, di, N, H, W, Cin, dw, db, KH, KW, Cout, stride, pad, groups, dout, act);
+  c.finish();
+}

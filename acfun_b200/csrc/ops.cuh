@@ -1,0 +1,22 @@
+// ops.cuh — device-pointer entry points of the bandwidth kernels (ops.cu), shared by the
+// public API wrappers, the convolution router and the model executor.
+#pragma once
+#include "runtime.cuh"
+
+namespace acf {
+bool relu_dev(Call& c, float* d, long long n, int six);
+bool maxpool_dev(Call& c, const float* in, int N, int H, int W, int C, int pool, int stride,
+                 int pad, float* out, int post_relu);
+bool softmax_dev(Call& c, const float* in, int rows, int cols, float* out);
+bool batchnorm_dev(Call& c, float* d, int size, int channels, const float* mean,
+                   const float* var, const float* gamma, const float* beta, float eps);
+bool quantize_u8_dev(Call& c, const float* in, uint8_t* out, long long n, float inv_s, int zp);
+bool dw_dev(Call& c, const float* in, int N, int H, int W, int C, const float* w,
+            const float* bias, int KH, int KW, int stride, int pad, float* out, int act);
+bool group_dev(Call& c, const float* in, int N, int H, int W, int Cin, const float* w,
+               const float* bias, int KH, int KW, int Cout, int stride, int pad, int groups,
+               float* out, int act);
+// fp32 GEMM on device operands via 3xTF32 (gemm.cu)
+bool gemm_f32(Call& c, const float* dA, long long lda, const float* dB, long long ldb, int M,
+              int N, int K, float* dC, long long ldc, const float* dbias, int act);
+}  // namespace acf

@@ -1,0 +1,26 @@
+import os
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA B200 (sm_100a) device")
+
+
+@pytest.fixture(scope="session")
+def acf():
+    """The product library; GPU tests fail (not skip) when it is missing."""
+    import acfun_b200
+    acfun_b200.lib()
+    return acfun_b200
+
+
+@pytest.fixture(scope="session")
+def orc():
+    from oracle import pyoracle
+    return pyoracle

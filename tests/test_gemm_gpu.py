@@ -1,0 +1,141 @@
+"""GPU parity: the tcgen05 GEMM family through the C ABI against the oracle and the golden
+vectors (bit-exact for int8, max-rel tolerance for float)."""
+import glob
+import os
+
+import numpy as np
+import pytest
+
+from helpers import TOL_BF16, TOL_F32, assert_bits_equal, max_rel
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def load(name):
+    return dict(np.load(os.path.join(GOLD, name + ".npz")))
+
+
+def torch_dev(a):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+# the reference's own gates (benchmark.cpp:53-77, :930-962) plus tcgen05 tile edges
+INT8_SHAPES = [(63, 63, 63), (100, 100, 100), (255, 255, 255), (512, 512, 512), (1023, 1023, 1023),
+               (64, 64, 64), (512, 17, 64), (63, 512, 33), (127, 129, 63), (1023, 4, 7),
+               (128, 256, 128), (129, 257, 129), (1, 1, 1), (300, 640, 2000), (2048, 384, 4096)]
+
+
+def rand_u8s8(g, M, N, K):
+    return (g.integers(0, 256, (M, K), dtype=np.uint8), g.integers(-128, 128, (K, N), dtype=np.int8))
+
+
+@pytest.mark.parametrize("M,N,K", INT8_SHAPES)
+def test_gemm_int8_exact(acf, orc, M, N, K):
+    g = np.random.default_rng(M * 7919 + N * 31 + K)
+    A, B = rand_u8s8(g, M, N, K)
+    ref = np.empty((M, N), np.int32)
+    orc.oracle().orc_gemm_int8(M, N, K, A, B, ref)
+    assert_bits_equal(acf.gemm_int8(A, B), ref, f"gemm_int8 {M}x{N}x{K} host")
+
+
+@pytest.mark.parametrize("M,N,K,act", [(64, 64, 64, 1), (100, 100, 100, 1), (255, 255, 255, 0),
+                                       (512, 17, 64, 1), (63, 512, 33, 1), (127, 129, 63, 0),
+                                       (1023, 4, 7, 1), (700, 300, 1111, 1)])
+def test_gemm_int8_epi_exact(acf, orc, M, N, K, act):
+    g = np.random.default_rng(K)
+    A, B = rand_u8s8(g, M, N, K)
+    al = g.uniform(1e-4, 1e-2, N).astype(np.float32)
+    be = g.uniform(-20, 20, N).astype(np.float32)
+    ref = np.empty((M, N), np.float32)
+    orc.oracle().orc_gemm_int8_epi(M, N, K, A, B, ref, al, be, act)
+    assert_bits_equal(acf.gemm_int8_epi(A, B, al, be, act), ref, f"epi {M}x{N}x{K}")
+
+
+def test_gemm_int8_device_pointers(acf, orc):
+    M, N, K = 384, 512, 640
+    g = np.random.default_rng(5)
+    A, B = rand_u8s8(g, M, N, K)
+    ref = np.empty((M, N), np.int32)
+    orc.oracle().orc_gemm_int8(M, N, K, A, B, ref)
+    out = acf.gemm_int8(torch_dev(A), torch_dev(B))
+    acf.synchronize()
+    assert_bits_equal(out.cpu().numpy(), ref, "device pointers")
+
+
+@pytest.mark.parametrize("name", sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLD, "gemm_int8_*.npz"))))
+def test_gemm_int8_golden(acf, name):
+    d = load(name)
+    if "_epi_" in name:
+        got = acf.gemm_int8_epi(d["A"], d["B"], d["alpha"], d["beta"], int(d["act"]))
+    else:
+        got = acf.gemm_int8(d["A"], d["B"])
+    assert_bits_equal(got, d["C"], name)
+
+
+@pytest.mark.parametrize("act", [0, 1])
+def test_gemm_s8_requant_golden(acf, act):
+    d = load(f"gemm_s8_requant_a{act}")
+    got = acf.gemm_s8_requant(d["A"], d["B"], d["bias"], d["scale"], act)
+    assert_bits_equal(got, d["C"], "s8 requant")
+
+
+@pytest.mark.parametrize("M,N,K", [(4096, 4096, 4096)])
+def test_gemm_s8_requant_full_size_sampled(acf, orc, M, N, K):
+    """BASELINE cfg2 at full size: every sampled row is bit-exact against the oracle."""
+    g = np.random.default_rng(2)
+    A = g.integers(-127, 128, (M, K), dtype=np.int8)
+    B = g.integers(-127, 128, (K, N), dtype=np.int8)
+    bias = g.integers(-1000, 1001, N, dtype=np.int32)
+    scale = g.uniform(1e-3, 1e-2, N).astype(np.float32)
+    got = acf.gemm_s8_requant(A, B, bias, scale, 1)
+    rows = np.sort(g.choice(M, 24, replace=False))
+    rows = np.concatenate([[0, 127, 128, M - 1], rows])
+    ref = np.empty((rows.size, N), np.int8)
+    orc.oracle().orc_gemm_s8_requant(rows.size, N, K, np.ascontiguousarray(A[rows]), B,
+                                     bias.ctypes.data, scale, ref, 1)
+    assert_bits_equal(got[rows], ref, "requant 4096^3 sampled rows")
+
+
+@pytest.mark.parametrize("M,N,K", [(64, 64, 64), (100, 100, 100), (255, 255, 255), (1024, 1024, 1024),
+                                   (33, 47, 129), (300, 24, 144), (1, 1000, 4096), (512, 17, 64)])
+def test_gemm_f32_tolerance(acf, orc, M, N, K):
+    g = np.random.default_rng(M + N + K)
+    A = g.uniform(-1, 1, (M, K)).astype(np.float32)
+    B = g.uniform(-1, 1, (K, N)).astype(np.float32)
+    bias = g.uniform(-1, 1, N).astype(np.float32)
+    ref = np.empty((M, N), np.float32)
+    orc.oracle().orc_gemm_f32(M, N, K, A, B, ref, bias.ctypes.data, 1)
+    got = acf.gemm(A, B, bias, 1)
+    assert max_rel(got, ref) < TOL_F32, max_rel(got, ref)
+
+
+@pytest.mark.parametrize("M,N,K", [(64, 64, 64), (33, 47, 129), (1024, 1024, 1024), (200, 520, 300)])
+def test_gemm_bf16_tolerance(acf, orc, M, N, K):
+    g = np.random.default_rng(M * N + K)
+    A = g.uniform(-1, 1, (M, K)).astype(np.float32)
+    B = g.uniform(-1, 1, (K, N)).astype(np.float32)
+    ref = np.empty((M, N), np.float32)
+    orc.oracle().orc_gemm_bf16(M, N, K, A, B, ref)
+    got = acf.gemm_bf16(A, B)
+    # same bf16 operands, fp32 accumulation: only the summation order differs
+    assert max_rel(got, ref) < 1e-4
+    exact = A.astype(np.float64) @ B.astype(np.float64)
+    assert max_rel(got, exact) < TOL_BF16
+
+
+@pytest.mark.parametrize("name", sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLD, "gemm_f32_*.npz"))))
+def test_gemm_float_golden(acf, name):
+    d = load(name)
+    assert max_rel(acf.gemm(d["A"], d["B"], d["bias"], 1), d["C_epi_relu"]) < TOL_F32
+    assert max_rel(acf.gemm_bf16(d["A"], d["B"]), d["C_bf16"]) < TOL_BF16
+
+
+def test_gemm_empty_and_bad_shapes_are_silent(acf):
+    L = acf.lib()
+    C = np.full((2, 2), 7, np.int32)
+    L.acfun_gemm_int8(0, 2, 2, None, None, acf.ptr(C))       # M<=0: returns, output untouched
+    L.acfun_gemm_int8(2, 2, -1, None, None, acf.ptr(C))
+    acf.check()
+    assert (C == 7).all()
