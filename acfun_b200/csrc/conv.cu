@@ -1,0 +1,311 @@
+// conv.cu — fp32 convolution router and FC.
+//
+// Routing mirrors conv2d_impl (hit-droid/Acfun src/layers.cpp:106-195):
+//   groups == Cin == Cout                   -> depthwise kernel           (layers.cpp:112-116)
+//   groups > 1, Cin/g <= 64, Cout/g <= 128  -> grouped direct kernel      (:126-130)
+//   groups > 1 otherwise                    -> per-group GEMM conv        (:134-153)
+//   1x1                                     -> GEMM, zero-copy when s1 p0 (:157-160, :66-101)
+//   3x3 s1 p1, H,W >= 3, Cin,Cout >= 4      -> the reference's Winograd F(4,3)/F(2,3) routes
+//   otherwise                               -> im2col + GEMM               (:178-194)
+// On B200 every GEMM-shaped route runs on tcgen05 tensor cores in 3xTF32 (fp32-class
+// error).  Stride-1 convolutions (the Winograd routes, 1x1, any KxK) are implicit GEMMs
+// over a zero-padded copy of the input: each K block is one (tap, 32-channel block), the
+// TMA producer shifts the A rows by kh*Wp + kw, and the epilogue keeps only the GEMM rows
+// that land on real output pixels.  Strided convolutions gather an explicit im2col matrix.
+// Bias and ReLU are fused into the TMEM drain.
+#include "api_export.cuh"
+#include "conv.cuh"
+#include "gemm.cuh"
+#include "ops.cuh"
+
+namespace acf {
+
+__device__ __forceinline__ float tf32_rne_c(float x) {
+  uint32_t u = __float_as_uint(x);
+  if ((u & 0x7f800000u) == 0x7f800000u) return x;
+  u += 0xfffu + ((u >> 13) & 1u);
+  return __uint_as_float(u & 0xffffe000u);
+}
+
+__device__ __forceinline__ void split_store(float* dst, long long op_stride, float x) {
+  const float hi = tf32_rne_c(x);
+  dst[0] = hi;
+  dst[op_stride] = tf32_rne_c(x - hi);
+}
+
+static int grid_ew(Call& c, long long work) {
+  long long b = (work + 255) / 256, cap = (long long)c.sm_count() * 16;
+  return (int)(b < 1 ? 1 : (b > cap ? cap : b));
+}
+
+// x: NHWC with channel stride Cs and channel offset coff (Cg channels used) ->
+// [2][N*Hp*Wp][Cpad] hi/lo, zero in the spatial border and in channels >= Cg.
+__global__ void k_pad_split(const float* __restrict__ x, int N, int H, int W, int Cs, int coff,
+                            int Cg, int pad, int Hp, int Wp, int Cpad, float* __restrict__ dst,
+                            long long op_stride) {
+  const long long total = (long long)N * Hp * Wp * Cpad;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int c = (int)(i % Cpad);
+    long long p = i / Cpad;
+    const int wp = (int)(p % Wp);
+    p /= Wp;
+    const int hp = (int)(p % Hp);
+    const int n = (int)(p / Hp);
+    const int ih = hp - pad, iw = wp - pad;
+    float v = 0.0f;
+    if (c < Cg && ih >= 0 && ih < H && iw >= 0 && iw < W)
+      v = x[(((long long)n * H + ih) * W + iw) * Cs + coff + c];
+    split_store(dst + i, op_stride, v);
+  }
+}
+
+// im2col for strided convs: row m = (n, oh, ow), column k = (kh*KW + kw)*Cg + c -> [2][M][Kpad]
+__global__ void k_im2col_split(const float* __restrict__ x, int N, int H, int W, int Cs, int coff,
+                               int Cg, int KH, int KW, int stride, int pad, int OH, int OW,
+                               int Kpad, float* __restrict__ dst, long long op_stride) {
+  const long long total = (long long)N * OH * OW * Kpad;
+  const int K = KH * KW * Cg;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int k = (int)(i % Kpad);
+    long long m = i / Kpad;
+    const int ow = (int)(m % OW);
+    m /= OW;
+    const int oh = (int)(m % OH);
+    const int n = (int)(m / OH);
+    float v = 0.0f;
+    if (k < K) {
+      const int tap = k / Cg, c = k - tap * Cg;
+      const int ih = oh * stride - pad + tap / KW, iw = ow * stride - pad + tap % KW;
+      if (ih >= 0 && ih < H && iw >= 0 && iw < W)
+        v = x[(((long long)n * H + ih) * W + iw) * Cs + coff + c];
+    }
+    split_store(dst + i, op_stride, v);
+  }
+}
+
+// weights [taps*Cg][Cout_g] (row stride ldw) -> [2][taps*Cpad][Np], zero rows for c >= Cg
+__global__ void k_weights_split(const float* __restrict__ w, int taps, int Cg, int Cout_g,
+                                long long ldw, int Cpad, int Np, float* __restrict__ dst,
+                                long long op_stride) {
+  const long long total = (long long)taps * Cpad * Np;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int j = (int)(i % Np);
+    const long long r = i / Np;
+    const int tap = (int)(r / Cpad), c = (int)(r % Cpad);
+    float v = 0.0f;
+    if (c < Cg && j < Cout_g) v = w[((long long)tap * Cg + c) * ldw + j];
+    split_store(dst + i, op_stride, v);
+  }
+}
+
+bool conv_f32_dev(Call& c, const float* x, int N, int H, int W, int Cs, int coff, int Cg,
+                  const float* w, long long ldw, const float* bias, int KH, int KW, int Cout_g,
+                  int stride, int pad, float* out, long long ldc, int act) {
+  const int OH = (H + 2 * pad - KH) / stride + 1, OW = (W + 2 * pad - KW) / stride + 1;
+  if (OH <= 0 || OW <= 0 || N <= 0 || Cout_g <= 0) return true;
+  const int taps = KH * KW;
+  const int Np = (int)align_up((size_t)Cout_g, 4);
+  EpiParams ep{};
+  ep.C = out;
+  ep.ldc = ldc;
+  ep.f0 = bias;
+  ep.act = act;
+  if (stride == 1) {
+    const int Hp = H + 2 * pad, Wp = W + 2 * pad;
+    const int Cpad = (int)align_up((size_t)Cg, 32);
+    const long long rows = (long long)N * Hp * Wp;
+    if (rows >= (1LL << 31)) {
+      set_error(kInvalid, "%s: tensor too large", c.name());
+      c.fail();
+      return false;
+    }
+    Operand A, B;
+    float* a = (float*)c.scratch((size_t)2 * rows * Cpad * 4);
+    float* b = (float*)c.scratch((size_t)2 * taps * Cpad * Np * 4);
+    if (!a || !b) return false;
+    k_pad_split<<<grid_ew(c, rows * Cpad), 256, 0, c.stream()>>>(x, N, H, W, Cs, coff, Cg, pad, Hp,
+                                                                 Wp, Cpad, a, rows * Cpad);
+    k_weights_split<<<grid_ew(c, (long long)taps * Cpad * Np), 256, 0, c.stream()>>>(
+        w, taps, Cg, Cout_g, ldw, Cpad, Np, b, (long long)taps * Cpad * Np);
+    if (!c.launched("conv prep")) return false;
+    A.p = a;
+    A.ld = Cpad;
+    A.op_stride = rows * Cpad;
+    B.p = b;
+    B.ld = Np;
+    B.op_stride = (long long)taps * Cpad * Np;
+    ep.remap = 1;
+    ep.img_rows = Hp * Wp;
+    ep.Wp = Wp;
+    ep.OH = OH;
+    ep.OW = OW;
+    ConvGeom cg{1, Cpad / 32, KW, Wp, Cpad, taps};
+    return gemm_launch(c, GemmKind::TF32X3, Epi::F32_BIAS, A, B, (int)rows, Cout_g, taps * Cpad,
+                       ep, cg);
+  }
+  const long long M = (long long)N * OH * OW;
+  const int K = taps * Cg, Kpad = (int)align_up((size_t)K, 4);
+  float* a = (float*)c.scratch((size_t)2 * M * Kpad * 4);
+  float* b = (float*)c.scratch((size_t)2 * K * Np * 4);
+  if (!a || !b) return false;
+  k_im2col_split<<<grid_ew(c, M * Kpad), 256, 0, c.stream()>>>(x, N, H, W, Cs, coff, Cg, KH, KW,
+                                                               stride, pad, OH, OW, Kpad, a, M * Kpad);
+  k_weights_split<<<grid_ew(c, (long long)K * Np), 256, 0, c.stream()>>>(w, 1, K, Cout_g, ldw, K,
+                                                                        Np, b, (long long)K * Np);
+  if (!c.launched("im2col prep")) return false;
+  Operand A, B;
+  A.p = a;
+  A.ld = Kpad;
+  A.op_stride = M * Kpad;
+  B.p = b;
+  B.ld = Np;
+  B.op_stride = (long long)K * Np;
+  return gemm_launch(c, GemmKind::TF32X3, Epi::F32_BIAS, A, B, (int)M, Cout_g, K, ep);
+}
+
+int conv_route(int H, int W, int Cin, int KH, int KW, int Cout, int stride, int pad, int groups) {
+  if (groups > 1) {
+    if (groups == Cin && groups == Cout) return kRouteDepthwise;
+    if (Cin / groups <= 64 && Cout / groups <= 128) return kRouteGroupedDirect;
+    return kRouteGroupedSplit;
+  }
+  if (KH == 1 && KW == 1) return kRoute1x1;
+  if (KH == 3 && KW == 3 && stride == 1 && pad == 1 && H >= 3 && W >= 3 && Cin >= 4 && Cout >= 4)
+    return (H >= 112 && W >= 112 && Cin >= 64 && Cout >= 64) ? kRouteWino43 : kRouteWino23;
+  return kRouteIm2col;
+}
+
+// conv2d_impl on device pointers; weights in the reference layouts.
+bool conv2d_dev(Call& c, const float* x, int N, int H, int W, int Cin, const float* w,
+                const float* bias, int KH, int KW, int Cout, int stride, int pad, int groups,
+                float* out, int act) {
+  const int route = conv_route(H, W, Cin, KH, KW, Cout, stride, pad, groups);
+  switch (route) {
+    case kRouteDepthwise:
+      return dw_dev(c, x, N, H, W, Cin, w, bias, KH, KW, stride, pad, out, act);
+    case kRouteGroupedDirect:
+      return group_dev(c, x, N, H, W, Cin, w, bias, KH, KW, Cout, stride, pad, groups, out, act);
+    case kRouteGroupedSplit: {
+      const int Cin_p = Cin / groups, Cout_p = Cout / groups;
+      for (int g = 0; g < groups; ++g) {
+        const float* wg = w + (size_t)g * Cout_p * KH * KW * Cin_p;
+        if (!conv_f32_dev(c, x, N, H, W, Cin, g * Cin_p, Cin_p, wg, Cout_p,
+                          bias ? bias + (size_t)g * Cout_p : nullptr, KH, KW, Cout_p, stride, pad,
+                          out + (size_t)g * Cout_p, Cout, act))
+          return false;
+      }
+      return true;
+    }
+    default:
+      return conv_f32_dev(c, x, N, H, W, Cin, 0, Cin, w, Cout, bias, KH, KW, Cout, stride, pad, out,
+                          Cout, act);
+  }
+}
+
+size_t conv_weight_elems(int Cin, int KH, int KW, int Cout, int groups) {
+  if (groups > 1 && groups == Cin && groups == Cout) return (size_t)Cin * KH * KW;
+  if (groups < 1) groups = 1;
+  return (size_t)KH * KW * (Cin / groups) * Cout;
+}
+
+}  // namespace acf
+
+using namespace acf;
+
+static void conv_api(const char* name, const float* input, int N, int H, int W, int Cin,
+                     const float* weight, const float* bias, int KH, int KW, int Cout, int stride,
+                     int pad, int groups, float* output, int act) {
+  if (!input || !weight || !output || N <= 0 || KH <= 0 || KW <= 0 || stride <= 0 || Cin <= 0 ||
+      Cout <= 0)
+    return;
+  if (groups < 1) groups = 1;
+  const int OH = (H + 2 * pad - KH) / stride + 1, OW = (W + 2 * pad - KW) / stride + 1;
+  if (OH <= 0 || OW <= 0) return;
+  Call c(name);
+  if (!c.ok()) return;
+  const float* dx = (const float*)c.in(input, (size_t)N * H * W * Cin * 4);
+  const float* dw =
+      (const float*)c.in(weight, conv_weight_elems(Cin, KH, KW, Cout, groups) * 4);
+  const float* db = bias ? (const float*)c.in(bias, (size_t)Cout * 4) : nullptr;
+  float* dout = (float*)c.out(output, (size_t)N * OH * OW * Cout * 4);
+  if (!c.ok()) return;
+  conv2d_dev(c, dx, N, H, W, Cin, dw, db, KH, KW, Cout, stride, pad, groups, dout, act);
+  c.finish();
+}
+
+extern "C" void acfun_conv2d(const float* input, int N, int H, int W, int Cin, const float* weight,
+                             const float* bias, int KH, int KW, int Cout, int stride, int pad,
+                             float* output) {
+  conv_api("acfun_conv2d", input, N, H, W, Cin, weight, bias, KH, KW, Cout, stride, pad, 1, output,
+           0);
+}
+
+extern "C" void acfun_conv2d_relu(const float* input, int N, int H, int W, int Cin,
+                                  const float* weight, const float* bias, int KH, int KW, int Cout,
+                                  int stride, int pad, float* output) {
+  conv_api("acfun_conv2d_relu", input, N, H, W, Cin, weight, bias, KH, KW, Cout, stride, pad, 1,
+           output, 1);
+}
+
+extern "C" void acfun_conv2d_g(const float* input, int N, int H, int W, int Cin,
+                               const float* weight, const float* bias, int KH, int KW, int Cout,
+                               int stride, int pad, int groups, float* output, int act) {
+  conv_api("acfun_conv2d_g", input, N, H, W, Cin, weight, bias, KH, KW, Cout, stride, pad,
+           groups > 1 ? groups : 1, output, act);
+}
+
+// internal.h:45-60 — the reference's Winograd entry points (3x3, s1, p1); here the same
+// implicit-GEMM convolution.
+static void wino_api(const char* name, const float* input, int N, int H, int W, int Cin,
+                     const float* weight, const float* bias, int Cout, float* output, int act) {
+  if (!input || !weight || !output || N <= 0 || H <= 0 || W <= 0 || Cin <= 0 || Cout <= 0) return;
+  Call c(name);
+  if (!c.ok()) return;
+  const float* dx = (const float*)c.in(input, (size_t)N * H * W * Cin * 4);
+  const float* dw = (const float*)c.in(weight, (size_t)9 * Cin * Cout * 4);
+  const float* db = bias ? (const float*)c.in(bias, (size_t)Cout * 4) : nullptr;
+  float* dout = (float*)c.out(output, (size_t)N * H * W * Cout * 4);
+  if (!c.ok()) return;
+  conv_f32_dev(c, dx, N, H, W, Cin, 0, Cin, dw, Cout, db, 3, 3, Cout, 1, 1, dout, Cout, act);
+  c.finish();
+}
+
+extern "C" void acfun_winograd_conv3x3(const float* input, int N, int H, int W, int Cin,
+                                       const float* weight, const float* bias, int Cout,
+                                       float* output, int act) {
+  wino_api("acfun_winograd_conv3x3", input, N, H, W, Cin, weight, bias, Cout, output, act);
+}
+
+extern "C" void acfun_winograd43_conv3x3(const float* input, int N, int H, int W, int Cin,
+                                         const float* weight, const float* bias, int Cout,
+                                         float* output, int act) {
+  wino_api("acfun_winograd43_conv3x3", input, N, H, W, Cin, weight, bias, Cout, output, act);
+}
+
+// acfun.h:92-97 (layers.cpp:19-36): FC = GEMM + bias (+ ReLU), fused into the drain.
+static void fc_api(const char* name, const float* input, int N, int Cin, const float* weight,
+                   const float* bias, int Cout, float* output, int act) {
+  if (!input || !weight || !output || N <= 0 || Cin <= 0 || Cout <= 0) return;
+  Call c(name);
+  if (!c.ok()) return;
+  const float* dx = (const float*)c.in(input, (size_t)N * Cin * 4);
+  const float* dw = (const float*)c.in(weight, (size_t)Cin * Cout * 4);
+  const float* db = bias ? (const float*)c.in(bias, (size_t)Cout * 4) : nullptr;
+  float* dout = (float*)c.out(output, (size_t)N * Cout * 4);
+  if (!c.ok()) return;
+  gemm_f32(c, dx, Cin, dw, Cout, N, Cout, Cin, dout, Cout, db, act);
+  c.finish();
+}
+
+extern "C" void acfun_fc(const float* input, int N, int Cin, const float* weight,
+                         const float* bias, int Cout, float* output) {
+  fc_api("acfun_fc", input, N, Cin, weight, bias, Cout, output, 0);
+}
+
+extern "C" void acfun_fc_relu(const float* input, int N, int Cin, const float* weight,
+                              const float* bias, int Cout, float* output) {
+  fc_api("acfun_fc_relu", input, N, Cin, weight, bias, Cout, output, 1);
+}

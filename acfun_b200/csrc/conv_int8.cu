@@ -1,0 +1,469 @@
+// conv_int8.cu — int8 convolution: router, quantisation kernels and the exact integer
+// convolution on tcgen05 kind::i8 tensor cores.
+//
+// Reference (hit-droid/Acfun): conv_int8.cpp:63-148 (router), winograd_int8.cpp:245-350,
+// conv_int8_direct.cpp:20-59, conv1x1_int8.cpp:21-36, int8_quantize_avx512.cpp:8-35.
+//
+// Every route of the reference computes an exact integer correlation of the u8 activations
+// (zero point 128, out-of-image taps read 128) with the s8 weights, then dequantises:
+//   direct / 1x1 / im2col routes: out = (float)acc * alpha[j] + beta[j]       (mul, then add)
+//   Winograd F(2,3) route:        out = fmaf(4*(float)(acc - 128*Sw[j]), wso[j], bias[j])
+// The Winograd route's transforms are exact in integers (G~ = 2G is integral, so the
+// output transform yields exactly 4x the centred correlation), which is why one integer
+// implicit GEMM serves every route bit-exactly; the routes differ only in the activation
+// rounding (round-half-even vs the Winograd path's half-away) and in the dequant formula.
+// Per-call scalars (max|x|, inv_s = 127/max, s_a = max/127) and per-channel factors are
+// derived on the device so a call never synchronises with the host mid-way.
+#include <float.h>
+#include <math.h>
+
+#include <vector>
+
+#include "api_export.cuh"
+#include "conv.cuh"
+#include "gemm.cuh"
+#include "ops.cuh"
+
+namespace acf {
+
+struct Int8Scalars {
+  unsigned maxa_bits;  // max|x| as float bits (non-negative floats order like unsigned)
+  float inv_s;         // 127 / maxa
+  float sa;            // maxa / 127
+  int zero;            // maxa < 1e-12: the reference writes an all-zero output
+};
+
+static int grid_n(Call& c, long long work) {
+  long long b = (work + 255) / 256, cap = (long long)c.sm_count() * 16;
+  return (int)(b < 1 ? 1 : (b > cap ? cap : b));
+}
+
+// conv_int8.cpp:75-77: maxa = max(maxa, |x|) (std::max keeps maxa when |x| is NaN)
+__global__ void k_absmax(const float* __restrict__ x, long long n, Int8Scalars* s) {
+  __shared__ float sh[32];
+  float m = 0.0f;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const float v = fabsf(x[i]);
+    m = (m < v) ? v : m;
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    const float u = __shfl_xor_sync(0xffffffffu, m, o);
+    m = (m < u) ? u : m;
+  }
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    m = threadIdx.x < (blockDim.x >> 5) ? sh[threadIdx.x] : 0.0f;
+    for (int o = 16; o > 0; o >>= 1) {
+      const float u = __shfl_xor_sync(0xffffffffu, m, o);
+      m = (m < u) ? u : m;
+    }
+    if (threadIdx.x == 0) atomicMax(&s->maxa_bits, __float_as_uint(m));
+  }
+}
+
+__global__ void k_int8_scalars(Int8Scalars* s) {
+  const float maxa = __uint_as_float(s->maxa_bits);
+  s->zero = maxa < 1e-12f ? 1 : 0;
+  s->inv_s = __fdiv_rn(127.0f, maxa);
+  s->sa = __fdiv_rn(maxa, 127.0f);
+}
+
+// Per output channel j (one warp each): Sw = sum_k wq[k][j]; alpha = sa*ws; beta =
+// bias - (alpha*128)*Sw (conv_int8.cpp:100-107, no contraction); wso = (sa*0.25)*ws
+// (winograd_int8.cpp:155).  sa comes from `s` when given, else from `sa_host`.
+__global__ void k_int8_colparams(const int8_t* __restrict__ wq, int K, int Cout,
+                                 const float* __restrict__ wscale, const float* __restrict__ bias,
+                                 const Int8Scalars* s, float sa_host, float* alpha, float* beta,
+                                 float* wso, int* Sw) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= Cout) return;
+  const int j = warp;
+  int sum = 0;
+  for (int k = lane; k < K; k += 32) sum += wq[(long long)k * Cout + j];
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  if (lane == 0) {
+    const float sa = s ? s->sa : sa_host;
+    const float a = __fmul_rn(sa, wscale[j]);
+    const float corr = __fmul_rn(__fmul_rn(a, 128.0f), (float)sum);
+    if (alpha) alpha[j] = a;
+    if (beta) beta[j] = __fsub_rn(bias ? bias[j] : 0.0f, corr);
+    if (wso) wso[j] = __fmul_rn(__fmul_rn(sa, 0.25f), wscale[j]);
+    if (Sw) Sw[j] = sum;
+  }
+}
+
+// lroundf semantics (ties away from zero), exact for |t| < 2^31
+__device__ __forceinline__ int round_half_away(float t) {
+  const float a = fabsf(t);
+  const float f = floorf(a);
+  const float r = (a - f >= 0.5f) ? f + 1.0f : f;
+  return (int)copysignf(r, t);
+}
+
+__device__ __forceinline__ uint8_t clamp_u8(int v) {
+  return (uint8_t)(v < 0 ? 0 : (v > 255 ? 255 : v));
+}
+
+// Activation quantisation (zp = 128) into a spatially padded NHWC buffer [N*Hp*Wp][Cpad];
+// border cells and padding channels hold the zero point.
+//   mode 0: cvt_rne(x*inv_s) + 128            (int8_quantize_avx512.cpp:16)
+//   mode 1: channels < Cin&~15: trunc(t + copysign(0.5, t)); tail channels: lroundf(t)
+//           (winograd_int8.cpp:306-325)
+__global__ void k_quant_pad_u8(const float* __restrict__ x, int N, int H, int W, int Cin, int pad,
+                               int Hp, int Wp, int Cpad, const Int8Scalars* s, float inv_host,
+                               int mode, uint8_t* __restrict__ dst) {
+  const float inv_s = s ? s->inv_s : inv_host;
+  const int cvec = Cin & ~15;
+  const long long total = (long long)N * Hp * Wp * Cpad;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int c = (int)(i % Cpad);
+    long long p = i / Cpad;
+    const int wp = (int)(p % Wp);
+    p /= Wp;
+    const int hp = (int)(p % Hp);
+    const int n = (int)(p / Hp);
+    const int ih = hp - pad, iw = wp - pad;
+    uint8_t q = 128;
+    if (c < Cin && ih >= 0 && ih < H && iw >= 0 && iw < W) {
+      const float t = __fmul_rn(x[(((long long)n * H + ih) * W + iw) * Cin + c], inv_s);
+      int v;
+      if (mode == 0) {
+        v = (fabsf(t) < 2147483648.0f) ? __float2int_rn(t) : (int)0x80000000;
+      } else if (c < cvec) {
+        const float r = __fadd_rn(t, copysignf(0.5f, t));
+        v = (fabsf(r) < 2147483648.0f) ? (int)truncf(r) : (int)0x80000000;
+      } else {
+        v = round_half_away(t);
+      }
+      q = clamp_u8((int)((unsigned)v + 128u));
+    }
+    dst[i] = q;
+  }
+}
+
+// pre-quantised u8 NHWC -> padded [N*Hp*Wp][Cpad] (border = zero point)
+__global__ void k_pad_u8(const uint8_t* __restrict__ xq, int N, int H, int W, int Cin, int pad,
+                         int Hp, int Wp, int Cpad, uint8_t* __restrict__ dst) {
+  const long long total = (long long)N * Hp * Wp * Cpad;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int c = (int)(i % Cpad);
+    long long p = i / Cpad;
+    const int wp = (int)(p % Wp);
+    p /= Wp;
+    const int hp = (int)(p % Hp);
+    const int n = (int)(p / Hp);
+    const int ih = hp - pad, iw = wp - pad;
+    uint8_t q = 128;
+    if (c < Cin && ih >= 0 && ih < H && iw >= 0 && iw < W)
+      q = xq[(((long long)n * H + ih) * W + iw) * Cin + c];
+    dst[i] = q;
+  }
+}
+
+// u8 im2col (im2col_u8, conv_int8.cpp:42-61): out-of-image taps hold the zero point
+__global__ void k_im2col_u8(const uint8_t* __restrict__ xq, int N, int H, int W, int Cin, int KH,
+                            int KW, int stride, int pad, int OH, int OW, int Kpad,
+                            uint8_t* __restrict__ dst) {
+  const long long total = (long long)N * OH * OW * Kpad;
+  const int K = KH * KW * Cin;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int k = (int)(i % Kpad);
+    long long m = i / Kpad;
+    const int ow = (int)(m % OW);
+    m /= OW;
+    const int oh = (int)(m % OH);
+    const int n = (int)(m / OH);
+    uint8_t q = 128;
+    if (k < K) {
+      const int tap = k / Cin, c = k - tap * Cin;
+      const int ih = oh * stride - pad + tap / KW, iw = ow * stride - pad + tap % KW;
+      if (ih >= 0 && ih < H && iw >= 0 && iw < W) q = xq[(((long long)n * H + ih) * W + iw) * Cin + c];
+    }
+    dst[i] = q;
+  }
+}
+
+// s8 weights [taps*Cin][Cout] -> [taps*Cpad][Np] with zero rows / columns in the padding
+__global__ void k_weights_s8(const int8_t* __restrict__ w, int taps, int Cin, int Cout, int Cpad,
+                             int Np, int8_t* __restrict__ dst) {
+  const long long total = (long long)taps * Cpad * Np;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int j = (int)(i % Np);
+    const long long r = i / Np;
+    const int tap = (int)(r / Cpad), c = (int)(r % Cpad);
+    dst[i] = (c < Cin && j < Cout) ? w[((long long)tap * Cin + c) * Cout + j] : (int8_t)0;
+  }
+}
+
+// Quantised input + exact integer conv + dequant epilogue.
+//   xf / xq: float input (quantised here with `qmode`, scalars from `s` or inv_host) or
+//            pre-quantised u8 input.
+struct Int8ConvArgs {
+  const float* xf = nullptr;
+  const uint8_t* xq = nullptr;
+  int qmode = 0;
+  const Int8Scalars* s = nullptr;
+  float inv_host = 0.0f;
+  Epi epi = Epi::F32_AB;
+  const float* f0 = nullptr;  // alpha | wso
+  const float* f1 = nullptr;  // beta | bias
+  const int* i0 = nullptr;    // Sw (Winograd epilogue)
+  const int* zero_flag = nullptr;
+};
+
+static bool int8_conv_gemm(Call& c, const Int8ConvArgs& a, int N, int H, int W, int Cin,
+                           const int8_t* wq, int KH, int KW, int Cout, int stride, int pad,
+                           float* out, int act) {
+  const int OH = (H + 2 * pad - KH) / stride + 1, OW = (W + 2 * pad - KW) / stride + 1;
+  if (OH <= 0 || OW <= 0) return true;
+  const int taps = KH * KW;
+  const int Np = (int)align_up((size_t)Cout, 16);
+  EpiParams ep{};
+  ep.C = out;
+  ep.ldc = Cout;
+  ep.f0 = a.f0;
+  ep.f1 = a.f1;
+  ep.i0 = a.i0;
+  ep.act = act;
+  ep.zero_flag = a.zero_flag;
+  uint8_t* xq_dense = nullptr;  // unpadded u8 input for the gather path
+  if (stride == 1 && Cin >= 32) {
+    // implicit GEMM over the zero-point-padded tensor
+    const int Hp = H + 2 * pad, Wp = W + 2 * pad, Cpad = (int)align_up((size_t)Cin, 128);
+    const long long rows = (long long)N * Hp * Wp;
+    uint8_t* A = (uint8_t*)c.scratch((size_t)rows * Cpad);
+    int8_t* B = (int8_t*)c.scratch((size_t)taps * Cpad * Np);
+    if (!A || !B) return false;
+    if (a.xf)
+      k_quant_pad_u8<<<grid_n(c, rows * Cpad), 256, 0, c.stream()>>>(
+          a.xf, N, H, W, Cin, pad, Hp, Wp, Cpad, a.s, a.inv_host, a.qmode, A);
+    else
+      k_pad_u8<<<grid_n(c, rows * Cpad), 256, 0, c.stream()>>>(a.xq, N, H, W, Cin, pad, Hp, Wp,
+                                                               Cpad, A);
+    k_weights_s8<<<grid_n(c, (long long)taps * Cpad * Np), 256, 0, c.stream()>>>(wq, taps, Cin, Cout,
+                                                                                Cpad, Np, B);
+    if (!c.launched("int8 implicit prep")) return false;
+    Operand Ao, Bo;
+    Ao.p = A;
+    Ao.ld = Cpad;
+    Bo.p = B;
+    Bo.ld = Np;
+    ep.remap = 1;
+    ep.img_rows = Hp * Wp;
+    ep.Wp = Wp;
+    ep.OH = OH;
+    ep.OW = OW;
+    ConvGeom cg{1, Cpad / 128, KW, Wp, Cpad, taps};
+    return gemm_launch(c, GemmKind::I8U, a.epi, Ao, Bo, (int)rows, Cout, taps * Cpad, ep, cg);
+  }
+  // explicit im2col over the quantised input
+  const uint8_t* src = a.xq;
+  if (a.xf) {
+    xq_dense = (uint8_t*)c.scratch((size_t)N * H * W * Cin);
+    if (!xq_dense) return false;
+    k_quant_pad_u8<<<grid_n(c, (long long)N * H * W * Cin), 256, 0, c.stream()>>>(
+        a.xf, N, H, W, Cin, 0, H, W, Cin, a.s, a.inv_host, a.qmode, xq_dense);
+    src = xq_dense;
+  }
+  const long long M = (long long)N * OH * OW;
+  const int K = taps * Cin, Kpad = (int)align_up((size_t)K, 16);
+  uint8_t* A = (uint8_t*)c.scratch((size_t)M * Kpad);
+  int8_t* B = (int8_t*)c.scratch((size_t)Kpad * Np);
+  if (!A || !B) return false;
+  k_im2col_u8<<<grid_n(c, M * Kpad), 256, 0, c.stream()>>>(src, N, H, W, Cin, KH, KW, stride, pad,
+                                                           OH, OW, Kpad, A);
+  k_weights_s8<<<grid_n(c, (long long)Kpad * Np), 256, 0, c.stream()>>>(wq, 1, K, Cout, Kpad, Np, B);
+  if (!c.launched("int8 im2col prep")) return false;
+  Operand Ao, Bo;
+  Ao.p = A;
+  Ao.ld = Kpad;
+  Bo.p = B;
+  Bo.ld = Np;
+  return gemm_launch(c, GemmKind::I8U, a.epi, Ao, Bo, (int)M, Cout, Kpad, ep);
+}
+
+static bool is_wino_route(int H, int W, int Cin, int KH, int KW, int Cout, int stride, int pad) {
+  return KH == 3 && KW == 3 && stride == 1 && pad == 1 && H >= 3 && W >= 3 && Cin >= 4 && Cout >= 4;
+}
+
+bool conv2d_int8_dev(Call& c, const float* x, int N, int H, int W, int Cin, const int8_t* wq,
+                     const float* wscale, const float* bias, int KH, int KW, int Cout, int stride,
+                     int pad, float* out, int act) {
+  const int K = KH * KW * Cin;
+  Int8Scalars* s = (Int8Scalars*)c.scratch(sizeof(Int8Scalars));
+  float* f0 = (float*)c.scratch((size_t)Cout * 4);
+  float* f1 = (float*)c.scratch((size_t)Cout * 4);
+  int* Sw = (int*)c.scratch((size_t)Cout * 4);
+  if (!s || !f0 || !f1 || !Sw) return false;
+  if (!ACF_CUDA_OK(cudaMemsetAsync(s, 0, sizeof(Int8Scalars), c.stream()))) return false;
+  const long long n = (long long)N * H * W * Cin;
+  k_absmax<<<grid_n(c, n), 256, 0, c.stream()>>>(x, n, s);
+  k_int8_scalars<<<1, 1, 0, c.stream()>>>(s);
+  const bool wino = is_wino_route(H, W, Cin, KH, KW, Cout, stride, pad);
+  // Winograd: f0 = wso, f1 = bias (or NULL); others: f0 = alpha, f1 = beta
+  k_int8_colparams<<<(Cout * 32 + 255) / 256, 256, 0, c.stream()>>>(
+      wq, K, Cout, wscale, bias, s, 0.0f, wino ? nullptr : f0, wino ? nullptr : f1,
+      wino ? f0 : nullptr, Sw);
+  if (!c.launched("int8 params")) return false;
+  Int8ConvArgs a;
+  a.xf = x;
+  a.s = s;
+  a.zero_flag = &s->zero;
+  if (wino) {
+    a.qmode = 1;
+    a.epi = Epi::I8_WINO;
+    a.f0 = f0;
+    a.f1 = bias;
+    a.i0 = Sw;
+  } else {
+    a.qmode = 0;
+    a.epi = Epi::F32_AB;
+    a.f0 = f0;
+    a.f1 = f1;
+  }
+  return int8_conv_gemm(c, a, N, H, W, Cin, wq, KH, KW, Cout, stride, pad, out, act);
+}
+
+}  // namespace acf
+
+using namespace acf;
+
+// conv_int8.cpp:24-37 — host-side: exact IEEE division + lroundf, like the reference.
+extern "C" void acfun_quantize_weights(const float* w, int K, int N, float* scales, int8_t* wq) {
+  if (!w || !scales || !wq || K <= 0 || N <= 0) return;
+  // device pointers are accepted too: stage through host memory
+  const bool dev_in = ptr_kind(w) == PtrKind::Device;
+  const bool dev_s = ptr_kind(scales) == PtrKind::Device;
+  const bool dev_q = ptr_kind(wq) == PtrKind::Device;
+  std::vector<float> hw, hs;
+  std::vector<int8_t> hq;
+  const float* W = w;
+  float* S = scales;
+  int8_t* Q = wq;
+  if (dev_in) {
+    hw.resize((size_t)K * N);
+    if (!ACF_CUDA_OK(cudaMemcpy(hw.data(), w, hw.size() * 4, cudaMemcpyDeviceToHost))) return;
+    W = hw.data();
+  }
+  if (dev_s) {
+    hs.resize(N);
+    S = hs.data();
+  }
+  if (dev_q) {
+    hq.resize((size_t)K * N);
+    Q = hq.data();
+  }
+  for (int j = 0; j < N; ++j) {
+    float maxa = 0.0f;
+    for (int k = 0; k < K; ++k) {
+      const float v = fabsf(W[(size_t)k * N + j]);
+      maxa = (maxa < v) ? v : maxa;
+    }
+    float s = maxa / 127.0f;
+    if (s <= 0.0f) s = 1.0f;
+    S[j] = s;
+    for (int k = 0; k < K; ++k) {
+      int v = (int)lroundf(W[(size_t)k * N + j] / s);
+      if (v > 127) v = 127;
+      else if (v < -128) v = -128;
+      Q[(size_t)k * N + j] = (int8_t)v;
+    }
+  }
+  if (dev_s) ACF_CUDA_OK(cudaMemcpy(scales, hs.data(), (size_t)N * 4, cudaMemcpyHostToDevice));
+  if (dev_q) ACF_CUDA_OK(cudaMemcpy(wq, hq.data(), (size_t)K * N, cudaMemcpyHostToDevice));
+}
+
+extern "C" void acfun_conv2d_int8(const float* input, int N, int H, int W, int Cin,
+                                  const int8_t* wq, const float* wscale, const float* bias, int KH,
+                                  int KW, int Cout, int stride, int pad, float s_in, float* output,
+                                  int act) {
+  (void)s_in;  // ignored, as in the reference (conv_int8.cpp:63-81)
+  if (!input || !wq || !wscale || !output || N <= 0 || Cin <= 0 || Cout <= 0 || KH <= 0 ||
+      KW <= 0 || stride <= 0)
+    return;
+  const int OH = (H + 2 * pad - KH) / stride + 1, OW = (W + 2 * pad - KW) / stride + 1;
+  if (OH <= 0 || OW <= 0) return;
+  Call c("acfun_conv2d_int8");
+  if (!c.ok()) return;
+  const float* dx = (const float*)c.in(input, (size_t)N * H * W * Cin * 4);
+  const int8_t* dw = (const int8_t*)c.in(wq, (size_t)KH * KW * Cin * Cout);
+  const float* ds = (const float*)c.in(wscale, (size_t)Cout * 4);
+  const float* db = bias ? (const float*)c.in(bias, (size_t)Cout * 4) : nullptr;
+  float* dout = (float*)c.out(output, (size_t)N * OH * OW * Cout * 4);
+  if (!c.ok()) return;
+  conv2d_int8_dev(c, dx, N, H, W, Cin, dw, ds, db, KH, KW, Cout, stride, pad, dout, act);
+  c.finish();
+}
+
+// internal.h:164 — pre-quantised u8 input, caller-supplied alpha / beta
+extern "C" void acfun_conv2d_int8_direct(const uint8_t* inQ, int N, int H, int W, int Cin,
+                                         const int8_t* wq, const float* alpha, const float* beta,
+                                         int KH, int KW, int Cout, int stride, int pad, int OH,
+                                         int OW, float* output, int act) {
+  if (!inQ || !wq || !alpha || !beta || !output || N <= 0 || Cin <= 0 || Cout <= 0 || KH <= 0 ||
+      KW <= 0 || stride <= 0 || OH <= 0 || OW <= 0)
+    return;
+  if (OH != (H + 2 * pad - KH) / stride + 1 || OW != (W + 2 * pad - KW) / stride + 1) {
+    set_error(kInvalid, "acfun_conv2d_int8_direct: OH/OW do not match the geometry");
+    return;
+  }
+  Call c("acfun_conv2d_int8_direct");
+  if (!c.ok()) return;
+  const uint8_t* dx = (const uint8_t*)c.in(inQ, (size_t)N * H * W * Cin);
+  const int8_t* dw = (const int8_t*)c.in(wq, (size_t)KH * KW * Cin * Cout);
+  const float* da = (const float*)c.in(alpha, (size_t)Cout * 4);
+  const float* db = (const float*)c.in(beta, (size_t)Cout * 4);
+  float* dout = (float*)c.out(output, (size_t)N * OH * OW * Cout * 4);
+  if (!c.ok()) return;
+  Int8ConvArgs a;
+  a.xq = dx;
+  a.epi = Epi::F32_AB;
+  a.f0 = da;
+  a.f1 = db;
+  int8_conv_gemm(c, a, N, H, W, Cin, dw, KH, KW, Cout, stride, pad, dout, act);
+  c.finish();
+}
+
+// internal.h:185 — 1x1 s1 p0 over A[M][K] = the fused int8 GEMM epilogue
+extern "C" void acfun_conv1x1_int8(const uint8_t* inQ, int M, int K, int Cout, const int8_t* wq,
+                                   const float* alpha, const float* beta, float* output, int act) {
+  acfun_gemm_int8_epi(M, Cout, K, inQ, wq, output, alpha, beta, act);
+}
+
+// internal.h:198 — Winograd F(2,3) int8 route with caller-supplied s_in / inv_s
+extern "C" void acfun_winograd_conv3x3_int8(const float* input, int N, int H, int W, int Cin,
+                                            const int8_t* wq, const float* wscale,
+                                            const float* bias, int Cout, float s_in, float inv_s,
+                                            float* output, int act) {
+  if (!input || !wq || !wscale || !output || N <= 0 || H <= 0 || W <= 0 || Cin <= 0 || Cout <= 0)
+    return;
+  Call c("acfun_winograd_conv3x3_int8");
+  if (!c.ok()) return;
+  const float* dx = (const float*)c.in(input, (size_t)N * H * W * Cin * 4);
+  const int8_t* dw = (const int8_t*)c.in(wq, (size_t)9 * Cin * Cout);
+  const float* ds = (const float*)c.in(wscale, (size_t)Cout * 4);
+  const float* db = bias ? (const float*)c.in(bias, (size_t)Cout * 4) : nullptr;
+  float* dout = (float*)c.out(output, (size_t)N * H * W * Cout * 4);
+  float* wso = (float*)c.scratch((size_t)Cout * 4);
+  int* Sw = (int*)c.scratch((size_t)Cout * 4);
+  if (!c.ok()) return;
+  k_int8_colparams<<<(Cout * 32 + 255) / 256, 256, 0, c.stream()>>>(
+      dw, 9 * Cin, Cout, ds, db, nullptr, s_in, nullptr, nullptr, wso, Sw);
+  if (!c.launched("int8 params")) return;
+  Int8ConvArgs a;
+  a.xf = dx;
+  a.qmode = 1;
+  a.inv_host = inv_s;
+  a.epi = Epi::I8_WINO;
+  a.f0 = wso;
+  a.f1 = db;
+  a.i0 = Sw;
+  int8_conv_gemm(c, a, N, H, W, Cin, dw, 3, 3, Cout, 1, 1, dout, act);
+  c.finish();
+}

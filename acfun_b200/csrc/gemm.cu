@@ -143,7 +143,7 @@ Operand to_tf32x2(Call& c, const float* src, int rows, int cols, long long lds) 
 // ------------------------------------------------------------------ launcher
 template <dev::MmaKind KIND, int BN, int STAGES, int NPASS, Epi EPI, bool AS>
 static bool launch_one(Call& c, const Operand& A, const Operand& B, int M, int N, int K,
-                       const EpiParams& ep) {
+                       const EpiParams& ep, const ConvGeom& cg) {
   using S = GemmShape<KIND, BN, STAGES, NPASS>;
   static_assert(S::SMEM <= 232448, "shared memory budget");
   const CUtensorMapDataType dt = (KIND == dev::MmaKind::I8) ? CU_TENSOR_MAP_DATA_TYPE_UINT8
@@ -151,13 +151,15 @@ static bool launch_one(Call& c, const Operand& A, const Operand& B, int M, int N
                                                                : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
   CUtensorMap ta, tb;
   const uint64_t E = S::ELEM;
+  const CUtensorMapSwizzle bswz =
+      (S::ELEM == 4) ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
   if (NPASS == 1) {
     const uint64_t dA[2] = {(uint64_t)K, (uint64_t)M}, sA[1] = {(uint64_t)A.ld * E};
     const uint32_t bA[2] = {(uint32_t)S::BKE, 128u};
     const uint64_t dB[2] = {(uint64_t)N, (uint64_t)K}, sB[1] = {(uint64_t)B.ld * E};
     const uint32_t bB[2] = {(uint32_t)(128 / S::ELEM), (uint32_t)S::BKE};
     if (!encode_tmap(&ta, dt, 2, A.p, dA, sA, bA, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !encode_tmap(&tb, dt, 2, B.p, dB, sB, bB, CU_TENSOR_MAP_SWIZZLE_128B)) {
+        !encode_tmap(&tb, dt, 2, B.p, dB, sB, bB, bswz)) {
       c.fail();
       return false;
     }
@@ -169,7 +171,7 @@ static bool launch_one(Call& c, const Operand& A, const Operand& B, int M, int N
     const uint64_t sB[2] = {(uint64_t)B.ld * E, (uint64_t)B.op_stride * E};
     const uint32_t bB[3] = {(uint32_t)(128 / S::ELEM), (uint32_t)S::BKE, 1u};
     if (!encode_tmap(&ta, dt, 3, A.p, dA, sA, bA, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !encode_tmap(&tb, dt, 3, B.p, dB, sB, bB, CU_TENSOR_MAP_SWIZZLE_128B)) {
+        !encode_tmap(&tb, dt, 3, B.p, dB, sB, bB, bswz)) {
       c.fail();
       return false;
     }
@@ -191,7 +193,7 @@ static bool launch_one(Call& c, const Operand& A, const Operand& B, int M, int N
     c.fail();
     return false;
   }
-  kern<<<grid, 192, S::SMEM, c.stream()>>>(ta, tb, ep, M, N, K, c.err());
+  kern<<<grid, 192, S::SMEM, c.stream()>>>(ta, tb, ep, cg, M, N, K, c.err());
   return c.launched("gemm_tc_kernel");
 }
 
@@ -199,8 +201,12 @@ static long long tiles(int M, int N, int bn) {
   return (long long)((M + 127) / 128) * ((N + bn - 1) / bn);
 }
 
+int gemm_bke(GemmKind kind) {
+  return kind == GemmKind::BF16 ? 64 : kind == GemmKind::TF32X3 ? 32 : 128;
+}
+
 bool gemm_launch(Call& c, GemmKind kind, Epi epi, const Operand& A, const Operand& B, int M,
-                 int N, int K, const EpiParams& ep) {
+                 int N, int K, const EpiParams& ep, const ConvGeom& cg) {
   if (!c.ok() || !A.p || !B.p) {
     c.fail();
     return false;
@@ -212,14 +218,14 @@ bool gemm_launch(Call& c, GemmKind kind, Epi epi, const Operand& A, const Operan
       const bool wide = N > 128 && tiles(M, N, 256) >= sms;
       switch (epi) {
         case Epi::S32:
-          return wide ? launch_one<MK::I8, 256, 4, 1, Epi::S32, false>(c, A, B, M, N, K, ep)
-                      : launch_one<MK::I8, 128, 6, 1, Epi::S32, false>(c, A, B, M, N, K, ep);
+          return wide ? launch_one<MK::I8, 256, 4, 1, Epi::S32, false>(c, A, B, M, N, K, ep, cg)
+                      : launch_one<MK::I8, 128, 6, 1, Epi::S32, false>(c, A, B, M, N, K, ep, cg);
         case Epi::F32_AB:
-          return wide ? launch_one<MK::I8, 256, 4, 1, Epi::F32_AB, false>(c, A, B, M, N, K, ep)
-                      : launch_one<MK::I8, 128, 6, 1, Epi::F32_AB, false>(c, A, B, M, N, K, ep);
+          return wide ? launch_one<MK::I8, 256, 4, 1, Epi::F32_AB, false>(c, A, B, M, N, K, ep, cg)
+                      : launch_one<MK::I8, 128, 6, 1, Epi::F32_AB, false>(c, A, B, M, N, K, ep, cg);
         case Epi::I8_WINO:
-          return wide ? launch_one<MK::I8, 256, 4, 1, Epi::I8_WINO, false>(c, A, B, M, N, K, ep)
-                      : launch_one<MK::I8, 128, 6, 1, Epi::I8_WINO, false>(c, A, B, M, N, K, ep);
+          return wide ? launch_one<MK::I8, 256, 4, 1, Epi::I8_WINO, false>(c, A, B, M, N, K, ep, cg)
+                      : launch_one<MK::I8, 128, 6, 1, Epi::I8_WINO, false>(c, A, B, M, N, K, ep, cg);
         default:
           break;
       }
@@ -228,25 +234,25 @@ bool gemm_launch(Call& c, GemmKind kind, Epi epi, const Operand& A, const Operan
     case GemmKind::I8S: {
       const bool wide = N > 128 && tiles(M, N, 256) >= sms;
       if (epi == Epi::S8_REQ)
-        return wide ? launch_one<MK::I8, 256, 4, 1, Epi::S8_REQ, true>(c, A, B, M, N, K, ep)
-                    : launch_one<MK::I8, 128, 6, 1, Epi::S8_REQ, true>(c, A, B, M, N, K, ep);
+        return wide ? launch_one<MK::I8, 256, 4, 1, Epi::S8_REQ, true>(c, A, B, M, N, K, ep, cg)
+                    : launch_one<MK::I8, 128, 6, 1, Epi::S8_REQ, true>(c, A, B, M, N, K, ep, cg);
       break;
     }
     case GemmKind::BF16: {
       if (epi != Epi::F32_BIAS) break;
       if (N > 128 && tiles(M, N, 256) >= sms)
-        return launch_one<MK::F16, 256, 4, 1, Epi::F32_BIAS, false>(c, A, B, M, N, K, ep);
+        return launch_one<MK::F16, 256, 4, 1, Epi::F32_BIAS, false>(c, A, B, M, N, K, ep, cg);
       if (N > 64 && tiles(M, N, 128) >= sms)
-        return launch_one<MK::F16, 128, 6, 1, Epi::F32_BIAS, false>(c, A, B, M, N, K, ep);
-      return launch_one<MK::F16, 64, 8, 1, Epi::F32_BIAS, false>(c, A, B, M, N, K, ep);
+        return launch_one<MK::F16, 128, 6, 1, Epi::F32_BIAS, false>(c, A, B, M, N, K, ep, cg);
+      return launch_one<MK::F16, 64, 8, 1, Epi::F32_BIAS, false>(c, A, B, M, N, K, ep, cg);
     }
     case GemmKind::TF32X3: {
       if (epi != Epi::F32_BIAS) break;
       if (N > 64 && tiles(M, N, 128) >= sms)
-        return launch_one<MK::TF32, 128, 3, 3, Epi::F32_BIAS, false>(c, A, B, M, N, K, ep);
+        return launch_one<MK::TF32, 128, 3, 3, Epi::F32_BIAS, false>(c, A, B, M, N, K, ep, cg);
       if (N > 32)
-        return launch_one<MK::TF32, 64, 4, 3, Epi::F32_BIAS, false>(c, A, B, M, N, K, ep);
-      return launch_one<MK::TF32, 32, 5, 3, Epi::F32_BIAS, false>(c, A, B, M, N, K, ep);
+        return launch_one<MK::TF32, 64, 4, 3, Epi::F32_BIAS, false>(c, A, B, M, N, K, ep, cg);
+      return launch_one<MK::TF32, 32, 5, 3, Epi::F32_BIAS, false>(c, A, B, M, N, K, ep, cg);
     }
   }
   set_error(kInvalid, "%s: unsupported GEMM kind/epilogue combination", c.name());

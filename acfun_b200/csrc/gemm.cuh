@@ -27,7 +27,10 @@ Operand to_tf32x2(Call& c, const float* src_dev, int rows, int cols, long long l
 enum class GemmKind { I8U, I8S, BF16, TF32X3 };
 
 // C-tile launch: chooses the tile width from the problem size and the SM count.
+// With cg.enabled, A is a padded NHWC tensor [rows][cpad] and B the weights
+// [taps][cpad][N] (implicit stride-1 convolution; K is then taps*cpad).
 bool gemm_launch(Call& c, GemmKind kind, Epi epi, const Operand& A, const Operand& B, int M,
-                 int N, int K, const EpiParams& ep);
+                 int N, int K, const EpiParams& ep, const ConvGeom& cg = ConvGeom{});
+int gemm_bke(GemmKind kind);  // K elements per pipeline block (128 bytes)
 
 }  // namespace acf

@@ -35,6 +35,20 @@ struct EpiParams {
   // output row (n*OH + oh)*OW + ow.
   int remap;
   int img_rows, Wp, OH, OW;
+  // when non-NULL and *zero_flag != 0 every stored value is 0 (int8 router: max|x| < 1e-12)
+  const int* zero_flag;
+};
+
+// Implicit convolution (stride 1) over a padded NHWC tensor viewed as A[rows][Cpad]:
+// K block kb = (tap, channel block); the A rows are shifted by kh*Wp + kw and the B rows
+// (weights [taps][Cpad][Cout]) start at tap*Cpad.
+struct ConvGeom {
+  int enabled;
+  int cblocks;  // Cpad / BKE
+  int KW;
+  int Wp;
+  int cpad;     // channels per tap in B
+  int taps;
 };
 
 template <dev::MmaKind KIND>
@@ -65,6 +79,11 @@ struct GemmShape {
   static constexpr int B_TILE = NCHUNK * CHUNK_B;
   static constexpr int STAGE = NOPS * (A_TILE + B_TILE);
   static constexpr int KSTEP_B = (32 / ELEM) * 128;    // B descriptor advance per MMA K-step
+  // MN-major 32-bit (tf32) operands only exist in the 128B swizzle with 32-byte atoms
+  // (4-row / 512-byte pattern, TMA SWIZZLE_128B_ATOM_32B); 8/16-bit use the 128B swizzle
+  // with 16-byte atoms (8-row / 1024-byte pattern).
+  static constexpr uint32_t B_LAYOUT = (ELEM == 4) ? dev::UMMA_SW128_B32 : dev::UMMA_SW128;
+  static constexpr int B_SBO = (ELEM == 4) ? 512 : 1024;
   static constexpr int SMEM = STAGES * STAGE + 1024 + 256;
   static constexpr int TMEM_COLS = BN;
   static_assert(BN * ELEM % 128 == 0, "B tile must be whole 128-byte chunks");
@@ -75,7 +94,7 @@ __device__ __forceinline__ float relu_max(float v) { return v > 0.0f ? v : 0.0f;
 
 template <Epi EPI>
 __device__ __forceinline__ void epi_store32(const EpiParams& ep, long long orow, int j0, int N,
-                                            const uint32_t (&r)[32]) {
+                                            const uint32_t (&r)[32], bool zero) {
   // compute 32 outputs for columns j0..j0+31 of output row `orow`
   const bool full = (j0 + 32 <= N);
   if constexpr (EPI == Epi::S32) {
@@ -133,7 +152,7 @@ __device__ __forceinline__ void epi_store32(const EpiParams& ep, long long orow,
         x = __fmaf_rn(__fmul_rn(4.0f, __int2float_rn(c)), ep.f0[jj], ep.f1 ? ep.f1[jj] : 0.0f);
       }
       if (ep.act) x = relu_max(x);
-      v[i] = x;
+      v[i] = zero ? 0.0f : x;
     }
     float* dst = reinterpret_cast<float*>(ep.C) + orow * ep.ldc + j0;
     if (full && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
@@ -150,7 +169,7 @@ __device__ __forceinline__ void epi_store32(const EpiParams& ep, long long orow,
 template <dev::MmaKind KIND, int BN, int STAGES, int NPASS, Epi EPI, bool A_SIGNED>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   EpiParams ep, int M, int N, int K, unsigned* err) {
+                   EpiParams ep, ConvGeom cg, int M, int N, int K, unsigned* err) {
   using S = GemmShape<KIND, BN, STAGES, NPASS>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -166,7 +185,7 @@ __global__ void __launch_bounds__(192, 1)
   const int lane = threadIdx.x & 31;
   const int m0 = blockIdx.x * S::BM;
   const int n0 = blockIdx.y * BN;
-  const int nkb = (K + S::BKE - 1) / S::BKE;
+  const int nkb = cg.enabled ? cg.taps * cg.cblocks : (K + S::BKE - 1) / S::BKE;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -202,23 +221,29 @@ __global__ void __launch_bounds__(192, 1)
       }
       uint8_t* st = smem + s * S::STAGE;
       dev::mbar_arrive_expect_tx(&full_bar[s], S::STAGE);
-      const int kx = kb * S::BKE;
+      int kx = kb * S::BKE, ay = m0, by = kb * S::BKE;
+      if (cg.enabled) {
+        const int tap = kb / cg.cblocks, cb = kb - tap * cg.cblocks;
+        kx = cb * S::BKE;
+        ay = m0 + (tap / cg.KW) * cg.Wp + (tap % cg.KW);
+        by = tap * cg.cpad + kx;
+      }
 #pragma unroll
       for (int op = 0; op < S::NOPS; ++op) {
         uint8_t* a_dst = st + op * S::A_TILE;
         uint8_t* b_dst = st + S::NOPS * S::A_TILE + op * S::B_TILE;
         if constexpr (S::NOPS == 1) {
-          dev::tma_load_2d(a_dst, &tmA, &full_bar[s], kx, m0);
+          dev::tma_load_2d(a_dst, &tmA, &full_bar[s], kx, ay);
 #pragma unroll
           for (int c = 0; c < S::NCHUNK; ++c)
             dev::tma_load_2d(b_dst + c * S::CHUNK_B, &tmB, &full_bar[s], n0 + c * (128 / S::ELEM),
-                             kx);
+                             by);
         } else {
-          dev::tma_load_3d(a_dst, &tmA, &full_bar[s], kx, m0, op);
+          dev::tma_load_3d(a_dst, &tmA, &full_bar[s], kx, ay, op);
 #pragma unroll
           for (int c = 0; c < S::NCHUNK; ++c)
             dev::tma_load_3d(b_dst + c * S::CHUNK_B, &tmB, &full_bar[s], n0 + c * (128 / S::ELEM),
-                             kx, op);
+                             by, op);
         }
       }
       ++issued;
@@ -254,8 +279,8 @@ __global__ void __launch_bounds__(192, 1)
       for (int ks = 0; ks < 4; ++ks) {
         if constexpr (NPASS == 1) {
           const uint64_t ad = dev::umma_sdesc(a_base + ks * 32, 16, 1024, dev::UMMA_SW128);
-          const uint64_t bd = dev::umma_sdesc(b_base + ks * S::KSTEP_B, S::CHUNK_B, 1024,
-                                              dev::UMMA_SW128);
+          const uint64_t bd = dev::umma_sdesc(b_base + ks * S::KSTEP_B, S::CHUNK_B, S::B_SBO,
+                                              S::B_LAYOUT);
           dev::umma<KIND>(tmem, ad, bd, idesc, (kb | ks) != 0);
         } else {
           // (a_op, b_op): lo*hi, hi*lo, hi*hi
@@ -265,7 +290,7 @@ __global__ void __launch_bounds__(192, 1)
             const uint64_t ad = dev::umma_sdesc(a_base + aop[p] * S::A_TILE + ks * 32, 16, 1024,
                                                 dev::UMMA_SW128);
             const uint64_t bd = dev::umma_sdesc(b_base + bop[p] * S::B_TILE + ks * S::KSTEP_B,
-                                                S::CHUNK_B, 1024, dev::UMMA_SW128);
+                                                S::CHUNK_B, S::B_SBO, S::B_LAYOUT);
             dev::umma<KIND>(tmem, ad, bd, idesc, (kb | ks | p) != 0);
           }
         }
@@ -286,6 +311,7 @@ __global__ void __launch_bounds__(192, 1)
     dev::tc_fence_after();
     if (ok && !*abort_flag) {
       const int r = m0 + q * 32 + lane;
+      const bool zero_out = ep.zero_flag && *ep.zero_flag;
       long long orow = r;
       bool store = r < M;
       if (ep.remap && store) {
@@ -300,7 +326,7 @@ __global__ void __launch_bounds__(192, 1)
         uint32_t v[32];
         dev::tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
         dev::tmem_ld_wait();
-        if (store) epi_store32<EPI>(ep, orow, n0 + c0, N, v);
+        if (store) epi_store32<EPI>(ep, orow, n0 + c0, N, v, zero_out);
       }
     }
   }

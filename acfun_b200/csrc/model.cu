@@ -1,0 +1,474 @@
+// model.cu — ACFUN0 loader, load-time fuser and the device-resident executor.
+//
+// Format and fusion rules follow hit-droid/Acfun src/model.cpp:
+//   parse   :106-196  magic "ACFUN0", u32 version, inC/inH/inW, num_layers, records
+//   fuse    :198-247  Conv/FC/ConvGrouped absorb [ReLU]? then [BN with ch == Cout] (folded
+//                     into weight/bias, :69-95); a ReLU followed by MaxPool is dropped
+//                     (:220-224, :232 — kept for parity although Pool(ReLU(x)) != Pool(x) for
+//                     all-negative windows); MaxPool absorbs a following ReLU (:241)
+//   execute :274-349  ping-pong buffers, FC flattens NHWC, Softmax over the whole per-image
+//                     tensor (:335), standalone ReLU / BN in place
+// Differences by design: records are bounds-checked (a truncated or corrupt file returns
+// NULL with error code 5 instead of reading past the blob), weights live on the GPU, and
+// acfun_model_infer_batch runs n images through each layer at once (batch-1 semantics per
+// image, Softmax per image).
+#include <math.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <memory>
+#include <mutex>
+#include <vector>
+
+#include "api_export.cuh"
+#include "conv.cuh"
+#include "ops.cuh"
+#include "runtime.cuh"
+
+namespace acf {
+
+struct MLayer {
+  int type = 0;
+  int p[8] = {0};
+  size_t wn = 0;
+  const float* w_host = nullptr;  // into the blob or into `owned`
+  const float* b_host = nullptr;
+  float* w = nullptr;  // device copies
+  float* b = nullptr;
+  int act = 0;
+  int post_relu = 0;
+};
+
+}  // namespace acf
+
+struct AcfunModel {
+  int inC = 0, inH = 0, inW = 0;
+  std::vector<acf::MLayer> layers;
+  std::vector<unsigned char> blob;
+  std::vector<std::unique_ptr<float[]>> owned;
+  int outSize = 0;
+  int device = 0;
+  float* dparams = nullptr;  // all weights / biases in one device allocation
+  float* buf[2] = {nullptr, nullptr};
+  size_t bufcap = 0;         // floats per buffer
+  std::mutex mu;
+};
+
+namespace acf {
+
+static bool rd_u32(const std::vector<unsigned char>& b, size_t& o, unsigned& v) {
+  if (o + 4 > b.size()) return false;
+  v = (unsigned)b[o] | ((unsigned)b[o + 1] << 8) | ((unsigned)b[o + 2] << 16) |
+      ((unsigned)b[o + 3] << 24);
+  o += 4;
+  return true;
+}
+
+static bool rd_f32(const std::vector<unsigned char>& b, size_t& o, size_t n, const float*& p) {
+  if (n > (b.size() - o) / 4 || o > b.size()) return false;
+  p = reinterpret_cast<const float*>(b.data() + o);
+  o += n * 4;
+  return true;
+}
+
+// model.cpp:69-95, group-aware; host arithmetic without contraction
+static void fold_bn(MLayer& F, const MLayer& bn, int Cout, AcfunModel* m) {
+  const int ch = bn.p[0];
+  const float* mean = bn.w_host;
+  const float* var = mean + ch;
+  const float* gamma = var + ch;
+  const float* beta = gamma + ch;
+  const int groups = F.p[5];
+  const int Cout_per = groups > 1 ? Cout / groups : Cout;
+  const size_t per_in = F.wn / (size_t)Cout;
+  std::unique_ptr<float[]> nw(new float[F.wn]), nb(new float[Cout]);
+  memcpy(nw.get(), F.w_host, F.wn * 4);
+  for (int c = 0; c < Cout; ++c) {
+    volatile float scale = gamma[c] / sqrtf(var[c] + 1e-5f);
+    volatile float ms = mean[c] * scale;
+    const float shift = beta[c] - ms;
+    const int gc = groups > 1 ? c / Cout_per : 0, oc = groups > 1 ? c % Cout_per : c;
+    for (size_t t = 0; t < per_in; ++t) nw[(size_t)gc * Cout_per * per_in + t * Cout_per + oc] *= scale;
+    volatile float bs = (F.b_host ? F.b_host[c] : 0.0f) * scale;
+    nb[c] = bs + shift;
+  }
+  F.w_host = nw.get();
+  F.b_host = nb.get();
+  m->owned.push_back(std::move(nw));
+  m->owned.push_back(std::move(nb));
+}
+
+static AcfunModel* load_blob(std::vector<unsigned char>&& blob) {
+  std::unique_ptr<AcfunModel> m(new AcfunModel());
+  m->blob = std::move(blob);
+  const auto& b = m->blob;
+  if (b.size() < 6 + 16 || memcmp(b.data(), "ACFUN0", 6) != 0) {
+    set_error(kFormat, "acfun_model_load: bad magic or short file");
+    return nullptr;
+  }
+  size_t o = 10;
+  unsigned inC, inH, inW, num;
+  rd_u32(b, o, inC);
+  rd_u32(b, o, inH);
+  rd_u32(b, o, inW);
+  rd_u32(b, o, num);
+  if (inC == 0 || inH == 0 || inW == 0 || inC > 65536 || inH > 65536 || inW > 65536) {
+    set_error(kFormat, "acfun_model_load: bad input dims %u x %u x %u", inC, inH, inW);
+    return nullptr;
+  }
+  m->inC = (int)inC;
+  m->inH = (int)inH;
+  m->inW = (int)inW;
+  std::vector<MLayer> raw;
+  raw.reserve(num < 100000 ? num : 100000);
+  int prevC = (int)inC;
+  auto bad = [&](unsigned i) {
+    set_error(kFormat, "acfun_model_load: layer %u truncated or malformed", i);
+    return (AcfunModel*)nullptr;
+  };
+  for (unsigned i = 0; i < num; ++i) {
+    MLayer L;
+    unsigned t;
+    if (!rd_u32(b, o, t)) return bad(i);
+    L.type = (int)t;
+    switch (t) {
+      case 1:
+      case 7: {
+        unsigned v[6] = {0, 0, 0, 0, 0, 1};
+        for (int k = 0; k < (t == 7 ? 6 : 5); ++k)
+          if (!rd_u32(b, o, v[k])) return bad(i);
+        if (!v[0] || !v[1] || !v[2] || !v[3] || !v[5] || v[0] > 64 || v[1] > 64 ||
+            v[2] > (1u << 20) || (t == 7 && (prevC % v[5] || v[2] % v[5])))
+          return bad(i);
+        for (int k = 0; k < 6; ++k) L.p[k] = (int)v[k];
+        if (t == 1) L.p[5] = 0;
+        L.wn = (size_t)v[0] * v[1] * prevC * v[2] / (t == 7 ? v[5] : 1);
+        if (!rd_f32(b, o, L.wn, L.w_host) || !rd_f32(b, o, v[2], L.b_host)) return bad(i);
+        L.p[6] = prevC;
+        prevC = (int)v[2];
+        break;
+      }
+      case 2: {
+        unsigned Cout, inDim;
+        if (!rd_u32(b, o, Cout) || !rd_u32(b, o, inDim) || !Cout || !inDim) return bad(i);
+        L.p[0] = (int)Cout;
+        L.p[1] = (int)inDim;
+        L.wn = (size_t)inDim * Cout;
+        if (!rd_f32(b, o, L.wn, L.w_host) || !rd_f32(b, o, Cout, L.b_host)) return bad(i);
+        prevC = (int)Cout;
+        break;
+      }
+      case 3:
+      case 5:
+        break;
+      case 4: {
+        unsigned v[3];
+        for (int k = 0; k < 3; ++k)
+          if (!rd_u32(b, o, v[k])) return bad(i);
+        if (!v[0] || !v[1]) return bad(i);
+        L.p[0] = (int)v[0];
+        L.p[1] = (int)v[1];
+        L.p[2] = (int)v[2];
+        break;
+      }
+      case 6: {
+        unsigned ch;
+        if (!rd_u32(b, o, ch) || !ch) return bad(i);
+        L.p[0] = (int)ch;
+        L.wn = (size_t)ch * 4;
+        if (!rd_f32(b, o, L.wn, L.w_host)) return bad(i);
+        break;
+      }
+      default:
+        set_error(kFormat, "acfun_model_load: unknown layer type %u at layer %u", t, i);
+        return nullptr;
+    }
+    raw.push_back(L);
+  }
+  // ---- fusion (model.cpp:198-247)
+  const int n = (int)raw.size();
+  std::vector<char> consumed(n, 0);
+  for (int i = 0; i < n; ++i) {
+    if (consumed[i]) continue;
+    MLayer& L = raw[i];
+    if (L.type == 1 || L.type == 2 || L.type == 7) {
+      MLayer F = L;
+      F.act = 0;
+      const int Cout = L.type == 2 ? L.p[0] : L.p[2];
+      int j = i + 1, relu_idx = -1;
+      if (j < n && raw[j].type == 3) relu_idx = j++;
+      if (j < n && raw[j].type == 6 && raw[j].p[0] == Cout) {
+        fold_bn(F, raw[j], Cout, m.get());
+        consumed[j] = 1;
+      }
+      if (relu_idx >= 0) {
+        consumed[relu_idx] = 1;
+        F.act = (j < n && raw[j].type == 4) ? 0 : 1;
+      }
+      m->layers.push_back(F);
+    } else if (L.type == 3) {
+      if (i + 1 < n && raw[i + 1].type == 4) {
+        consumed[i] = 1;
+        continue;
+      }
+      m->layers.push_back(L);
+    } else if (L.type == 4) {
+      MLayer F = L;
+      if (i + 1 < n && raw[i + 1].type == 3) {
+        F.post_relu = 1;
+        consumed[i + 1] = 1;
+      }
+      m->layers.push_back(F);
+    } else {
+      m->layers.push_back(L);
+    }
+  }
+  // ---- shape check and device upload
+  int H = m->inH, W = m->inW, C = m->inC;
+  size_t total = 0, maxact = (size_t)H * W * C;
+  for (auto& L : m->layers) {
+    if (L.type == 1 || L.type == 7) {
+      if (L.p[6] != C) {
+        set_error(kFormat, "acfun_model_load: channel mismatch");
+        return nullptr;
+      }
+      const int OH = (H + 2 * L.p[4] - L.p[0]) / L.p[3] + 1, OW = (W + 2 * L.p[4] - L.p[1]) / L.p[3] + 1;
+      if (OH <= 0 || OW <= 0) {
+        set_error(kFormat, "acfun_model_load: conv produces an empty map");
+        return nullptr;
+      }
+      H = OH;
+      W = OW;
+      C = L.p[2];
+      total += L.wn + (size_t)C;
+    } else if (L.type == 2) {
+      if ((size_t)L.p[1] != (size_t)H * W * C) {
+        set_error(kFormat, "acfun_model_load: FC inDim %d != %d", L.p[1], H * W * C);
+        return nullptr;
+      }
+      H = W = 1;
+      C = L.p[0];
+      total += L.wn + (size_t)C;
+    } else if (L.type == 4) {
+      const int OH = (H + 2 * L.p[2] - L.p[0]) / L.p[1] + 1, OW = (W + 2 * L.p[2] - L.p[0]) / L.p[1] + 1;
+      if (OH <= 0 || OW <= 0) {
+        set_error(kFormat, "acfun_model_load: pool produces an empty map");
+        return nullptr;
+      }
+      H = OH;
+      W = OW;
+    } else if (L.type == 6) {
+      total += L.wn;
+    }
+    const size_t a = (size_t)H * W * C;
+    if (a > maxact) maxact = a;
+  }
+  m->outSize = H * W * C;
+  m->bufcap = 0;
+  m->device = current_device();
+  DeviceState* ds = device_state();
+  if (!ds || !ACF_CUDA_OK(cudaSetDevice(m->device))) return nullptr;
+  if (!ACF_CUDA_OK(cudaMalloc(&m->dparams, (total ? total : 1) * 4))) return nullptr;
+  size_t off = 0;
+  for (auto& L : m->layers) {
+    if (L.wn) {
+      L.w = m->dparams + off;
+      if (!ACF_CUDA_OK(cudaMemcpy(L.w, L.w_host, L.wn * 4, cudaMemcpyHostToDevice))) return nullptr;
+      off += L.wn;
+    }
+    if (L.type == 1 || L.type == 7 || L.type == 2) {
+      const int Cout = L.type == 2 ? L.p[0] : L.p[2];
+      L.b = m->dparams + off;
+      if (!ACF_CUDA_OK(cudaMemcpy(L.b, L.b_host, (size_t)Cout * 4, cudaMemcpyHostToDevice)))
+        return nullptr;
+      off += Cout;
+    }
+  }
+  (void)maxact;
+  return m.release();
+}
+
+static size_t max_activation(const AcfunModel* m) {
+  int H = m->inH, W = m->inW, C = m->inC;
+  size_t mx = (size_t)H * W * C;
+  for (auto& L : m->layers) {
+    if (L.type == 1 || L.type == 7) {
+      H = (H + 2 * L.p[4] - L.p[0]) / L.p[3] + 1;
+      W = (W + 2 * L.p[4] - L.p[1]) / L.p[3] + 1;
+      C = L.p[2];
+    } else if (L.type == 2) {
+      H = W = 1;
+      C = L.p[0];
+    } else if (L.type == 4) {
+      H = (H + 2 * L.p[2] - L.p[0]) / L.p[1] + 1;
+      W = (W + 2 * L.p[2] - L.p[0]) / L.p[1] + 1;
+    }
+    const size_t a = (size_t)H * W * C;
+    if (a > mx) mx = a;
+  }
+  return mx;
+}
+
+// Runs `n` images (batch-1 semantics each) from device input `x` into device output `y`.
+static bool run_model(Call& c, AcfunModel* m, int n, const float* x, float* y) {
+  const size_t need = max_activation(m) * (size_t)n;
+  if (need > m->bufcap) {
+    cudaStreamSynchronize(c.stream());
+    cudaFree(m->buf[0]);
+    cudaFree(m->buf[1]);
+    m->buf[0] = m->buf[1] = nullptr;
+    m->bufcap = 0;
+    if (!ACF_CUDA_OK(cudaMalloc(&m->buf[0], need * 4)) ||
+        !ACF_CUDA_OK(cudaMalloc(&m->buf[1], need * 4))) {
+      c.fail();
+      return false;
+    }
+    m->bufcap = need;
+  }
+  int H = m->inH, W = m->inW, C = m->inC;
+  const float* cur = x;
+  int which = 0;
+  for (auto& L : m->layers) {
+    float* next = m->buf[which];
+    bool ok = true;
+    switch (L.type) {
+      case 1:
+      case 7: {
+        const int KH = L.p[0], KW = L.p[1], Cout = L.p[2], st = L.p[3], pd = L.p[4];
+        const int groups = L.type == 7 ? L.p[5] : 1;
+        ok = conv2d_dev(c, cur, n, H, W, C, L.w, L.b, KH, KW, Cout, st, pd, groups, next, L.act);
+        H = (H + 2 * pd - KH) / st + 1;
+        W = (W + 2 * pd - KW) / st + 1;
+        C = Cout;
+        cur = next;
+        which ^= 1;
+        break;
+      }
+      case 2: {
+        const int Cout = L.p[0], inDim = H * W * C;
+        ok = gemm_f32(c, cur, inDim, L.w, Cout, n, Cout, inDim, next, Cout, L.b, L.act);
+        H = W = 1;
+        C = Cout;
+        cur = next;
+        which ^= 1;
+        break;
+      }
+      case 3:
+        if (cur == x) {  // never write the caller's input: ReLU out of place
+          ok = ACF_CUDA_OK(cudaMemcpyAsync(next, cur, (size_t)n * H * W * C * 4,
+                                           cudaMemcpyDeviceToDevice, c.stream()));
+          cur = next;
+          which ^= 1;
+        }
+        ok = ok && relu_dev(c, const_cast<float*>(cur), (long long)n * H * W * C, 0);
+        break;
+      case 4: {
+        const int pool = L.p[0], st = L.p[1], pd = L.p[2];
+        ok = maxpool_dev(c, cur, n, H, W, C, pool, st, pd, next, L.post_relu);
+        H = (H + 2 * pd - pool) / st + 1;
+        W = (W + 2 * pd - pool) / st + 1;
+        cur = next;
+        which ^= 1;
+        break;
+      }
+      case 5:
+        ok = softmax_dev(c, cur, n, H * W * C, next);
+        cur = next;
+        which ^= 1;
+        break;
+      case 6: {
+        if (cur == x) {
+          ok = ACF_CUDA_OK(cudaMemcpyAsync(next, cur, (size_t)n * H * W * C * 4,
+                                           cudaMemcpyDeviceToDevice, c.stream()));
+          cur = next;
+          which ^= 1;
+        }
+        const int ch = L.p[0];
+        const size_t per = (size_t)H * W * C;
+        // per image: the reference's `spatial = size / channels` floor is per call
+        if (per % ch == 0) {
+          ok = ok && batchnorm_dev(c, const_cast<float*>(cur), (int)(per * n), ch, L.w, L.w + ch,
+                                   L.w + 2 * ch, L.w + 3 * ch, 1e-5f);
+        } else {
+          for (int k = 0; k < n && ok; ++k)
+            ok = batchnorm_dev(c, const_cast<float*>(cur) + per * k, (int)per, ch, L.w, L.w + ch,
+                               L.w + 2 * ch, L.w + 3 * ch, 1e-5f);
+        }
+        break;
+      }
+    }
+    if (!ok) {
+      c.fail();
+      return false;
+    }
+  }
+  return ACF_CUDA_OK(cudaMemcpyAsync(y, cur, (size_t)n * m->outSize * 4, cudaMemcpyDeviceToDevice,
+                                     c.stream()));
+}
+
+}  // namespace acf
+
+using namespace acf;
+
+extern "C" AcfunModel* acfun_model_load(const char* path) {
+  if (!path) return nullptr;
+  FILE* f = fopen(path, "rb");
+  if (!f) {
+    set_error(kInvalid, "acfun_model_load: cannot open %s", path);
+    return nullptr;
+  }
+  std::vector<unsigned char> blob;
+  fseek(f, 0, SEEK_END);
+  const long sz = ftell(f);
+  fseek(f, 0, SEEK_SET);
+  if (sz > 0) {
+    blob.resize((size_t)sz);
+    if (fread(blob.data(), 1, (size_t)sz, f) != (size_t)sz) {
+      fclose(f);
+      set_error(kFormat, "acfun_model_load: short read");
+      return nullptr;
+    }
+  }
+  fclose(f);
+  return load_blob(std::move(blob));
+}
+
+extern "C" void acfun_model_destroy(AcfunModel* m) {
+  if (!m) return;
+  cudaSetDevice(m->device);
+  cudaDeviceSynchronize();
+  cudaFree(m->dparams);
+  cudaFree(m->buf[0]);
+  cudaFree(m->buf[1]);
+  delete m;
+}
+
+extern "C" int acfun_model_output_size(AcfunModel* m) { return m ? m->outSize : 0; }
+
+extern "C" void acfun_model_input_dims(AcfunModel* m, int* Cin, int* Hin, int* Win) {
+  if (!m) return;
+  if (Cin) *Cin = m->inC;
+  if (Hin) *Hin = m->inH;
+  if (Win) *Win = m->inW;
+}
+
+extern "C" int acfun_model_infer_batch(AcfunModel* m, int n, const float* input, float* output) {
+  if (!m || n <= 0 || !input || !output) return 0;
+  std::lock_guard<std::mutex> g(m->mu);
+  tctx().device = m->device;
+  Call c("acfun_model_infer");
+  if (!c.ok()) return 0;
+  const size_t in_elems = (size_t)n * m->inH * m->inW * m->inC;
+  const float* dx = (const float*)c.in(input, in_elems * 4);
+  float* dy = (float*)c.out(output, (size_t)n * m->outSize * 4);
+  if (!c.ok()) return 0;
+  if (!run_model(c, m, n, dx, dy)) {
+    c.finish();
+    return 0;
+  }
+  return c.finish() ? m->outSize : 0;
+}
+
+extern "C" int acfun_model_infer(AcfunModel* m, const float* input, float* output) {
+  return acfun_model_infer_batch(m, 1, input, output);
+}

@@ -1,0 +1,74 @@
+"""GPU parity: acfun_model_load / acfun_model_infer(_batch) over ACFUN0 against the
+reference's golden outputs and the oracle executor."""
+import os
+
+import numpy as np
+import pytest
+
+from helpers import TOL_F32, max_rel
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def test_model_demo_golden(acf, tmp_path):
+    d = dict(np.load(os.path.join(GOLD, "model_demo.npz")))
+    p = tmp_path / "demo.acfun"
+    p.write_bytes(d["blob"].tobytes())
+    m = acf.Model(str(p))
+    assert m.in_dims == (32, 32, 3)
+    for k in range(d["x"].shape[0]):
+        y = m.infer(np.ascontiguousarray(d["x"][k]))
+        assert y.shape == d["out"][k].shape
+        assert max_rel(y, d["out"][k]) < TOL_F32
+    yb = m.infer_batch(np.ascontiguousarray(d["x"]))
+    assert max_rel(yb, d["out"]) < TOL_F32
+    m.close()
+
+
+def test_model_vgg_small_vs_oracle(acf, tmp_path):
+    from acfun_b200 import acfun0
+    from oracle.model_oracle import OracleModel
+    blob = acfun0.vgg11(seed=3, in_hw=64, width_div=8, fc_dims=(128, 64, 10)).tobytes()
+    p = tmp_path / "v.acfun"
+    p.write_bytes(blob)
+    m = acf.Model(str(p))
+    x = np.random.default_rng(4).uniform(0, 1, (3, 64, 64, 3)).astype(np.float32)
+    y = m.infer_batch(x)
+    om = OracleModel(blob)
+    for k in range(3):
+        assert max_rel(y[k], om.infer(x[k])) < TOL_F32
+
+
+def test_model_device_pointers(acf, tmp_path):
+    import torch
+    d = dict(np.load(os.path.join(GOLD, "model_demo.npz")))
+    p = tmp_path / "demo.acfun"
+    p.write_bytes(d["blob"].tobytes())
+    m = acf.Model(str(p))
+    x = torch.from_numpy(np.ascontiguousarray(d["x"])).cuda()
+    out = torch.empty((2, 10), device="cuda")
+    m.infer_batch(x, out)
+    acf.synchronize()
+    assert max_rel(out.cpu().numpy(), d["out"]) < TOL_F32
+
+
+@pytest.mark.parametrize("mutate", ["truncate", "magic", "type", "dims"])
+def test_model_load_rejects_corrupt_files(acf, tmp_path, mutate):
+    from acfun_b200 import acfun0
+    blob = bytearray(acfun0.demo_net(seed=1).tobytes())
+    if mutate == "truncate":
+        blob = blob[: len(blob) // 2]
+    elif mutate == "magic":
+        blob[0:6] = b"ACFUN9"
+    elif mutate == "type":
+        blob[26:30] = (99).to_bytes(4, "little")
+    elif mutate == "dims":
+        blob[10:14] = (0).to_bytes(4, "little")
+    p = tmp_path / "bad.acfun"
+    p.write_bytes(bytes(blob))
+    L = acf.lib()
+    assert not L.acfun_model_load(str(p).encode())
+    assert L.acfun_last_error_code() == 5
+    L.acfun_clear_error()
+    assert L.acfun_model_infer(None, None, None) == 0
