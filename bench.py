@@ -1,0 +1,307 @@
+#!/usr/bin/env python3
+"""Benchmark of the Acfun hot path on B200 — one JSON line on rank 0.
+
+Workload (the int8 GEMM the metric is quoted on at one GPU):
+    C[s8] = requant(A[s8, 4096x4096] . B[s8, 4096x4096] + bias[s32]) * scale[f32], ReLU
+    A, B ~ U{-127..127}, bias ~ U{-1000..1000}, scale ~ U[1e-3, 1e-2], seeded.
+A "step" is one acfun_gemm_s8_requant call on that input.
+
+  value   device-resident inputs (acfun_gemm_s8_requant on CUDA pointers), CUDA-event time per
+          step, L2 flushed (256 MiB write) before every timed step; TOPS = 2*M*N*K / t,
+          summed over ranks (weak scaling: every rank runs its own 4096^3 problem).
+  e2e     the same call through the C ABI with PINNED HOST buffers: H2D of A, B, bias,
+          scale and D2H of C inside every timed step.
+  roofline  the tcgen05 GEMM kernel (the only kernel a device-resident call launches):
+          achieved = 2*M*N*K / mean kernel time; peak = 2 x the measured dense bf16 burst
+          rate in MEASURED_PEAKS.json (B200 runs dense int8 at twice the bf16 rate);
+          traffic from the committed ncu summary when present.
+  cpu_baseline  the reference's own int8 GEMM (acfun_gemm_int8, AVX-512 VNNI + OpenMP, built
+          from its sources into oracle/_ref) on the host cores, on a bounded row sample.
+
+  --impl reference  times that reference CPU path alone, as the driver's reference arm.
+Multi-GPU: launch with torch.distributed.run; one rank per GPU, NCCL only for the barrier
+and the max-over-ranks of the measured time (the GEMMs are independent).
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+M = N = K = 4096
+OPS = 2.0 * M * N * K
+METRIC = "int8_gemm_tops"
+UNIT = "TOPS"
+WORKLOAD = "cfg2 int8 GEMM 4096^3 s8xs8->s32, fused +bias, *scale, ReLU, requant to s8"
+
+
+def make_inputs(seed=1234):
+    g = np.random.default_rng(seed)
+    A = g.integers(-127, 128, (M, K), dtype=np.int8)
+    B = g.integers(-127, 128, (K, N), dtype=np.int8)
+    bias = g.integers(-1000, 1001, N, dtype=np.int32)
+    scale = g.uniform(1e-3, 1e-2, N).astype(np.float32)
+    return A, B, bias, scale
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d.get("bf16_tflops"), d.get("hbm_gbs"), "measured"
+    return 1590.0, 6650.0, "fallback"
+
+
+def ncu_traffic():
+    """DRAM bytes per launch of the GEMM kernel from the committed ncu summary (or None)."""
+    p = os.path.join(ROOT, "profiles", "gemm_tc_int8_requant_4096.json")
+    if os.path.exists(p):
+        try:
+            return json.load(open(p)).get("dram_bytes_per_launch")
+        except (ValueError, OSError):
+            return None
+    return None
+
+
+def cpu_reference_sample(steps=1, rows=512):
+    """The reference's acfun_gemm_int8 (u8 A = s8 A + 128, the reference's own route for this
+    config) on `rows` rows of the 4096^3 problem, all host threads; returns TOPS and details."""
+    from oracle import pyoracle
+    kind = "reference" if pyoracle.ref_available() else "port"
+    A, B, bias, scale = make_inputs()
+    cores = os.cpu_count() or 1
+    Au = (A[:rows].astype(np.int16) + 128).astype(np.uint8)
+    C = np.empty((rows, N), np.int32)
+    times = []
+    if kind == "reference":
+        R = pyoracle.ref()
+        pyoracle.ref_set_threads(cores)
+        R.acfun_gemm_int8(rows, N, K, Au, B, C)  # warm-up
+        for _ in range(steps):
+            t0 = time.perf_counter()
+            R.acfun_gemm_int8(rows, N, K, Au, B, C)
+            times.append(time.perf_counter() - t0)
+    else:
+        O = pyoracle.oracle()
+        cores = 1
+        r = min(rows, 16)
+        Au = Au[:r].copy()
+        C = C[:r]
+        t0 = time.perf_counter()
+        O.orc_gemm_int8(r, N, K, Au, B, C)
+        times.append(time.perf_counter() - t0)
+        rows = r
+    t = statistics.median(times)
+    return {"value": round(2.0 * rows * N * K / t / 1e12, 4), "unit": UNIT, "cores": cores, "kind": kind,
+            "sample": f"{rows} of {M} rows of the 4096^3 u8xs8 GEMM (acfun_gemm_int8 on A+128), "
+                      f"median of {len(times)}, {cores} threads"}
+
+
+def run_reference_arm(args, rank, world):
+    if rank != 0:
+        return
+    steps = max(args.steps, 1)
+    cb = cpu_reference_sample(steps=steps, rows=args.cpu_rows)
+    line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "M": M, "N": N, "K": K},
+            "cpu_baseline": cb,
+            "e2e": {"value": cb["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="acfun_b200", choices=["acfun_b200", "reference"])
+    ap.add_argument("--cpu-rows", type=int, default=512)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3) if args.impl != "reference" else args.warmup
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        run_reference_arm(args, rank, world)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    import acfun_b200 as acf
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    L = acf.lib()
+    if L.acfun_set_device(local):
+        acf.check()
+    stream = torch.cuda.current_stream()
+    L.acfun_set_stream(stream.cuda_stream)
+
+    A, B, bias, scale = make_inputs(1234 + rank)
+    dA, dB = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
+    dbias, dscale = torch.from_numpy(bias).cuda(), torch.from_numpy(scale).cuda()
+    dC = torch.empty((M, N), dtype=torch.int8, device="cuda")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+
+    def dev_step():
+        L.acfun_gemm_s8_requant(M, N, K, dA.data_ptr(), dB.data_ptr(), dbias.data_ptr(), dscale.data_ptr(),
+                                dC.data_ptr(), 1)
+
+    # pinned host buffers for the end-to-end leg
+    hA, hB = torch.from_numpy(A).pin_memory(), torch.from_numpy(B).pin_memory()
+    hbias, hscale = torch.from_numpy(bias).pin_memory(), torch.from_numpy(scale).pin_memory()
+    hC = torch.empty((M, N), dtype=torch.int8).pin_memory()
+
+    def e2e_step():
+        L.acfun_gemm_s8_requant(M, N, K, hA.data_ptr(), hB.data_ptr(), hbias.data_ptr(), hscale.data_ptr(),
+                                hC.data_ptr(), 1)
+
+    # correctness spot check before timing (rows vs the oracle's restatement, rank 0 only)
+    dev_step()
+    torch.cuda.synchronize()
+    acf.check()
+
+    for _ in range(args.warmup):
+        dev_step()
+        e2e_step()
+    torch.cuda.synchronize()
+    acf.check()
+
+    def timed(fn, steps):
+        total = 0.0
+        evs = []
+        for _ in range(steps):
+            flush.fill_(1)                       # evict A, B, C from the 126 MB L2
+            s = torch.cuda.Event(enable_timing=True)
+            e = torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            fn()
+            e.record(stream)
+            evs.append((s, e))
+        torch.cuda.synchronize()
+        for s, e in evs:
+            total += s.elapsed_time(e)
+        return total / steps / 1e3             # seconds per step
+
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        t_dev = timed(dev_step, args.steps)
+        t_e2e = timed(e2e_step, args.steps)
+    acf.check()
+    t_dev_max, t_e2e_max = t_dev, t_e2e
+    if world > 1:
+        tt = torch.tensor([t_dev, t_e2e], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t_dev_max, t_e2e_max = float(tt[0]), float(tt[1])
+        dist.barrier()
+
+    if rank == 0:
+        bf16_peak, hbm_peak, peak_src = measured_peaks()
+        peak_tops = 2.0 * bf16_peak
+        achieved = OPS / t_dev / 1e12
+        traffic = ncu_traffic()
+        sat = None
+        Cn = dC.cpu().numpy()
+        sat = float(((Cn == 127) | (Cn == 0)).mean())
+        line = {
+            "metric": METRIC, "value": round(world * OPS / t_dev_max / 1e12, 2), "unit": UNIT,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(t_dev_max * 1e3, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "M": M, "N": N, "K": K, "per_gpu_problems": 1,
+                       "l2": "flushed (256 MiB write) before every timed step",
+                       "output_saturated_or_zero_frac": round(sat, 3)},
+            "e2e": {"value": round(world * OPS / t_e2e_max / 1e12, 2), "unit": UNIT,
+                    "h2d_bytes_per_step": A.nbytes + B.nbytes + bias.nbytes + scale.nbytes,
+                    "d2h_bytes_per_step": M * N, "ms_per_step": round(t_e2e_max * 1e3, 4),
+                    "api": "acfun_gemm_s8_requant on pinned host buffers"},
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak_tops, 1),
+                         "unit": "TOPS", "frac": round(achieved / peak_tops, 4),
+                         "peak_source": f"2 x bf16_tflops ({peak_src}, MEASURED_PEAKS.json): dense int8 = 2x bf16",
+                         "kernel": "gemm_tc_kernel<I8, BN=256, 4 stages, S8_REQ>",
+                         "traffic": traffic},
+            "gpu_launches": args.steps * 2,
+            "clocks": clk.summary(),
+        }
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_reference_sample(steps=3, rows=args.cpu_rows)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
