@@ -187,12 +187,14 @@ static bool launch_one(Call& c, const Operand& A, const Operand& B, int M, int N
     }
     attr_done[dv] = true;
   }
-  const dim3 grid((M + 127) / 128, (N + BN - 1) / BN);
-  if (grid.y > 65535u) {
-    set_error(kInvalid, "%s: N=%d too large", c.name(), N);
+  const long long tiles = (long long)((M + 127) / 128) * ((N + BN - 1) / BN);
+  if (tiles >= (1LL << 31)) {
+    set_error(kInvalid, "%s: problem too large", c.name());
     c.fail();
     return false;
   }
+  // persistent: one CTA per SM (1 CTA/SM by shared memory), tiles strided over the grid
+  const dim3 grid((unsigned)(tiles < c.sm_count() ? tiles : c.sm_count()));
   kern<<<grid, 192, S::SMEM, c.stream()>>>(ta, tb, ep, cg, M, N, K, c.err());
   return c.launched("gemm_tc_kernel");
 }

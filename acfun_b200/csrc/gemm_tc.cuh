@@ -85,17 +85,36 @@ struct GemmShape {
   static constexpr uint32_t B_LAYOUT = (ELEM == 4) ? dev::UMMA_SW128_B32 : dev::UMMA_SW128;
   static constexpr int B_SBO = (ELEM == 4) ? 512 : 1024;
   static constexpr int SMEM = STAGES * STAGE + 1024 + 256;
-  static constexpr int TMEM_COLS = BN;
+  static constexpr int TMEM_COLS = 2 * BN;  // double-buffered accumulator
   static_assert(BN * ELEM % 128 == 0, "B tile must be whole 128-byte chunks");
   static_assert(BN == 32 || BN == 64 || BN == 128 || BN == 256, "TMEM columns");
 };
 
 __device__ __forceinline__ float relu_max(float v) { return v > 0.0f ? v : 0.0f; }
 
+// 32 consecutive per-column parameters (broadcast across the warp): 8 x 16-byte loads when
+// the run is whole and aligned, guarded scalar loads otherwise.
+template <typename T>
+__device__ __forceinline__ void load_cols32(const T* p, int j0, int N, T (&o)[32]) {
+  if (j0 + 32 <= N && ((reinterpret_cast<uintptr_t>(p + j0) & 15) == 0)) {
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(p + j0 + i));
+      o[i] = __builtin_bit_cast(T, u.x);
+      o[i + 1] = __builtin_bit_cast(T, u.y);
+      o[i + 2] = __builtin_bit_cast(T, u.z);
+      o[i + 3] = __builtin_bit_cast(T, u.w);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) o[i] = (j0 + i < N) ? p[j0 + i] : T(0);
+  }
+}
+
 template <Epi EPI>
 __device__ __forceinline__ void epi_store32(const EpiParams& ep, long long orow, int j0, int N,
                                             const uint32_t (&r)[32], bool zero) {
-  // compute 32 outputs for columns j0..j0+31 of output row `orow`
+  // 32 outputs for columns j0..j0+31 of output row `orow`
   const bool full = (j0 + 32 <= N);
   if constexpr (EPI == Epi::S32) {
     int32_t* dst = reinterpret_cast<int32_t*>(ep.C) + orow * ep.ldc + j0;
@@ -108,21 +127,26 @@ __device__ __forceinline__ void epi_store32(const EpiParams& ep, long long orow,
         if (j0 + i < N) dst[i] = (int32_t)r[i];
     }
   } else if constexpr (EPI == Epi::S8_REQ) {
+    float sc[32];
+    int32_t bi[32];
+    load_cols32(ep.f0, j0, N, sc);
+    if (ep.i0) {
+      load_cols32(ep.i0, j0, N, bi);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) bi[i] = 0;
+    }
     uint32_t packed[8];
 #pragma unroll
     for (int i = 0; i < 32; i += 4) {
       uint32_t w = 0;
 #pragma unroll
       for (int t = 0; t < 4; ++t) {
-        const int j = j0 + i + t;
-        int q = 0;
-        if (j < N) {
-          int32_t s = (int32_t)((uint32_t)r[i + t] + (uint32_t)(ep.i0 ? ep.i0[j] : 0));
-          float v = __fmul_rn(__int2float_rn(s), ep.f0[j]);
-          if (ep.act) v = relu_max(v);
-          q = __float2int_rn(v);
-          q = q > 127 ? 127 : (q < -128 ? -128 : q);
-        }
+        const int32_t s = (int32_t)((uint32_t)r[i + t] + (uint32_t)bi[i + t]);
+        float v = __fmul_rn(__int2float_rn(s), sc[i + t]);
+        if (ep.act) v = relu_max(v);
+        int q = __float2int_rn(v);
+        q = q > 127 ? 127 : (q < -128 ? -128 : q);
         w |= (uint32_t)(q & 0xFF) << (8 * t);
       }
       packed[i / 4] = w;
@@ -136,20 +160,39 @@ __device__ __forceinline__ void epi_store32(const EpiParams& ep, long long orow,
         if (j0 + i < N) dst[i] = (int8_t)((packed[i / 4] >> (8 * (i % 4))) & 0xFF);
     }
   } else {
+    float p0[32], p1[32];
+    int32_t pi[32];
+    if constexpr (EPI == Epi::F32_AB) {
+      load_cols32(ep.f0, j0, N, p0);
+      load_cols32(ep.f1, j0, N, p1);
+    } else if constexpr (EPI == Epi::F32_BIAS) {
+      if (ep.f0) {
+        load_cols32(ep.f0, j0, N, p0);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) p0[i] = 0.0f;
+      }
+    } else {  // I8_WINO
+      load_cols32(ep.f0, j0, N, p0);
+      load_cols32(ep.i0, j0, N, pi);
+      if (ep.f1) {
+        load_cols32(ep.f1, j0, N, p1);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) p1[i] = 0.0f;
+      }
+    }
     float v[32];
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
-      const int j = j0 + i;
-      const int jj = j < N ? j : 0;
       float x;
       if constexpr (EPI == Epi::F32_AB) {
-        x = __fadd_rn(__fmul_rn(__int2float_rn((int32_t)r[i]), ep.f0[jj]), ep.f1[jj]);
+        x = __fadd_rn(__fmul_rn(__int2float_rn((int32_t)r[i]), p0[i]), p1[i]);
       } else if constexpr (EPI == Epi::F32_BIAS) {
-        x = __uint_as_float(r[i]);
-        if (ep.f0) x = __fadd_rn(x, ep.f0[jj]);
+        x = __fadd_rn(__uint_as_float(r[i]), p0[i]);
       } else {  // I8_WINO
-        int32_t c = (int32_t)r[i] - 128 * ep.i0[jj];
-        x = __fmaf_rn(__fmul_rn(4.0f, __int2float_rn(c)), ep.f0[jj], ep.f1 ? ep.f1[jj] : 0.0f);
+        const int32_t c = (int32_t)r[i] - 128 * pi[i];
+        x = __fmaf_rn(__fmul_rn(4.0f, __int2float_rn(c)), p0[i], p1[i]);
       }
       if (ep.act) x = relu_max(x);
       v[i] = zero ? 0.0f : x;
@@ -166,6 +209,10 @@ __device__ __forceinline__ void epi_store32(const EpiParams& ep, long long orow,
   }
 }
 
+// Persistent kernel: grid = min(#tiles, #SMs); CTA b walks tiles b, b+grid, ...  The smem
+// ring runs continuously across tiles, and the accumulator is double-buffered in TMEM
+// (2 x BN columns): the UMMA warp fills buffer i&1 while the epilogue warps drain the
+// other, so a tile's epilogue overlaps the next tile's MMAs.
 template <dev::MmaKind KIND, int BN, int STAGES, int NPASS, Epi EPI, bool A_SIGNED>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -176,15 +223,17 @@ __global__ void __launch_bounds__(192, 1)
                                              ~uintptr_t(1023));
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * S::STAGE);
   uint64_t* empty_bar = full_bar + STAGES;
-  uint64_t* done_bar = empty_bar + STAGES;   // accumulator complete
-  uint64_t* drain_bar = done_bar + 1;        // error-path MMA drain
+  uint64_t* tfull_bar = empty_bar + STAGES;   // [2] accumulator buffer ready for the epilogue
+  uint64_t* tempty_bar = tfull_bar + 2;       // [2] accumulator buffer drained
+  uint64_t* drain_bar = tempty_bar + 2;       // error-path MMA drain
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * S::BM;
-  const int n0 = blockIdx.y * BN;
+  const int tiles_m = (M + S::BM - 1) / S::BM;
+  const int tiles_n = (N + BN - 1) / BN;
+  const int num_tiles = tiles_m * tiles_n;
   const int nkb = cg.enabled ? cg.taps * cg.cblocks : (K + S::BKE - 1) / S::BKE;
 
   if (threadIdx.x == 0) {
@@ -192,7 +241,10 @@ __global__ void __launch_bounds__(192, 1)
       dev::mbar_init(&full_bar[s], 1);
       dev::mbar_init(&empty_bar[s], 1);
     }
-    dev::mbar_init(done_bar, 1);
+    for (int b = 0; b < 2; ++b) {
+      dev::mbar_init(&tfull_bar[b], 1);
+      dev::mbar_init(&tempty_bar[b], 4);  // one arrive per epilogue warp
+    }
     dev::mbar_init(drain_bar, 1);
     *abort_flag = 0;
     dev::fence_mbar_init();
@@ -210,49 +262,50 @@ __global__ void __launch_bounds__(192, 1)
 
   if (warp == 0 && lane == 0) {
     // ---------------- TMA producer
-    int issued = 0;
-    for (int kb = 0; kb < nkb; ++kb) {
-      const int s = kb % STAGES;
-      const uint32_t ph = (kb / STAGES) & 1;
-      if (*abort_flag) break;
-      if (!dev::mbar_wait(&empty_bar[s], ph ^ 1, err)) {
-        *abort_flag = 1;
-        break;
-      }
-      uint8_t* st = smem + s * S::STAGE;
-      dev::mbar_arrive_expect_tx(&full_bar[s], S::STAGE);
-      int kx = kb * S::BKE, ay = m0, by = kb * S::BKE;
-      if (cg.enabled) {
-        const int tap = kb / cg.cblocks, cb = kb - tap * cg.cblocks;
-        kx = cb * S::BKE;
-        ay = m0 + (tap / cg.KW) * cg.Wp + (tap % cg.KW);
-        by = tap * cg.cpad + kx;
-      }
+    uint32_t it = 0;  // global K-block counter (ring position)
+    for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+      const int m0 = (t / tiles_n) * S::BM, n0 = (t % tiles_n) * BN;
+      for (int kb = 0; kb < nkb; ++kb, ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        if (*abort_flag || !dev::mbar_wait(&empty_bar[s], ph ^ 1, err)) {
+          *abort_flag = 1;
+          break;
+        }
+        uint8_t* st = smem + s * S::STAGE;
+        dev::mbar_arrive_expect_tx(&full_bar[s], S::STAGE);
+        int kx = kb * S::BKE, ay = m0, by = kb * S::BKE;
+        if (cg.enabled) {
+          const int tap = kb / cg.cblocks, cb = kb - tap * cg.cblocks;
+          kx = cb * S::BKE;
+          ay = m0 + (tap / cg.KW) * cg.Wp + (tap % cg.KW);
+          by = tap * cg.cpad + kx;
+        }
 #pragma unroll
-      for (int op = 0; op < S::NOPS; ++op) {
-        uint8_t* a_dst = st + op * S::A_TILE;
-        uint8_t* b_dst = st + S::NOPS * S::A_TILE + op * S::B_TILE;
-        if constexpr (S::NOPS == 1) {
-          dev::tma_load_2d(a_dst, &tmA, &full_bar[s], kx, ay);
+        for (int op = 0; op < S::NOPS; ++op) {
+          uint8_t* a_dst = st + op * S::A_TILE;
+          uint8_t* b_dst = st + S::NOPS * S::A_TILE + op * S::B_TILE;
+          if constexpr (S::NOPS == 1) {
+            dev::tma_load_2d(a_dst, &tmA, &full_bar[s], kx, ay);
 #pragma unroll
-          for (int c = 0; c < S::NCHUNK; ++c)
-            dev::tma_load_2d(b_dst + c * S::CHUNK_B, &tmB, &full_bar[s], n0 + c * (128 / S::ELEM),
-                             by);
-        } else {
-          dev::tma_load_3d(a_dst, &tmA, &full_bar[s], kx, ay, op);
+            for (int c = 0; c < S::NCHUNK; ++c)
+              dev::tma_load_2d(b_dst + c * S::CHUNK_B, &tmB, &full_bar[s],
+                               n0 + c * (128 / S::ELEM), by);
+          } else {
+            dev::tma_load_3d(a_dst, &tmA, &full_bar[s], kx, ay, op);
 #pragma unroll
-          for (int c = 0; c < S::NCHUNK; ++c)
-            dev::tma_load_3d(b_dst + c * S::CHUNK_B, &tmB, &full_bar[s], n0 + c * (128 / S::ELEM),
-                             by, op);
+            for (int c = 0; c < S::NCHUNK; ++c)
+              dev::tma_load_3d(b_dst + c * S::CHUNK_B, &tmB, &full_bar[s],
+                               n0 + c * (128 / S::ELEM), by, op);
+          }
         }
       }
-      ++issued;
     }
     if (*abort_flag) {
       // drain copies that may still be in flight before the CTA releases its smem
-      const int first = issued > STAGES ? issued - STAGES : 0;
-      for (int kb = first; kb < issued; ++kb)
-        dev::mbar_wait(&full_bar[kb % STAGES], (kb / STAGES) & 1, nullptr, 200000000ull);
+      const uint32_t first = it > (uint32_t)STAGES ? it - STAGES : 0;
+      for (uint32_t k = first; k < it; ++k)
+        dev::mbar_wait(&full_bar[k % STAGES], (k / STAGES) & 1, nullptr, 200000000ull);
     }
   } else if (warp == 1 && lane == 0) {
     // ---------------- UMMA issuer
@@ -264,52 +317,66 @@ __global__ void __launch_bounds__(192, 1)
     constexpr uint32_t idesc = dev::umma_idesc(c_fmt, a_fmt, b_fmt, 0u, 1u, 128u, (uint32_t)BN);
     const uint32_t smem_base = dev::smem_u32(smem);
     bool ok = true;
-    for (int kb = 0; kb < nkb; ++kb) {
-      const int s = kb % STAGES;
-      const uint32_t ph = (kb / STAGES) & 1;
-      if (*abort_flag || !dev::mbar_wait(&full_bar[s], ph, err)) {
-        *abort_flag = 1;
+    uint32_t it = 0, local = 0;
+    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local) {
+      const uint32_t buf = local & 1, use = local >> 1;
+      if (!dev::mbar_wait(&tempty_bar[buf], (use & 1) ^ 1, err)) {
         ok = false;
         break;
       }
       dev::tc_fence_after();
-      const uint32_t a_base = smem_base + s * S::STAGE;
-      const uint32_t b_base = a_base + S::NOPS * S::A_TILE;
+      const uint32_t d_tmem = tmem + buf * BN;
+      for (int kb = 0; kb < nkb; ++kb, ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        if (*abort_flag || !dev::mbar_wait(&full_bar[s], ph, err)) {
+          ok = false;
+          break;
+        }
+        dev::tc_fence_after();
+        const uint32_t a_base = smem_base + s * S::STAGE;
+        const uint32_t b_base = a_base + S::NOPS * S::A_TILE;
 #pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
-        if constexpr (NPASS == 1) {
-          const uint64_t ad = dev::umma_sdesc(a_base + ks * 32, 16, 1024, dev::UMMA_SW128);
-          const uint64_t bd = dev::umma_sdesc(b_base + ks * S::KSTEP_B, S::CHUNK_B, S::B_SBO,
-                                              S::B_LAYOUT);
-          dev::umma<KIND>(tmem, ad, bd, idesc, (kb | ks) != 0);
-        } else {
-          // (a_op, b_op): lo*hi, hi*lo, hi*hi
-          const int aop[3] = {1, 0, 0}, bop[3] = {0, 1, 0};
+        for (int ks = 0; ks < 4; ++ks) {
+          if constexpr (NPASS == 1) {
+            const uint64_t ad = dev::umma_sdesc(a_base + ks * 32, 16, 1024, dev::UMMA_SW128);
+            const uint64_t bd = dev::umma_sdesc(b_base + ks * S::KSTEP_B, S::CHUNK_B, S::B_SBO,
+                                                S::B_LAYOUT);
+            dev::umma<KIND>(d_tmem, ad, bd, idesc, (kb | ks) != 0);
+          } else {
+            // (a_op, b_op): lo*hi, hi*lo, hi*hi
+            const int aop[3] = {1, 0, 0}, bop[3] = {0, 1, 0};
 #pragma unroll
-          for (int p = 0; p < 3; ++p) {
-            const uint64_t ad = dev::umma_sdesc(a_base + aop[p] * S::A_TILE + ks * 32, 16, 1024,
-                                                dev::UMMA_SW128);
-            const uint64_t bd = dev::umma_sdesc(b_base + bop[p] * S::B_TILE + ks * S::KSTEP_B,
-                                                S::CHUNK_B, S::B_SBO, S::B_LAYOUT);
-            dev::umma<KIND>(tmem, ad, bd, idesc, (kb | ks | p) != 0);
+            for (int p = 0; p < 3; ++p) {
+              const uint64_t ad = dev::umma_sdesc(a_base + aop[p] * S::A_TILE + ks * 32, 16, 1024,
+                                                  dev::UMMA_SW128);
+              const uint64_t bd = dev::umma_sdesc(b_base + bop[p] * S::B_TILE + ks * S::KSTEP_B,
+                                                  S::CHUNK_B, S::B_SBO, S::B_LAYOUT);
+              dev::umma<KIND>(d_tmem, ad, bd, idesc, (kb | ks | p) != 0);
+            }
           }
         }
+        dev::umma_commit(&empty_bar[s]);
       }
-      dev::umma_commit(&empty_bar[s]);
+      if (ok) dev::umma_commit(&tfull_bar[buf]);
     }
-    if (ok) {
-      dev::umma_commit(done_bar);
-    } else {
+    if (!ok) {
+      *abort_flag = 1;
       dev::umma_commit(drain_bar);
       dev::mbar_wait(drain_bar, 0, nullptr, 200000000ull);
-      dev::mbar_arrive(done_bar);  // release the epilogue warps (they see abort_flag)
+      dev::mbar_arrive(&tfull_bar[0]);  // release epilogue warps (they see abort_flag)
+      dev::mbar_arrive(&tfull_bar[1]);
     }
   } else if (warp >= 2) {
     // ---------------- epilogue
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
-    const bool ok = dev::mbar_wait(done_bar, 0, err);
-    dev::tc_fence_after();
-    if (ok && !*abort_flag) {
+    uint32_t local = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+      const uint32_t buf = local & 1, use = local >> 1;
+      const bool ok = dev::mbar_wait(&tfull_bar[buf], use & 1, err);
+      dev::tc_fence_after();
+      if (!ok || *abort_flag) break;
+      const int m0 = (t / tiles_n) * S::BM, n0 = (t % tiles_n) * BN;
       const int r = m0 + q * 32 + lane;
       const bool zero_out = ep.zero_flag && *ep.zero_flag;
       long long orow = r;
@@ -324,10 +391,13 @@ __global__ void __launch_bounds__(192, 1)
       for (int c0 = 0; c0 < BN; c0 += 32) {
         if (n0 + c0 >= N) break;  // warp-uniform
         uint32_t v[32];
-        dev::tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
+        dev::tmem_ld32(tmem + buf * BN + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
         dev::tmem_ld_wait();
         if (store) epi_store32<EPI>(ep, orow, n0 + c0, N, v, zero_out);
       }
+      dev::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) dev::mbar_arrive(&tempty_bar[buf]);
     }
   }
 

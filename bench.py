@@ -53,7 +53,8 @@ def make_inputs(seed=1234):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks / throttle reasons, sampled every 100 ms (line-buffered into a file)
+    for the whole timed region, plus synchronous samples taken while queued work runs."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -62,22 +63,27 @@ class ClockSampler:
     def __init__(self, index):
         self.index = index
         self.proc = None
-        self.lines = []
+        self.extra = []
+        import tempfile
+        self.path = tempfile.mktemp(prefix="acfun_clocks_", suffix=".csv")
 
     def __enter__(self):
         try:
+            self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
+                ["stdbuf", "-oL", "nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "100"], stdout=self.fh, stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def sample_now(self):
+        try:
+            out = subprocess.run(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                  "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=10)
+            self.extra += [ln for ln in out.stdout.splitlines() if ln.strip()]
+        except (OSError, subprocess.TimeoutExpired):
+            pass
 
     def __exit__(self, *a):
         if self.proc:
@@ -86,11 +92,18 @@ class ClockSampler:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
+            self.fh.close()
 
     def summary(self):
+        lines = list(self.extra)
+        try:
+            lines += open(self.path).read().splitlines()
+            os.unlink(self.path)
+        except OSError:
+            pass
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in lines:
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue
@@ -176,7 +189,7 @@ def run_reference_arm(args, rank, world):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="acfun_b200", choices=["acfun_b200", "reference"])
     ap.add_argument("--cpu-rows", type=int, default=512)
@@ -237,10 +250,12 @@ def main():
     torch.cuda.synchronize()
     acf.check()
 
-    def timed(fn, steps):
+    def timed(fn, steps, clk=None):
         total = 0.0
         evs = []
-        for _ in range(steps):
+        for i in range(steps):
+            if clk is not None and i == steps // 2:
+                clk.sample_now()                 # the GPU is busy with the queued steps
             flush.fill_(1)                       # evict A, B, C from the 126 MB L2
             s = torch.cuda.Event(enable_timing=True)
             e = torch.cuda.Event(enable_timing=True)
@@ -257,7 +272,7 @@ def main():
         dist.barrier()
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
-        t_dev = timed(dev_step, args.steps)
+        t_dev = timed(dev_step, args.steps, clk)
         t_e2e = timed(e2e_step, args.steps)
     acf.check()
     t_dev_max, t_e2e_max = t_dev, t_e2e
