@@ -24,6 +24,11 @@ Operand to_bf16(Call& c, const float* src_dev, int rows, int cols, long long lds
 // fp32 -> [2][rows][ldp] (hi = tf32-rounded, lo = tf32-rounded residual) for 3xTF32.
 Operand to_tf32x2(Call& c, const float* src_dev, int rows, int cols, long long lds);
 
+// fp32 [rows][cols] -> hi/lo pair at dst / dst + op_stride, row pitch ldp (multiple of 4),
+// zero in the padding columns (defined in gemm.cu, used by to_tf32x2).
+__global__ void k_to_tf32x2(const float* __restrict__ src, long long lds, int rows, int cols,
+                            float* __restrict__ dst, long long ldp, long long op_stride);
+
 enum class GemmKind { I8U, I8S, BF16, TF32X3 };
 
 // C-tile launch: chooses the tile width from the problem size and the SM count.

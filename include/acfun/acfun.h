@@ -120,6 +120,19 @@ int acfun_model_infer_batch(AcfunModel* m, int n, const float* input, float* out
 void acfun_gemm_s8_requant(int M, int N, int K, const int8_t* A, const int8_t* B,
                            const int32_t* bias, const float* scale, int8_t* C, int act);
 
+/* acfun_gemm_epi for callers that cannot allocate device memory (no counterpart in the
+ * reference).  Such callers exist: processes that reserve all device memory up front in
+ * their own pool, code running in an out-of-memory handler or allocator callback, and
+ * latency-critical loops where cudaMalloc/cudaFree would synchronise the device.  Same
+ * result as acfun_gemm_epi, but nothing is allocated: the 3xTF32 operand copies live in one
+ * fixed 16 MiB device array compiled into the library (held by every GPU that loads it),
+ * so 2*(M*K + K*N) must stay <= 4 Mi floats (K, N rounded up to 4).  All tensors must be
+ * device pointers.  The first call on a device resolves the array's address; make it
+ * before any stream capture.  Calls share the array: calls that overlap on the GPU race.
+ * Runs on the acfun stream and returns once it is done: 0, or an error code. */
+int acfun_gemm_epi_noalloc(int M, int N, int K, const float* A, const float* B, float* C,
+                           const float* bias, int act);
+
 /* Stream for device-pointer calls (a cudaStream_t passed as void*; NULL = legacy default). */
 void acfun_set_stream(void* stream);
 void* acfun_get_stream(void);
