@@ -186,6 +186,196 @@ def run_reference_arm(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def _he(g, shape, fan_in):
+    lim = np.sqrt(6.0 / fan_in)
+    return g.uniform(-lim, lim, size=shape).astype(np.float32)
+
+
+def _bn_fold(g, w, cout):
+    """cfg3: BN gamma U[.5,1.5], beta U[-.1,.1], mean U[-.1,.1], var U[.5,1.5] folded into the
+    conv (model.cpp:69-95 expression order), bias 0 before the fold."""
+    gamma = g.uniform(0.5, 1.5, cout).astype(np.float32)
+    beta = g.uniform(-0.1, 0.1, cout).astype(np.float32)
+    mean = g.uniform(-0.1, 0.1, cout).astype(np.float32)
+    var = g.uniform(0.5, 1.5, cout).astype(np.float32)
+    s = (gamma / np.sqrt(var + np.float32(1e-5))).astype(np.float32)
+    return (w * s).astype(np.float32), (beta - mean * s).astype(np.float32)
+
+
+def measure_configs(acf, torch, stream, flush, steps, with_cpu=True, cfg_filter=None):
+    """Every BASELINE config on one GPU (device-resident tensors, CUDA events, L2 flushed
+    before each timed step), with its roofline and the reference timed on the host cores on a
+    bounded sample of the same workload."""
+    from oracle import pyoracle as P
+    L = acf.lib()
+    bf16, hbm, src = measured_peaks()
+    peak = {"int8": (2 * bf16, "TOPS", f"2 x bf16 ({src})"), "bf16": (bf16, "TFLOP/s", src),
+            "f32x3": (bf16 / 6, "TFLOP/s", f"3xTF32 ceiling = bf16/2/3 ({src})"),
+            "hbm": (hbm, "GB/s", src)}
+    cores = os.cpu_count() or 1
+    R = P.ref() if (with_cpu and P.ref_available()) else None
+    if R is not None:
+        P.ref_set_threads(cores)
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    out = {}
+
+    def timeit(fn, n):
+        fn()
+        torch.cuda.synchronize()
+        acf.check()
+        evs = []
+        for _ in range(n):
+            flush.fill_(1)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            fn()
+            e.record(stream)
+            evs.append((s, e))
+        torch.cuda.synchronize()
+        acf.check()
+        return sum(s.elapsed_time(e) for s, e in evs) / n / 1e3
+
+    def cpu(fn, units, unit_scale):
+        """median seconds of the reference on `units` (images / rows) -> value per unit."""
+        if R is None:
+            return None
+        fn()
+        ts = []
+        for _ in range(2):
+            t0 = time.perf_counter()
+            fn()
+            ts.append(time.perf_counter() - t0)
+        return units * unit_scale / statistics.median(ts)
+
+    def record(name, t, work, unit_div, bound, cpu_val=None, cpu_sample="", extra=None):
+        pk, punit, psrc = peak[bound]
+        achieved = work / t / unit_div
+        r = {"ms": round(t * 1e3, 4), "value": round(achieved, 3), "unit": punit,
+             "roofline": {"bound": "hbm" if bound == "hbm" else "tensor", "achieved": round(achieved, 2),
+                          "peak": round(pk, 1), "unit": punit, "frac": round(achieved / pk, 4),
+                          "peak_source": psrc}}
+        if cpu_val is not None:
+            r["cpu_baseline"] = {"value": round(cpu_val, 4), "unit": punit, "cores": cores,
+                                 "kind": "reference", "sample": cpu_sample}
+        if extra:
+            r.update(extra)
+        out[name] = r
+
+    want = (lambda n: cfg_filter is None or n in cfg_filter)
+    g = np.random.default_rng(2024)
+
+    if want("cfg1_sgemm_1024"):
+        A = g.uniform(-1, 1, (1024, 1024)).astype(np.float32)
+        B = g.uniform(-1, 1, (1024, 1024)).astype(np.float32)
+        dA, dB, dC = dev(A), dev(B), torch.empty((1024, 1024), device="cuda")
+        t = timeit(lambda: L.acfun_gemm(1024, 1024, 1024, dA.data_ptr(), dB.data_ptr(), dC.data_ptr()), steps)
+        Cc = np.empty((1024, 1024), np.float32)
+        cv = cpu(lambda: R.acfun_gemm(1024, 1024, 1024, A, B, Cc), 2 * 1024 ** 3, 1e-12)
+        record("cfg1_sgemm_1024", t, 2 * 1024 ** 3, 1e12, "f32x3", cv, "full 1024^3 acfun_gemm")
+
+    if want("cfg2_bf16_4096"):
+        A = g.uniform(-1, 1, (4096, 4096)).astype(np.float32)
+        B = g.uniform(-1, 1, (4096, 4096)).astype(np.float32)
+        dA, dB, dC = dev(A), dev(B), torch.empty((4096, 4096), device="cuda")
+        t = timeit(lambda: L.acfun_gemm_bf16(4096, 4096, 4096, dA.data_ptr(), dB.data_ptr(), dC.data_ptr()), steps)
+        rows = 256
+        Cc = np.empty((rows, 4096), np.float32)
+        As = np.ascontiguousarray(A[:rows])
+        cv = cpu(lambda: R.acfun_gemm_bf16(rows, 4096, 4096, As, B, Cc), 2 * rows * 4096 * 4096, 1e-12)
+        record("cfg2_bf16_4096", t, 2 * 4096 ** 3, 1e12, "bf16", cv, f"{rows} rows of 4096^3 acfun_gemm_bf16",
+               {"note": "fp32 in/out API: includes the fp32->bf16 operand conversion"})
+
+    def conv_cfg(name, N, H, W, Cin, Cout, KH, st, pd, int8=False, groups=1, dw=False, bound=None):
+        if not want(name):
+            return
+        OH, OW = (H + 2 * pd - KH) // st + 1, (W + 2 * pd - KH) // st + 1
+        x = g.uniform(0, 1, (N, H, W, Cin)).astype(np.float32)
+        if dw:
+            w = _he(g, (Cin, KH, KH), KH * KH)
+            b = g.uniform(-0.1, 0.1, Cin).astype(np.float32)
+        elif groups > 1:
+            w = _he(g, (groups, KH * KH * (Cin // groups), Cout // groups), KH * KH * (Cin // groups))
+            b = g.uniform(-0.1, 0.1, Cout).astype(np.float32)
+        else:
+            w, b = _bn_fold(g, _he(g, (KH * KH * Cin, Cout), KH * KH * Cin), Cout)
+        flops = 2.0 * N * OH * OW * Cout * KH * KH * (Cin // groups if not dw else 1)
+        nbytes = 4.0 * (N * H * W * Cin + N * OH * OW * Cout)
+        dx, dout = dev(x), torch.empty((N, OH, OW, Cout), device="cuda")
+        db = dev(b)
+        ns = 2 if N >= 2 else 1
+        xs = np.ascontiguousarray(x[:ns])
+        os_ = np.empty((ns, OH, OW, Cout), np.float32)
+        if int8:
+            ws = np.empty(Cout, np.float32)
+            wq = np.empty((KH * KH * Cin, Cout), np.int8)
+            L.acfun_quantize_weights(acf.ptr(w), KH * KH * Cin, Cout, acf.ptr(ws), acf.ptr(wq))
+            dwq, dws = dev(wq), dev(ws)
+            fn = lambda: L.acfun_conv2d_int8(dx.data_ptr(), N, H, W, Cin, dwq.data_ptr(), dws.data_ptr(),
+                                             db.data_ptr(), KH, KH, Cout, st, pd, 0.0, dout.data_ptr(), 1)
+            cfn = lambda: R.acfun_conv2d_int8(xs, ns, H, W, Cin, wq, ws, b.ctypes.data, KH, KH, Cout, st, pd,
+                                              0.0, os_, 1)
+        elif dw:
+            dw_ = dev(w)
+            fn = lambda: L.acfun_conv2d_dw(dx.data_ptr(), N, H, W, Cin, dw_.data_ptr(), db.data_ptr(), KH, KH,
+                                           st, pd, dout.data_ptr(), 1)
+            cfn = lambda: R.acfun_conv2d_dw(xs, ns, H, W, Cin, w, b.ctypes.data, KH, KH, st, pd, os_, 1)
+        else:
+            dw_ = dev(w)
+            fn = lambda: L.acfun_conv2d_g(dx.data_ptr(), N, H, W, Cin, dw_.data_ptr(), db.data_ptr(), KH, KH,
+                                          Cout, st, pd, groups, dout.data_ptr(), 1)
+            cfn = lambda: R.acfun_conv2d_g(xs, ns, H, W, Cin, np.ascontiguousarray(w), b.ctypes.data, KH, KH,
+                                           Cout, st, pd, groups, os_, 1)
+        t = timeit(fn, steps)
+        bound = bound or ("int8" if int8 else "f32x3")
+        if bound == "hbm":
+            cv = cpu(cfn, ns * nbytes / N, 1e-9)
+            record(name, t, nbytes, 1e9, "hbm", cv, f"{ns} of {N} images, reference route",
+                   {"us": round(t * 1e6, 2), "gflop": round(flops / 1e9, 4), "mbytes": round(nbytes / 1e6, 2),
+                    "img_per_s": round(N / t, 1)})
+        else:
+            cv = cpu(cfn, ns * flops / N, 1e-12)
+            record(name, t, flops, 1e12, bound, cv, f"{ns} of {N} images, reference route",
+                   {"gflop_direct_count": round(flops / 1e9, 4), "img_per_s": round(N / t, 1)})
+
+    conv_cfg("cfg3a_conv3x3_f23_f32", 32, 56, 56, 64, 64, 3, 1, 1)
+    conv_cfg("cfg3b_conv3x3_f43_f32", 8, 112, 112, 64, 64, 3, 1, 1)
+    conv_cfg("cfg3a_conv3x3_int8", 32, 56, 56, 64, 64, 3, 1, 1, int8=True)
+    conv_cfg("cfg4_depthwise_3x3", 32, 56, 56, 144, 144, 3, 1, 1, dw=True, bound="hbm")
+    conv_cfg("cfg4_grouped_s1", 32, 14, 14, 24, 48, 3, 1, 1, groups=6, bound="hbm")
+    conv_cfg("cfg4_grouped_s2", 32, 14, 14, 24, 48, 3, 2, 1, groups=6, bound="hbm")
+    conv_cfg("cfg4_pointwise_s1", 32, 56, 56, 144, 24, 1, 1, 0, bound="hbm")
+    conv_cfg("cfg4_pointwise_s2", 32, 56, 56, 32, 64, 1, 2, 0, bound="hbm")
+
+    if want("cfg5_vgg11_b256"):
+        import tempfile
+
+        from acfun_b200 import acfun0
+        path = os.path.join(tempfile.gettempdir(), "acfun_vgg11_seed5.acfun")
+        if not os.path.exists(path):
+            acfun0.vgg11(seed=5).save(path)
+        m = acf.Model(path)
+        n = 256
+        x = g.uniform(0, 1, (n, 224, 224, 3)).astype(np.float32)
+        dx, dy = dev(x), torch.empty((n, 1000), device="cuda")
+        t = timeit(lambda: L.acfun_model_infer_batch(m.h, n, dx.data_ptr(), dy.data_ptr()), max(2, steps // 4))
+        cv = None
+        if R is not None:
+            h = R.acfun_model_load(path.encode())
+            o = np.empty(1000, np.float32)
+            x0 = np.ascontiguousarray(x[0])
+            cv = cpu(lambda: [R.acfun_model_infer(h, x0, o) for _ in range(2)], 2, 1.0)
+            R.acfun_model_destroy(h)
+        gf = 15.218e9
+        record("cfg5_vgg11_b256", t, n * gf, 1e12, "f32x3", None, "",
+               {"img_per_s": round(n / t, 1), "gflop_per_img": 15.218})
+        if cv is not None:
+            out["cfg5_vgg11_b256"]["cpu_baseline"] = {"value": round(cv, 3), "unit": "img/s", "cores": cores,
+                                                      "kind": "reference",
+                                                      "sample": "2 sequential acfun_model_infer calls (batch-1 API)"}
+        m.close()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -194,6 +384,9 @@ def main():
     ap.add_argument("--impl", default="acfun_b200", choices=["acfun_b200", "reference"])
     ap.add_argument("--cpu-rows", type=int, default=512)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the per-config measurements (every BASELINE config, N=1 only)")
+    ap.add_argument("--configs", default=None, help="comma-separated subset of config names")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl != "reference" else args.warmup
 
@@ -312,6 +505,10 @@ def main():
         }
         if not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_reference_sample(steps=3, rows=args.cpu_rows)
+        if world == 1 and not args.no_configs:
+            filt = set(args.configs.split(",")) if args.configs else None
+            line["configs"] = measure_configs(acf, torch, stream, flush, steps=max(5, min(args.steps, 20)),
+                                              with_cpu=not args.no_cpu_baseline, cfg_filter=filt)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
