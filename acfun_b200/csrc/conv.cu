@@ -60,6 +60,38 @@ __global__ void k_pad_split(const float* __restrict__ x, int N, int H, int W, in
   }
 }
 
+// Same as k_pad_split, one thread per (padded pixel, 4 channels) with 32-bit index math and
+// 16-byte loads / stores; used whenever the padded tensor has < 2^31 float4 groups.
+__global__ void k_pad_split4(const float* __restrict__ x, int H, int W, int Cs, int coff, int Cg,
+                             int pad, int Hp, int Wp, int C4, unsigned total, int vec_in,
+                             float4* __restrict__ dst, size_t op_stride4) {
+  for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const unsigned c4 = i % C4, p = i / C4;
+    const unsigned wp = p % Wp, t = p / Wp;
+    const unsigned hp = t % Hp, n = t / Hp;
+    const int ih = (int)hp - pad, iw = (int)wp - pad, c = (int)c4 * 4;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    if (c < Cg && ih >= 0 && ih < H && iw >= 0 && iw < W) {
+      const float* src = x + (((size_t)n * H + ih) * W + iw) * Cs + coff + c;
+      if (vec_in && c + 4 <= Cg) {
+        const float4 q = __ldg(reinterpret_cast<const float4*>(src));
+        v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+      } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) v[k] = (c + k < Cg) ? src[k] : 0.f;
+      }
+    }
+    float hi[4], lo[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      hi[k] = tf32_rne_c(v[k]);
+      lo[k] = tf32_rne_c(v[k] - hi[k]);
+    }
+    dst[i] = make_float4(hi[0], hi[1], hi[2], hi[3]);
+    dst[i + op_stride4] = make_float4(lo[0], lo[1], lo[2], lo[3]);
+  }
+}
+
 // im2col for strided convs: row m = (n, oh, ow), column k = (kh*KW + kw)*Cg + c -> [2][M][Kpad]
 __global__ void k_im2col_split(const float* __restrict__ x, int N, int H, int W, int Cs, int coff,
                                int Cg, int KH, int KW, int stride, int pad, int OH, int OW,
@@ -101,12 +133,108 @@ __global__ void k_weights_split(const float* __restrict__ w, int taps, int Cg, i
   }
 }
 
+// Narrow 1x1 convolution (pad 0, any stride, Cout <= NB) on CUDA cores: HBM-bound, so the
+// activations are read exactly once (no padded / split copy).  One thread per output pixel
+// keeps NB fp32 accumulators; the weights [Cin][Cout] and bias sit in shared memory and are
+// read as warp-wide broadcasts.  out = relu?(sum_k x[k]*w[k][j] + bias[j]), fp32 FMA chain.
+template <int NB>
+__global__ void __launch_bounds__(128) k_pw_simt(const float* __restrict__ x, int H, int W, int Cs,
+                                                 int coff, int Cin, const float* __restrict__ w,
+                                                 long long ldw, const float* __restrict__ bias,
+                                                 int Cout, int stride, int OH, int OW, unsigned M,
+                                                 float* __restrict__ out, long long ldc, int act,
+                                                 int vec_in, int vec_out) {
+  extern __shared__ float4 pw_sm4[];
+  float* ws = reinterpret_cast<float*>(pw_sm4);  // [Cin][NB]
+  float* bs = ws + Cin * NB;
+  for (int i = threadIdx.x; i < Cin * NB; i += blockDim.x) {
+    const int k = i / NB, j = i - k * NB;
+    ws[i] = (j < Cout) ? w[(long long)k * ldw + j] : 0.0f;
+  }
+  for (int j = threadIdx.x; j < NB; j += blockDim.x) bs[j] = (bias && j < Cout) ? bias[j] : 0.0f;
+  __syncthreads();
+  for (unsigned m = blockIdx.x * blockDim.x + threadIdx.x; m < M; m += gridDim.x * blockDim.x) {
+    const unsigned ow = m % OW, t = m / OW, oh = t % OH, n = t / OH;
+    const float* src = x + (((size_t)n * H + oh * stride) * W + ow * stride) * Cs + coff;
+    float acc[NB];
+#pragma unroll
+    for (int j = 0; j < NB; ++j) acc[j] = 0.0f;
+    int k = 0;
+    if (vec_in) {
+      for (; k + 4 <= Cin; k += 4) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(src + k));
+        const float xv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float* wr = ws + (k + u) * NB;
+#pragma unroll
+          for (int j = 0; j < NB; ++j) acc[j] = __fmaf_rn(xv[u], wr[j], acc[j]);
+        }
+      }
+    }
+    for (; k < Cin; ++k) {
+      const float xv = src[k];
+      const float* wr = ws + k * NB;
+#pragma unroll
+      for (int j = 0; j < NB; ++j) acc[j] = __fmaf_rn(xv, wr[j], acc[j]);
+    }
+    float* dst = out + (size_t)m * ldc;
+#pragma unroll
+    for (int j = 0; j < NB; ++j) {
+      float v = __fadd_rn(acc[j], bs[j]);
+      acc[j] = act ? (v > 0.0f ? v : 0.0f) : v;
+    }
+    if (vec_out) {
+#pragma unroll
+      for (int j = 0; j < NB; j += 4)
+        if (j < Cout)
+          *reinterpret_cast<float4*>(dst + j) = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < NB; ++j)
+        if (j < Cout) dst[j] = acc[j];
+    }
+  }
+}
+
+// Returns true when the narrow CUDA-core path handled the convolution.
+static bool pw_simt(Call& c, const float* x, int N, int H, int W, int Cs, int coff, int Cg,
+                    const float* w, long long ldw, const float* bias, int Cout, int stride,
+                    float* out, long long ldc, int act, bool* handled) {
+  *handled = false;
+  const int OH = (H - 1) / stride + 1, OW = (W - 1) / stride + 1;
+  const long long M = (long long)N * OH * OW;
+  const int NB = Cout <= 16 ? 16 : (Cout <= 32 ? 32 : 64);
+  const size_t smem = ((size_t)Cg * NB + NB) * 4;
+  if (Cout > 64 || smem > 48 * 1024 || M >= (1LL << 31)) return true;
+  *handled = true;
+  const int vec_in = (Cs % 4 == 0) && (coff % 4 == 0) && aligned16(x);
+  const int vec_out = (Cout % 4 == 0) && (ldc % 4 == 0) && aligned16(out);
+  const int grid = grid_ew(c, 2 * M);  // ceil(M / 128) blocks of 128 threads, capped
+  if (NB == 16)
+    k_pw_simt<16><<<grid, 128, smem, c.stream()>>>(x, H, W, Cs, coff, Cg, w, ldw, bias, Cout,
+                                                   stride, OH, OW, (unsigned)M, out, ldc, act, vec_in, vec_out);
+  else if (NB == 32)
+    k_pw_simt<32><<<grid, 128, smem, c.stream()>>>(x, H, W, Cs, coff, Cg, w, ldw, bias, Cout,
+                                                   stride, OH, OW, (unsigned)M, out, ldc, act, vec_in, vec_out);
+  else
+    k_pw_simt<64><<<grid, 128, smem, c.stream()>>>(x, H, W, Cs, coff, Cg, w, ldw, bias, Cout,
+                                                   stride, OH, OW, (unsigned)M, out, ldc, act, vec_in, vec_out);
+  return c.launched("k_pw_simt");
+}
+
 bool conv_f32_dev(Call& c, const float* x, int N, int H, int W, int Cs, int coff, int Cg,
                   const float* w, long long ldw, const float* bias, int KH, int KW, int Cout_g,
                   int stride, int pad, float* out, long long ldc, int act) {
   const int OH = (H + 2 * pad - KH) / stride + 1, OW = (W + 2 * pad - KW) / stride + 1;
   if (OH <= 0 || OW <= 0 || N <= 0 || Cout_g <= 0) return true;
   const int taps = KH * KW;
+  if (KH == 1 && KW == 1 && pad == 0) {  // narrow pointwise: CUDA cores, activations read once
+    bool handled = false;
+    if (!pw_simt(c, x, N, H, W, Cs, coff, Cg, w, ldw, bias, Cout_g, stride, out, ldc, act, &handled))
+      return false;
+    if (handled) return true;
+  }
   const int Np = (int)align_up((size_t)Cout_g, 4);
   EpiParams ep{};
   ep.C = out;
@@ -126,8 +254,16 @@ bool conv_f32_dev(Call& c, const float* x, int N, int H, int W, int Cs, int coff
     float* a = (float*)c.scratch((size_t)2 * rows * Cpad * 4);
     float* b = (float*)c.scratch((size_t)2 * taps * Cpad * Np * 4);
     if (!a || !b) return false;
-    k_pad_split<<<grid_ew(c, rows * Cpad), 256, 0, c.stream()>>>(x, N, H, W, Cs, coff, Cg, pad, Hp,
-                                                                 Wp, Cpad, a, rows * Cpad);
+    const long long groups4 = rows * (Cpad / 4);
+    if (groups4 < (1LL << 31)) {
+      const int vec_in = (Cs % 4 == 0) && (coff % 4 == 0) && aligned16(x);
+      k_pad_split4<<<grid_ew(c, groups4), 256, 0, c.stream()>>>(
+          x, H, W, Cs, coff, Cg, pad, Hp, Wp, Cpad / 4, (unsigned)groups4, vec_in, (float4*)a,
+          (size_t)(rows * Cpad / 4));
+    } else {
+      k_pad_split<<<grid_ew(c, rows * Cpad), 256, 0, c.stream()>>>(x, N, H, W, Cs, coff, Cg, pad, Hp,
+                                                                   Wp, Cpad, a, rows * Cpad);
+    }
     k_weights_split<<<grid_ew(c, (long long)taps * Cpad * Np), 256, 0, c.stream()>>>(
         w, taps, Cg, Cout_g, ldw, Cpad, Np, b, (long long)taps * Cpad * Np);
     if (!c.launched("conv prep")) return false;

@@ -144,6 +144,57 @@ __global__ void k_quant_pad_u8(const float* __restrict__ x, int N, int H, int W,
   }
 }
 
+__device__ __forceinline__ uint8_t quant_one(float xv, float inv_s, int mode, bool vec_lane) {
+  const float t = __fmul_rn(xv, inv_s);
+  int v;
+  if (mode == 0) {
+    v = (fabsf(t) < 2147483648.0f) ? __float2int_rn(t) : (int)0x80000000;
+  } else if (vec_lane) {
+    const float r = __fadd_rn(t, copysignf(0.5f, t));
+    v = (fabsf(r) < 2147483648.0f) ? (int)truncf(r) : (int)0x80000000;
+  } else {
+    v = round_half_away(t);
+  }
+  return clamp_u8((int)((unsigned)v + 128u));
+}
+
+// k_quant_pad_u8 with one thread per (padded pixel, 16 channels), 32-bit index math and one
+// 16-byte store (Cpad is a multiple of 16); used when the tensor has < 2^31 such groups.
+__global__ void k_quant_pad_u8_16(const float* __restrict__ x, int H, int W, int Cin, int pad,
+                                  int Hp, int Wp, int C16, unsigned total, int vec_in,
+                                  const Int8Scalars* s, float inv_host, int mode,
+                                  uint4* __restrict__ dst) {
+  const float inv_s = s ? s->inv_s : inv_host;
+  const int cvec = Cin & ~15;
+  for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const unsigned cg = i % C16, p = i / C16;
+    const unsigned wp = p % Wp, t = p / Wp;
+    const unsigned hp = t % Hp, n = t / Hp;
+    const int ih = (int)hp - pad, iw = (int)wp - pad, c0 = (int)cg * 16;
+    uint32_t w[4] = {0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u};
+    if (c0 < Cin && ih >= 0 && ih < H && iw >= 0 && iw < W) {
+      const float* src = x + (((size_t)n * H + ih) * W + iw) * Cin + c0;
+      float v[16];
+      if (vec_in && c0 + 16 <= Cin) {
+#pragma unroll
+        for (int k = 0; k < 16; k += 4) {
+          const float4 q = __ldg(reinterpret_cast<const float4*>(src + k));
+          v[k] = q.x; v[k + 1] = q.y; v[k + 2] = q.z; v[k + 3] = q.w;
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < 16; ++k) v[k] = (c0 + k < Cin) ? src[k] : 0.0f;
+      }
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const uint8_t q = (c0 + k < Cin) ? quant_one(v[k], inv_s, mode, c0 + k < cvec) : (uint8_t)128;
+        w[k >> 2] = (w[k >> 2] & ~(0xFFu << (8 * (k & 3)))) | ((uint32_t)q << (8 * (k & 3)));
+      }
+    }
+    dst[i] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
 // pre-quantised u8 NHWC -> padded [N*Hp*Wp][Cpad] (border = zero point)
 __global__ void k_pad_u8(const uint8_t* __restrict__ xq, int N, int H, int W, int Cin, int pad,
                          int Hp, int Wp, int Cpad, uint8_t* __restrict__ dst) {
@@ -240,7 +291,13 @@ static bool int8_conv_gemm(Call& c, const Int8ConvArgs& a, int N, int H, int W, 
     uint8_t* A = (uint8_t*)c.scratch((size_t)rows * Cpad);
     int8_t* B = (int8_t*)c.scratch((size_t)taps * Cpad * Np);
     if (!A || !B) return false;
-    if (a.xf)
+    if (a.xf && rows * (Cpad / 16) < (1LL << 31)) {
+      const long long g16 = rows * (Cpad / 16);
+      const int vec_in = (Cin % 4 == 0) && aligned16(a.xf);
+      k_quant_pad_u8_16<<<grid_n(c, g16), 256, 0, c.stream()>>>(
+          a.xf, H, W, Cin, pad, Hp, Wp, Cpad / 16, (unsigned)g16, vec_in, a.s, a.inv_host, a.qmode,
+          (uint4*)A);
+    } else if (a.xf)
       k_quant_pad_u8<<<grid_n(c, rows * Cpad), 256, 0, c.stream()>>>(
           a.xf, N, H, W, Cin, pad, Hp, Wp, Cpad, a.s, a.inv_host, a.qmode, A);
     else

@@ -286,6 +286,55 @@ __global__ void k_dw4(const float* __restrict__ in, int N, int H, int W, int C,
   }
 }
 
+// One block per output row (n, oh): the block transposes the weights to wT[k][C] in shared
+// memory once, then threads walk (ow, 4-channel group) items of the row with float4 loads.
+// Same per-lane FMA chain as k_dw4 (bias, then taps in kh, kw order, zeros outside).
+__global__ void k_dw_row(const float* __restrict__ in, int H, int W, int C,
+                         const float* __restrict__ w, const float* __restrict__ bias, int KH,
+                         int KW, int stride, int pad, int OH, int OW, float* __restrict__ out,
+                         int act) {
+  extern __shared__ float4 dsm4[];
+  float* wT = reinterpret_cast<float*>(dsm4);
+  const int K = KH * KW;
+  float* bs = wT + K * C;
+  for (int i = threadIdx.x; i < K * C; i += blockDim.x) {
+    const int k = i / C, c = i - k * C;
+    wT[i] = w[c * K + k];
+  }
+  for (int i = threadIdx.x; i < C; i += blockDim.x) bs[i] = bias ? bias[i] : 0.0f;
+  __syncthreads();
+  const int n = blockIdx.x / OH, oh = blockIdx.x - n * OH;
+  const int C4 = C >> 2, items = OW * C4;
+  const float* img = in + (size_t)n * H * W * C;
+  float* orow = out + ((size_t)n * OH + oh) * OW * C;
+  for (int it = threadIdx.x; it < items; it += blockDim.x) {
+    const int ow = it / C4, c = (it - ow * C4) * 4;
+    float4 acc = *reinterpret_cast<const float4*>(bs + c);
+    for (int kh = 0; kh < KH; ++kh) {
+      const int ih = oh * stride - pad + kh;
+      const bool rok = ih >= 0 && ih < H;
+      for (int kw = 0; kw < KW; ++kw) {
+        const int iw = ow * stride - pad + kw;
+        float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (rok && iw >= 0 && iw < W)
+          x = __ldg(reinterpret_cast<const float4*>(img + ((size_t)ih * W + iw) * C + c));
+        const float4 wv = *reinterpret_cast<const float4*>(wT + (kh * KW + kw) * C + c);
+        acc.x = __fmaf_rn(x.x, wv.x, acc.x);
+        acc.y = __fmaf_rn(x.y, wv.y, acc.y);
+        acc.z = __fmaf_rn(x.z, wv.z, acc.z);
+        acc.w = __fmaf_rn(x.w, wv.w, acc.w);
+      }
+    }
+    if (act == 1) {
+      acc.x = acc.x > 0.f ? acc.x : 0.f;
+      acc.y = acc.y > 0.f ? acc.y : 0.f;
+      acc.z = acc.z > 0.f ? acc.z : 0.f;
+      acc.w = acc.w > 0.f ? acc.w : 0.f;
+    }
+    *reinterpret_cast<float4*>(orow + (size_t)ow * C + c) = acc;
+  }
+}
+
 __global__ void k_dw1(const float* __restrict__ in, int N, int H, int W, int C,
                       const float* __restrict__ w, const float* __restrict__ bias, int KH, int KW,
                       int stride, int pad, int OH, int OW, float* __restrict__ out, int act) {
@@ -317,6 +366,13 @@ bool dw_dev(Call& c, const float* in, int N, int H, int W, int C, const float* w
             const float* bias, int KH, int KW, int stride, int pad, float* out, int act) {
   const int OH = (H + 2 * pad - KH) / stride + 1, OW = (W + 2 * pad - KW) / stride + 1;
   if (OH <= 0 || OW <= 0 || N <= 0 || C <= 0) return true;
+  const size_t smem = ((size_t)KH * KW * C + C) * 4;
+  if (C % 4 == 0 && aligned16(in) && aligned16(out) && smem <= 48 * 1024 &&
+      (long long)N * OH < (1LL << 31) && (long long)H * W * C < (1LL << 31)) {
+    k_dw_row<<<N * OH, 256, smem, c.stream()>>>(in, H, W, C, w, bias, KH, KW, stride, pad, OH, OW,
+                                                out, act);
+    return c.launched("k_dw_row");
+  }
   if (C % 4 == 0 && aligned16(in) && aligned16(out) && (!bias || aligned16(bias))) {
     const long long total = (long long)N * OH * OW * (C / 4);
     k_dw4<<<grid_for(c, total), 256, 0, c.stream()>>>(in, N, H, W, C, w, bias, KH, KW, stride, pad,
