@@ -58,6 +58,7 @@ SIGNATURES = {
     "acfun_model_infer_batch": (i, [vp, i, vp, vp]),
     "acfun_gemm_s8_requant": (None, [i, i, i, vp, vp, vp, vp, vp, i]),
     "acfun_gemm_epi_noalloc": (i, [i, i, i, vp, vp, vp, vp, i]),
+    "acfun_set_fp32_math": (i, [i]),
     "acfun_set_stream": (None, [vp]),
     "acfun_get_stream": (vp, []),
     "acfun_set_device": (i, [i]),

@@ -16,22 +16,10 @@
 #include "api_export.cuh"
 #include "conv.cuh"
 #include "gemm.cuh"
+#include "numerics.cuh"
 #include "ops.cuh"
 
 namespace acf {
-
-__device__ __forceinline__ float tf32_rne_c(float x) {
-  uint32_t u = __float_as_uint(x);
-  if ((u & 0x7f800000u) == 0x7f800000u) return x;
-  u += 0xfffu + ((u >> 13) & 1u);
-  return __uint_as_float(u & 0xffffe000u);
-}
-
-__device__ __forceinline__ void split_store(float* dst, long long op_stride, float x) {
-  const float hi = tf32_rne_c(x);
-  dst[0] = hi;
-  dst[op_stride] = tf32_rne_c(x - hi);
-}
 
 static int grid_ew(Call& c, long long work) {
   long long b = (work + 255) / 256, cap = (long long)c.sm_count() * 16;
@@ -39,32 +27,12 @@ static int grid_ew(Call& c, long long work) {
 }
 
 // x: NHWC with channel stride Cs and channel offset coff (Cg channels used) ->
-// [2][N*Hp*Wp][Cpad] hi/lo, zero in the spatial border and in channels >= Cg.
-__global__ void k_pad_split(const float* __restrict__ x, int N, int H, int W, int Cs, int coff,
-                            int Cg, int pad, int Hp, int Wp, int Cpad, float* __restrict__ dst,
-                            long long op_stride) {
-  const long long total = (long long)N * Hp * Wp * Cpad;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
-    const int c = (int)(i % Cpad);
-    long long p = i / Cpad;
-    const int wp = (int)(p % Wp);
-    p /= Wp;
-    const int hp = (int)(p % Hp);
-    const int n = (int)(p / Hp);
-    const int ih = hp - pad, iw = wp - pad;
-    float v = 0.0f;
-    if (c < Cg && ih >= 0 && ih < H && iw >= 0 && iw < W)
-      v = x[(((long long)n * H + ih) * W + iw) * Cs + coff + c];
-    split_store(dst + i, op_stride, v);
-  }
-}
-
-// Same as k_pad_split, one thread per (padded pixel, 4 channels) with 32-bit index math and
-// 16-byte loads / stores; used whenever the padded tensor has < 2^31 float4 groups.
+// [2][N*Hp*Wp][Cpad] split planes (hi, lo), zero in the spatial border and in channels >= Cg.
+// One thread per (padded pixel, 4 channels); 32-bit index math (callers check the size).
+template <bool BF>
 __global__ void k_pad_split4(const float* __restrict__ x, int H, int W, int Cs, int coff, int Cg,
                              int pad, int Hp, int Wp, int C4, unsigned total, int vec_in,
-                             float4* __restrict__ dst, size_t op_stride4) {
+                             void* __restrict__ dst, size_t op_stride) {
   for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
     const unsigned c4 = i % C4, p = i / C4;
     const unsigned wp = p % Wp, t = p / Wp;
@@ -81,21 +49,15 @@ __global__ void k_pad_split4(const float* __restrict__ x, int H, int W, int Cs, 
         for (int k = 0; k < 4; ++k) v[k] = (c + k < Cg) ? src[k] : 0.f;
       }
     }
-    float hi[4], lo[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      hi[k] = tf32_rne_c(v[k]);
-      lo[k] = tf32_rne_c(v[k] - hi[k]);
-    }
-    dst[i] = make_float4(hi[0], hi[1], hi[2], hi[3]);
-    dst[i + op_stride4] = make_float4(lo[0], lo[1], lo[2], lo[3]);
+    nx_store_split4<BF>(dst, i, op_stride, v);
   }
 }
 
 // im2col for strided convs: row m = (n, oh, ow), column k = (kh*KW + kw)*Cg + c -> [2][M][Kpad]
+template <bool BF>
 __global__ void k_im2col_split(const float* __restrict__ x, int N, int H, int W, int Cs, int coff,
                                int Cg, int KH, int KW, int stride, int pad, int OH, int OW,
-                               int Kpad, float* __restrict__ dst, long long op_stride) {
+                               int Kpad, void* __restrict__ dst, long long op_stride) {
   const long long total = (long long)N * OH * OW * Kpad;
   const int K = KH * KW * Cg;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
@@ -113,13 +75,14 @@ __global__ void k_im2col_split(const float* __restrict__ x, int N, int H, int W,
       if (ih >= 0 && ih < H && iw >= 0 && iw < W)
         v = x[(((long long)n * H + ih) * W + iw) * Cs + coff + c];
     }
-    split_store(dst + i, op_stride, v);
+    nx_store_split1<BF>(dst, (size_t)i, (size_t)op_stride, v);
   }
 }
 
 // weights [taps*Cg][Cout_g] (row stride ldw) -> [2][taps*Cpad][Np], zero rows for c >= Cg
+template <bool BF>
 __global__ void k_weights_split(const float* __restrict__ w, int taps, int Cg, int Cout_g,
-                                long long ldw, int Cpad, int Np, float* __restrict__ dst,
+                                long long ldw, int Cpad, int Np, void* __restrict__ dst,
                                 long long op_stride) {
   const long long total = (long long)taps * Cpad * Np;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
@@ -129,25 +92,29 @@ __global__ void k_weights_split(const float* __restrict__ w, int taps, int Cg, i
     const int tap = (int)(r / Cpad), c = (int)(r % Cpad);
     float v = 0.0f;
     if (c < Cg && j < Cout_g) v = w[((long long)tap * Cg + c) * ldw + j];
-    split_store(dst + i, op_stride, v);
+    nx_store_split1<BF>(dst, (size_t)i, (size_t)op_stride, v);
   }
 }
 
-// Narrow 1x1 convolution (pad 0, any stride, Cout <= NB) on CUDA cores: HBM-bound, so the
-// activations are read exactly once (no padded / split copy).  One thread per output pixel
-// keeps NB fp32 accumulators; the weights [Cin][Cout] and bias sit in shared memory and are
-// read as warp-wide broadcasts.  out = relu?(sum_k x[k]*w[k][j] + bias[j]), fp32 FMA chain.
+// Narrow convolutions on CUDA cores: Cout <= NB (64) and either a 1x1 pad-0 conv (any
+// stride) or a small reduction (KH*KW*Cin <= 64, e.g. the 3-channel first layer of VGG).
+// These are HBM-bound, so the activations are read once with no padded or split copy; one
+// thread per output pixel keeps NB fp32 accumulators and the weights [taps*Cin][Cout] sit in
+// shared memory as warp-wide broadcasts.  out = relu?(sum_taps,k x*w + bias[j]) with an fp32
+// FMA chain (taps outside the image are skipped).
 template <int NB>
-__global__ void __launch_bounds__(128) k_pw_simt(const float* __restrict__ x, int H, int W, int Cs,
-                                                 int coff, int Cin, const float* __restrict__ w,
-                                                 long long ldw, const float* __restrict__ bias,
-                                                 int Cout, int stride, int OH, int OW, unsigned M,
-                                                 float* __restrict__ out, long long ldc, int act,
-                                                 int vec_in, int vec_out) {
-  extern __shared__ float4 pw_sm4[];
-  float* ws = reinterpret_cast<float*>(pw_sm4);  // [Cin][NB]
-  float* bs = ws + Cin * NB;
-  for (int i = threadIdx.x; i < Cin * NB; i += blockDim.x) {
+__global__ void __launch_bounds__(128) k_conv_simt(const float* __restrict__ x, int H, int W,
+                                                   int Cs, int coff, int Cin,
+                                                   const float* __restrict__ w, long long ldw,
+                                                   const float* __restrict__ bias, int Cout, int KH,
+                                                   int KW, int stride, int pad, int OH, int OW,
+                                                   unsigned M, float* __restrict__ out,
+                                                   long long ldc, int act, int vec_in, int vec_out) {
+  extern __shared__ float4 cs_sm4[];
+  float* ws = reinterpret_cast<float*>(cs_sm4);  // [taps*Cin][NB]
+  const int K = KH * KW * Cin;
+  float* bs = ws + K * NB;
+  for (int i = threadIdx.x; i < K * NB; i += blockDim.x) {
     const int k = i / NB, j = i - k * NB;
     ws[i] = (j < Cout) ? w[(long long)k * ldw + j] : 0.0f;
   }
@@ -155,33 +122,42 @@ __global__ void __launch_bounds__(128) k_pw_simt(const float* __restrict__ x, in
   __syncthreads();
   for (unsigned m = blockIdx.x * blockDim.x + threadIdx.x; m < M; m += gridDim.x * blockDim.x) {
     const unsigned ow = m % OW, t = m / OW, oh = t % OH, n = t / OH;
-    const float* src = x + (((size_t)n * H + oh * stride) * W + ow * stride) * Cs + coff;
     float acc[NB];
 #pragma unroll
     for (int j = 0; j < NB; ++j) acc[j] = 0.0f;
-    int k = 0;
-    if (vec_in) {
-      for (; k + 4 <= Cin; k += 4) {
-        const float4 v = __ldg(reinterpret_cast<const float4*>(src + k));
-        const float xv[4] = {v.x, v.y, v.z, v.w};
+    for (int kh = 0; kh < KH; ++kh) {
+      const int ih = (int)oh * stride - pad + kh;
+      if (ih < 0 || ih >= H) continue;
+      for (int kw = 0; kw < KW; ++kw) {
+        const int iw = (int)ow * stride - pad + kw;
+        if (iw < 0 || iw >= W) continue;
+        const float* src = x + (((size_t)n * H + ih) * W + iw) * Cs + coff;
+        const float* wt = ws + (kh * KW + kw) * Cin * NB;
+        int k = 0;
+        if (vec_in) {
+          for (; k + 4 <= Cin; k += 4) {
+            const float4 v = __ldg(reinterpret_cast<const float4*>(src + k));
+            const float xv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float* wr = ws + (k + u) * NB;
+            for (int u = 0; u < 4; ++u) {
+              const float* wr = wt + (k + u) * NB;
 #pragma unroll
-          for (int j = 0; j < NB; ++j) acc[j] = __fmaf_rn(xv[u], wr[j], acc[j]);
+              for (int j = 0; j < NB; ++j) acc[j] = __fmaf_rn(xv[u], wr[j], acc[j]);
+            }
+          }
+        }
+        for (; k < Cin; ++k) {
+          const float xv = src[k];
+          const float* wr = wt + k * NB;
+#pragma unroll
+          for (int j = 0; j < NB; ++j) acc[j] = __fmaf_rn(xv, wr[j], acc[j]);
         }
       }
-    }
-    for (; k < Cin; ++k) {
-      const float xv = src[k];
-      const float* wr = ws + k * NB;
-#pragma unroll
-      for (int j = 0; j < NB; ++j) acc[j] = __fmaf_rn(xv, wr[j], acc[j]);
     }
     float* dst = out + (size_t)m * ldc;
 #pragma unroll
     for (int j = 0; j < NB; ++j) {
-      float v = __fadd_rn(acc[j], bs[j]);
+      const float v = __fadd_rn(acc[j], bs[j]);
       acc[j] = act ? (v > 0.0f ? v : 0.0f) : v;
     }
     if (vec_out) {
@@ -197,74 +173,69 @@ __global__ void __launch_bounds__(128) k_pw_simt(const float* __restrict__ x, in
   }
 }
 
-// Returns true when the narrow CUDA-core path handled the convolution.
-static bool pw_simt(Call& c, const float* x, int N, int H, int W, int Cs, int coff, int Cg,
-                    const float* w, long long ldw, const float* bias, int Cout, int stride,
-                    float* out, long long ldc, int act, bool* handled) {
+// Returns true when the CUDA-core path applies (and has been launched).
+static bool conv_simt(Call& c, const float* x, int N, int H, int W, int Cs, int coff, int Cg,
+                      const float* w, long long ldw, const float* bias, int KH, int KW, int Cout,
+                      int stride, int pad, float* out, long long ldc, int act, bool* handled) {
   *handled = false;
-  const int OH = (H - 1) / stride + 1, OW = (W - 1) / stride + 1;
+  const int OH = (H + 2 * pad - KH) / stride + 1, OW = (W + 2 * pad - KW) / stride + 1;
   const long long M = (long long)N * OH * OW;
+  const int K = KH * KW * Cg;
+  const bool narrow = (KH == 1 && KW == 1 && pad == 0) || K <= 64;
   const int NB = Cout <= 16 ? 16 : (Cout <= 32 ? 32 : 64);
-  const size_t smem = ((size_t)Cg * NB + NB) * 4;
-  if (Cout > 64 || smem > 48 * 1024 || M >= (1LL << 31)) return true;
+  const size_t smem = ((size_t)K * NB + NB) * 4;
+  if (!narrow || Cout > 64 || smem > 48 * 1024 || M >= (1LL << 31)) return true;
   *handled = true;
   const int vec_in = (Cs % 4 == 0) && (coff % 4 == 0) && aligned16(x);
   const int vec_out = (Cout % 4 == 0) && (ldc % 4 == 0) && aligned16(out);
   const int grid = grid_ew(c, 2 * M);  // ceil(M / 128) blocks of 128 threads, capped
+#define ACF_CONV_SIMT(NBV)                                                                      \
+  k_conv_simt<NBV><<<grid, 128, smem, c.stream()>>>(x, H, W, Cs, coff, Cg, w, ldw, bias, Cout, KH, \
+                                                    KW, stride, pad, OH, OW, (unsigned)M, out,   \
+                                                    ldc, act, vec_in, vec_out)
   if (NB == 16)
-    k_pw_simt<16><<<grid, 128, smem, c.stream()>>>(x, H, W, Cs, coff, Cg, w, ldw, bias, Cout,
-                                                   stride, OH, OW, (unsigned)M, out, ldc, act, vec_in, vec_out);
+    ACF_CONV_SIMT(16);
   else if (NB == 32)
-    k_pw_simt<32><<<grid, 128, smem, c.stream()>>>(x, H, W, Cs, coff, Cg, w, ldw, bias, Cout,
-                                                   stride, OH, OW, (unsigned)M, out, ldc, act, vec_in, vec_out);
+    ACF_CONV_SIMT(32);
   else
-    k_pw_simt<64><<<grid, 128, smem, c.stream()>>>(x, H, W, Cs, coff, Cg, w, ldw, bias, Cout,
-                                                   stride, OH, OW, (unsigned)M, out, ldc, act, vec_in, vec_out);
-  return c.launched("k_pw_simt");
+    ACF_CONV_SIMT(64);
+#undef ACF_CONV_SIMT
+  return c.launched("k_conv_simt");
 }
 
-bool conv_f32_dev(Call& c, const float* x, int N, int H, int W, int Cs, int coff, int Cg,
-                  const float* w, long long ldw, const float* bias, int KH, int KW, int Cout_g,
-                  int stride, int pad, float* out, long long ldc, int act) {
+template <bool BF>
+static bool conv_tc(Call& c, const float* x, int N, int H, int W, int Cs, int coff, int Cg,
+                    const float* w, long long ldw, const float* bias, int KH, int KW, int Cout_g,
+                    int stride, int pad, float* out, long long ldc, int act) {
   const int OH = (H + 2 * pad - KH) / stride + 1, OW = (W + 2 * pad - KW) / stride + 1;
-  if (OH <= 0 || OW <= 0 || N <= 0 || Cout_g <= 0) return true;
   const int taps = KH * KW;
-  if (KH == 1 && KW == 1 && pad == 0) {  // narrow pointwise: CUDA cores, activations read once
-    bool handled = false;
-    if (!pw_simt(c, x, N, H, W, Cs, coff, Cg, w, ldw, bias, Cout_g, stride, out, ldc, act, &handled))
-      return false;
-    if (handled) return true;
-  }
-  const int Np = (int)align_up((size_t)Cout_g, 4);
+  const int E = BF ? 2 : 4;             // bytes per split element
+  const int BKE = BF ? 64 : 32;         // channels per 128-byte K block
+  const int Np = (int)align_up((size_t)Cout_g, BF ? 8 : 4);
+  const GemmKind kind = BF ? GemmKind::BF16X3 : GemmKind::TF32X3;
   EpiParams ep{};
   ep.C = out;
   ep.ldc = ldc;
   ep.f0 = bias;
   ep.act = act;
+  Operand A, B;
   if (stride == 1) {
     const int Hp = H + 2 * pad, Wp = W + 2 * pad;
-    const int Cpad = (int)align_up((size_t)Cg, 32);
+    const int Cpad = (int)align_up((size_t)Cg, BKE);
     const long long rows = (long long)N * Hp * Wp;
-    if (rows >= (1LL << 31)) {
+    const long long groups4 = rows * (Cpad / 4);
+    if (rows >= (1LL << 31) || groups4 >= (1LL << 32)) {
       set_error(kInvalid, "%s: tensor too large", c.name());
       c.fail();
       return false;
     }
-    Operand A, B;
-    float* a = (float*)c.scratch((size_t)2 * rows * Cpad * 4);
-    float* b = (float*)c.scratch((size_t)2 * taps * Cpad * Np * 4);
+    void* a = c.scratch((size_t)2 * rows * Cpad * E);
+    void* b = c.scratch((size_t)2 * taps * Cpad * Np * E);
     if (!a || !b) return false;
-    const long long groups4 = rows * (Cpad / 4);
-    if (groups4 < (1LL << 31)) {
-      const int vec_in = (Cs % 4 == 0) && (coff % 4 == 0) && aligned16(x);
-      k_pad_split4<<<grid_ew(c, groups4), 256, 0, c.stream()>>>(
-          x, H, W, Cs, coff, Cg, pad, Hp, Wp, Cpad / 4, (unsigned)groups4, vec_in, (float4*)a,
-          (size_t)(rows * Cpad / 4));
-    } else {
-      k_pad_split<<<grid_ew(c, rows * Cpad), 256, 0, c.stream()>>>(x, N, H, W, Cs, coff, Cg, pad, Hp,
-                                                                   Wp, Cpad, a, rows * Cpad);
-    }
-    k_weights_split<<<grid_ew(c, (long long)taps * Cpad * Np), 256, 0, c.stream()>>>(
+    const int vec_in = (Cs % 4 == 0) && (coff % 4 == 0) && aligned16(x);
+    k_pad_split4<BF><<<grid_ew(c, groups4), 256, 0, c.stream()>>>(
+        x, H, W, Cs, coff, Cg, pad, Hp, Wp, Cpad / 4, (unsigned)groups4, vec_in, a, (size_t)(rows * Cpad));
+    k_weights_split<BF><<<grid_ew(c, (long long)taps * Cpad * Np), 256, 0, c.stream()>>>(
         w, taps, Cg, Cout_g, ldw, Cpad, Np, b, (long long)taps * Cpad * Np);
     if (!c.launched("conv prep")) return false;
     A.p = a;
@@ -278,28 +249,43 @@ bool conv_f32_dev(Call& c, const float* x, int N, int H, int W, int Cs, int coff
     ep.Wp = Wp;
     ep.OH = OH;
     ep.OW = OW;
-    ConvGeom cg{1, Cpad / 32, KW, Wp, Cpad, taps};
-    return gemm_launch(c, GemmKind::TF32X3, Epi::F32_BIAS, A, B, (int)rows, Cout_g, taps * Cpad,
-                       ep, cg);
+    ConvGeom cg{1, Cpad / BKE, KW, Wp, Cpad, taps};
+    return gemm_launch(c, kind, Epi::F32_BIAS, A, B, (int)rows, Cout_g, taps * Cpad, ep, cg);
   }
   const long long M = (long long)N * OH * OW;
-  const int K = taps * Cg, Kpad = (int)align_up((size_t)K, 4);
-  float* a = (float*)c.scratch((size_t)2 * M * Kpad * 4);
-  float* b = (float*)c.scratch((size_t)2 * K * Np * 4);
+  const int K = taps * Cg, Kpad = (int)align_up((size_t)K, BF ? 8 : 4);
+  void* a = c.scratch((size_t)2 * M * Kpad * E);
+  void* b = c.scratch((size_t)2 * K * Np * E);
   if (!a || !b) return false;
-  k_im2col_split<<<grid_ew(c, M * Kpad), 256, 0, c.stream()>>>(x, N, H, W, Cs, coff, Cg, KH, KW,
-                                                               stride, pad, OH, OW, Kpad, a, M * Kpad);
-  k_weights_split<<<grid_ew(c, (long long)K * Np), 256, 0, c.stream()>>>(w, 1, K, Cout_g, ldw, K,
-                                                                        Np, b, (long long)K * Np);
+  k_im2col_split<BF><<<grid_ew(c, M * Kpad), 256, 0, c.stream()>>>(x, N, H, W, Cs, coff, Cg, KH, KW,
+                                                                   stride, pad, OH, OW, Kpad, a, M * Kpad);
+  k_weights_split<BF><<<grid_ew(c, (long long)K * Np), 256, 0, c.stream()>>>(w, 1, K, Cout_g, ldw, K,
+                                                                            Np, b, (long long)K * Np);
   if (!c.launched("im2col prep")) return false;
-  Operand A, B;
   A.p = a;
   A.ld = Kpad;
   A.op_stride = M * Kpad;
   B.p = b;
   B.ld = Np;
   B.op_stride = (long long)K * Np;
-  return gemm_launch(c, GemmKind::TF32X3, Epi::F32_BIAS, A, B, (int)M, Cout_g, K, ep);
+  return gemm_launch(c, kind, Epi::F32_BIAS, A, B, (int)M, Cout_g, K, ep);
+}
+
+bool conv_f32_dev(Call& c, const float* x, int N, int H, int W, int Cs, int coff, int Cg,
+                  const float* w, long long ldw, const float* bias, int KH, int KW, int Cout_g,
+                  int stride, int pad, float* out, long long ldc, int act) {
+  const int OH = (H + 2 * pad - KH) / stride + 1, OW = (W + 2 * pad - KW) / stride + 1;
+  if (OH <= 0 || OW <= 0 || N <= 0 || Cout_g <= 0) return true;
+  bool handled = false;
+  if (!conv_simt(c, x, N, H, W, Cs, coff, Cg, w, ldw, bias, KH, KW, Cout_g, stride, pad, out, ldc,
+                 act, &handled))
+    return false;
+  if (handled) return true;
+  if (fp32_math(Fp32Use::Conv) == Fp32Math::BF16X3)
+    return conv_tc<true>(c, x, N, H, W, Cs, coff, Cg, w, ldw, bias, KH, KW, Cout_g, stride, pad, out,
+                         ldc, act);
+  return conv_tc<false>(c, x, N, H, W, Cs, coff, Cg, w, ldw, bias, KH, KW, Cout_g, stride, pad, out,
+                        ldc, act);
 }
 
 int conv_route(int H, int W, int Cin, int KH, int KW, int Cout, int stride, int pad, int groups) {
@@ -432,7 +418,7 @@ static void fc_api(const char* name, const float* input, int N, int Cin, const f
   const float* db = bias ? (const float*)c.in(bias, (size_t)Cout * 4) : nullptr;
   float* dout = (float*)c.out(output, (size_t)N * Cout * 4);
   if (!c.ok()) return;
-  gemm_f32(c, dx, Cin, dw, Cout, N, Cout, Cin, dout, Cout, db, act);
+  gemm_f32(c, dx, Cin, dw, Cout, N, Cout, Cin, dout, Cout, db, act, Fp32Use::Conv);
   c.finish();
 }
 

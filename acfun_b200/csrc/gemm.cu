@@ -7,6 +7,10 @@
 //   acfun_gemm_int8_epi           + (float)acc*alpha + beta    [gemm_int8.cpp:69-75]
 //   acfun_gemm_s8_requant         s8 x s8 -> requantised s8    [no counterpart]
 #include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <atomic>
 
 #include "api_export.cuh"
 #include "gemm.cuh"
@@ -140,6 +144,85 @@ Operand to_tf32x2(Call& c, const float* src, int rows, int cols, long long lds) 
   return o;
 }
 
+// Round-to-nearest-even fp32 -> bf16 with NaN kept quiet (for the 3xBF16 split; the
+// bf16 GEMM entry point keeps the reference's bit trick, bf16_bits_ref).
+__device__ __forceinline__ uint16_t bf16_rne(float f) {
+  const uint32_t x = __float_as_uint(f);
+  if ((x & 0x7f800000u) == 0x7f800000u) return (uint16_t)((x >> 16) | ((x & 0xffffu) ? 0x40u : 0u));
+  return (uint16_t)((x + 0x7fffu + ((x >> 16) & 1u)) >> 16);
+}
+__device__ __forceinline__ float bf16_val(uint16_t h) { return __uint_as_float((uint32_t)h << 16); }
+
+// 3xBF16 split: x = hi + lo + r with hi = bf16(x), lo = bf16(x - hi), |r| <= 2^-18 |x|;
+// fp32 [rows][cols] -> [2][rows][ldp] bf16, zero padding (ldp a multiple of 8).
+__global__ void k_to_bf16x2(const float* __restrict__ src, long long lds, int rows, int cols,
+                            uint16_t* __restrict__ dst, long long ldp, long long op_stride) {
+  const long long groups = ldp / 4;
+  const long long total = (long long)rows * groups;
+  for (long long g = blockIdx.x * (long long)blockDim.x + threadIdx.x; g < total;
+       g += (long long)gridDim.x * blockDim.x) {
+    const long long r = g / groups;
+    const int j = (int)(g - r * groups) * 4;
+    const float* s = src + r * lds;
+    uint32_t hi2[2], lo2[2];
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      uint32_t hp = 0, lp = 0;
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int jj = j + 2 * t + u;
+        const float x = jj < cols ? s[jj] : 0.0f;
+        const uint16_t h = bf16_rne(x);
+        const uint16_t l = bf16_rne(x - bf16_val(h));
+        hp |= (uint32_t)h << (16 * u);
+        lp |= (uint32_t)l << (16 * u);
+      }
+      hi2[t] = hp;
+      lo2[t] = lp;
+    }
+    *reinterpret_cast<uint2*>(dst + r * ldp + j) = make_uint2(hi2[0], hi2[1]);
+    *reinterpret_cast<uint2*>(dst + op_stride + r * ldp + j) = make_uint2(lo2[0], lo2[1]);
+  }
+}
+
+Operand to_bf16x2(Call& c, const float* src, int rows, int cols, long long lds) {
+  Operand o;
+  if (!c.ok()) return o;
+  const long long ldp = (long long)align_up((size_t)cols, 8);
+  uint16_t* d = (uint16_t*)c.scratch((size_t)2 * rows * ldp * 2);
+  if (!d) return o;
+  k_to_bf16x2<<<ew_grid(c, rows * (ldp / 4)), 256, 0, c.stream()>>>(src, lds, rows, cols, d, ldp,
+                                                                      (long long)rows * ldp);
+  if (!c.launched("k_to_bf16x2")) return o;
+  o.p = d;
+  o.ld = ldp;
+  o.op_stride = (long long)rows * ldp;
+  return o;
+}
+
+// 0: per use (SGEMM API 3xTF32, convolution / FC / model 3xBF16); 1: 3xTF32 everywhere;
+// 2: 3xBF16 everywhere.  Initialised from ACFUN_FP32_MATH, changed by acfun_set_fp32_math.
+static std::atomic<int> g_fp32_mode{-1};
+
+static int fp32_mode() {
+  int m = g_fp32_mode.load();
+  if (m < 0) {
+    const char* e = getenv("ACFUN_FP32_MATH");
+    m = !e ? 0 : (!strcmp(e, "tf32x3") ? 1 : (!strcmp(e, "bf16x3") ? 2 : 0));
+    int expect = -1;
+    g_fp32_mode.compare_exchange_strong(expect, m);
+    m = g_fp32_mode.load();
+  }
+  return m;
+}
+
+Fp32Math fp32_math(Fp32Use use) {
+  const int m = fp32_mode();
+  if (m == 1) return Fp32Math::TF32X3;
+  if (m == 2) return Fp32Math::BF16X3;
+  return use == Fp32Use::GemmApi ? Fp32Math::TF32X3 : Fp32Math::BF16X3;
+}
+
 // ------------------------------------------------------------------ launcher
 template <dev::MmaKind KIND, int BN, int STAGES, int NPASS, Epi EPI, bool AS>
 static bool launch_one(Call& c, const Operand& A, const Operand& B, int M, int N, int K,
@@ -204,7 +287,8 @@ static long long tiles(int M, int N, int bn) {
 }
 
 int gemm_bke(GemmKind kind) {
-  return kind == GemmKind::BF16 ? 64 : kind == GemmKind::TF32X3 ? 32 : 128;
+  return (kind == GemmKind::BF16 || kind == GemmKind::BF16X3) ? 64
+         : kind == GemmKind::TF32X3 ? 32 : 128;
 }
 
 bool gemm_launch(Call& c, GemmKind kind, Epi epi, const Operand& A, const Operand& B, int M,
@@ -248,6 +332,12 @@ bool gemm_launch(Call& c, GemmKind kind, Epi epi, const Operand& A, const Operan
         return launch_one<MK::F16, 128, 6, 1, Epi::F32_BIAS, false>(c, A, B, M, N, K, ep, cg);
       return launch_one<MK::F16, 64, 8, 1, Epi::F32_BIAS, false>(c, A, B, M, N, K, ep, cg);
     }
+    case GemmKind::BF16X3: {
+      if (epi != Epi::F32_BIAS) break;
+      if (N > 64 && tiles(M, N, 128) >= sms)
+        return launch_one<MK::F16, 128, 3, 3, Epi::F32_BIAS, false>(c, A, B, M, N, K, ep, cg);
+      return launch_one<MK::F16, 64, 4, 3, Epi::F32_BIAS, false>(c, A, B, M, N, K, ep, cg);
+    }
     case GemmKind::TF32X3: {
       if (epi != Epi::F32_BIAS) break;
       if (N > 64 && tiles(M, N, 128) >= sms)
@@ -264,15 +354,16 @@ bool gemm_launch(Call& c, GemmKind kind, Epi epi, const Operand& A, const Operan
 
 // fp32 GEMM (+bias, +ReLU) on device operands, used by GEMM, FC and conv routes.
 bool gemm_f32(Call& c, const float* dA, long long lda, const float* dB, long long ldb, int M,
-              int N, int K, float* dC, long long ldc, const float* dbias, int act) {
-  Operand a = to_tf32x2(c, dA, M, K, lda);
-  Operand b = to_tf32x2(c, dB, K, N, ldb);
+              int N, int K, float* dC, long long ldc, const float* dbias, int act, Fp32Use use) {
+  const bool bf = fp32_math(use) == Fp32Math::BF16X3;
+  Operand a = bf ? to_bf16x2(c, dA, M, K, lda) : to_tf32x2(c, dA, M, K, lda);
+  Operand b = bf ? to_bf16x2(c, dB, K, N, ldb) : to_tf32x2(c, dB, K, N, ldb);
   EpiParams ep{};
   ep.C = dC;
   ep.ldc = ldc;
   ep.f0 = dbias;
   ep.act = act;
-  return gemm_launch(c, GemmKind::TF32X3, Epi::F32_BIAS, a, b, M, N, K, ep);
+  return gemm_launch(c, bf ? GemmKind::BF16X3 : GemmKind::TF32X3, Epi::F32_BIAS, a, b, M, N, K, ep);
 }
 
 }  // namespace acf
@@ -297,7 +388,7 @@ extern "C" void acfun_gemm_epi(int M, int N, int K, const float* A, const float*
   const float* db = bias ? (const float*)c.in(bias, (size_t)N * 4) : nullptr;
   float* dC = (float*)c.out(C, (size_t)M * N * 4);
   if (!c.ok()) return;
-  gemm_f32(c, dA, K, dB, N, M, N, K, dC, N, db, act ? 1 : 0);
+  gemm_f32(c, dA, K, dB, N, M, N, K, dC, N, db, act ? 1 : 0, Fp32Use::GemmApi);
   c.finish();
 }
 
@@ -387,4 +478,14 @@ extern "C" void acfun_gemm_s8_requant(int M, int N, int K, const int8_t* A, cons
   ep.act = act ? 1 : 0;
   gemm_launch(c, GemmKind::I8S, Epi::S8_REQ, a, b, M, N, K, ep);
   c.finish();
+}
+
+extern "C" int acfun_set_fp32_math(int mode) {
+  if (mode < 0 || mode > 2) {
+    set_error(kInvalid, "acfun_set_fp32_math: mode must be 0, 1 or 2");
+    return kInvalid;
+  }
+  fp32_mode();
+  g_fp32_mode.store(mode);
+  return 0;
 }

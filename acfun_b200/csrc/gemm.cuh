@@ -29,7 +29,17 @@ Operand to_tf32x2(Call& c, const float* src_dev, int rows, int cols, long long l
 __global__ void k_to_tf32x2(const float* __restrict__ src, long long lds, int rows, int cols,
                             float* __restrict__ dst, long long ldp, long long op_stride);
 
-enum class GemmKind { I8U, I8S, BF16, TF32X3 };
+enum class GemmKind { I8U, I8S, BF16, TF32X3, BF16X3 };
+
+// fp32 math on tensor cores: 3xTF32 (tf32 hi/lo, ~2^-21 per product) or 3xBF16 (bf16
+// hi/lo on kind::f16: twice the MMA rate and half the operand bytes of 3xTF32, ~2^-17 per
+// product).  The public SGEMM entry points default to 3xTF32, convolutions / FC / the model
+// to 3xBF16; ACFUN_FP32_MATH=tf32x3|bf16x3 forces one mode everywhere.
+enum class Fp32Math { TF32X3, BF16X3 };
+enum class Fp32Use { GemmApi, Conv };
+Fp32Math fp32_math(Fp32Use use);
+// fp32 -> [2][rows][ldp] bf16 (hi, lo) for 3xBF16, ldp a multiple of 8.
+Operand to_bf16x2(Call& c, const float* src_dev, int rows, int cols, long long lds);
 
 // C-tile launch: chooses the tile width from the problem size and the SM count.
 // With cg.enabled, A is a padded NHWC tensor [rows][cpad] and B the weights

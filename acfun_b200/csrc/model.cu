@@ -22,6 +22,7 @@
 
 #include "api_export.cuh"
 #include "conv.cuh"
+#include "gemm.cuh"
 #include "ops.cuh"
 #include "runtime.cuh"
 
@@ -328,15 +329,24 @@ static bool run_model(Call& c, AcfunModel* m, int n, const float* x, float* y) {
   int H = m->inH, W = m->inW, C = m->inC;
   const float* cur = x;
   int which = 0;
-  for (auto& L : m->layers) {
+  const size_t nl = m->layers.size();
+  for (size_t li = 0; li < nl; ++li) {
+    auto& L = m->layers[li];
     float* next = m->buf[which];
     bool ok = true;
+    // A standalone ReLU right after a Conv / FC (the loader keeps Conv->BN->ReLU's ReLU
+    // separate, model.cpp:211-226) is applied in that layer's epilogue instead of a pass.
+    int act = L.act;
+    if ((L.type == 1 || L.type == 2 || L.type == 7) && li + 1 < nl && m->layers[li + 1].type == 3) {
+      act = 1;
+      ++li;
+    }
     switch (L.type) {
       case 1:
       case 7: {
         const int KH = L.p[0], KW = L.p[1], Cout = L.p[2], st = L.p[3], pd = L.p[4];
         const int groups = L.type == 7 ? L.p[5] : 1;
-        ok = conv2d_dev(c, cur, n, H, W, C, L.w, L.b, KH, KW, Cout, st, pd, groups, next, L.act);
+        ok = conv2d_dev(c, cur, n, H, W, C, L.w, L.b, KH, KW, Cout, st, pd, groups, next, act);
         H = (H + 2 * pd - KH) / st + 1;
         W = (W + 2 * pd - KW) / st + 1;
         C = Cout;
@@ -346,7 +356,7 @@ static bool run_model(Call& c, AcfunModel* m, int n, const float* x, float* y) {
       }
       case 2: {
         const int Cout = L.p[0], inDim = H * W * C;
-        ok = gemm_f32(c, cur, inDim, L.w, Cout, n, Cout, inDim, next, Cout, L.b, L.act);
+        ok = gemm_f32(c, cur, inDim, L.w, Cout, n, Cout, inDim, next, Cout, L.b, act, Fp32Use::Conv);
         H = W = 1;
         C = Cout;
         cur = next;

@@ -1,0 +1,73 @@
+// numerics.cuh — operand splitting for fp32 math on tensor cores.
+//   3xTF32: x -> (tf32(x), tf32(x - tf32(x))), both stored as fp32 bit patterns
+//   3xBF16: x -> (bf16(x), bf16(x - bf16(x))), stored as bf16
+// Rounding is to nearest even; Inf / NaN pass through the high part.
+#pragma once
+#include <stdint.h>
+
+namespace acf {
+
+static __device__ __forceinline__ float nx_tf32_rne(float x) {
+  uint32_t u = __float_as_uint(x);
+  if ((u & 0x7f800000u) == 0x7f800000u) return x;
+  u += 0xfffu + ((u >> 13) & 1u);
+  return __uint_as_float(u & 0xffffe000u);
+}
+
+static __device__ __forceinline__ uint16_t nx_bf16_rne(float f) {
+  const uint32_t x = __float_as_uint(f);
+  if ((x & 0x7f800000u) == 0x7f800000u) return (uint16_t)((x >> 16) | ((x & 0xffffu) ? 0x40u : 0u));
+  return (uint16_t)((x + 0x7fffu + ((x >> 16) & 1u)) >> 16);
+}
+
+static __device__ __forceinline__ float nx_bf16_val(uint16_t h) {
+  return __uint_as_float((uint32_t)h << 16);
+}
+
+// Store the split of 4 consecutive values at element index 4*i of the hi plane and the same
+// index of the lo plane (op_stride elements further).
+template <bool BF>
+static __device__ __forceinline__ void nx_store_split4(void* dst, size_t i4, size_t op_stride,
+                                                       const float (&v)[4]) {
+  if constexpr (BF) {
+    uint16_t h[4], l[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      h[k] = nx_bf16_rne(v[k]);
+      l[k] = nx_bf16_rne(v[k] - nx_bf16_val(h[k]));
+    }
+    uint16_t* d = reinterpret_cast<uint16_t*>(dst) + 4 * i4;
+    *reinterpret_cast<uint2*>(d) =
+        make_uint2((uint32_t)h[0] | ((uint32_t)h[1] << 16), (uint32_t)h[2] | ((uint32_t)h[3] << 16));
+    *reinterpret_cast<uint2*>(d + op_stride) =
+        make_uint2((uint32_t)l[0] | ((uint32_t)l[1] << 16), (uint32_t)l[2] | ((uint32_t)l[3] << 16));
+  } else {
+    float h[4], l[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      h[k] = nx_tf32_rne(v[k]);
+      l[k] = nx_tf32_rne(v[k] - h[k]);
+    }
+    float* d = reinterpret_cast<float*>(dst) + 4 * i4;
+    *reinterpret_cast<float4*>(d) = make_float4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<float4*>(d + op_stride) = make_float4(l[0], l[1], l[2], l[3]);
+  }
+}
+
+// Scalar store of one split value at element index i.
+template <bool BF>
+static __device__ __forceinline__ void nx_store_split1(void* dst, size_t i, size_t op_stride, float x) {
+  if constexpr (BF) {
+    const uint16_t h = nx_bf16_rne(x);
+    uint16_t* d = reinterpret_cast<uint16_t*>(dst) + i;
+    d[0] = h;
+    d[op_stride] = nx_bf16_rne(x - nx_bf16_val(h));
+  } else {
+    const float h = nx_tf32_rne(x);
+    float* d = reinterpret_cast<float*>(dst) + i;
+    d[0] = h;
+    d[op_stride] = nx_tf32_rne(x - h);
+  }
+}
+
+}  // namespace acf

@@ -16,7 +16,8 @@ bool dw_dev(Call& c, const float* in, int N, int H, int W, int C, const float* w
 bool group_dev(Call& c, const float* in, int N, int H, int W, int Cin, const float* w,
                const float* bias, int KH, int KW, int Cout, int stride, int pad, int groups,
                float* out, int act);
-// fp32 GEMM on device operands via 3xTF32 (gemm.cu)
+// fp32 GEMM on device operands on tensor cores (3xTF32 or 3xBF16 per fp32_math, gemm.cu)
+enum class Fp32Use;
 bool gemm_f32(Call& c, const float* dA, long long lda, const float* dB, long long ldb, int M,
-              int N, int K, float* dC, long long ldc, const float* dbias, int act);
+              int N, int K, float* dC, long long ldc, const float* dbias, int act, Fp32Use use);
 }  // namespace acf

@@ -211,6 +211,7 @@ def measure_configs(acf, torch, stream, flush, steps, with_cpu=True, cfg_filter=
     bf16, hbm, src = measured_peaks()
     peak = {"int8": (2 * bf16, "TOPS", f"2 x bf16 ({src})"), "bf16": (bf16, "TFLOP/s", src),
             "f32x3": (bf16 / 6, "TFLOP/s", f"3xTF32 ceiling = bf16/2/3 ({src})"),
+            "f32bf3": (bf16 / 3, "TFLOP/s", f"3xBF16 ceiling = bf16/3 ({src})"),
             "hbm": (hbm, "GB/s", src)}
     cores = os.cpu_count() or 1
     R = P.ref() if (with_cpu and P.ref_available()) else None
@@ -326,7 +327,7 @@ def measure_configs(acf, torch, stream, flush, steps, with_cpu=True, cfg_filter=
             cfn = lambda: R.acfun_conv2d_g(xs, ns, H, W, Cin, np.ascontiguousarray(w), b.ctypes.data, KH, KH,
                                            Cout, st, pd, groups, os_, 1)
         t = timeit(fn, steps)
-        bound = bound or ("int8" if int8 else "f32x3")
+        bound = bound or ("int8" if int8 else "f32bf3")
         if bound == "hbm":
             cv = cpu(cfn, ns * nbytes / N, 1e-9)
             record(name, t, nbytes, 1e9, "hbm", cv, f"{ns} of {N} images, reference route",
@@ -366,7 +367,7 @@ def measure_configs(acf, torch, stream, flush, steps, with_cpu=True, cfg_filter=
             cv = cpu(lambda: [R.acfun_model_infer(h, x0, o) for _ in range(2)], 2, 1.0)
             R.acfun_model_destroy(h)
         gf = 15.218e9
-        record("cfg5_vgg11_b256", t, n * gf, 1e12, "f32x3", None, "",
+        record("cfg5_vgg11_b256", t, n * gf, 1e12, "f32bf3", None, "",
                {"img_per_s": round(n / t, 1), "gflop_per_img": 15.218})
         if cv is not None:
             out["cfg5_vgg11_b256"]["cpu_baseline"] = {"value": round(cv, 3), "unit": "img/s", "cores": cores,
