@@ -377,6 +377,76 @@ def measure_configs(acf, torch, stream, flush, steps, with_cpu=True, cfg_filter=
     return out
 
 
+def vgg_model_path(rank, world, dist):
+    """The cfg5 VGG-11 ACFUN0 file (generated once per box by rank 0, seeded)."""
+    import tempfile
+
+    from acfun_b200 import acfun0
+    path = os.path.join(tempfile.gettempdir(), "acfun_vgg11_seed5.acfun")
+    if rank == 0 and not os.path.exists(path):
+        tmp = path + ".part"
+        acfun0.vgg11(seed=5).save(tmp)
+        os.replace(tmp, path)
+    if world > 1:
+        dist.barrier()
+    return path
+
+
+def measure_vgg_sharded(acf, torch, dist, stream, flush, rank, world, steps, n=256):
+    """cfg5 across `world` GPUs: rank r infers its contiguous share of the 256-image batch
+    (acfun_model_infer_batch, device-resident), then the [256, 1000] outputs are all-gathered
+    over NCCL.  Time per step = max over ranks of (inference + gather); img/s = 256 / t."""
+    from acfun_b200.shard import gather_outputs, shard_bounds
+    L = acf.lib()
+    path = vgg_model_path(rank, world, dist)
+    m = acf.Model(path)
+    b, e = shard_bounds(n, world, rank)
+    g = np.random.default_rng(77)
+    x_all = g.uniform(0, 1, (n, 224, 224, 3)).astype(np.float32)
+    dx = torch.from_numpy(np.ascontiguousarray(x_all[b:e])).cuda()
+    dy = torch.empty((e - b, 1000), device="cuda")
+
+    def step():
+        if L.acfun_model_infer_batch(m.h, e - b, dx.data_ptr(), dy.data_ptr()) <= 0:
+            acf.check()
+        if world > 1:
+            return gather_outputs(dist, dy, n, world)
+        return dy
+
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    acf.check()
+    total = 0.0
+    for _ in range(steps):
+        flush.fill_(1)
+        if world > 1:
+            dist.barrier()
+        s, t = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        out = step()
+        t.record(stream)
+        torch.cuda.synchronize()
+        total += s.elapsed_time(t) / 1e3
+    tt = total / steps
+    if world > 1:
+        tv = torch.tensor([tt], device="cuda")
+        dist.all_reduce(tv, op=dist.ReduceOp.MAX)
+        tt = float(tv[0])
+    acf.check()
+    ok = bool(torch.isfinite(out).all()) and abs(float(out.sum()) - n) < 1e-2 * n  # softmax rows
+    m.close()
+    bf16, _, src = measured_peaks()
+    pk = bf16 / 3
+    achieved = n * 15.218e9 / tt / 1e12
+    return {"ms": round(tt * 1e3, 3), "value": round(n / tt, 1), "unit": "img/s", "n_gpus": world,
+            "images_per_gpu": e - b, "outputs_valid": ok,
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(pk * world, 1),
+                         "unit": "TFLOP/s", "frac": round(achieved / (pk * world), 4),
+                         "peak_source": f"3xBF16 ceiling = bf16/3 ({src}) x n_gpus"},
+            "collective": "NCCL all-gather of the [256,1000] outputs (1 MB) only" if world > 1 else None}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -388,6 +458,8 @@ def main():
     ap.add_argument("--no-configs", action="store_true",
                     help="skip the per-config measurements (every BASELINE config, N=1 only)")
     ap.add_argument("--configs", default=None, help="comma-separated subset of config names")
+    ap.add_argument("--only-configs", action="store_true",
+                    help="print only the per-config measurements (profiling runs; not the bench line)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl != "reference" else args.warmup
 
@@ -413,6 +485,14 @@ def main():
         acf.check()
     stream = torch.cuda.current_stream()
     L.acfun_set_stream(stream.cuda_stream)
+
+    if args.only_configs:
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+        filt = set(args.configs.split(",")) if args.configs else None
+        res = measure_configs(acf, torch, stream, flush, steps=max(1, args.steps),
+                              with_cpu=not args.no_cpu_baseline, cfg_filter=filt)
+        print(json.dumps({"configs": res}), flush=True)
+        return
 
     A, B, bias, scale = make_inputs(1234 + rank)
     dA, dB = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
@@ -476,6 +556,10 @@ def main():
         t_dev_max, t_e2e_max = float(tt[0]), float(tt[1])
         dist.barrier()
 
+    vgg = None
+    if world > 1 and not args.no_configs:
+        vgg = measure_vgg_sharded(acf, torch, dist, stream, flush, rank, world, steps=max(3, min(args.steps, 10)))
+
     if rank == 0:
         bf16_peak, hbm_peak, peak_src = measured_peaks()
         peak_tops = 2.0 * bf16_peak
@@ -510,6 +594,8 @@ def main():
             filt = set(args.configs.split(",")) if args.configs else None
             line["configs"] = measure_configs(acf, torch, stream, flush, steps=max(5, min(args.steps, 20)),
                                               with_cpu=not args.no_cpu_baseline, cfg_filter=filt)
+        if vgg is not None:
+            line["configs"] = {"cfg5_vgg11_b256_sharded": vgg}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
