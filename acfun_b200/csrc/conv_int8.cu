@@ -42,10 +42,29 @@ static int grid_n(Call& c, long long work) {
 __global__ void k_absmax(const float* __restrict__ x, long long n, Int8Scalars* s) {
   __shared__ float sh[32];
   float m = 0.0f;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
-       i += (long long)gridDim.x * blockDim.x) {
-    const float v = fabsf(x[i]);
-    m = (m < v) ? v : m;
+  if ((reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+    const long long n4 = n >> 2;
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4;
+         i += (long long)gridDim.x * blockDim.x) {
+      const float4 q = __ldg(x4 + i);
+      const float a = fabsf(q.x), b = fabsf(q.y), cc = fabsf(q.z), d = fabsf(q.w);
+      m = (m < a) ? a : m;
+      m = (m < b) ? b : m;
+      m = (m < cc) ? cc : m;
+      m = (m < d) ? d : m;
+    }
+    for (long long i = (n4 << 2) + blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x) {
+      const float v = fabsf(x[i]);
+      m = (m < v) ? v : m;
+    }
+  } else {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x) {
+      const float v = fabsf(x[i]);
+      m = (m < v) ? v : m;
+    }
   }
   for (int o = 16; o > 0; o >>= 1) {
     const float u = __shfl_xor_sync(0xffffffffu, m, o);
@@ -360,7 +379,7 @@ bool conv2d_int8_dev(Call& c, const float* x, int N, int H, int W, int Cin, cons
   if (!s || !f0 || !f1 || !Sw) return false;
   if (!ACF_CUDA_OK(cudaMemsetAsync(s, 0, sizeof(Int8Scalars), c.stream()))) return false;
   const long long n = (long long)N * H * W * Cin;
-  k_absmax<<<grid_n(c, n), 256, 0, c.stream()>>>(x, n, s);
+  k_absmax<<<grid_n(c, n / 4 + 1), 256, 0, c.stream()>>>(x, n, s);
   k_int8_scalars<<<1, 1, 0, c.stream()>>>(s);
   const bool wino = is_wino_route(H, W, Cin, KH, KW, Cout, stride, pad);
   // Winograd: f0 = wso, f1 = bias (or NULL); others: f0 = alpha, f1 = beta

@@ -335,6 +335,82 @@ __global__ void k_dw_row(const float* __restrict__ in, int H, int W, int C,
   }
 }
 
+// Register-tiled depthwise: one block per output row, one thread per (strip of TW outputs
+// along W, 4 channels).  For each kernel row the thread loads the (TW-1)*stride+KW input
+// columns of its strip once and reuses them across the window; per output the FMA order is
+// the reference's (bias, then kh outer, kw inner, zeros for taps outside the image), so the
+// result is bit-identical to k_dw_row.  KW and the stride are template parameters so the
+// column window stays in registers.
+template <int TW, int KW, int STRIDE>
+__global__ void k_dw_strip(const float* __restrict__ in, int H, int W, int C,
+                           const float* __restrict__ w, const float* __restrict__ bias, int KH,
+                           int pad, int OH, int OW, float* __restrict__ out, int act) {
+  constexpr int NCOL = (TW - 1) * STRIDE + KW;
+  constexpr int stride = STRIDE;
+  extern __shared__ float4 dss4[];
+  float* wT = reinterpret_cast<float*>(dss4);
+  const int K = KH * KW;
+  float* bs = wT + K * C;
+  for (int i = threadIdx.x; i < K * C; i += blockDim.x) {
+    const int k = i / C, c = i - k * C;
+    wT[i] = w[c * K + k];
+  }
+  for (int i = threadIdx.x; i < C; i += blockDim.x) bs[i] = bias ? bias[i] : 0.0f;
+  __syncthreads();
+  const int n = blockIdx.x / OH, oh = blockIdx.x - n * OH;
+  const int C4 = C >> 2, strips = (OW + TW - 1) / TW, items = strips * C4;
+  const float* img = in + (size_t)n * H * W * C;
+  float* orow = out + ((size_t)n * OH + oh) * OW * C;
+  for (int it = threadIdx.x; it < items; it += blockDim.x) {
+    const int s = it / C4, c = (it - s * C4) * 4;
+    const int ow0 = s * TW, iw0 = ow0 * stride - pad;
+    float4 acc[TW];
+    const float4 b4 = *reinterpret_cast<const float4*>(bs + c);
+#pragma unroll
+    for (int t = 0; t < TW; ++t) acc[t] = b4;
+    for (int kh = 0; kh < KH; ++kh) {
+      const int ih = oh * stride - pad + kh;
+      if (ih < 0 || ih >= H) continue;  // out-of-image taps are skipped, not multiplied by 0
+      float4 xc[NCOL];
+      unsigned ok = 0;
+#pragma unroll
+      for (int j = 0; j < NCOL; ++j) {
+        const int iw = iw0 + j;
+        xc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (iw >= 0 && iw < W) {
+          xc[j] = __ldg(reinterpret_cast<const float4*>(img + ((size_t)ih * W + iw) * C + c));
+          ok |= 1u << j;
+        }
+      }
+#pragma unroll
+      for (int kw = 0; kw < KW; ++kw) {
+        const float4 wv = *reinterpret_cast<const float4*>(wT + (kh * KW + kw) * C + c);
+#pragma unroll
+        for (int t = 0; t < TW; ++t) {
+          if (!((ok >> (t * STRIDE + kw)) & 1u)) continue;
+          const float4 x = xc[t * STRIDE + kw];
+          acc[t].x = __fmaf_rn(x.x, wv.x, acc[t].x);
+          acc[t].y = __fmaf_rn(x.y, wv.y, acc[t].y);
+          acc[t].z = __fmaf_rn(x.z, wv.z, acc[t].z);
+          acc[t].w = __fmaf_rn(x.w, wv.w, acc[t].w);
+        }
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < TW; ++t) {
+      if (ow0 + t >= OW) break;
+      float4 a = acc[t];
+      if (act == 1) {
+        a.x = a.x > 0.f ? a.x : 0.f;
+        a.y = a.y > 0.f ? a.y : 0.f;
+        a.z = a.z > 0.f ? a.z : 0.f;
+        a.w = a.w > 0.f ? a.w : 0.f;
+      }
+      *reinterpret_cast<float4*>(orow + (size_t)(ow0 + t) * C + c) = a;
+    }
+  }
+}
+
 __global__ void k_dw1(const float* __restrict__ in, int N, int H, int W, int C,
                       const float* __restrict__ w, const float* __restrict__ bias, int KH, int KW,
                       int stride, int pad, int OH, int OW, float* __restrict__ out, int act) {
@@ -367,8 +443,18 @@ bool dw_dev(Call& c, const float* in, int N, int H, int W, int C, const float* w
   const int OH = (H + 2 * pad - KH) / stride + 1, OW = (W + 2 * pad - KW) / stride + 1;
   if (OH <= 0 || OW <= 0 || N <= 0 || C <= 0) return true;
   const size_t smem = ((size_t)KH * KW * C + C) * 4;
-  if (C % 4 == 0 && aligned16(in) && aligned16(out) && smem <= 48 * 1024 &&
-      (long long)N * OH < (1LL << 31) && (long long)H * W * C < (1LL << 31)) {
+  const bool rowk = C % 4 == 0 && aligned16(in) && aligned16(out) && smem <= 48 * 1024 &&
+                    (long long)N * OH < (1LL << 31) && (long long)H * W * C < (1LL << 31);
+  if (rowk && KW == 3 && (stride == 1 || stride == 2)) {
+    if (stride == 1)
+      k_dw_strip<4, 3, 1><<<N * OH, 128, smem, c.stream()>>>(in, H, W, C, w, bias, KH, pad, OH, OW,
+                                                             out, act);
+    else
+      k_dw_strip<4, 3, 2><<<N * OH, 128, smem, c.stream()>>>(in, H, W, C, w, bias, KH, pad, OH, OW,
+                                                             out, act);
+    return c.launched("k_dw_strip");
+  }
+  if (rowk) {
     k_dw_row<<<N * OH, 256, smem, c.stream()>>>(in, H, W, C, w, bias, KH, KW, stride, pad, OH, OW,
                                                 out, act);
     return c.launched("k_dw_row");

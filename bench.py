@@ -221,7 +221,15 @@ def measure_configs(acf, torch, stream, flush, steps, with_cpu=True, cfg_filter=
     out = {}
 
     def timeit(fn, n):
-        fn()
+        # >= 3 warm-up calls and ~0.2 s of work: first calls grow the scratch workspace and
+        # load modules, and an idle GPU needs a moment to reach its working clocks
+        t0 = time.perf_counter()
+        for i in range(200):
+            fn()
+            if i >= 2:
+                torch.cuda.synchronize()
+                if time.perf_counter() - t0 > 0.2:
+                    break
         torch.cuda.synchronize()
         acf.check()
         evs = []
