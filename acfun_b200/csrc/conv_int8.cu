@@ -258,18 +258,29 @@ __global__ void k_im2col_u8(const uint8_t* __restrict__ xq, int N, int H, int W,
   }
 }
 
-// s8 weights [taps*Cin][Cout] -> [taps*Cpad][Np] with zero rows / columns in the padding
-__global__ void k_weights_s8(const int8_t* __restrict__ w, int taps, int Cin, int Cout, int Cpad,
-                             int Np, int8_t* __restrict__ dst) {
-  const long long total = (long long)taps * Cpad * Np;
+// s8 weights [taps*Cin][Cout] -> K-major [Cout][taps*Cpad] (row n holds output channel n's
+// taps, each tap's Cin weights followed by zeros up to Cpad).  One thread per 4 K bytes.
+__global__ void k_weights_s8k(const int8_t* __restrict__ w, int taps, int Cin, int Cout, int Cpad,
+                              int8_t* __restrict__ dst) {
+  const int K4 = taps * Cpad / 4;
+  const long long total = (long long)Cout * K4;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
-    const int j = (int)(i % Np);
-    const long long r = i / Np;
-    const int tap = (int)(r / Cpad), c = (int)(r % Cpad);
-    dst[i] = (c < Cin && j < Cout) ? w[((long long)tap * Cin + c) * Cout + j] : (int8_t)0;
+    const int n = (int)(i / K4), k = (int)(i - (long long)n * K4) * 4;
+    const int tap = k / Cpad, c0 = k - tap * Cpad;
+    uint32_t packed = 0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int c = c0 + e;
+      const int8_t v = c < Cin ? w[((long long)tap * Cin + c) * Cout + n] : (int8_t)0;
+      packed |= (uint32_t)(uint8_t)v << (8 * e);
+    }
+    reinterpret_cast<uint32_t*>(dst)[i] = packed;
   }
 }
+
+// 64-byte K blocks when they cut the channel padding (Cin mod 128 in 1..64), else 128
+static int int8_kblock(int k) { return (k % 128 != 0 && k % 128 <= 64) ? 64 : 128; }
 
 // Quantised input + exact integer conv + dequant epilogue.
 //   xf / xq: float input (quantised here with `qmode`, scalars from `s` or inv_host) or
@@ -293,7 +304,6 @@ static bool int8_conv_gemm(Call& c, const Int8ConvArgs& a, int N, int H, int W, 
   const int OH = (H + 2 * pad - KH) / stride + 1, OW = (W + 2 * pad - KW) / stride + 1;
   if (OH <= 0 || OW <= 0) return true;
   const int taps = KH * KW;
-  const int Np = (int)align_up((size_t)Cout, 16);
   EpiParams ep{};
   ep.C = out;
   ep.ldc = Cout;
@@ -305,10 +315,11 @@ static bool int8_conv_gemm(Call& c, const Int8ConvArgs& a, int N, int H, int W, 
   uint8_t* xq_dense = nullptr;  // unpadded u8 input for the gather path
   if (stride == 1 && Cin >= 32) {
     // implicit GEMM over the zero-point-padded tensor
-    const int Hp = H + 2 * pad, Wp = W + 2 * pad, Cpad = (int)align_up((size_t)Cin, 128);
+    const int bkb = int8_kblock(Cin);
+    const int Hp = H + 2 * pad, Wp = W + 2 * pad, Cpad = (int)align_up((size_t)Cin, bkb);
     const long long rows = (long long)N * Hp * Wp;
     uint8_t* A = (uint8_t*)c.scratch((size_t)rows * Cpad);
-    int8_t* B = (int8_t*)c.scratch((size_t)taps * Cpad * Np);
+    int8_t* B = (int8_t*)c.scratch((size_t)Cout * taps * Cpad);
     if (!A || !B) return false;
     if (a.xf && rows * (Cpad / 16) < (1LL << 31)) {
       const long long g16 = rows * (Cpad / 16);
@@ -322,21 +333,21 @@ static bool int8_conv_gemm(Call& c, const Int8ConvArgs& a, int N, int H, int W, 
     else
       k_pad_u8<<<grid_n(c, rows * Cpad), 256, 0, c.stream()>>>(a.xq, N, H, W, Cin, pad, Hp, Wp,
                                                                Cpad, A);
-    k_weights_s8<<<grid_n(c, (long long)taps * Cpad * Np), 256, 0, c.stream()>>>(wq, taps, Cin, Cout,
-                                                                                Cpad, Np, B);
+    k_weights_s8k<<<grid_n(c, (long long)Cout * taps * Cpad / 4), 256, 0, c.stream()>>>(
+        wq, taps, Cin, Cout, Cpad, B);
     if (!c.launched("int8 implicit prep")) return false;
     Operand Ao, Bo;
     Ao.p = A;
     Ao.ld = Cpad;
     Bo.p = B;
-    Bo.ld = Np;
+    Bo.ld = (long long)taps * Cpad;
     ep.remap = 1;
     ep.img_rows = Hp * Wp;
     ep.Wp = Wp;
     ep.OH = OH;
     ep.OW = OW;
-    ConvGeom cg{1, Cpad / 128, KW, Wp, Cpad, taps};
-    return gemm_launch(c, GemmKind::I8U, a.epi, Ao, Bo, (int)rows, Cout, taps * Cpad, ep, cg);
+    ConvGeom cg{1, Cpad / bkb, KW, Wp, Cpad, taps};
+    return gemm_launch_i8k(c, a.epi, Ao, Bo, (int)rows, Cout, taps * Cpad, ep, cg, bkb);
   }
   // explicit im2col over the quantised input
   const uint8_t* src = a.xq;
@@ -350,18 +361,19 @@ static bool int8_conv_gemm(Call& c, const Int8ConvArgs& a, int N, int H, int W, 
   const long long M = (long long)N * OH * OW;
   const int K = taps * Cin, Kpad = (int)align_up((size_t)K, 16);
   uint8_t* A = (uint8_t*)c.scratch((size_t)M * Kpad);
-  int8_t* B = (int8_t*)c.scratch((size_t)Kpad * Np);
+  int8_t* B = (int8_t*)c.scratch((size_t)Cout * Kpad);
   if (!A || !B) return false;
   k_im2col_u8<<<grid_n(c, M * Kpad), 256, 0, c.stream()>>>(src, N, H, W, Cin, KH, KW, stride, pad,
                                                            OH, OW, Kpad, A);
-  k_weights_s8<<<grid_n(c, (long long)Kpad * Np), 256, 0, c.stream()>>>(wq, 1, K, Cout, Kpad, Np, B);
+  k_weights_s8k<<<grid_n(c, (long long)Cout * Kpad / 4), 256, 0, c.stream()>>>(wq, 1, K, Cout,
+                                                                              Kpad, B);
   if (!c.launched("int8 im2col prep")) return false;
   Operand Ao, Bo;
   Ao.p = A;
   Ao.ld = Kpad;
   Bo.p = B;
-  Bo.ld = Np;
-  return gemm_launch(c, GemmKind::I8U, a.epi, Ao, Bo, (int)M, Cout, Kpad, ep);
+  Bo.ld = Kpad;
+  return gemm_launch_i8k(c, a.epi, Ao, Bo, (int)M, Cout, Kpad, ep, ConvGeom{}, int8_kblock(Kpad));
 }
 
 static bool is_wino_route(int H, int W, int Cin, int KH, int KW, int Cout, int stride, int pad) {

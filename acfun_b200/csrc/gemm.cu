@@ -224,24 +224,31 @@ Fp32Math fp32_math(Fp32Use use) {
 }
 
 // ------------------------------------------------------------------ launcher
-template <dev::MmaKind KIND, int BN, int STAGES, int NPASS, Epi EPI, bool AS>
+template <dev::MmaKind KIND, int BN, int STAGES, int NPASS, Epi EPI, bool AS, int BKB = 128,
+          bool BKM = false>
 static bool launch_one(Call& c, const Operand& A, const Operand& B, int M, int N, int K,
                        const EpiParams& ep, const ConvGeom& cg) {
-  using S = GemmShape<KIND, BN, STAGES, NPASS>;
+  using S = GemmShape<KIND, BN, STAGES, NPASS, BKB, BKM>;
   static_assert(S::SMEM <= 232448, "shared memory budget");
   const CUtensorMapDataType dt = (KIND == dev::MmaKind::I8) ? CU_TENSOR_MAP_DATA_TYPE_UINT8
                                  : (KIND == dev::MmaKind::F16) ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                                : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
   CUtensorMap ta, tb;
   const uint64_t E = S::ELEM;
-  const CUtensorMapSwizzle bswz =
-      (S::ELEM == 4) ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
+  const CUtensorMapSwizzle kswz =
+      (BKB == 128) ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  const CUtensorMapSwizzle bswz = BKM ? kswz
+                                  : (S::ELEM == 4) ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+                                                   : CU_TENSOR_MAP_SWIZZLE_128B;
   if (NPASS == 1) {
     const uint64_t dA[2] = {(uint64_t)K, (uint64_t)M}, sA[1] = {(uint64_t)A.ld * E};
     const uint32_t bA[2] = {(uint32_t)S::BKE, 128u};
-    const uint64_t dB[2] = {(uint64_t)N, (uint64_t)K}, sB[1] = {(uint64_t)B.ld * E};
-    const uint32_t bB[2] = {(uint32_t)(128 / S::ELEM), (uint32_t)S::BKE};
-    if (!encode_tmap(&ta, dt, 2, A.p, dA, sA, bA, CU_TENSOR_MAP_SWIZZLE_128B) ||
+    // K-major B: [N][K] rows, one BN-row box; MN-major B: [K][N], 128-byte N chunks
+    const uint64_t dB[2] = {BKM ? (uint64_t)K : (uint64_t)N, BKM ? (uint64_t)N : (uint64_t)K};
+    const uint64_t sB[1] = {(uint64_t)B.ld * E};
+    const uint32_t bB[2] = {BKM ? (uint32_t)S::BKE : (uint32_t)(128 / S::ELEM),
+                            BKM ? (uint32_t)BN : (uint32_t)S::BKE};
+    if (!encode_tmap(&ta, dt, 2, A.p, dA, sA, bA, kswz) ||
         !encode_tmap(&tb, dt, 2, B.p, dB, sB, bB, bswz)) {
       c.fail();
       return false;
@@ -253,13 +260,13 @@ static bool launch_one(Call& c, const Operand& A, const Operand& B, int M, int N
     const uint64_t dB[3] = {(uint64_t)N, (uint64_t)K, 2};
     const uint64_t sB[2] = {(uint64_t)B.ld * E, (uint64_t)B.op_stride * E};
     const uint32_t bB[3] = {(uint32_t)(128 / S::ELEM), (uint32_t)S::BKE, 1u};
-    if (!encode_tmap(&ta, dt, 3, A.p, dA, sA, bA, CU_TENSOR_MAP_SWIZZLE_128B) ||
+    if (!encode_tmap(&ta, dt, 3, A.p, dA, sA, bA, kswz) ||
         !encode_tmap(&tb, dt, 3, B.p, dB, sB, bB, bswz)) {
       c.fail();
       return false;
     }
   }
-  auto kern = gemm_tc_kernel<KIND, BN, STAGES, NPASS, EPI, AS>;
+  auto kern = gemm_tc_kernel<KIND, BN, STAGES, NPASS, EPI, AS, BKB, BKM>;
   static bool attr_done[64] = {false};
   const int dv = current_device();
   if (dv >= 0 && dv < 64 && !attr_done[dv]) {
@@ -289,6 +296,40 @@ static long long tiles(int M, int N, int bn) {
 int gemm_bke(GemmKind kind) {
   return (kind == GemmKind::BF16 || kind == GemmKind::BF16X3) ? 64
          : kind == GemmKind::TF32X3 ? 32 : 128;
+}
+
+template <Epi EPI>
+static bool launch_i8k(Call& c, const Operand& A, const Operand& B, int M, int N, int K,
+                       const EpiParams& ep, const ConvGeom& cg, int bkb) {
+  using MK = dev::MmaKind;
+  const int sms = c.sm_count();
+  const int bn = N <= 64 ? 64 : (N <= 128 ? (tiles(M, N, 128) >= sms ? 128 : 64)
+                                          : (tiles(M, N, 256) >= sms ? 256 : 128));
+  if (bkb == 64) {
+    if (bn == 64) return launch_one<MK::I8, 64, 16, 1, EPI, false, 64, true>(c, A, B, M, N, K, ep, cg);
+    return launch_one<MK::I8, 128, 12, 1, EPI, false, 64, true>(c, A, B, M, N, K, ep, cg);
+  }
+  if (bn == 64) return launch_one<MK::I8, 64, 8, 1, EPI, false, 128, true>(c, A, B, M, N, K, ep, cg);
+  if (bn == 128) return launch_one<MK::I8, 128, 6, 1, EPI, false, 128, true>(c, A, B, M, N, K, ep, cg);
+  return launch_one<MK::I8, 256, 4, 1, EPI, false, 128, true>(c, A, B, M, N, K, ep, cg);
+}
+
+bool gemm_launch_i8k(Call& c, Epi epi, const Operand& A, const Operand& B, int M, int N, int K,
+                     const EpiParams& ep, const ConvGeom& cg, int bkb) {
+  if (!c.ok() || !A.p || !B.p || (bkb != 64 && bkb != 128)) {
+    c.fail();
+    return false;
+  }
+  switch (epi) {
+    case Epi::F32_AB:
+      return launch_i8k<Epi::F32_AB>(c, A, B, M, N, K, ep, cg, bkb);
+    case Epi::I8_WINO:
+      return launch_i8k<Epi::I8_WINO>(c, A, B, M, N, K, ep, cg, bkb);
+    default:
+      set_error(kInvalid, "%s: unsupported int8 epilogue", c.name());
+      c.fail();
+      return false;
+  }
 }
 
 bool gemm_launch(Call& c, GemmKind kind, Epi epi, const Operand& A, const Operand& B, int M,

@@ -48,4 +48,11 @@ bool gemm_launch(Call& c, GemmKind kind, Epi epi, const Operand& A, const Operan
                  int N, int K, const EpiParams& ep, const ConvGeom& cg = ConvGeom{});
 int gemm_bke(GemmKind kind);  // K elements per pipeline block (128 bytes)
 
+// u8 x s8 GEMM with a K-major B ([N][K] rows, ld = row pitch in bytes) and `bkb`-byte K
+// blocks (64 or 128): tiles 64..256 wide, so narrow outputs (N <= 64) waste no MMA work.
+// With cg.enabled, B is [N][taps*cpad] and cg.cblocks counts bkb-byte channel blocks.
+// Epilogues: F32_AB, I8_WINO.
+bool gemm_launch_i8k(Call& c, Epi epi, const Operand& A, const Operand& B, int M, int N, int K,
+                     const EpiParams& ep, const ConvGeom& cg, int bkb);
+
 }  // namespace acf

@@ -66,27 +66,37 @@ struct KindTraits<dev::MmaKind::TF32> {
   static constexpr int ELEM = 4;
 };
 
-template <dev::MmaKind KIND, int BN, int STAGES, int NPASS>
+// BKB_ = K bytes per pipeline block (128: SW128 K-major rows; 64: SW64, for operands whose
+// K run per tap is 64 bytes).  B_KMAJ: B is stored [N][K] (K contiguous) and loaded like A as
+// one BN-row tile; otherwise B is [K][N] (MN-major) and loaded in 128-byte N chunks.
+template <dev::MmaKind KIND, int BN, int STAGES, int NPASS, int BKB_ = 128, bool B_KMAJ = false>
 struct GemmShape {
   static constexpr int ELEM = KindTraits<KIND>::ELEM;
   static constexpr int BM = 128;
-  static constexpr int BKB = 128;                      // K bytes per block
+  static constexpr int BKB = BKB_;                     // K bytes per block
   static constexpr int BKE = BKB / ELEM;               // K elements per block
+  static constexpr int KSTEPS = BKB / 32;              // 32-byte MMA K-steps per block
   static constexpr int NOPS = (NPASS == 3) ? 2 : 1;    // hi/lo operand copies
-  static constexpr int A_TILE = BM * BKB;              // 16 KB
-  static constexpr int NCHUNK = BN * ELEM / 128;       // 128-byte N chunks of B
-  static constexpr int CHUNK_B = BKE * 128;            // bytes per N chunk
+  static constexpr int A_TILE = BM * BKB;
+  static constexpr uint32_t K_LAYOUT = (BKB == 128) ? dev::UMMA_SW128 : dev::UMMA_SW64;
+  static constexpr int K_SBO = 8 * BKB;                // 8-row core-matrix group stride
+  static constexpr int NCHUNK = B_KMAJ ? 1 : BN * ELEM / 128;  // TMA boxes per B tile
+  static constexpr int CHUNK_B = B_KMAJ ? BN * BKB : BKE * 128;
   static constexpr int B_TILE = NCHUNK * CHUNK_B;
   static constexpr int STAGE = NOPS * (A_TILE + B_TILE);
-  static constexpr int KSTEP_B = (32 / ELEM) * 128;    // B descriptor advance per MMA K-step
+  // B descriptor advance per MMA K-step
+  static constexpr int KSTEP_B = B_KMAJ ? 32 : (32 / ELEM) * 128;
   // MN-major 32-bit (tf32) operands only exist in the 128B swizzle with 32-byte atoms
   // (4-row / 512-byte pattern, TMA SWIZZLE_128B_ATOM_32B); 8/16-bit use the 128B swizzle
-  // with 16-byte atoms (8-row / 1024-byte pattern).
-  static constexpr uint32_t B_LAYOUT = (ELEM == 4) ? dev::UMMA_SW128_B32 : dev::UMMA_SW128;
-  static constexpr int B_SBO = (ELEM == 4) ? 512 : 1024;
+  // with 16-byte atoms (8-row / 1024-byte pattern).  K-major B uses A's layout.
+  static constexpr uint32_t B_LAYOUT =
+      B_KMAJ ? K_LAYOUT : (ELEM == 4) ? dev::UMMA_SW128_B32 : dev::UMMA_SW128;
+  static constexpr int B_SBO = B_KMAJ ? K_SBO : (ELEM == 4) ? 512 : 1024;
+  static constexpr int B_LBO = B_KMAJ ? 16 : CHUNK_B;
   static constexpr int SMEM = STAGES * STAGE + 1024 + 256;
   static constexpr int TMEM_COLS = 2 * BN;  // double-buffered accumulator
-  static_assert(BN * ELEM % 128 == 0, "B tile must be whole 128-byte chunks");
+  static_assert(BKB == 128 || (BKB == 64 && B_KMAJ && NPASS == 1), "64-byte K blocks: K-major B");
+  static_assert(B_KMAJ || BN * ELEM % 128 == 0, "B tile must be whole 128-byte chunks");
   static_assert(BN == 32 || BN == 64 || BN == 128 || BN == 256, "TMEM columns");
 };
 
@@ -213,11 +223,12 @@ __device__ __forceinline__ void epi_store32(const EpiParams& ep, long long orow,
 // ring runs continuously across tiles, and the accumulator is double-buffered in TMEM
 // (2 x BN columns): the UMMA warp fills buffer i&1 while the epilogue warps drain the
 // other, so a tile's epilogue overlaps the next tile's MMAs.
-template <dev::MmaKind KIND, int BN, int STAGES, int NPASS, Epi EPI, bool A_SIGNED>
+template <dev::MmaKind KIND, int BN, int STAGES, int NPASS, Epi EPI, bool A_SIGNED, int BKB = 128,
+          bool B_KMAJ = false>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    EpiParams ep, ConvGeom cg, int M, int N, int K, unsigned* err) {
-  using S = GemmShape<KIND, BN, STAGES, NPASS>;
+  using S = GemmShape<KIND, BN, STAGES, NPASS, BKB, B_KMAJ>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -285,7 +296,10 @@ __global__ void __launch_bounds__(192, 1)
         for (int op = 0; op < S::NOPS; ++op) {
           uint8_t* a_dst = st + op * S::A_TILE;
           uint8_t* b_dst = st + S::NOPS * S::A_TILE + op * S::B_TILE;
-          if constexpr (S::NOPS == 1) {
+          if constexpr (B_KMAJ) {
+            dev::tma_load_2d(a_dst, &tmA, &full_bar[s], kx, ay);
+            dev::tma_load_2d(b_dst, &tmB, &full_bar[s], by, n0);
+          } else if constexpr (S::NOPS == 1) {
             dev::tma_load_2d(a_dst, &tmA, &full_bar[s], kx, ay);
 #pragma unroll
             for (int c = 0; c < S::NCHUNK; ++c)
@@ -314,7 +328,8 @@ __global__ void __launch_bounds__(192, 1)
                                : (KIND == dev::MmaKind::F16) ? 1u : 2u;
     constexpr uint32_t b_fmt = (KIND == dev::MmaKind::I8) ? 1u
                                : (KIND == dev::MmaKind::F16) ? 1u : 2u;
-    constexpr uint32_t idesc = dev::umma_idesc(c_fmt, a_fmt, b_fmt, 0u, 1u, 128u, (uint32_t)BN);
+    constexpr uint32_t idesc =
+        dev::umma_idesc(c_fmt, a_fmt, b_fmt, 0u, B_KMAJ ? 0u : 1u, 128u, (uint32_t)BN);
     const uint32_t smem_base = dev::smem_u32(smem);
     bool ok = true;
     uint32_t it = 0, local = 0;
@@ -337,10 +352,10 @@ __global__ void __launch_bounds__(192, 1)
         const uint32_t a_base = smem_base + s * S::STAGE;
         const uint32_t b_base = a_base + S::NOPS * S::A_TILE;
 #pragma unroll
-        for (int ks = 0; ks < 4; ++ks) {
+        for (int ks = 0; ks < S::KSTEPS; ++ks) {
           if constexpr (NPASS == 1) {
-            const uint64_t ad = dev::umma_sdesc(a_base + ks * 32, 16, 1024, dev::UMMA_SW128);
-            const uint64_t bd = dev::umma_sdesc(b_base + ks * S::KSTEP_B, S::CHUNK_B, S::B_SBO,
+            const uint64_t ad = dev::umma_sdesc(a_base + ks * 32, 16, S::K_SBO, S::K_LAYOUT);
+            const uint64_t bd = dev::umma_sdesc(b_base + ks * S::KSTEP_B, S::B_LBO, S::B_SBO,
                                                 S::B_LAYOUT);
             dev::umma<KIND>(d_tmem, ad, bd, idesc, (kb | ks) != 0);
           } else {
@@ -348,10 +363,10 @@ __global__ void __launch_bounds__(192, 1)
             const int aop[3] = {1, 0, 0}, bop[3] = {0, 1, 0};
 #pragma unroll
             for (int p = 0; p < 3; ++p) {
-              const uint64_t ad = dev::umma_sdesc(a_base + aop[p] * S::A_TILE + ks * 32, 16, 1024,
-                                                  dev::UMMA_SW128);
+              const uint64_t ad = dev::umma_sdesc(a_base + aop[p] * S::A_TILE + ks * 32, 16,
+                                                  S::K_SBO, S::K_LAYOUT);
               const uint64_t bd = dev::umma_sdesc(b_base + bop[p] * S::B_TILE + ks * S::KSTEP_B,
-                                                  S::CHUNK_B, S::B_SBO, S::B_LAYOUT);
+                                                  S::B_LBO, S::B_SBO, S::B_LAYOUT);
               dev::umma<KIND>(d_tmem, ad, bd, idesc, (kb | ks | p) != 0);
             }
           }

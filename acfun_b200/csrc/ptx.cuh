@@ -123,6 +123,7 @@ __device__ __forceinline__ uint64_t umma_sdesc(uint32_t saddr, uint32_t lbo, uin
 }
 constexpr uint32_t UMMA_SW128 = 2;      // 128B swizzle, 16-byte atoms
 constexpr uint32_t UMMA_SW128_B32 = 1;  // 128B swizzle, 32-byte atoms (MN-major tf32)
+constexpr uint32_t UMMA_SW64 = 4;       // 64B swizzle, 16-byte atoms
 
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(

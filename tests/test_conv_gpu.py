@@ -84,6 +84,11 @@ def test_conv_int8_golden_exact(acf, name):
     ("im2col_s2", 1, 21, 17, 48, 3, 3, 24, 2, 1, 1),
     ("direct_small_cin_s1", 2, 15, 15, 4, 3, 3, 8, 1, 1, 1),
     ("k5p2", 1, 14, 14, 36, 5, 5, 12, 1, 2, 0),
+    # K-block / tile-width variants: 128-byte K blocks, 128- and 256-wide tiles
+    ("c128_o160", 2, 12, 12, 128, 3, 3, 160, 1, 1, 1),
+    ("c200_o300", 1, 10, 11, 200, 3, 3, 300, 1, 1, 0),
+    ("im2col_k224_o70", 1, 9, 9, 24, 3, 3, 70, 2, 1, 1),
+    ("wide_m_o200", 8, 40, 40, 64, 3, 3, 200, 1, 1, 1),
 ])
 def test_conv_int8_vs_oracle_exact(acf, orc, cfg):
     tag, N, H, W, Cin, KH, KW, Cout, st, pd, act = cfg
