@@ -31,6 +31,19 @@ struct Int8Scalars {
   float inv_s;         // 127 / maxa
   float sa;            // maxa / 127
   int zero;            // maxa < 1e-12: the reference writes an all-zero output
+  unsigned done;       // blocks of k_absmax finished (the last one derives the rest)
+};
+
+// Per-output-channel dequantisation factors that k_absmax's last block derives once sa is
+// known (same expressions as k_int8_colparams).
+struct Int8ColArgs {
+  const float* wscale;
+  const float* bias;
+  const int* Sw;
+  int Cout;
+  int wino;  // 1: f0 = wso; 0: f0 = alpha, f1 = beta
+  float* f0;
+  float* f1;
 };
 
 static int grid_n(Call& c, long long work) {
@@ -39,8 +52,9 @@ static int grid_n(Call& c, long long work) {
 }
 
 // conv_int8.cpp:75-77: maxa = max(maxa, |x|) (std::max keeps maxa when |x| is NaN)
-__global__ void k_absmax(const float* __restrict__ x, long long n, Int8Scalars* s) {
+__global__ void k_absmax(const float* __restrict__ x, long long n, Int8Scalars* s, Int8ColArgs ca) {
   __shared__ float sh[32];
+  __shared__ int last;
   float m = 0.0f;
   if ((reinterpret_cast<uintptr_t>(x) & 15) == 0) {
     const long long n4 = n >> 2;
@@ -78,15 +92,33 @@ __global__ void k_absmax(const float* __restrict__ x, long long n, Int8Scalars* 
       const float u = __shfl_xor_sync(0xffffffffu, m, o);
       m = (m < u) ? u : m;
     }
-    if (threadIdx.x == 0) atomicMax(&s->maxa_bits, __float_as_uint(m));
+    if (threadIdx.x == 0) {
+      atomicMax(&s->maxa_bits, __float_as_uint(m));
+      __threadfence();
+      last = (atomicAdd(&s->done, 1u) == gridDim.x - 1) ? 1 : 0;
+    }
   }
-}
-
-__global__ void k_int8_scalars(Int8Scalars* s) {
-  const float maxa = __uint_as_float(s->maxa_bits);
-  s->zero = maxa < 1e-12f ? 1 : 0;
-  s->inv_s = __fdiv_rn(127.0f, maxa);
-  s->sa = __fdiv_rn(maxa, 127.0f);
+  __syncthreads();
+  if (!last) return;
+  // last block to finish: every block's maximum is visible (each fenced before counting)
+  __threadfence();
+  const float maxa = __uint_as_float(atomicOr(&s->maxa_bits, 0u));
+  const float sa = __fdiv_rn(maxa, 127.0f);
+  if (threadIdx.x == 0) {
+    s->zero = maxa < 1e-12f ? 1 : 0;
+    s->inv_s = __fdiv_rn(127.0f, maxa);
+    s->sa = sa;
+  }
+  for (int j = threadIdx.x; j < ca.Cout; j += blockDim.x) {
+    if (ca.wino) {
+      ca.f0[j] = __fmul_rn(__fmul_rn(sa, 0.25f), ca.wscale[j]);
+    } else {
+      const float a = __fmul_rn(sa, ca.wscale[j]);
+      const float corr = __fmul_rn(__fmul_rn(a, 128.0f), (float)ca.Sw[j]);
+      ca.f0[j] = a;
+      ca.f1[j] = __fsub_rn(ca.bias ? ca.bias[j] : 0.0f, corr);
+    }
+  }
 }
 
 // Per output channel j (one warp each): Sw = sum_k wq[k][j]; alpha = sa*ws; beta =
@@ -177,12 +209,41 @@ __device__ __forceinline__ uint8_t quant_one(float xv, float inv_s, int mode, bo
   return clamp_u8((int)((unsigned)v + 128u));
 }
 
+// Integer rounding on the FMA pipe (no conversion-unit instruction): adding 1.5 * 2^23
+// (resp. 2^23 with round-toward-zero) leaves the rounded value in the low mantissa bits.
+// rne_small: round-half-even of t, |t| <= 2^22.  floor_small: floor of a in [0, 2^23).
+__device__ __forceinline__ int rne_small(float t) {
+  return __float_as_int(__fadd_rn(t, 12582912.0f)) - 0x4B400000;
+}
+__device__ __forceinline__ int floor_small(float a) {
+  return __float_as_int(__fadd_rz(a, 8388608.0f)) - 0x4B000000;
+}
+
+// Same result as quant_one for a vector lane (mode 0: cvt_rne; mode 1: trunc(t + copysign(.5,
+// t))), |t| >= 2^31 and NaN giving the x86 "integer indefinite" INT_MIN, i.e. byte 0.
+template <int MODE>
+__device__ __forceinline__ uint32_t quant_fast(float xv, float inv_s) {
+  const float t = __fmul_rn(xv, inv_s);
+  int v;
+  if constexpr (MODE == 0) {
+    if (!(fabsf(t) < 2147483648.0f)) return 0u;
+    v = rne_small(fminf(fmaxf(t, -256.0f), 256.0f));
+  } else {
+    const float r = __fadd_rn(t, copysignf(0.5f, t));
+    if (!(fabsf(r) < 2147483648.0f)) return 0u;
+    const int f = floor_small(fminf(fabsf(r), 256.0f));
+    v = r < 0.0f ? -f : f;
+  }
+  v += 128;
+  return (uint32_t)(v < 0 ? 0 : (v > 255 ? 255 : v));
+}
+
 // k_quant_pad_u8 with one thread per (padded pixel, 16 channels), 32-bit index math and one
 // 16-byte store (Cpad is a multiple of 16); used when the tensor has < 2^31 such groups.
+template <int MODE>
 __global__ void k_quant_pad_u8_16(const float* __restrict__ x, int H, int W, int Cin, int pad,
                                   int Hp, int Wp, int C16, unsigned total, int vec_in,
-                                  const Int8Scalars* s, float inv_host, int mode,
-                                  uint4* __restrict__ dst) {
+                                  const Int8Scalars* s, float inv_host, uint4* __restrict__ dst) {
   const float inv_s = s ? s->inv_s : inv_host;
   const int cvec = Cin & ~15;
   for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
@@ -193,21 +254,21 @@ __global__ void k_quant_pad_u8_16(const float* __restrict__ x, int H, int W, int
     uint32_t w[4] = {0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u};
     if (c0 < Cin && ih >= 0 && ih < H && iw >= 0 && iw < W) {
       const float* src = x + (((size_t)n * H + ih) * W + iw) * Cin + c0;
-      float v[16];
       if (vec_in && c0 + 16 <= Cin) {
+        // whole group of vector lanes: no per-lane checks
 #pragma unroll
-        for (int k = 0; k < 16; k += 4) {
-          const float4 q = __ldg(reinterpret_cast<const float4*>(src + k));
-          v[k] = q.x; v[k + 1] = q.y; v[k + 2] = q.z; v[k + 3] = q.w;
+        for (int k = 0; k < 4; ++k) {
+          const float4 q = __ldg(reinterpret_cast<const float4*>(src + 4 * k));
+          w[k] = quant_fast<MODE>(q.x, inv_s) | (quant_fast<MODE>(q.y, inv_s) << 8) |
+                 (quant_fast<MODE>(q.z, inv_s) << 16) | (quant_fast<MODE>(q.w, inv_s) << 24);
         }
       } else {
 #pragma unroll
-        for (int k = 0; k < 16; ++k) v[k] = (c0 + k < Cin) ? src[k] : 0.0f;
-      }
-#pragma unroll
-      for (int k = 0; k < 16; ++k) {
-        const uint8_t q = (c0 + k < Cin) ? quant_one(v[k], inv_s, mode, c0 + k < cvec) : (uint8_t)128;
-        w[k >> 2] = (w[k >> 2] & ~(0xFFu << (8 * (k & 3)))) | ((uint32_t)q << (8 * (k & 3)));
+        for (int k = 0; k < 16; ++k) {
+          const uint8_t q =
+              (c0 + k < Cin) ? quant_one(src[k], inv_s, MODE, c0 + k < cvec) : (uint8_t)128;
+          w[k >> 2] = (w[k >> 2] & ~(0xFFu << (8 * (k & 3)))) | ((uint32_t)q << (8 * (k & 3)));
+        }
       }
     }
     dst[i] = make_uint4(w[0], w[1], w[2], w[3]);
@@ -279,6 +340,41 @@ __global__ void k_weights_s8k(const int8_t* __restrict__ w, int taps, int Cin, i
   }
 }
 
+// k_weights_s8k plus, per output channel (one block each), the column sum Sw[n] of its s8
+// weights; block 0 also clears the per-call scalars that k_absmax accumulates into.
+__global__ void k_int8_wprep(const int8_t* __restrict__ w, int taps, int Cin, int Cout, int Cpad,
+                             int8_t* __restrict__ dst, int* __restrict__ Sw, Int8Scalars* s) {
+  __shared__ int red[32];
+  const int n = blockIdx.x;
+  if (n == 0 && threadIdx.x == 0 && s) {
+    s->maxa_bits = 0u;
+    s->done = 0u;
+  }
+  const int K4 = taps * Cpad / 4;
+  uint32_t* row = reinterpret_cast<uint32_t*>(dst + (size_t)n * taps * Cpad);
+  int sum = 0;
+  for (int i = threadIdx.x; i < K4; i += blockDim.x) {
+    const int k = i * 4, tap = k / Cpad, c0 = k - tap * Cpad;
+    uint32_t packed = 0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int c = c0 + e;
+      const int8_t v = c < Cin ? w[((long long)tap * Cin + c) * Cout + n] : (int8_t)0;
+      sum += v;
+      packed |= (uint32_t)(uint8_t)v << (8 * e);
+    }
+    row[i] = packed;
+  }
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sum;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int t = 0;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t += red[i];
+    Sw[n] = t;
+  }
+}
+
 // 64-byte K blocks when they cut the channel padding (Cin mod 128 in 1..64), else 128
 static int int8_kblock(int k) { return (k % 128 != 0 && k % 128 <= 64) ? 64 : 128; }
 
@@ -298,9 +394,33 @@ struct Int8ConvArgs {
   const int* zero_flag = nullptr;
 };
 
+// K-major weight layout a convolution's GEMM uses: implicit route (stride 1, Cin >= 32):
+// `taps` taps of Cpad channels; im2col route: one "tap" of Cpad = align(KH*KW*Cin, 16).
+struct Int8BLayout {
+  bool implicit;
+  int taps, cin, cpad, bkb;
+};
+static Int8BLayout int8_b_layout(int Cin, int KH, int KW, int stride) {
+  Int8BLayout L;
+  L.implicit = stride == 1 && Cin >= 32;
+  if (L.implicit) {
+    L.taps = KH * KW;
+    L.cin = Cin;
+    L.bkb = int8_kblock(Cin);
+    L.cpad = (int)align_up((size_t)Cin, L.bkb);
+  } else {
+    L.taps = 1;
+    L.cin = KH * KW * Cin;
+    L.cpad = (int)align_up((size_t)L.cin, 16);
+    L.bkb = int8_kblock(L.cpad);
+  }
+  return L;
+}
+
+// wk: weights already in int8_b_layout's K-major form (else prepared here from wq)
 static bool int8_conv_gemm(Call& c, const Int8ConvArgs& a, int N, int H, int W, int Cin,
                            const int8_t* wq, int KH, int KW, int Cout, int stride, int pad,
-                           float* out, int act) {
+                           float* out, int act, const int8_t* wk = nullptr) {
   const int OH = (H + 2 * pad - KH) / stride + 1, OW = (W + 2 * pad - KW) / stride + 1;
   if (OH <= 0 || OW <= 0) return true;
   const int taps = KH * KW;
@@ -313,28 +433,35 @@ static bool int8_conv_gemm(Call& c, const Int8ConvArgs& a, int N, int H, int W, 
   ep.act = act;
   ep.zero_flag = a.zero_flag;
   uint8_t* xq_dense = nullptr;  // unpadded u8 input for the gather path
-  if (stride == 1 && Cin >= 32) {
+  const Int8BLayout lay = int8_b_layout(Cin, KH, KW, stride);
+  if (lay.implicit) {
     // implicit GEMM over the zero-point-padded tensor
-    const int bkb = int8_kblock(Cin);
-    const int Hp = H + 2 * pad, Wp = W + 2 * pad, Cpad = (int)align_up((size_t)Cin, bkb);
+    const int bkb = lay.bkb, Cpad = lay.cpad;
+    const int Hp = H + 2 * pad, Wp = W + 2 * pad;
     const long long rows = (long long)N * Hp * Wp;
     uint8_t* A = (uint8_t*)c.scratch((size_t)rows * Cpad);
-    int8_t* B = (int8_t*)c.scratch((size_t)Cout * taps * Cpad);
+    int8_t* B = wk ? const_cast<int8_t*>(wk) : (int8_t*)c.scratch((size_t)Cout * taps * Cpad);
     if (!A || !B) return false;
     if (a.xf && rows * (Cpad / 16) < (1LL << 31)) {
       const long long g16 = rows * (Cpad / 16);
       const int vec_in = (Cin % 4 == 0) && aligned16(a.xf);
-      k_quant_pad_u8_16<<<grid_n(c, g16), 256, 0, c.stream()>>>(
-          a.xf, H, W, Cin, pad, Hp, Wp, Cpad / 16, (unsigned)g16, vec_in, a.s, a.inv_host, a.qmode,
-          (uint4*)A);
+      if (a.qmode == 0)
+        k_quant_pad_u8_16<0><<<grid_n(c, g16), 256, 0, c.stream()>>>(
+            a.xf, H, W, Cin, pad, Hp, Wp, Cpad / 16, (unsigned)g16, vec_in, a.s, a.inv_host,
+            (uint4*)A);
+      else
+        k_quant_pad_u8_16<1><<<grid_n(c, g16), 256, 0, c.stream()>>>(
+            a.xf, H, W, Cin, pad, Hp, Wp, Cpad / 16, (unsigned)g16, vec_in, a.s, a.inv_host,
+            (uint4*)A);
     } else if (a.xf)
       k_quant_pad_u8<<<grid_n(c, rows * Cpad), 256, 0, c.stream()>>>(
           a.xf, N, H, W, Cin, pad, Hp, Wp, Cpad, a.s, a.inv_host, a.qmode, A);
     else
       k_pad_u8<<<grid_n(c, rows * Cpad), 256, 0, c.stream()>>>(a.xq, N, H, W, Cin, pad, Hp, Wp,
                                                                Cpad, A);
-    k_weights_s8k<<<grid_n(c, (long long)Cout * taps * Cpad / 4), 256, 0, c.stream()>>>(
-        wq, taps, Cin, Cout, Cpad, B);
+    if (!wk)
+      k_weights_s8k<<<grid_n(c, (long long)Cout * taps * Cpad / 4), 256, 0, c.stream()>>>(
+          wq, taps, Cin, Cout, Cpad, B);
     if (!c.launched("int8 implicit prep")) return false;
     Operand Ao, Bo;
     Ao.p = A;
@@ -359,21 +486,22 @@ static bool int8_conv_gemm(Call& c, const Int8ConvArgs& a, int N, int H, int W, 
     src = xq_dense;
   }
   const long long M = (long long)N * OH * OW;
-  const int K = taps * Cin, Kpad = (int)align_up((size_t)K, 16);
+  const int K = lay.cin, Kpad = lay.cpad;
   uint8_t* A = (uint8_t*)c.scratch((size_t)M * Kpad);
-  int8_t* B = (int8_t*)c.scratch((size_t)Cout * Kpad);
+  int8_t* B = wk ? const_cast<int8_t*>(wk) : (int8_t*)c.scratch((size_t)Cout * Kpad);
   if (!A || !B) return false;
   k_im2col_u8<<<grid_n(c, M * Kpad), 256, 0, c.stream()>>>(src, N, H, W, Cin, KH, KW, stride, pad,
                                                            OH, OW, Kpad, A);
-  k_weights_s8k<<<grid_n(c, (long long)Cout * Kpad / 4), 256, 0, c.stream()>>>(wq, 1, K, Cout,
-                                                                              Kpad, B);
+  if (!wk)
+    k_weights_s8k<<<grid_n(c, (long long)Cout * Kpad / 4), 256, 0, c.stream()>>>(wq, 1, K, Cout,
+                                                                                Kpad, B);
   if (!c.launched("int8 im2col prep")) return false;
   Operand Ao, Bo;
   Ao.p = A;
   Ao.ld = Kpad;
   Bo.p = B;
   Bo.ld = Kpad;
-  return gemm_launch_i8k(c, a.epi, Ao, Bo, (int)M, Cout, Kpad, ep, ConvGeom{}, int8_kblock(Kpad));
+  return gemm_launch_i8k(c, a.epi, Ao, Bo, (int)M, Cout, Kpad, ep, ConvGeom{}, lay.bkb);
 }
 
 static bool is_wino_route(int H, int W, int Cin, int KH, int KW, int Cout, int stride, int pad) {
@@ -383,21 +511,21 @@ static bool is_wino_route(int H, int W, int Cin, int KH, int KW, int Cout, int s
 bool conv2d_int8_dev(Call& c, const float* x, int N, int H, int W, int Cin, const int8_t* wq,
                      const float* wscale, const float* bias, int KH, int KW, int Cout, int stride,
                      int pad, float* out, int act) {
-  const int K = KH * KW * Cin;
+  // 4 launches: weights -> K-major + Sw (+ clear scalars); max|x| whose last block derives
+  // inv_s / sa / per-channel factors; quantise + pad; the integer GEMM with its epilogue.
+  const Int8BLayout lay = int8_b_layout(Cin, KH, KW, stride);
   Int8Scalars* s = (Int8Scalars*)c.scratch(sizeof(Int8Scalars));
   float* f0 = (float*)c.scratch((size_t)Cout * 4);
   float* f1 = (float*)c.scratch((size_t)Cout * 4);
   int* Sw = (int*)c.scratch((size_t)Cout * 4);
-  if (!s || !f0 || !f1 || !Sw) return false;
-  if (!ACF_CUDA_OK(cudaMemsetAsync(s, 0, sizeof(Int8Scalars), c.stream()))) return false;
-  const long long n = (long long)N * H * W * Cin;
-  k_absmax<<<grid_n(c, n / 4 + 1), 256, 0, c.stream()>>>(x, n, s);
-  k_int8_scalars<<<1, 1, 0, c.stream()>>>(s);
+  int8_t* wk = (int8_t*)c.scratch((size_t)Cout * lay.taps * lay.cpad);
+  if (!s || !f0 || !f1 || !Sw || !wk) return false;
+  k_int8_wprep<<<Cout, 128, 0, c.stream()>>>(wq, lay.taps, lay.cin, Cout, lay.cpad, wk, Sw, s);
   const bool wino = is_wino_route(H, W, Cin, KH, KW, Cout, stride, pad);
   // Winograd: f0 = wso, f1 = bias (or NULL); others: f0 = alpha, f1 = beta
-  k_int8_colparams<<<(Cout * 32 + 255) / 256, 256, 0, c.stream()>>>(
-      wq, K, Cout, wscale, bias, s, 0.0f, wino ? nullptr : f0, wino ? nullptr : f1,
-      wino ? f0 : nullptr, Sw);
+  const Int8ColArgs ca{wscale, bias, Sw, Cout, wino ? 1 : 0, f0, f1};
+  const long long n = (long long)N * H * W * Cin;
+  k_absmax<<<grid_n(c, n / 4 + 1), 256, 0, c.stream()>>>(x, n, s, ca);
   if (!c.launched("int8 params")) return false;
   Int8ConvArgs a;
   a.xf = x;
@@ -415,7 +543,7 @@ bool conv2d_int8_dev(Call& c, const float* x, int N, int H, int W, int Cin, cons
     a.f0 = f0;
     a.f1 = f1;
   }
-  return int8_conv_gemm(c, a, N, H, W, Cin, wq, KH, KW, Cout, stride, pad, out, act);
+  return int8_conv_gemm(c, a, N, H, W, Cin, wq, KH, KW, Cout, stride, pad, out, act, wk);
 }
 
 }  // namespace acf

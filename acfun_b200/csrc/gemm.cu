@@ -285,7 +285,7 @@ static bool launch_one(Call& c, const Operand& A, const Operand& B, int M, int N
   }
   // persistent: one CTA per SM (1 CTA/SM by shared memory), tiles strided over the grid
   const dim3 grid((unsigned)(tiles < c.sm_count() ? tiles : c.sm_count()));
-  kern<<<grid, 192, S::SMEM, c.stream()>>>(ta, tb, ep, cg, M, N, K, c.err());
+  kern<<<grid, S::THREADS, S::SMEM, c.stream()>>>(ta, tb, ep, cg, M, N, K, c.err());
   return c.launched("gemm_tc_kernel");
 }
 

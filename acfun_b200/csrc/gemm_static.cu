@@ -87,7 +87,7 @@ static int noalloc_launch(const NoAllocDevice* d, int device, cudaStream_t st, c
   }
   const long long tiles = (long long)((M + 127) / 128) * ((N + BN - 1) / BN);
   const unsigned grid = (unsigned)(tiles < d->sms ? tiles : d->sms);
-  kern<<<grid, 192, S::SMEM, st>>>(ta, tb, ep, ConvGeom{}, M, N, K, d->err);
+  kern<<<grid, S::THREADS, S::SMEM, st>>>(ta, tb, ep, ConvGeom{}, M, N, K, d->err);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_error(kCuda, "acfun_gemm_epi_noalloc: launch failed: %s", cudaGetErrorString(e));

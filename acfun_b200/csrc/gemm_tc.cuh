@@ -1,13 +1,15 @@
 // gemm_tc.cuh — tcgen05 (5th-gen tensor core) GEMM for sm_100a.
 //
 // One CTA computes a 128 x BN tile of C = A[M,K] * B[K,N]:
-//   warp 0        TMA producer: per 128-byte K block, A tile (128 rows, K-major, SW128)
-//                 and B tile (K rows x BN, MN-major, SW128, split in 128-byte N chunks)
-//                 into a STAGES-deep shared-memory ring guarded by full/empty mbarriers;
+//   warp 0        TMA producer: per 128-byte (SW128) or 64-byte (SW64) K block, the A tile
+//                 (128 rows, K-major) and the B tile (K rows x BN MN-major in 128-byte N
+//                 chunks, or BN rows K-major like A) into a STAGES-deep shared-memory ring
+//                 guarded by full/empty mbarriers;
 //   warp 1        TMEM owner + single-thread UMMA issuer (cta_group::1, M=128, N=BN),
-//                 4 K-steps of 32 bytes per block; tcgen05.commit frees a stage as soon
+//                 one MMA per 32-byte K-step; tcgen05.commit frees a stage as soon
 //                 as its MMAs retire and finally signals the epilogue;
-//   warps 2..5    epilogue: tcgen05.ld 32 columns at a time from their TMEM lane quadrant,
+//   warps 2..9    epilogue: tcgen05.ld 32 columns at a time from their TMEM lane quadrant
+//                 (two warps per quadrant, even / odd 32-column chunks),
 //                 fused epilogue (int32 store / dequant mul+add / requant to s8 / bias +
 //                 ReLU / int8-Winograd dequant fma), vectorised global stores.
 // 3xTF32 (NPASS = 3): A and B arrive as [2][rows][cols] (hi, lo) pairs; each K-step issues
@@ -49,6 +51,16 @@ struct ConvGeom {
   int Wp;
   int cpad;     // channels per tap in B
   int taps;
+};
+
+// Per-column epilogue parameters of one 32-column chunk, staged in the epilogue warp's own
+// shared-memory slice: pa / pb (float) and pc (int32), 32 entries each, zero past column N.
+//   S8_REQ: pa = scale, pc = int32 bias | F32_AB: pa = alpha, pb = beta | F32_BIAS: pa = bias
+//   I8_WINO: pa = wso, pb = bias, pc = column sums of the weights
+struct ColSlice {
+  float a[32];
+  float b[32];
+  int32_t c[32];
 };
 
 template <dev::MmaKind KIND>
@@ -93,8 +105,16 @@ struct GemmShape {
       B_KMAJ ? K_LAYOUT : (ELEM == 4) ? dev::UMMA_SW128_B32 : dev::UMMA_SW128;
   static constexpr int B_SBO = B_KMAJ ? K_SBO : (ELEM == 4) ? 512 : 1024;
   static constexpr int B_LBO = B_KMAJ ? 16 : CHUNK_B;
-  static constexpr int SMEM = STAGES * STAGE + 1024 + 256;
   static constexpr int TMEM_COLS = 2 * BN;  // double-buffered accumulator
+  // warps 0 (TMA) and 1 (MMA / TMEM), then EPI_WARPS epilogue warps: two per TMEM lane
+  // quadrant, splitting the tile's 32-column chunks between them (even / odd chunks)
+  static constexpr int EPI_WARPS = 8;
+  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+  static constexpr int CHUNKS_PER_WARP = (BN / 32 + 1) / 2;
+  // full/empty per stage, tfull[2], tempty[2], drain; TMEM slot; abort flag
+  static constexpr int BAR_BYTES = ((2 * STAGES + 5) * 8 + 8 + 15) / 16 * 16;
+  static constexpr int PARAM_BYTES = EPI_WARPS * CHUNKS_PER_WARP * (int)sizeof(ColSlice);
+  static constexpr int SMEM = 1024 + STAGES * STAGE + BAR_BYTES + PARAM_BYTES;
   static_assert(BKB == 128 || (BKB == 64 && B_KMAJ && NPASS == 1), "64-byte K blocks: K-major B");
   static_assert(B_KMAJ || BN * ELEM % 128 == 0, "B tile must be whole 128-byte chunks");
   static_assert(BN == 32 || BN == 64 || BN == 128 || BN == 256, "TMEM columns");
@@ -102,28 +122,41 @@ struct GemmShape {
 
 __device__ __forceinline__ float relu_max(float v) { return v > 0.0f ? v : 0.0f; }
 
-// 32 consecutive per-column parameters (broadcast across the warp): 8 x 16-byte loads when
-// the run is whole and aligned, guarded scalar loads otherwise.
+template <Epi EPI>
+__device__ __forceinline__ void epi_stage_cols(const EpiParams& ep, int col, int N, int lane,
+                                               ColSlice& s) {
+  const bool in = col < N;
+  if constexpr (EPI == Epi::S8_REQ) {
+    s.a[lane] = in ? ep.f0[col] : 0.0f;
+    s.c[lane] = (in && ep.i0) ? ep.i0[col] : 0;
+  } else if constexpr (EPI == Epi::F32_AB) {
+    s.a[lane] = in ? ep.f0[col] : 0.0f;
+    s.b[lane] = in ? ep.f1[col] : 0.0f;
+  } else if constexpr (EPI == Epi::F32_BIAS) {
+    s.a[lane] = (in && ep.f0) ? ep.f0[col] : 0.0f;
+  } else if constexpr (EPI == Epi::I8_WINO) {
+    s.a[lane] = in ? ep.f0[col] : 0.0f;
+    s.b[lane] = (in && ep.f1) ? ep.f1[col] : 0.0f;
+    s.c[lane] = in ? ep.i0[col] : 0;
+  }
+}
+
 template <typename T>
-__device__ __forceinline__ void load_cols32(const T* p, int j0, int N, T (&o)[32]) {
-  if (j0 + 32 <= N && ((reinterpret_cast<uintptr_t>(p + j0) & 15) == 0)) {
+__device__ __forceinline__ void lds32(const T* p, T (&o)[32]) {
 #pragma unroll
-    for (int i = 0; i < 32; i += 4) {
-      const uint4 u = __ldg(reinterpret_cast<const uint4*>(p + j0 + i));
-      o[i] = __builtin_bit_cast(T, u.x);
-      o[i + 1] = __builtin_bit_cast(T, u.y);
-      o[i + 2] = __builtin_bit_cast(T, u.z);
-      o[i + 3] = __builtin_bit_cast(T, u.w);
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < 32; ++i) o[i] = (j0 + i < N) ? p[j0 + i] : T(0);
+  for (int i = 0; i < 32; i += 4) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p + i);  // warp-wide broadcast
+    o[i] = __builtin_bit_cast(T, u.x);
+    o[i + 1] = __builtin_bit_cast(T, u.y);
+    o[i + 2] = __builtin_bit_cast(T, u.z);
+    o[i + 3] = __builtin_bit_cast(T, u.w);
   }
 }
 
 template <Epi EPI>
 __device__ __forceinline__ void epi_store32(const EpiParams& ep, long long orow, int j0, int N,
-                                            const uint32_t (&r)[32], bool zero) {
+                                            const uint32_t (&r)[32], const ColSlice& P,
+                                            bool zero) {
   // 32 outputs for columns j0..j0+31 of output row `orow`
   const bool full = (j0 + 32 <= N);
   if constexpr (EPI == Epi::S32) {
@@ -139,13 +172,8 @@ __device__ __forceinline__ void epi_store32(const EpiParams& ep, long long orow,
   } else if constexpr (EPI == Epi::S8_REQ) {
     float sc[32];
     int32_t bi[32];
-    load_cols32(ep.f0, j0, N, sc);
-    if (ep.i0) {
-      load_cols32(ep.i0, j0, N, bi);
-    } else {
-#pragma unroll
-      for (int i = 0; i < 32; ++i) bi[i] = 0;
-    }
+    lds32(P.a, sc);
+    lds32(P.c, bi);
     uint32_t packed[8];
 #pragma unroll
     for (int i = 0; i < 32; i += 4) {
@@ -173,24 +201,14 @@ __device__ __forceinline__ void epi_store32(const EpiParams& ep, long long orow,
     float p0[32], p1[32];
     int32_t pi[32];
     if constexpr (EPI == Epi::F32_AB) {
-      load_cols32(ep.f0, j0, N, p0);
-      load_cols32(ep.f1, j0, N, p1);
+      lds32(P.a, p0);
+      lds32(P.b, p1);
     } else if constexpr (EPI == Epi::F32_BIAS) {
-      if (ep.f0) {
-        load_cols32(ep.f0, j0, N, p0);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) p0[i] = 0.0f;
-      }
+      lds32(P.a, p0);
     } else {  // I8_WINO
-      load_cols32(ep.f0, j0, N, p0);
-      load_cols32(ep.i0, j0, N, pi);
-      if (ep.f1) {
-        load_cols32(ep.f1, j0, N, p1);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) p1[i] = 0.0f;
-      }
+      lds32(P.a, p0);
+      lds32(P.b, p1);
+      lds32(P.c, pi);
     }
     float v[32];
 #pragma unroll
@@ -225,7 +243,7 @@ __device__ __forceinline__ void epi_store32(const EpiParams& ep, long long orow,
 // other, so a tile's epilogue overlaps the next tile's MMAs.
 template <dev::MmaKind KIND, int BN, int STAGES, int NPASS, Epi EPI, bool A_SIGNED, int BKB = 128,
           bool B_KMAJ = false>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    EpiParams ep, ConvGeom cg, int M, int N, int K, unsigned* err) {
   using S = GemmShape<KIND, BN, STAGES, NPASS, BKB, B_KMAJ>;
@@ -239,6 +257,8 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* drain_bar = tempty_bar + 2;       // error-path MMA drain
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  ColSlice* col_slices = reinterpret_cast<ColSlice*>(smem + STAGES * S::STAGE + S::BAR_BYTES);
+  static_assert(S::THREADS == 320, "launch bounds");
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -254,7 +274,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int b = 0; b < 2; ++b) {
       dev::mbar_init(&tfull_bar[b], 1);
-      dev::mbar_init(&tempty_bar[b], 4);  // one arrive per epilogue warp
+      dev::mbar_init(&tempty_bar[b], S::EPI_WARPS);  // one arrive per epilogue warp
     }
     dev::mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -273,24 +293,41 @@ __global__ void __launch_bounds__(192, 1)
 
   if (warp == 0 && lane == 0) {
     // ---------------- TMA producer
+    // The loop body is one thread's serial instruction stream, so it carries no divisions:
+    // ring slot / phase and the convolution's (tap, channel block) advance incrementally.
     uint32_t it = 0;  // global K-block counter (ring position)
-    for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+    uint32_t s = 0, ph = 0;
+    bool stop = false;
+    for (int t = blockIdx.x; t < num_tiles && !stop; t += gridDim.x) {
+      if (*abort_flag) break;
       const int m0 = (t / tiles_n) * S::BM, n0 = (t % tiles_n) * BN;
-      for (int kb = 0; kb < nkb; ++kb, ++it) {
-        const int s = it % STAGES;
-        const uint32_t ph = (it / STAGES) & 1;
-        if (*abort_flag || !dev::mbar_wait(&empty_bar[s], ph ^ 1, err)) {
+      int cb = 0, kw = 0, row_off = 0, tap_k = 0;  // conv: channel block, kw, A row shift, B k
+      for (int kb = 0; kb < nkb; ++kb) {
+        if (!dev::mbar_wait(&empty_bar[s], ph ^ 1, err)) {
           *abort_flag = 1;
+          stop = true;
           break;
         }
         uint8_t* st = smem + s * S::STAGE;
         dev::mbar_arrive_expect_tx(&full_bar[s], S::STAGE);
-        int kx = kb * S::BKE, ay = m0, by = kb * S::BKE;
+        int kx, ay, by;
         if (cg.enabled) {
-          const int tap = kb / cg.cblocks, cb = kb - tap * cg.cblocks;
           kx = cb * S::BKE;
-          ay = m0 + (tap / cg.KW) * cg.Wp + (tap % cg.KW);
-          by = tap * cg.cpad + kx;
+          ay = m0 + row_off;
+          by = tap_k + kx;
+          if (++cb == cg.cblocks) {
+            cb = 0;
+            tap_k += cg.cpad;
+            ++row_off;
+            if (++kw == cg.KW) {
+              kw = 0;
+              row_off += cg.Wp - cg.KW;
+            }
+          }
+        } else {
+          kx = kb * S::BKE;
+          ay = m0;
+          by = kx;
         }
 #pragma unroll
         for (int op = 0; op < S::NOPS; ++op) {
@@ -313,6 +350,11 @@ __global__ void __launch_bounds__(192, 1)
                                n0 + c * (128 / S::ELEM), by, op);
           }
         }
+        ++it;
+        if (++s == STAGES) {
+          s = 0;
+          ph ^= 1;
+        }
       }
     }
     if (*abort_flag) {
@@ -330,48 +372,54 @@ __global__ void __launch_bounds__(192, 1)
                                : (KIND == dev::MmaKind::F16) ? 1u : 2u;
     constexpr uint32_t idesc =
         dev::umma_idesc(c_fmt, a_fmt, b_fmt, 0u, B_KMAJ ? 0u : 1u, 128u, (uint32_t)BN);
+    // Shared-memory descriptors are built once; a stage / K-step / operand offset is an add
+    // to the 14-bit start-address field (addresses are below 256 KB, so it never carries).
     const uint32_t smem_base = dev::smem_u32(smem);
+    const uint64_t a_desc0 = dev::umma_sdesc(smem_base, 16, S::K_SBO, S::K_LAYOUT);
+    const uint64_t b_desc0 = dev::umma_sdesc(smem_base + S::NOPS * S::A_TILE, S::B_LBO, S::B_SBO,
+                                             S::B_LAYOUT);
     bool ok = true;
     uint32_t it = 0, local = 0;
+    uint32_t s = 0, ph = 0;
     for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local) {
       const uint32_t buf = local & 1, use = local >> 1;
-      if (!dev::mbar_wait(&tempty_bar[buf], (use & 1) ^ 1, err)) {
+      if (*abort_flag || !dev::mbar_wait(&tempty_bar[buf], (use & 1) ^ 1, err)) {
         ok = false;
         break;
       }
       dev::tc_fence_after();
       const uint32_t d_tmem = tmem + buf * BN;
       for (int kb = 0; kb < nkb; ++kb, ++it) {
-        const int s = it % STAGES;
-        const uint32_t ph = (it / STAGES) & 1;
-        if (*abort_flag || !dev::mbar_wait(&full_bar[s], ph, err)) {
+        if (!dev::mbar_wait(&full_bar[s], ph, err)) {
           ok = false;
           break;
         }
         dev::tc_fence_after();
-        const uint32_t a_base = smem_base + s * S::STAGE;
-        const uint32_t b_base = a_base + S::NOPS * S::A_TILE;
+        const uint64_t soff = (uint64_t)((s * (uint32_t)S::STAGE) >> 4);
 #pragma unroll
         for (int ks = 0; ks < S::KSTEPS; ++ks) {
           if constexpr (NPASS == 1) {
-            const uint64_t ad = dev::umma_sdesc(a_base + ks * 32, 16, S::K_SBO, S::K_LAYOUT);
-            const uint64_t bd = dev::umma_sdesc(b_base + ks * S::KSTEP_B, S::B_LBO, S::B_SBO,
-                                                S::B_LAYOUT);
+            const uint64_t ad = a_desc0 + soff + (uint64_t)(ks * 32 / 16);
+            const uint64_t bd = b_desc0 + soff + (uint64_t)(ks * S::KSTEP_B / 16);
             dev::umma<KIND>(d_tmem, ad, bd, idesc, (kb | ks) != 0);
           } else {
             // (a_op, b_op): lo*hi, hi*lo, hi*hi
             const int aop[3] = {1, 0, 0}, bop[3] = {0, 1, 0};
 #pragma unroll
             for (int p = 0; p < 3; ++p) {
-              const uint64_t ad = dev::umma_sdesc(a_base + aop[p] * S::A_TILE + ks * 32, 16,
-                                                  S::K_SBO, S::K_LAYOUT);
-              const uint64_t bd = dev::umma_sdesc(b_base + bop[p] * S::B_TILE + ks * S::KSTEP_B,
-                                                  S::B_LBO, S::B_SBO, S::B_LAYOUT);
+              const uint64_t ad =
+                  a_desc0 + soff + (uint64_t)((aop[p] * S::A_TILE + ks * 32) / 16);
+              const uint64_t bd =
+                  b_desc0 + soff + (uint64_t)((bop[p] * S::B_TILE + ks * S::KSTEP_B) / 16);
               dev::umma<KIND>(d_tmem, ad, bd, idesc, (kb | ks | p) != 0);
             }
           }
         }
         dev::umma_commit(&empty_bar[s]);
+        if (++s == STAGES) {
+          s = 0;
+          ph ^= 1;
+        }
       }
       if (ok) dev::umma_commit(&tfull_bar[buf]);
     }
@@ -384,14 +432,29 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else if (warp >= 2) {
     // ---------------- epilogue
-    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int q = warp & 3;           // TMEM lane quadrant this warp may access
+    const int h = (warp - 2) >> 2;    // chunk parity: columns h*32 + 64*k
+    ColSlice* my = col_slices + (warp - 2) * S::CHUNKS_PER_WARP;
     uint32_t local = 0;
+    int staged_n0 = -1;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
       const uint32_t buf = local & 1, use = local >> 1;
+      const int m0 = (t / tiles_n) * S::BM, n0 = (t % tiles_n) * BN;
+      if constexpr (EPI != Epi::S32) {
+        // per-column parameters of this tile's chunks, loaded before the accumulator is
+        // ready (and only when the column block changes)
+        if (n0 != staged_n0) {
+          __syncwarp();
+#pragma unroll
+          for (int k = 0; k < S::CHUNKS_PER_WARP; ++k)
+            epi_stage_cols<EPI>(ep, n0 + h * 32 + 64 * k + lane, N, lane, my[k]);
+          __syncwarp();
+          staged_n0 = n0;
+        }
+      }
       const bool ok = dev::mbar_wait(&tfull_bar[buf], use & 1, err);
       dev::tc_fence_after();
       if (!ok || *abort_flag) break;
-      const int m0 = (t / tiles_n) * S::BM, n0 = (t % tiles_n) * BN;
       const int r = m0 + q * 32 + lane;
       const bool zero_out = ep.zero_flag && *ep.zero_flag;
       long long orow = r;
@@ -403,12 +466,13 @@ __global__ void __launch_bounds__(192, 1)
         orow = ((long long)n * ep.OH + oh) * ep.OW + ow;
       }
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
-        if (n0 + c0 >= N) break;  // warp-uniform
+      for (int k = 0; k < S::CHUNKS_PER_WARP; ++k) {
+        const int c0 = h * 32 + 64 * k;
+        if (c0 >= BN || n0 + c0 >= N) break;  // warp-uniform
         uint32_t v[32];
         dev::tmem_ld32(tmem + buf * BN + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
         dev::tmem_ld_wait();
-        if (store) epi_store32<EPI>(ep, orow, n0 + c0, N, v, zero_out);
+        if (store) epi_store32<EPI>(ep, orow, n0 + c0, N, v, my[k], zero_out);
       }
       dev::tc_fence_before();
       __syncwarp();
