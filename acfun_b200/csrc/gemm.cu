@@ -454,19 +454,82 @@ extern "C" void acfun_gemm_bf16(int M, int N, int K, const float* A, const float
   c.finish();
 }
 
+// Row-chunked GEMM call.  With host A and host C the rows are split into chunks (~2 MB of
+// A each, at most 8) and chunk i's H2D (copy-in stream), GEMM (call stream) and D2H of its C
+// rows (copy-out stream) overlap with the neighbouring chunks', so a host-buffer call costs
+// about its PCIe transfer time instead of copies + math in series.  Otherwise one launch.
+// B (and the epilogue's column vectors in `ep`) must already be staged on the call stream.
+static void gemm_rows(Call& c, GemmKind kind, Epi epi, const void* A, int M, int K, int elemA,
+                      const Operand& b, int N, EpiParams ep, void* C, int elemC) {
+  if (!c.ok()) return;
+  const size_t pitchA = (size_t)K * elemA, crow = (size_t)N * elemC;
+  const bool host_io = ptr_kind(A) == PtrKind::Host && ptr_kind(C) == PtrKind::Host;
+  const size_t want = ((size_t)M * pitchA) >> 21;
+  const int nch_want = (int)(want > 8 ? 8 : want);
+  if (!host_io || nch_want < 2 || M < 256) {
+    Operand a = tma_operand(c, A, M, K, elemA);
+    void* dC = c.out(C, (size_t)M * crow);
+    if (!c.ok()) return;
+    ep.C = dC;
+    ep.ldc = N;
+    gemm_launch(c, kind, epi, a, b, M, N, K, ep);
+    return;
+  }
+  const size_t ldp = align_up(pitchA, 16);
+  uint8_t* dA = (uint8_t*)c.scratch((size_t)M * ldp);
+  uint8_t* dC = (uint8_t*)c.scratch((size_t)M * crow);
+  if (!dA || !dC) return;
+  const int R = (int)align_up((size_t)((M + nch_want - 1) / nch_want), 128);
+  const int nch = (M + R - 1) / R;
+  const cudaStream_t cs = c.stream(), hs = c.copy_in(), ds = c.copy_out();
+  c.note_host();
+  // the copy streams start behind the work already queued on the call stream (an earlier
+  // call may still read this scratch) ...
+  if (!ACF_CUDA_OK(cudaEventRecord(c.event(0), cs)) ||
+      !ACF_CUDA_OK(cudaStreamWaitEvent(hs, c.event(0))) ||
+      !ACF_CUDA_OK(cudaStreamWaitEvent(ds, c.event(0)))) {
+    c.fail();
+    return;
+  }
+  bool ok = true;
+  for (int i = 0; ok && i < nch; ++i) {
+    const int r0 = i * R, rows = (M - r0 < R) ? M - r0 : R;
+    ok = ACF_CUDA_OK(cudaMemcpy2DAsync(dA + (size_t)r0 * ldp, ldp,
+                                       (const uint8_t*)A + (size_t)r0 * pitchA, pitchA, pitchA,
+                                       rows, cudaMemcpyHostToDevice, hs)) &&
+         ACF_CUDA_OK(cudaEventRecord(c.event(2 + i), hs));
+  }
+  for (int i = 0; ok && i < nch; ++i) {
+    const int r0 = i * R, rows = (M - r0 < R) ? M - r0 : R;
+    ok = ACF_CUDA_OK(cudaStreamWaitEvent(cs, c.event(2 + i)));
+    Operand a;
+    a.p = dA + (size_t)r0 * ldp;
+    a.ld = (long long)(ldp / elemA);
+    EpiParams e = ep;
+    e.C = dC + (size_t)r0 * crow;
+    e.ldc = N;
+    ok = ok && gemm_launch(c, kind, epi, a, b, rows, N, K, e) &&
+         ACF_CUDA_OK(cudaEventRecord(c.event(2 + nch + i), cs)) &&
+         ACF_CUDA_OK(cudaStreamWaitEvent(ds, c.event(2 + nch + i))) &&
+         ACF_CUDA_OK(cudaMemcpyAsync((uint8_t*)C + (size_t)r0 * crow, dC + (size_t)r0 * crow,
+                                     (size_t)rows * crow, cudaMemcpyDeviceToHost, ds));
+  }
+  // ... and the call stream ends behind both copy streams, on every path, so finish()'s
+  // synchronise covers every copy that touches caller memory
+  cudaEventRecord(c.event(1), hs);
+  cudaStreamWaitEvent(cs, c.event(1));
+  cudaEventRecord(c.event(1), ds);
+  cudaStreamWaitEvent(cs, c.event(1));
+  if (!ok) c.fail();
+}
+
 extern "C" void acfun_gemm_int8(int M, int N, int K, const uint8_t* A, const int8_t* B,
                                 int32_t* C) {
   if (M <= 0 || N <= 0 || K <= 0 || bad_ptrs("acfun_gemm_int8", A, B, C)) return;
   Call c("acfun_gemm_int8");
   if (!c.ok()) return;
-  Operand a = tma_operand(c, A, M, K, 1);
   Operand b = tma_operand(c, B, K, N, 1);
-  int32_t* dC = (int32_t*)c.out(C, (size_t)M * N * 4);
-  if (!c.ok()) return;
-  EpiParams ep{};
-  ep.C = dC;
-  ep.ldc = N;
-  gemm_launch(c, GemmKind::I8U, Epi::S32, a, b, M, N, K, ep);
+  gemm_rows(c, GemmKind::I8U, Epi::S32, A, M, K, 1, b, N, EpiParams{}, C, 4);
   c.finish();
 }
 
@@ -479,19 +542,12 @@ extern "C" void acfun_gemm_int8_epi(int M, int N, int K, const uint8_t* A, const
   }
   Call c("acfun_gemm_int8_epi");
   if (!c.ok()) return;
-  Operand a = tma_operand(c, A, M, K, 1);
   Operand b = tma_operand(c, B, K, N, 1);
-  const float* da = (const float*)c.in(alpha, (size_t)N * 4);
-  const float* db = (const float*)c.in(beta, (size_t)N * 4);
-  float* dC = (float*)c.out(C, (size_t)M * N * 4);
-  if (!c.ok()) return;
   EpiParams ep{};
-  ep.C = dC;
-  ep.ldc = N;
-  ep.f0 = da;
-  ep.f1 = db;
+  ep.f0 = (const float*)c.in(alpha, (size_t)N * 4);
+  ep.f1 = (const float*)c.in(beta, (size_t)N * 4);
   ep.act = act ? 1 : 0;
-  gemm_launch(c, GemmKind::I8U, Epi::F32_AB, a, b, M, N, K, ep);
+  gemm_rows(c, GemmKind::I8U, Epi::F32_AB, A, M, K, 1, b, N, ep, C, 4);
   c.finish();
 }
 
@@ -505,19 +561,12 @@ extern "C" void acfun_gemm_s8_requant(int M, int N, int K, const int8_t* A, cons
   }
   Call c("acfun_gemm_s8_requant");
   if (!c.ok()) return;
-  Operand a = tma_operand(c, A, M, K, 1);
   Operand b = tma_operand(c, B, K, N, 1);
-  const int32_t* dbias = bias ? (const int32_t*)c.in(bias, (size_t)N * 4) : nullptr;
-  const float* dscale = (const float*)c.in(scale, (size_t)N * 4);
-  int8_t* dC = (int8_t*)c.out(C, (size_t)M * N);
-  if (!c.ok()) return;
   EpiParams ep{};
-  ep.C = dC;
-  ep.ldc = N;
-  ep.f0 = dscale;
-  ep.i0 = dbias;
+  ep.f0 = (const float*)c.in(scale, (size_t)N * 4);
+  ep.i0 = bias ? (const int32_t*)c.in(bias, (size_t)N * 4) : nullptr;
   ep.act = act ? 1 : 0;
-  gemm_launch(c, GemmKind::I8S, Epi::S8_REQ, a, b, M, N, K, ep);
+  gemm_rows(c, GemmKind::I8S, Epi::S8_REQ, A, M, K, 1, b, N, ep, C, 1);
   c.finish();
 }
 

@@ -112,6 +112,11 @@ DeviceState* device_state() {
   int sms = 0;
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, d) == cudaSuccess && sms > 0)
     s->sm_count = sms;
+  if (!ACF_CUDA_OK(cudaStreamCreateWithFlags(&s->copy_in, cudaStreamNonBlocking)) ||
+      !ACF_CUDA_OK(cudaStreamCreateWithFlags(&s->copy_out, cudaStreamNonBlocking)))
+    return nullptr;
+  for (int i = 0; i < DeviceState::kEvents; ++i)
+    if (!ACF_CUDA_OK(cudaEventCreateWithFlags(&s->ev[i], cudaEventDisableTiming))) return nullptr;
   s->device = d;
   s->ok = true;
   return s;

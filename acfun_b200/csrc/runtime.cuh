@@ -64,6 +64,10 @@ struct DeviceState {
   std::mutex mu;                  // one call at a time owns the workspace
   cudaStream_t ws_stream = nullptr;
   int sm_count = 148;
+  // host-buffer calls overlap their H2D / D2H copies with the math on these streams
+  cudaStream_t copy_in = nullptr, copy_out = nullptr;
+  static constexpr int kEvents = 40;
+  cudaEvent_t ev[kEvents] = {};
   bool ok = false;
 };
 
@@ -109,6 +113,11 @@ class Call {
   bool finish();
   const char* name() const { return name_; }
   void fail() { ok_ = false; }
+  // Copy streams and a pool of timing-free events (indices < DeviceState::kEvents) for
+  // calls that pipeline host copies; owned by the device, valid while the call holds it.
+  cudaStream_t copy_in() const { return dev_->copy_in; }
+  cudaStream_t copy_out() const { return dev_->copy_out; }
+  cudaEvent_t event(int i) const { return dev_->ev[i]; }
 
  private:
   struct Pending {

@@ -139,3 +139,39 @@ def test_gemm_empty_and_bad_shapes_are_silent(acf):
     L.acfun_gemm_int8(2, 2, -1, None, None, acf.ptr(C))
     acf.check()
     assert (C == 7).all()
+
+
+@pytest.mark.parametrize("M,N,K", [(1100, 96, 4100), (2047, 200, 2304)])
+def test_host_buffer_row_pipeline_exact(acf, orc, M, N, K):
+    """Host A and C of >= 4 MB take the row-chunked path (H2D / GEMM / D2H overlapped on
+    three streams; ragged last chunk, A pitch not a multiple of 16): bit-identical to the
+    oracle and to the device-pointer call."""
+    g = np.random.default_rng(M + K)
+    A, B = rand_u8s8(g, M, N, K)
+    ref = np.empty((M, N), np.int32)
+    orc.oracle().orc_gemm_int8(M, N, K, A, B, ref)
+    assert_bits_equal(acf.gemm_int8(A, B), ref, f"gemm_int8 pipelined {M}x{N}x{K}")
+    al = g.uniform(1e-4, 1e-2, N).astype(np.float32)
+    be = g.uniform(-20, 20, N).astype(np.float32)
+    ref_e = np.empty((M, N), np.float32)
+    orc.oracle().orc_gemm_int8_epi(M, N, K, A, B, ref_e, al, be, 1)
+    assert_bits_equal(acf.gemm_int8_epi(A, B, al, be, 1), ref_e, "epi pipelined")
+    As = (A.astype(np.int16) - 128).astype(np.int8)
+    bias = g.integers(-1000, 1001, N, dtype=np.int32)
+    scale = g.uniform(1e-4, 1e-3, N).astype(np.float32)
+    ref_q = np.empty((M, N), np.int8)
+    orc.oracle().orc_gemm_s8_requant(M, N, K, As, B, bias.ctypes.data, scale, ref_q, 0)
+    got_host = acf.gemm_s8_requant(As, B, bias, scale, 0)
+    assert_bits_equal(got_host, ref_q, "s8 requant pipelined")
+    got_dev = acf.gemm_s8_requant(torch_dev(As), torch_dev(B), torch_dev(bias), torch_dev(scale), 0)
+    acf.synchronize()
+    assert_bits_equal(got_dev.cpu().numpy(), got_host, "s8 requant device vs host path")
+    # mixed: host A, device C -> single-launch path
+    import torch
+    Cd = torch.empty((M, N), dtype=torch.int8, device="cuda")
+    Bd = torch_dev(B)
+    acf.lib().acfun_gemm_s8_requant(M, N, K, acf.ptr(As), Bd.data_ptr(), acf.ptr(bias), acf.ptr(scale),
+                                    Cd.data_ptr(), 0)
+    acf.synchronize()
+    acf.check()
+    assert_bits_equal(Cd.cpu().numpy(), ref_q, "s8 requant host A / device C")
