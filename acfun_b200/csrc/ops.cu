@@ -10,6 +10,7 @@
 //   quantize    clamp(cvt_rne(x * inv_s) + zp, 0, 255)               (int8_quantize_avx512.cpp:8-35)
 //   max-pool    vector lanes: acc = acc > v ? acc : v (vmaxps);       (maxpool_avx512.cpp:15-66)
 //               scalar tail lanes: if (v > mx) mx = v
+#include <algorithm>
 #include <float.h>
 
 #include "api_export.cuh"
@@ -508,6 +509,183 @@ __global__ void k_group(const float* __restrict__ in, int N, int H, int W, int C
   }
 }
 
+// Grouped conv, one block per output row (n, oh): all groups' weights (+ bias) staged in shared
+// memory with the per-group stride padded so that the groups one warp touches fall in
+// different banks; thread item = (ow, output channel), consecutive threads write consecutive
+// channels.  Same accumulation as k_group (bias, then kh -> kw -> ic).
+__global__ void k_group_row(const float* __restrict__ in, int H, int W, int Cin,
+                            const float* __restrict__ w, const float* __restrict__ bias, int KH,
+                            int KW, int Cout, int stride, int pad, int groups, int OH, int OW,
+                            int sstride, float* __restrict__ out, int act, int fma_chain) {
+  extern __shared__ float gs[];
+  const int Cin_p = Cin / groups, Cout_p = Cout / groups;
+  const int wg = Cout_p * KH * KW * Cin_p;
+  float* bs = gs + groups * sstride;
+  for (int i = threadIdx.x; i < groups * wg; i += blockDim.x) {
+    const int g = i / wg, r = i - g * wg;
+    gs[g * sstride + r] = w[i];
+  }
+  for (int i = threadIdx.x; i < Cout; i += blockDim.x) bs[i] = bias ? bias[i] : 0.0f;
+  __syncthreads();
+  const int n = blockIdx.x / OH, oh = blockIdx.x - n * OH;
+  const float* img = in + (size_t)n * H * W * Cin;
+  float* orow = out + ((size_t)n * OH + oh) * OW * Cout;
+  const int items = OW * Cout;
+  for (int it = threadIdx.x; it < items; it += blockDim.x) {
+    const int ow = it / Cout, oc_g = it - ow * Cout;
+    const int g = oc_g / Cout_p, oc = oc_g - g * Cout_p;
+    const float* wgp = gs + g * sstride + oc;
+    float s = bs[oc_g];
+    for (int kh = 0; kh < KH; ++kh) {
+      const int ih = oh * stride - pad + kh;
+      if (ih < 0 || ih >= H) continue;
+      for (int kw = 0; kw < KW; ++kw) {
+        const int iw = ow * stride - pad + kw;
+        if (iw < 0 || iw >= W) continue;
+        const float* ip = img + ((size_t)ih * W + iw) * Cin + g * Cin_p;
+        const float* wp = wgp + (kh * KW + kw) * Cin_p * Cout_p;
+        for (int ic = 0; ic < Cin_p; ++ic) {
+          const float x = __ldg(ip + ic), wv = wp[ic * Cout_p];
+          s = fma_chain ? __fmaf_rn(x, wv, s) : __fadd_rn(s, __fmul_rn(x, wv));
+        }
+      }
+    }
+    if (act == 1) s = fma_chain ? (s > 0.f ? s : 0.f) : (s < 0.f ? 0.f : s);
+    orow[it] = s;
+  }
+}
+
+// Grouped conv, one thread per (output pixel, group) computing all COUT_P channels of the group.
+// A block owns R consecutive output rows of one image: it first stages, with one cooperative
+// load, the group weights ([tap][ic][COUT_P] per group, per-group stride = 4 (mod 32) floats so
+// a warp's groups read float4s from distinct banks) and the input rows those outputs touch;
+// the accumulation then reads shared memory only.  Per-output arithmetic as k_group: bias, then
+// kh -> kw -> ic over in-image taps, fma chain for COUT_P >= 8, mul+add below.
+template <int COUT_P, int CIN_P>  // CIN_P = Cin/groups when known at compile time, else 0
+__global__ void __launch_bounds__(256) k_group_tile(const float* __restrict__ in, int H, int W,
+                                                    int Cin, const float* __restrict__ w,
+                                                    const float* __restrict__ bias, int KH, int KW,
+                                                    int stride, int pad, int groups, int OH, int OW,
+                                                    int R, int sstride, float* __restrict__ out,
+                                                    int act) {
+  static_assert(COUT_P % 4 == 0, "float4 weight rows");
+  extern __shared__ float4 gs4[];
+  float* gs = reinterpret_cast<float*>(gs4);
+  const int Cin_p = CIN_P > 0 ? CIN_P : Cin / groups, Cout = groups * COUT_P;
+  const int wg = COUT_P * KH * KW * Cin_p;
+  float* bs = gs + groups * sstride;
+  float* tile = bs + ((Cout + 3) & ~3);
+  const int blocks_per_img = (OH + R - 1) / R;
+  const int n = blockIdx.x / blocks_per_img, oh0 = (blockIdx.x - n * blocks_per_img) * R;
+  const int oh1 = min(OH, oh0 + R);
+  const int ih0 = max(0, oh0 * stride - pad), ih1 = min(H, (oh1 - 1) * stride - pad + KH);
+  // staging: every thread issues all of its 16-byte loads before its first shared store, so
+  // the block waits for one memory round trip instead of one per loop iteration
+  constexpr int U = 4;
+  const int wg4 = wg / 4, w_tot4 = groups * wg4;  // wg and sstride are multiples of 4
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  for (int base = threadIdx.x; base < w_tot4; base += U * blockDim.x) {
+    float4 v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = base + u * blockDim.x;
+      if (i < w_tot4) v[u] = __ldg(w4 + i);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = base + u * blockDim.x;
+      if (i < w_tot4) {
+        const int g = i / wg4;
+        gs4[g * (sstride / 4) + (i - g * wg4)] = v[u];
+      }
+    }
+  }
+  for (int i = threadIdx.x; i < Cout; i += blockDim.x) bs[i] = bias ? bias[i] : 0.0f;
+  const int tile_4 = (ih1 - ih0) * W * Cin / 4;  // W * Cin is a multiple of 4
+  const float4* src4 = reinterpret_cast<const float4*>(in + ((size_t)n * H + ih0) * W * Cin);
+  float4* tile4 = reinterpret_cast<float4*>(tile);
+  for (int base = threadIdx.x; base < tile_4; base += U * blockDim.x) {
+    float4 v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = base + u * blockDim.x;
+      if (i < tile_4) v[u] = __ldg(src4 + i);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = base + u * blockDim.x;
+      if (i < tile_4) tile4[i] = v[u];
+    }
+  }
+  __syncthreads();
+  const int items = (oh1 - oh0) * OW * groups;
+  for (int it = threadIdx.x; it < items; it += blockDim.x) {
+    const int g = it % groups;
+    const int p = it / groups;
+    const int oh = oh0 + p / OW, ow = p % OW;
+    float acc[COUT_P];
+#pragma unroll
+    for (int oc = 0; oc < COUT_P; ++oc) acc[oc] = bs[g * COUT_P + oc];
+    const float* wgp = gs + g * sstride;
+    for (int kh = 0; kh < KH; ++kh) {
+      const int ih = oh * stride - pad + kh;
+      if (ih < 0 || ih >= H) continue;
+      for (int kw = 0; kw < KW; ++kw) {
+        const int iw = ow * stride - pad + kw;
+        if (iw < 0 || iw >= W) continue;
+        const float* ip = tile + ((ih - ih0) * W + iw) * Cin + g * Cin_p;
+        const float4* wp = reinterpret_cast<const float4*>(wgp + (kh * KW + kw) * Cin_p * COUT_P);
+        float xs[CIN_P > 0 ? CIN_P : 1];
+        if constexpr (CIN_P % 4 == 0 && CIN_P > 0) {
+#pragma unroll
+          for (int i = 0; i < CIN_P; i += 4) {
+            const float4 q4 = *reinterpret_cast<const float4*>(ip + i);
+            xs[i] = q4.x; xs[i + 1] = q4.y; xs[i + 2] = q4.z; xs[i + 3] = q4.w;
+          }
+        }
+#pragma unroll
+        for (int ic = 0; ic < (CIN_P > 0 ? CIN_P : Cin_p); ++ic) {
+          float x;
+          if constexpr (CIN_P % 4 == 0 && CIN_P > 0)
+            x = xs[ic];
+          else
+            x = ip[ic];
+#pragma unroll
+          for (int q = 0; q < COUT_P / 4; ++q) {
+            const float4 wv = wp[ic * (COUT_P / 4) + q];
+            if constexpr (COUT_P >= 8) {
+              acc[4 * q] = __fmaf_rn(x, wv.x, acc[4 * q]);
+              acc[4 * q + 1] = __fmaf_rn(x, wv.y, acc[4 * q + 1]);
+              acc[4 * q + 2] = __fmaf_rn(x, wv.z, acc[4 * q + 2]);
+              acc[4 * q + 3] = __fmaf_rn(x, wv.w, acc[4 * q + 3]);
+            } else {
+              acc[4 * q] = __fadd_rn(acc[4 * q], __fmul_rn(x, wv.x));
+              acc[4 * q + 1] = __fadd_rn(acc[4 * q + 1], __fmul_rn(x, wv.y));
+              acc[4 * q + 2] = __fadd_rn(acc[4 * q + 2], __fmul_rn(x, wv.z));
+              acc[4 * q + 3] = __fadd_rn(acc[4 * q + 3], __fmul_rn(x, wv.w));
+            }
+          }
+        }
+      }
+    }
+    float* op = out + (((size_t)n * OH + oh) * OW + ow) * Cout + g * COUT_P;
+#pragma unroll
+    for (int q = 0; q < COUT_P / 4; ++q) {
+      float4 v = make_float4(acc[4 * q], acc[4 * q + 1], acc[4 * q + 2], acc[4 * q + 3]);
+      if (act == 1) {
+        if constexpr (COUT_P >= 8) {
+          v.x = v.x > 0.f ? v.x : 0.f; v.y = v.y > 0.f ? v.y : 0.f;
+          v.z = v.z > 0.f ? v.z : 0.f; v.w = v.w > 0.f ? v.w : 0.f;
+        } else {
+          v.x = v.x < 0.f ? 0.f : v.x; v.y = v.y < 0.f ? 0.f : v.y;
+          v.z = v.z < 0.f ? 0.f : v.z; v.w = v.w < 0.f ? 0.f : v.w;
+        }
+      }
+      reinterpret_cast<float4*>(op)[q] = v;
+    }
+  }
+}
+
 bool group_dev(Call& c, const float* in, int N, int H, int W, int Cin, const float* w,
                const float* bias, int KH, int KW, int Cout, int stride, int pad, int groups,
                float* out, int act) {
@@ -515,6 +693,43 @@ bool group_dev(Call& c, const float* in, int N, int H, int W, int Cin, const flo
   if (OH <= 0 || OW <= 0 || N <= 0) return true;
   const int Cout_p = Cout / groups;
   const long long total = (long long)N * OH * OW * Cout;
+  const long long wg = (long long)Cout_p * KH * KW * (Cin / groups);
+  // pad the per-group stride to Cout_p (mod 32) so a warp's groups hit different banks
+  const long long sstride = Cout_p < 32 ? wg + (((Cout_p - wg % 32) % 32) + 32) % 32 : wg;
+  const long long smem = (groups * sstride + Cout) * 4;
+  // k_group_tile: R output rows per block (about 256 items), weights + input rows in smem
+  const long long sstride4 = wg + (((4 - wg % 32) % 32) + 32) % 32;  // = 4 (mod 32)
+  const long long per_row = (long long)OW * groups;
+  const int R = (int)(per_row >= 256 ? 1 : (256 / per_row < OH ? 256 / per_row : OH));
+  const long long rows_in = std::min<long long>(H, (long long)(R - 1) * stride + KH);
+  const long long smem_t = (groups * sstride4 + ((Cout + 3) & ~3) + rows_in * W * Cin) * 4;
+  if ((Cout_p == 4 || Cout_p == 8 || Cout_p == 16) && smem_t <= 48 * 1024 && aligned16(in) &&
+      aligned16(w) && (W * Cin) % 4 == 0 &&
+      (long long)N * ((OH + R - 1) / R) < (1LL << 31) && (long long)N * H * W * Cin < (1LL << 31) &&
+      aligned16(out)) {
+    const int grid = N * ((OH + R - 1) / R);
+#define ACF_GROUP_TILE(CP, CI)                                                               \
+  k_group_tile<CP, CI><<<grid, 256, (size_t)smem_t, c.stream()>>>(                           \
+      in, H, W, Cin, w, bias, KH, KW, stride, pad, groups, OH, OW, R, (int)sstride4, out, act)
+    // Cin/groups = 4 (with 16-byte aligned group slices) gets a compile-time channel loop
+    const bool ci4 = Cin / groups == 4;
+    if (Cout_p == 4) {
+      if (ci4) ACF_GROUP_TILE(4, 4); else ACF_GROUP_TILE(4, 0);
+    } else if (Cout_p == 8) {
+      if (ci4) ACF_GROUP_TILE(8, 4); else ACF_GROUP_TILE(8, 0);
+    } else {
+      if (ci4) ACF_GROUP_TILE(16, 4); else ACF_GROUP_TILE(16, 0);
+    }
+#undef ACF_GROUP_TILE
+    return c.launched("k_group_tile");
+  }
+  if (smem <= 48 * 1024 && (long long)H * W * Cin < (1LL << 31) && (long long)N * OH < (1LL << 31) &&
+      (long long)OW * Cout < (1LL << 31)) {
+    k_group_row<<<N * OH, 256, (size_t)smem, c.stream()>>>(
+        in, H, W, Cin, w, bias, KH, KW, Cout, stride, pad, groups, OH, OW, (int)sstride, out, act,
+        Cout_p >= 8 ? 1 : 0);
+    return c.launched("k_group_row");
+  }
   k_group<<<grid_for(c, total), 256, 0, c.stream()>>>(in, N, H, W, Cin, w, bias, KH, KW, Cout,
                                                       stride, pad, groups, OH, OW, out, act,
                                                       Cout_p >= 8 ? 1 : 0);

@@ -256,13 +256,25 @@ def measure_configs(acf, torch, stream, flush, steps, with_cpu=True, cfg_filter=
             ts.append(time.perf_counter() - t0)
         return units * unit_scale / statistics.median(ts)
 
-    def record(name, t, work, unit_div, bound, cpu_val=None, cpu_sample="", extra=None):
+    def record(name, t, work, unit_div, bound, cpu_val=None, cpu_sample="", extra=None, nbytes=None):
         pk, punit, psrc = peak[bound]
         achieved = work / t / unit_div
         r = {"ms": round(t * 1e3, 4), "value": round(achieved, 3), "unit": punit,
              "roofline": {"bound": "hbm" if bound == "hbm" else "tensor", "achieved": round(achieved, 2),
                           "peak": round(pk, 1), "unit": punit, "frac": round(achieved / pk, 4),
                           "peak_source": psrc}}
+        if nbytes is not None and bound != "hbm":
+            # a tensor-core config whose compulsory HBM traffic takes longer than its math at
+            # peak is HBM-bound: report that roofline, keep the tensor fraction beside it
+            hpk = peak["hbm"][0]
+            t_tensor, t_hbm = work / unit_div / pk, nbytes / 1e9 / hpk
+            r["roofline"]["tensor_frac"] = round(achieved / pk, 4)
+            r["roofline"]["hbm_frac"] = round(nbytes / 1e9 / t / hpk, 4)
+            r["roofline"]["ideal_us"] = {"tensor": round(t_tensor * 1e6, 2), "hbm": round(t_hbm * 1e6, 2)}
+            if t_hbm > t_tensor:
+                r["roofline"].update({"bound": "hbm", "achieved": round(nbytes / 1e9 / t, 2), "peak": round(hpk, 1),
+                                      "unit": "GB/s", "frac": round(nbytes / 1e9 / t / hpk, 4),
+                                      "peak_source": peak["hbm"][2]})
         if cpu_val is not None:
             r["cpu_baseline"] = {"value": round(cpu_val, 4), "unit": punit, "cores": cores,
                                  "kind": "reference", "sample": cpu_sample}
@@ -344,7 +356,8 @@ def measure_configs(acf, torch, stream, flush, steps, with_cpu=True, cfg_filter=
         else:
             cv = cpu(cfn, ns * flops / N, 1e-12)
             record(name, t, flops, 1e12, bound, cv, f"{ns} of {N} images, reference route",
-                   {"gflop_direct_count": round(flops / 1e9, 4), "img_per_s": round(N / t, 1)})
+                   {"gflop_direct_count": round(flops / 1e9, 4), "mbytes": round(nbytes / 1e6, 2),
+                    "img_per_s": round(N / t, 1)}, nbytes=nbytes)
 
     conv_cfg("cfg3a_conv3x3_f23_f32", 32, 56, 56, 64, 64, 3, 1, 1)
     conv_cfg("cfg3b_conv3x3_f43_f32", 8, 112, 112, 64, 64, 3, 1, 1)

@@ -108,3 +108,17 @@ def test_grouped_golden(acf, name):
     N, H, W, Cin, KH, KW, Cout, st, pd, act, gr = (int(v) for v in d["shape"])
     got = acf.conv2d(d["x"], np.ascontiguousarray(d["w"]), d["b"], KH, KW, Cout, st, pd, act, groups=gr)
     assert_bits_equal(got, d["out"], name)
+
+
+@pytest.mark.parametrize("st", [1, 2])
+def test_grouped_cout16_vs_oracle(acf, orc, st):
+    """Cout/g = 16 (the 16-accumulator grouped kernel) against the oracle's restatement."""
+    g = np.random.default_rng(16 + st)
+    N, H, W, Cin, Cout, gr = 2, 9, 11, 12, 48, 3
+    x = g.uniform(-1, 1, (N, H, W, Cin)).astype(np.float32)
+    w = g.uniform(-0.5, 0.5, (gr, 9 * (Cin // gr), Cout // gr)).astype(np.float32)
+    b = g.uniform(-0.1, 0.1, Cout).astype(np.float32)
+    got = acf.conv2d(x, w, b, 3, 3, Cout, st, 1, 1, groups=gr)
+    ref = np.empty_like(got)
+    orc.oracle().orc_conv2d(x, N, H, W, Cin, w, b.ctypes.data, 3, 3, Cout, st, 1, gr, ref, 1)
+    assert max_rel(got, ref) < TOL_F32
