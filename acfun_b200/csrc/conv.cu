@@ -13,6 +13,7 @@
 // TMA producer shifts the A rows by kh*Wp + kw, and the epilogue keeps only the GEMM rows
 // that land on real output pixels.  Strided convolutions gather an explicit im2col matrix.
 // Bias and ReLU are fused into the TMEM drain.
+#include <algorithm>
 #include "api_export.cuh"
 #include "conv.cuh"
 #include "gemm.cuh"
@@ -171,6 +172,269 @@ __global__ void __launch_bounds__(128) k_conv_simt(const float* __restrict__ x, 
         if (j < Cout) dst[j] = acc[j];
     }
   }
+}
+
+// Small-K convolution fused with the 2x2 / stride-2 / pad-0 max-pool that follows it (an ACFUN0
+// Conv -> MaxPool pair): a block owns one pooled output row; it stages the conv weights
+// [K][Cout], the bias and the input rows that row needs in shared memory, then one thread per
+// (pooled pixel, 16-channel block) computes the four conv outputs of its pool window (weights
+// loaded once per k and reused by the four) and writes only their maximum.  Per conv output
+// the arithmetic is k_conv_simt's: fma chain from 0 over k = (kh, kw, ic) of the in-image
+// taps, + bias, then act; the pool is k_maxpool4's: start -1e30, window order (0,0) (0,1)
+// (1,0) (1,1), then the pool's post-ReLU.
+template <int CB>
+__global__ void __launch_bounds__(128) k_conv_pool_simt(
+    const float* __restrict__ x, int H, int W, int Cin, const float* __restrict__ w,
+    const float* __restrict__ bias, int Cout, int KH, int KW, int stride, int pad, int PH, int PW,
+    int rows_in, float* __restrict__ out, int act, int post_relu) {
+  extern __shared__ float4 cp_sm4[];
+  float* ws = reinterpret_cast<float*>(cp_sm4);  // [K][Cout]
+  const int K = KH * KW * Cin;
+  float* bs = ws + K * Cout;
+  float* tile = bs + ((Cout + 3) & ~3);
+  const int n = blockIdx.x / PH, ph = blockIdx.x - n * PH;
+  const int ih0 = max(0, 2 * ph * stride - pad);
+  const int ih1 = min(H, (2 * ph + 1) * stride - pad + KH);
+  for (int i = threadIdx.x; i < K * Cout; i += blockDim.x) ws[i] = w[i];
+  for (int i = threadIdx.x; i < Cout; i += blockDim.x) bs[i] = bias ? bias[i] : 0.0f;
+  {
+    const int tn = (ih1 - ih0) * W * Cin;
+    const float* src = x + ((size_t)n * H + ih0) * W * Cin;
+    constexpr int U = 8;
+    for (int base = threadIdx.x; base < tn; base += U * blockDim.x) {
+      float v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = base + u * blockDim.x;
+        if (i < tn) v[u] = __ldg(src + i);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = base + u * blockDim.x;
+        if (i < tn) tile[i] = v[u];
+      }
+    }
+  }
+  (void)rows_in;
+  __syncthreads();
+  const int nb = Cout / CB, items = PW * nb;
+  for (int it = threadIdx.x; it < items; it += blockDim.x) {
+    const int pw = it / nb, cb = it - pw * nb;
+    float acc[4][CB];
+#pragma unroll
+    for (int p = 0; p < 4; ++p)
+#pragma unroll
+      for (int j = 0; j < CB; ++j) acc[p][j] = 0.0f;
+    for (int kh = 0; kh < KH; ++kh) {
+      for (int kw = 0; kw < KW; ++kw) {
+        // the pool window's four conv pixels: (2ph + dy, 2pw + dx)
+        int xoff[4];
+        bool ok[4];
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          const int ih = (2 * ph + (p >> 1)) * stride - pad + kh;
+          const int iw = (2 * pw + (p & 1)) * stride - pad + kw;
+          ok[p] = ih >= 0 && ih < H && iw >= 0 && iw < W;
+          xoff[p] = ((ih - ih0) * W + iw) * Cin;
+        }
+        for (int ic = 0; ic < Cin; ++ic) {
+          const float4* wr = reinterpret_cast<const float4*>(ws + ((kh * KW + kw) * Cin + ic) * Cout + cb * CB);
+          float wv[CB];
+#pragma unroll
+          for (int q = 0; q < CB / 4; ++q) {
+            const float4 t = wr[q];
+            wv[4 * q] = t.x; wv[4 * q + 1] = t.y; wv[4 * q + 2] = t.z; wv[4 * q + 3] = t.w;
+          }
+#pragma unroll
+          for (int p = 0; p < 4; ++p) {
+            if (!ok[p]) continue;
+            const float xv = tile[xoff[p] + ic];
+#pragma unroll
+            for (int j = 0; j < CB; ++j) acc[p][j] = __fmaf_rn(xv, wv[j], acc[p][j]);
+          }
+        }
+      }
+    }
+    float m[CB];
+#pragma unroll
+    for (int j = 0; j < CB; ++j) m[j] = -1e30f;
+#pragma unroll
+    for (int p = 0; p < 4; ++p)
+#pragma unroll
+      for (int j = 0; j < CB; ++j) {
+        float v = __fadd_rn(acc[p][j], bs[cb * CB + j]);
+        v = act ? (v > 0.0f ? v : 0.0f) : v;
+        m[j] = m[j] > v ? m[j] : v;
+      }
+    float* dst = out + (((size_t)n * PH + ph) * PW + pw) * Cout + cb * CB;
+#pragma unroll
+    for (int q = 0; q < CB / 4; ++q) {
+      float4 r = make_float4(m[4 * q], m[4 * q + 1], m[4 * q + 2], m[4 * q + 3]);
+      if (post_relu) {
+        r.x = r.x > 0.f ? r.x : 0.f; r.y = r.y > 0.f ? r.y : 0.f;
+        r.z = r.z > 0.f ? r.z : 0.f; r.w = r.w > 0.f ? r.w : 0.f;
+      }
+      reinterpret_cast<float4*>(dst)[q] = r;
+    }
+  }
+}
+
+// k_conv_pool_simt specialised at compile time for the first layer of an image network
+// (3x3, stride 1, pad 1, Cin = 3): the input tile is split by column parity and keeps the
+// channels of a pixel together ([row][iw & 1][iw >> 1][CIN]), so for every tap the four
+// pixels of a pool window read fixed offsets from one per-thread base and a warp's reads
+// are CIN words apart (conflict-free for odd CIN); all 27 taps unroll.  Border items take
+// the bounds-checked loop.  Arithmetic identical to k_conv_pool_simt.
+template <int CIN, int CB>
+__global__ void __launch_bounds__(128) k_conv_pool_3x3s1(
+    const float* __restrict__ x, int H, int W, const float* __restrict__ w,
+    const float* __restrict__ bias, int Cout, int PH, int PW, float* __restrict__ out, int act,
+    int post_relu) {
+  constexpr int KH = 3, KW = 3, K = KH * KW * CIN, ROWS = 1 + KH;  // stride 1, pad 1
+  extern __shared__ float4 cf_sm4[];
+  float* ws = reinterpret_cast<float*>(cf_sm4);  // [K][Cout]
+  float* bs = ws + K * Cout;
+  float* tile = bs + ((Cout + 3) & ~3);  // [ROWS][2][hw][CIN]
+  const int hw = (W + 1) >> 1, plane = hw * CIN;
+  const int n = blockIdx.x / PH, ph = blockIdx.x - n * PH;
+  const int r0 = 2 * ph - 1;  // input row of tile row 0
+  const int ih0 = max(0, r0), ih1 = min(H, r0 + ROWS);
+  for (int i = threadIdx.x; i < K * Cout; i += blockDim.x) ws[i] = w[i];
+  for (int i = threadIdx.x; i < Cout; i += blockDim.x) bs[i] = bias ? bias[i] : 0.0f;
+  {
+    const int tn = (ih1 - ih0) * W * CIN;
+    const float* src = x + ((size_t)n * H + ih0) * W * CIN;
+    const int base_r = ih0 - r0;
+    constexpr int U = 8;
+    for (int b0 = threadIdx.x; b0 < tn; b0 += U * blockDim.x) {
+      float v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = b0 + u * blockDim.x;
+        if (i < tn) v[u] = __ldg(src + i);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = b0 + u * blockDim.x;
+        if (i < tn) {
+          const int pix = i / CIN, ic = i - pix * CIN;
+          const int r = pix / W, iw = pix - r * W;
+          tile[((base_r + r) * 2 + (iw & 1)) * plane + (iw >> 1) * CIN + ic] = v[u];
+        }
+      }
+    }
+  }
+  __syncthreads();
+  const int nb = Cout / CB, items = PW * nb;
+  for (int it = threadIdx.x; it < items; it += blockDim.x) {
+    const int cb = it / PW, pw = it - cb * PW;
+    float acc[4][CB];
+#pragma unroll
+    for (int p = 0; p < 4; ++p)
+#pragma unroll
+      for (int j = 0; j < CB; ++j) acc[p][j] = 0.0f;
+    const bool interior = r0 >= 0 && r0 + ROWS <= H && pw >= 1 && 2 * pw + 2 < W;
+    if (interior) {
+      // pixel (dy, dx), tap (kh, kw): tile row dy + kh, column 2pw + dx - 1 + kw
+      const float* tb = tile + (pw - 1) * CIN;
+#pragma unroll
+      for (int kh = 0; kh < KH; ++kh)
+#pragma unroll
+        for (int kw = 0; kw < KW; ++kw)
+#pragma unroll
+          for (int ic = 0; ic < CIN; ++ic) {
+            const int k = (kh * KW + kw) * CIN + ic;
+            const float4* wr = reinterpret_cast<const float4*>(ws + k * Cout + cb * CB);
+            float wv[CB];
+#pragma unroll
+            for (int q = 0; q < CB / 4; ++q) {
+              const float4 t = wr[q];
+              wv[4 * q] = t.x; wv[4 * q + 1] = t.y; wv[4 * q + 2] = t.z; wv[4 * q + 3] = t.w;
+            }
+#pragma unroll
+            for (int p = 0; p < 4; ++p) {
+              const int dy = p >> 1, dx = p & 1;
+              const int col = 2 + dx - 1 + kw;  // column relative to 2*(pw-1)
+              const float xv = tb[((dy + kh) * 2 + (col & 1)) * plane + (col >> 1) * CIN + ic];
+#pragma unroll
+              for (int j = 0; j < CB; ++j) acc[p][j] = __fmaf_rn(xv, wv[j], acc[p][j]);
+            }
+          }
+    } else {
+      for (int kh = 0; kh < KH; ++kh)
+        for (int kw = 0; kw < KW; ++kw)
+#pragma unroll
+          for (int ic = 0; ic < CIN; ++ic) {
+            const int k = (kh * KW + kw) * CIN + ic;
+            const float4* wr = reinterpret_cast<const float4*>(ws + k * Cout + cb * CB);
+            float wv[CB];
+#pragma unroll
+            for (int q = 0; q < CB / 4; ++q) {
+              const float4 t = wr[q];
+              wv[4 * q] = t.x; wv[4 * q + 1] = t.y; wv[4 * q + 2] = t.z; wv[4 * q + 3] = t.w;
+            }
+#pragma unroll
+            for (int p = 0; p < 4; ++p) {
+              const int dy = p >> 1, dx = p & 1;
+              const int ih = 2 * ph + dy - 1 + kh, iw = 2 * pw + dx - 1 + kw;
+              if (ih < 0 || ih >= H || iw < 0 || iw >= W) continue;
+              const float xv = tile[((ih - r0) * 2 + (iw & 1)) * plane + (iw >> 1) * CIN + ic];
+#pragma unroll
+              for (int j = 0; j < CB; ++j) acc[p][j] = __fmaf_rn(xv, wv[j], acc[p][j]);
+            }
+          }
+    }
+    float m[CB];
+#pragma unroll
+    for (int j = 0; j < CB; ++j) m[j] = -1e30f;
+#pragma unroll
+    for (int p = 0; p < 4; ++p)
+#pragma unroll
+      for (int j = 0; j < CB; ++j) {
+        float v = __fadd_rn(acc[p][j], bs[cb * CB + j]);
+        v = act ? (v > 0.0f ? v : 0.0f) : v;
+        m[j] = m[j] > v ? m[j] : v;
+      }
+    float* dst = out + (((size_t)n * PH + ph) * PW + pw) * Cout + cb * CB;
+#pragma unroll
+    for (int q = 0; q < CB / 4; ++q) {
+      float4 r = make_float4(m[4 * q], m[4 * q + 1], m[4 * q + 2], m[4 * q + 3]);
+      if (post_relu) {
+        r.x = r.x > 0.f ? r.x : 0.f; r.y = r.y > 0.f ? r.y : 0.f;
+        r.z = r.z > 0.f ? r.z : 0.f; r.w = r.w > 0.f ? r.w : 0.f;
+      }
+      reinterpret_cast<float4*>(dst)[q] = r;
+    }
+  }
+}
+
+bool conv_pool_dev(Call& c, const float* x, int N, int H, int W, int Cin, const float* w,
+                   const float* bias, int KH, int KW, int Cout, int stride, int pad, int act,
+                   int pool, int pst, int ppd, int post_relu, float* out, bool* handled) {
+  *handled = false;
+  const int OH = (H + 2 * pad - KH) / stride + 1, OW = (W + 2 * pad - KW) / stride + 1;
+  if (pool != 2 || pst != 2 || ppd != 0 || OH < 2 || OW < 2 || Cout % 16 != 0) return true;
+  const int K = KH * KW * Cin;
+  const int PH = (OH - 2) / 2 + 1, PW = (OW - 2) / 2 + 1;
+  if (K > 64 || Cout > 64 || !aligned16(w) || !aligned16(out) || (long long)N * PH >= (1LL << 31))
+    return true;
+  if (KH == 3 && KW == 3 && stride == 1 && pad == 1 && Cin == 3) {
+    const long long smem3 = ((long long)K * Cout + ((Cout + 3) & ~3) + 4LL * 2 * ((W + 1) / 2) * 3) * 4;
+    if (smem3 <= 48 * 1024 && (long long)4 * W * 3 < (1LL << 31)) {
+      k_conv_pool_3x3s1<3, 16><<<N * PH, 128, (size_t)smem3, c.stream()>>>(
+          x, H, W, w, bias, Cout, PH, PW, out, act, post_relu);
+      *handled = true;
+      return c.launched("k_conv_pool_3x3s1");
+    }
+  }
+  const long long rows_in = std::min<long long>(H, (long long)stride + KH);
+  const long long smem = ((long long)K * Cout + ((Cout + 3) & ~3) + rows_in * W * Cin) * 4;
+  // same cases as conv_simt (K <= 64, Cout <= 64), so the fused result equals conv + pool
+  if (smem > 48 * 1024 || (long long)rows_in * W * Cin >= (1LL << 31)) return true;
+  k_conv_pool_simt<16><<<N * PH, 128, (size_t)smem, c.stream()>>>(
+      x, H, W, Cin, w, bias, Cout, KH, KW, stride, pad, PH, PW, (int)rows_in, out, act, post_relu);
+  *handled = true;
+  return c.launched("k_conv_pool_simt");
 }
 
 // Returns true when the CUDA-core path applies (and has been launched).

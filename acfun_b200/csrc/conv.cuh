@@ -29,6 +29,13 @@ bool conv_f32_dev(Call& c, const float* x, int N, int H, int W, int Cs, int coff
                   const float* w, long long ldw, const float* bias, int KH, int KW, int Cout_g,
                   int stride, int pad, float* out, long long ldc, int act);
 
+// Dense conv (groups 1) immediately followed by max-pool(pool, pst, ppd, post_relu), fused when
+// the conv takes the CUDA-core small-K route and the pool is 2x2 / stride 2 / pad 0 (sets
+// *handled; otherwise nothing is launched).  Same result as the two layers run in turn.
+bool conv_pool_dev(Call& c, const float* x, int N, int H, int W, int Cin, const float* w,
+                   const float* bias, int KH, int KW, int Cout, int stride, int pad, int act,
+                   int pool, int pst, int ppd, int post_relu, float* out, bool* handled);
+
 // int8 conv router (conv_int8.cpp:63-148) on device pointers.
 bool conv2d_int8_dev(Call& c, const float* x, int N, int H, int W, int Cin, const int8_t* wq,
                      const float* wscale, const float* bias, int KH, int KW, int Cout, int stride,

@@ -26,10 +26,11 @@ def test_model_demo_golden(acf, tmp_path):
     m.close()
 
 
-def test_model_vgg_small_vs_oracle(acf, tmp_path):
+@pytest.mark.parametrize("width_div", [8, 4])   # 4: conv1 has 16 channels -> fused conv + pool
+def test_model_vgg_small_vs_oracle(acf, tmp_path, width_div):
     from acfun_b200 import acfun0
     from oracle.model_oracle import OracleModel
-    blob = acfun0.vgg11(seed=3, in_hw=64, width_div=8, fc_dims=(128, 64, 10)).tobytes()
+    blob = acfun0.vgg11(seed=3, in_hw=64, width_div=width_div, fc_dims=(128, 64, 10)).tobytes()
     p = tmp_path / "v.acfun"
     p.write_bytes(blob)
     m = acf.Model(str(p))
@@ -72,3 +73,26 @@ def test_model_load_rejects_corrupt_files(acf, tmp_path, mutate):
     assert L.acfun_last_error_code() == 5
     L.acfun_clear_error()
     assert L.acfun_model_infer(None, None, None) == 0
+
+
+def test_model_conv_pool_fusion_vs_oracle(acf, tmp_path):
+    """Conv -> MaxPool pairs that run fused (small-K conv, 2x2/2 pool): odd spatial sizes
+    (ragged pool edge, image borders), a strided 1x1 conv, a pool with post-ReLU."""
+    from acfun_b200.acfun0 import Acfun0Writer, bn_params
+    from oracle.model_oracle import OracleModel
+    g = np.random.default_rng(11)
+    u = lambda *s: g.uniform(-0.3, 0.3, size=s).astype(np.float32)
+    Wr = Acfun0Writer(3, 37, 29)
+    Wr.conv(u(27, 16), u(16), 3, 3, 16, 1, 1).bn(*bn_params(g, 16)).relu().maxpool(2, 2, 0)   # 18x14
+    Wr.conv(u(16, 32), u(32), 1, 1, 32, 2, 0).maxpool(2, 2, 0).relu()                          # 9x7 -> 4x3
+    Wr.fc(u(4 * 3 * 32, 10), u(10), 4 * 3 * 32, 10).softmax()
+    blob = Wr.tobytes()
+    p = tmp_path / "cp.acfun"
+    p.write_bytes(blob)
+    m = acf.Model(str(p))
+    x = np.random.default_rng(12).uniform(-1, 1, (5, 37, 29, 3)).astype(np.float32)
+    y = m.infer_batch(x)
+    om = OracleModel(blob)
+    for k in range(5):
+        assert max_rel(y[k], om.infer(x[k])) < TOL_F32
+    m.close()
