@@ -202,7 +202,7 @@ def _bn_fold(g, w, cout):
     return (w * s).astype(np.float32), (beta - mean * s).astype(np.float32)
 
 
-def measure_configs(acf, torch, stream, flush, steps, with_cpu=True, cfg_filter=None):
+def measure_configs(acf, torch, stream, flush, steps, with_cpu=True, cfg_filter=None, vgg_images=256):
     """Every BASELINE config on one GPU (device-resident tensors, CUDA events, L2 flushed
     before each timed step), with its roofline and the reference timed on the host cores on a
     bounded sample of the same workload."""
@@ -376,7 +376,7 @@ def measure_configs(acf, torch, stream, flush, steps, with_cpu=True, cfg_filter=
         if not os.path.exists(path):
             acfun0.vgg11(seed=5).save(path)
         m = acf.Model(path)
-        n = 256
+        n = vgg_images   # 256 = the config; smaller only for profiling captures
         x = g.uniform(0, 1, (n, 224, 224, 3)).astype(np.float32)
         dx, dy = dev(x), torch.empty((n, 1000), device="cuda")
         t = timeit(lambda: L.acfun_model_infer_batch(m.h, n, dx.data_ptr(), dy.data_ptr()), max(2, steps // 4))
@@ -389,7 +389,7 @@ def measure_configs(acf, torch, stream, flush, steps, with_cpu=True, cfg_filter=
             R.acfun_model_destroy(h)
         gf = 15.218e9
         record("cfg5_vgg11_b256", t, n * gf, 1e12, "f32bf3", None, "",
-               {"img_per_s": round(n / t, 1), "gflop_per_img": 15.218})
+               {"img_per_s": round(n / t, 1), "gflop_per_img": 15.218, "images": n})
         if cv is not None:
             out["cfg5_vgg11_b256"]["cpu_baseline"] = {"value": round(cv, 3), "unit": "img/s", "cores": cores,
                                                       "kind": "reference",
@@ -479,6 +479,8 @@ def main():
     ap.add_argument("--no-configs", action="store_true",
                     help="skip the per-config measurements (every BASELINE config, N=1 only)")
     ap.add_argument("--configs", default=None, help="comma-separated subset of config names")
+    ap.add_argument("--vgg-images", type=int, default=256,
+                    help="cfg5 batch (256 = the config; smaller only for --only-configs profiling runs)")
     ap.add_argument("--only-configs", action="store_true",
                     help="print only the per-config measurements (profiling runs; not the bench line)")
     args = ap.parse_args()
@@ -510,7 +512,7 @@ def main():
     if args.only_configs:
         flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
         filt = set(args.configs.split(",")) if args.configs else None
-        res = measure_configs(acf, torch, stream, flush, steps=max(1, args.steps),
+        res = measure_configs(acf, torch, stream, flush, steps=max(1, args.steps), vgg_images=args.vgg_images,
                               with_cpu=not args.no_cpu_baseline, cfg_filter=filt)
         print(json.dumps({"configs": res}), flush=True)
         return
