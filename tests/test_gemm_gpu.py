@@ -24,7 +24,8 @@ def torch_dev(a):
 # the reference's own gates (benchmark.cpp:53-77, :930-962) plus tcgen05 tile edges
 INT8_SHAPES = [(63, 63, 63), (100, 100, 100), (255, 255, 255), (512, 512, 512), (1023, 1023, 1023),
                (64, 64, 64), (512, 17, 64), (63, 512, 33), (127, 129, 63), (1023, 4, 7),
-               (128, 256, 128), (129, 257, 129), (1, 1, 1), (300, 640, 2000), (2048, 384, 4096)]
+               (128, 256, 128), (129, 257, 129), (1, 1, 1), (300, 640, 2000), (2048, 384, 4096),
+               (2560, 2048, 640), (2600, 2000, 200)]   # > 148 tiles: more than one wave, ragged
 
 
 def rand_u8s8(g, M, N, K):
@@ -42,7 +43,7 @@ def test_gemm_int8_exact(acf, orc, M, N, K):
 
 @pytest.mark.parametrize("M,N,K,act", [(64, 64, 64, 1), (100, 100, 100, 1), (255, 255, 255, 0),
                                        (512, 17, 64, 1), (63, 512, 33, 1), (127, 129, 63, 0),
-                                       (1023, 4, 7, 1), (700, 300, 1111, 1)])
+                                       (1023, 4, 7, 1), (700, 300, 1111, 1), (2560, 2048, 384, 1)])
 def test_gemm_int8_epi_exact(acf, orc, M, N, K, act):
     g = np.random.default_rng(K)
     A, B = rand_u8s8(g, M, N, K)
@@ -175,3 +176,23 @@ def test_host_buffer_row_pipeline_exact(acf, orc, M, N, K):
     acf.synchronize()
     acf.check()
     assert_bits_equal(Cd.cpu().numpy(), ref_q, "s8 requant host A / device C")
+
+
+def test_s8_requant_two_waves_device(acf, orc):
+    """160 tiles of 128x256 on 148 persistent CTAs (a second, partial wave) through the
+    device-pointer path; every row of the last 3 row blocks is compared."""
+    M, N, K = 2560, 2048, 1000
+    g = np.random.default_rng(31)
+    A = g.integers(-127, 128, (M, K), dtype=np.int8)
+    B = g.integers(-127, 128, (K, N), dtype=np.int8)
+    bias = g.integers(-1000, 1001, N, dtype=np.int32)
+    scale = g.uniform(1e-4, 1e-3, N).astype(np.float32)
+    got = acf.gemm_s8_requant(torch_dev(A), torch_dev(B), torch_dev(bias), torch_dev(scale), 1)
+    acf.synchronize()
+    got = got.cpu().numpy()
+    rows = np.arange(M - 384, M)            # the second wave's tiles cover rows 2304..2559
+    rows = np.concatenate([[0, 1, 1000], rows])
+    ref = np.empty((rows.size, N), np.int8)
+    orc.oracle().orc_gemm_s8_requant(rows.size, N, K, np.ascontiguousarray(A[rows]), B, bias.ctypes.data,
+                                     scale, ref, 1)
+    assert_bits_equal(got[rows], ref, "requant two waves")
