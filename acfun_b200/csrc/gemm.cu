@@ -200,8 +200,8 @@ Operand to_bf16x2(Call& c, const float* src, int rows, int cols, long long lds) 
   return o;
 }
 
-// 0: per use (SGEMM API 3xTF32, convolution / FC / model 3xBF16); 1: 3xTF32 everywhere;
-// 2: 3xBF16 everywhere.  Initialised from ACFUN_FP32_MATH, changed by acfun_set_fp32_math.
+// 0 (default) and 2: 3xBF16 everywhere; 1: 3xTF32 everywhere.  Initialised from
+// ACFUN_FP32_MATH, changed by acfun_set_fp32_math.
 static std::atomic<int> g_fp32_mode{-1};
 
 static int fp32_mode() {
@@ -220,7 +220,8 @@ Fp32Math fp32_math(Fp32Use use) {
   const int m = fp32_mode();
   if (m == 1) return Fp32Math::TF32X3;
   if (m == 2) return Fp32Math::BF16X3;
-  return use == Fp32Use::GemmApi ? Fp32Math::TF32X3 : Fp32Math::BF16X3;
+  (void)use;
+  return Fp32Math::BF16X3;
 }
 
 // ------------------------------------------------------------------ launcher

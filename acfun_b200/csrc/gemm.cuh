@@ -31,10 +31,10 @@ __global__ void k_to_tf32x2(const float* __restrict__ src, long long lds, int ro
 
 enum class GemmKind { I8U, I8S, BF16, TF32X3, BF16X3 };
 
-// fp32 math on tensor cores: 3xTF32 (tf32 hi/lo, ~2^-21 per product) or 3xBF16 (bf16
-// hi/lo on kind::f16: twice the MMA rate and half the operand bytes of 3xTF32, ~2^-17 per
-// product).  The public SGEMM entry points default to 3xTF32, convolutions / FC / the model
-// to 3xBF16; ACFUN_FP32_MATH=tf32x3|bf16x3 forces one mode everywhere.
+// fp32 math on tensor cores: 3xTF32 (tf32 hi/lo, ~2^-21 per product) or 3xBF16 (bf16 hi/lo on
+// kind::f16: twice the MMA rate and half the operand bytes of 3xTF32, ~2^-17 per product).
+// 3xBF16 is the default everywhere; ACFUN_FP32_MATH=tf32x3 (or acfun_set_fp32_math(1))
+// selects 3xTF32.
 enum class Fp32Math { TF32X3, BF16X3 };
 enum class Fp32Use { GemmApi, Conv };
 Fp32Math fp32_math(Fp32Use use);

@@ -292,7 +292,7 @@ def measure_configs(acf, torch, stream, flush, steps, with_cpu=True, cfg_filter=
         t = timeit(lambda: L.acfun_gemm(1024, 1024, 1024, dA.data_ptr(), dB.data_ptr(), dC.data_ptr()), steps)
         Cc = np.empty((1024, 1024), np.float32)
         cv = cpu(lambda: R.acfun_gemm(1024, 1024, 1024, A, B, Cc), 2 * 1024 ** 3, 1e-12)
-        record("cfg1_sgemm_1024", t, 2 * 1024 ** 3, 1e12, "f32x3", cv, "full 1024^3 acfun_gemm")
+        record("cfg1_sgemm_1024", t, 2 * 1024 ** 3, 1e12, "f32bf3", cv, "full 1024^3 acfun_gemm")
 
     if want("cfg2_bf16_4096"):
         A = g.uniform(-1, 1, (4096, 4096)).astype(np.float32)

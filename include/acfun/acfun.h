@@ -124,7 +124,8 @@ void acfun_gemm_s8_requant(int M, int N, int K, const int8_t* A, const int8_t* B
  * reference).  Such callers exist: processes that reserve all device memory up front in
  * their own pool, code running in an out-of-memory handler or allocator callback, and
  * latency-critical loops where cudaMalloc/cudaFree would synchronise the device.  Same
- * result as acfun_gemm_epi in its default 3xTF32 mode, but nothing is allocated: the 3xTF32 operand copies live in one
+ * result as acfun_gemm_epi in 3xTF32 mode (acfun_set_fp32_math(1)), but nothing is
+ * allocated: the 3xTF32 operand copies live in one
  * fixed 16 MiB device array compiled into the library (held by every GPU that loads it),
  * so 2*(M*K + K*N) must stay <= 4 Mi floats (K, N rounded up to 4).  All tensors must be
  * device pointers.  The first call on a device resolves the array's address; make it
@@ -139,7 +140,8 @@ int acfun_gemm_epi_noalloc(int M, int N, int K, const float* A, const float* B, 
  *   1  3xTF32 everywhere   (tf32 parts, ~2^-21 relative per product)
  *   2  3xBF16 everywhere   (bf16 parts, ~2^-17 per product; twice the tensor rate and half the
  *                           operand bytes of 3xTF32)
- *   0  default: acfun_gemm / acfun_gemm_epi in 3xTF32, convolutions / FC / the model in 3xBF16.
+ *   0  default: 3xBF16 everywhere (measured max-rel vs float64 on the parity shapes is at
+ *      or below 3xTF32's there: the fp32 accumulation dominates both).
  * The initial mode comes from $ACFUN_FP32_MATH ("tf32x3" / "bf16x3").  Returns 0 or 1 (bad
  * mode).  Process-wide. */
 int acfun_set_fp32_math(int mode);
