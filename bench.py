@@ -608,7 +608,9 @@ def main():
                          "peak_source": f"2 x bf16_tflops ({peak_src}, MEASURED_PEAKS.json): dense int8 = 2x bf16",
                          "kernel": "gemm_tc_kernel<I8, BN=256, 4 stages, S8_REQ>",
                          "traffic": traffic},
-            "gpu_launches": args.steps * 2,
+            # our kernels in the two timed loops: one GEMM per device-resident call; the host-
+            # buffer call splits A into min(8, A bytes / 2 MiB) row chunks, one GEMM each
+            "gpu_launches": args.steps * (1 + max(1, min(8, (M * K) >> 21))),
             "clocks": clk.summary(),
         }
         if not args.no_cpu_baseline:
