@@ -155,3 +155,18 @@ def test_fc_golden(acf):
     d = load("fc")
     assert max_rel(acf.fc(d["x"], d["w"], d["b"], 0), d["out"]) < TOL_F32
     assert max_rel(acf.fc(d["x"], d["w"], d["b"], 1), d["out_relu"]) < TOL_F32
+
+
+def test_conv_f32_last_wave_images(acf, orc):
+    """8 x 56 x 56, 64 -> 128: 211 implicit-GEMM tiles on 148 persistent CTAs; the second,
+    partial wave covers the last images, which are the ones checked here."""
+    N, H, W, Cin, Cout = 8, 56, 56, 64, 128
+    g = np.random.default_rng(211)
+    x = g.uniform(-1, 1, (N, H, W, Cin)).astype(np.float32)
+    w = he(g, (9 * Cin, Cout), 9 * Cin)
+    b = g.uniform(-0.1, 0.1, Cout).astype(np.float32)
+    got = acf.conv2d(x, w, b, 3, 3, Cout, 1, 1, 1)
+    ref = np.empty((3, H, W, Cout), np.float32)
+    orc.oracle().orc_conv2d(np.ascontiguousarray(x[N - 3:]), 3, H, W, Cin, w, b.ctypes.data, 3, 3, Cout, 1, 1,
+                            1, ref, 1)
+    assert max_rel(got[N - 3:], ref) < TOL_F32, max_rel(got[N - 3:], ref)

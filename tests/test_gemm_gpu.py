@@ -112,7 +112,8 @@ def test_gemm_f32_tolerance(acf, orc, M, N, K):
     assert max_rel(got, ref) < TOL_F32, max_rel(got, ref)
 
 
-@pytest.mark.parametrize("M,N,K", [(64, 64, 64), (33, 47, 129), (1024, 1024, 1024), (200, 520, 300)])
+@pytest.mark.parametrize("M,N,K", [(64, 64, 64), (33, 47, 129), (1024, 1024, 1024), (200, 520, 300),
+                                   (2560, 2048, 256)])   # 160 tiles: a second, partial wave
 def test_gemm_bf16_tolerance(acf, orc, M, N, K):
     g = np.random.default_rng(M * N + K)
     A = g.uniform(-1, 1, (M, K)).astype(np.float32)
