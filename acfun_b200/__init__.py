@@ -56,6 +56,7 @@ SIGNATURES = {
     "acfun_model_output_size": (i, [vp]),
     "acfun_model_input_dims": (None, [vp, vp, vp, vp]),
     "acfun_model_infer_batch": (i, [vp, i, vp, vp]),
+    "acfun_model_set_int8": (i, [vp, i]),
     "acfun_gemm_s8_requant": (None, [i, i, i, vp, vp, vp, vp, vp, i]),
     "acfun_gemm_epi_noalloc": (i, [i, i, i, vp, vp, vp, vp, i]),
     "acfun_set_fp32_math": (i, [i]),
@@ -299,6 +300,14 @@ class Model:
         if r <= 0:
             raise AcfunError("acfun_model_infer_batch returned 0")
         return out
+
+    def set_int8(self, enable: bool = True) -> None:
+        """Dense convolutions through the int8 router, one activation scale per image
+        (acfun_model_set_int8; FC / pooling / softmax stay fp32)."""
+        rc = lib().acfun_model_set_int8(self.h, 1 if enable else 0)
+        check()
+        if rc != 0:
+            raise AcfunError(f"acfun_model_set_int8 failed ({rc})")
 
     def output_size(self) -> int:
         return lib().acfun_model_output_size(self.h)

@@ -36,6 +36,12 @@ bool conv_pool_dev(Call& c, const float* x, int N, int H, int W, int Cin, const 
                    const float* bias, int KH, int KW, int Cout, int stride, int pad, int act,
                    int pool, int pst, int ppd, int post_relu, float* out, bool* handled);
 
+// The same router over a batch with one activation scale per image, i.e. N separate
+// calls of acfun_conv2d_int8 (the reference's per-image model harness) in one pass.
+bool conv2d_int8_batch_dev(Call& c, const float* x, int N, int H, int W, int Cin,
+                           const int8_t* wq, const float* wscale, const float* bias, int KH,
+                           int KW, int Cout, int stride, int pad, float* out, int act);
+
 // int8 conv router (conv_int8.cpp:63-148) on device pointers.
 bool conv2d_int8_dev(Call& c, const float* x, int N, int H, int W, int Cin, const int8_t* wq,
                      const float* wscale, const float* bias, int KH, int KW, int Cout, int stride,

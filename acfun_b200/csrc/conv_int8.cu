@@ -28,10 +28,10 @@ namespace acf {
 
 struct Int8Scalars {
   unsigned maxa_bits;  // max|x| as float bits (non-negative floats order like unsigned)
+  unsigned done;       // blocks of k_absmax finished (the last one derives the rest)
   float inv_s;         // 127 / maxa
   float sa;            // maxa / 127
   int zero;            // maxa < 1e-12: the reference writes an all-zero output
-  unsigned done;       // blocks of k_absmax finished (the last one derives the rest)
 };
 
 // Per-output-channel dequantisation factors that k_absmax's last block derives once sa is
@@ -164,8 +164,9 @@ __device__ __forceinline__ uint8_t clamp_u8(int v) {
 //           (winograd_int8.cpp:306-325)
 __global__ void k_quant_pad_u8(const float* __restrict__ x, int N, int H, int W, int Cin, int pad,
                                int Hp, int Wp, int Cpad, const Int8Scalars* s, float inv_host,
-                               int mode, uint8_t* __restrict__ dst) {
-  const float inv_s = s ? s->inv_s : inv_host;
+                               const float* __restrict__ img_inv, int mode,
+                               uint8_t* __restrict__ dst) {
+  const float inv_all = s ? s->inv_s : inv_host;
   const int cvec = Cin & ~15;
   const long long total = (long long)N * Hp * Wp * Cpad;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
@@ -179,6 +180,7 @@ __global__ void k_quant_pad_u8(const float* __restrict__ x, int N, int H, int W,
     const int ih = hp - pad, iw = wp - pad;
     uint8_t q = 128;
     if (c < Cin && ih >= 0 && ih < H && iw >= 0 && iw < W) {
+      const float inv_s = img_inv ? img_inv[n] : inv_all;
       const float t = __fmul_rn(x[(((long long)n * H + ih) * W + iw) * Cin + c], inv_s);
       int v;
       if (mode == 0) {
@@ -243,8 +245,9 @@ __device__ __forceinline__ uint32_t quant_fast(float xv, float inv_s) {
 template <int MODE>
 __global__ void k_quant_pad_u8_16(const float* __restrict__ x, int H, int W, int Cin, int pad,
                                   int Hp, int Wp, int C16, unsigned total, int vec_in,
-                                  const Int8Scalars* s, float inv_host, uint4* __restrict__ dst) {
-  const float inv_s = s ? s->inv_s : inv_host;
+                                  const Int8Scalars* s, float inv_host,
+                                  const float* __restrict__ img_inv, uint4* __restrict__ dst) {
+  const float inv_all = s ? s->inv_s : inv_host;
   const int cvec = Cin & ~15;
   for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
     const unsigned cg = i % C16, p = i / C16;
@@ -254,6 +257,7 @@ __global__ void k_quant_pad_u8_16(const float* __restrict__ x, int H, int W, int
     uint32_t w[4] = {0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u};
     if (c0 < Cin && ih >= 0 && ih < H && iw >= 0 && iw < W) {
       const float* src = x + (((size_t)n * H + ih) * W + iw) * Cin + c0;
+      const float inv_s = img_inv ? img_inv[n] : inv_all;
       if (vec_in && c0 + 16 <= Cin) {
         // whole group of vector lanes: no per-lane checks
 #pragma unroll
@@ -341,15 +345,14 @@ __global__ void k_weights_s8k(const int8_t* __restrict__ w, int taps, int Cin, i
 }
 
 // k_weights_s8k plus, per output channel (one block each), the column sum Sw[n] of its s8
-// weights; block 0 also clears the per-call scalars that k_absmax accumulates into.
+// weights; block 0 also clears the nclear words that k_absmax accumulates into.
 __global__ void k_int8_wprep(const int8_t* __restrict__ w, int taps, int Cin, int Cout, int Cpad,
-                             int8_t* __restrict__ dst, int* __restrict__ Sw, Int8Scalars* s) {
+                             int8_t* __restrict__ dst, int* __restrict__ Sw,
+                             unsigned* __restrict__ clear, int nclear) {
   __shared__ int red[32];
   const int n = blockIdx.x;
-  if (n == 0 && threadIdx.x == 0 && s) {
-    s->maxa_bits = 0u;
-    s->done = 0u;
-  }
+  if (n == 0)
+    for (int i = threadIdx.x; i < nclear; i += blockDim.x) clear[i] = 0u;
   const int K4 = taps * Cpad / 4;
   uint32_t* row = reinterpret_cast<uint32_t*>(dst + (size_t)n * taps * Cpad);
   int sum = 0;
@@ -392,6 +395,11 @@ struct Int8ConvArgs {
   const float* f1 = nullptr;  // beta | bias
   const int* i0 = nullptr;    // Sw (Winograd epilogue)
   const int* zero_flag = nullptr;
+  // one activation scale per image (batch-1 semantics): 127/max and max/127 of image n,
+  // its all-zero flag; f0 / f1 / i0 are then weight scale / bias / Sw
+  const float* img_inv = nullptr;
+  const float* img_sa = nullptr;
+  const int* img_zero = nullptr;
 };
 
 // K-major weight layout a convolution's GEMM uses: implicit route (stride 1, Cin >= 32):
@@ -432,6 +440,8 @@ static bool int8_conv_gemm(Call& c, const Int8ConvArgs& a, int N, int H, int W, 
   ep.i0 = a.i0;
   ep.act = act;
   ep.zero_flag = a.zero_flag;
+  ep.img_sa = a.img_sa;
+  ep.img_zero = a.img_zero;
   uint8_t* xq_dense = nullptr;  // unpadded u8 input for the gather path
   const Int8BLayout lay = int8_b_layout(Cin, KH, KW, stride);
   if (lay.implicit) {
@@ -448,14 +458,14 @@ static bool int8_conv_gemm(Call& c, const Int8ConvArgs& a, int N, int H, int W, 
       if (a.qmode == 0)
         k_quant_pad_u8_16<0><<<grid_n(c, g16), 256, 0, c.stream()>>>(
             a.xf, H, W, Cin, pad, Hp, Wp, Cpad / 16, (unsigned)g16, vec_in, a.s, a.inv_host,
-            (uint4*)A);
+            a.img_inv, (uint4*)A);
       else
         k_quant_pad_u8_16<1><<<grid_n(c, g16), 256, 0, c.stream()>>>(
             a.xf, H, W, Cin, pad, Hp, Wp, Cpad / 16, (unsigned)g16, vec_in, a.s, a.inv_host,
-            (uint4*)A);
+            a.img_inv, (uint4*)A);
     } else if (a.xf)
       k_quant_pad_u8<<<grid_n(c, rows * Cpad), 256, 0, c.stream()>>>(
-          a.xf, N, H, W, Cin, pad, Hp, Wp, Cpad, a.s, a.inv_host, a.qmode, A);
+          a.xf, N, H, W, Cin, pad, Hp, Wp, Cpad, a.s, a.inv_host, a.img_inv, a.qmode, A);
     else
       k_pad_u8<<<grid_n(c, rows * Cpad), 256, 0, c.stream()>>>(a.xq, N, H, W, Cin, pad, Hp, Wp,
                                                                Cpad, A);
@@ -482,7 +492,7 @@ static bool int8_conv_gemm(Call& c, const Int8ConvArgs& a, int N, int H, int W, 
     xq_dense = (uint8_t*)c.scratch((size_t)N * H * W * Cin);
     if (!xq_dense) return false;
     k_quant_pad_u8<<<grid_n(c, (long long)N * H * W * Cin), 256, 0, c.stream()>>>(
-        a.xf, N, H, W, Cin, 0, H, W, Cin, a.s, a.inv_host, a.qmode, xq_dense);
+        a.xf, N, H, W, Cin, 0, H, W, Cin, a.s, a.inv_host, a.img_inv, a.qmode, xq_dense);
     src = xq_dense;
   }
   const long long M = (long long)N * OH * OW;
@@ -496,6 +506,7 @@ static bool int8_conv_gemm(Call& c, const Int8ConvArgs& a, int N, int H, int W, 
     k_weights_s8k<<<grid_n(c, (long long)Cout * Kpad / 4), 256, 0, c.stream()>>>(wq, 1, K, Cout,
                                                                                 Kpad, B);
   if (!c.launched("int8 im2col prep")) return false;
+  ep.img_rows = OH * OW;  // GEMM rows per image (per-image scales; no remap on this route)
   Operand Ao, Bo;
   Ao.p = A;
   Ao.ld = Kpad;
@@ -520,7 +531,8 @@ bool conv2d_int8_dev(Call& c, const float* x, int N, int H, int W, int Cin, cons
   int* Sw = (int*)c.scratch((size_t)Cout * 4);
   int8_t* wk = (int8_t*)c.scratch((size_t)Cout * lay.taps * lay.cpad);
   if (!s || !f0 || !f1 || !Sw || !wk) return false;
-  k_int8_wprep<<<Cout, 128, 0, c.stream()>>>(wq, lay.taps, lay.cin, Cout, lay.cpad, wk, Sw, s);
+  k_int8_wprep<<<Cout, 128, 0, c.stream()>>>(wq, lay.taps, lay.cin, Cout, lay.cpad, wk, Sw,
+                                              &s->maxa_bits, 2);
   const bool wino = is_wino_route(H, W, Cin, KH, KW, Cout, stride, pad);
   // Winograd: f0 = wso, f1 = bias (or NULL); others: f0 = alpha, f1 = beta
   const Int8ColArgs ca{wscale, bias, Sw, Cout, wino ? 1 : 0, f0, f1};
@@ -543,6 +555,104 @@ bool conv2d_int8_dev(Call& c, const float* x, int N, int H, int W, int Cin, cons
     a.f0 = f0;
     a.f1 = f1;
   }
+  return int8_conv_gemm(c, a, N, H, W, Cin, wq, KH, KW, Cout, stride, pad, out, act, wk);
+}
+
+// Per-image max|x| for an int8 convolution over a batch with batch-1 semantics (the reference
+// quantises per call, conv_int8.cpp:75-81, and its model harness calls per image): grid
+// (blocks, images); the last block of image n derives inv[n] = 127/max, sa[n] = max/127 and
+// zero[n].  maxa[] and done[] are cleared by k_int8_wprep.
+__global__ void k_absmax_img(const float* __restrict__ x, long long per_img, unsigned* maxa,
+                             unsigned* done, float* inv, float* sa, int* zero) {
+  __shared__ float sh[32];
+  __shared__ int last;
+  const int n = blockIdx.y;
+  const float* xi = x + (size_t)n * per_img;
+  float m = 0.0f;
+  long long i0 = 0;
+  if ((reinterpret_cast<uintptr_t>(xi) & 15) == 0) {
+    const long long n4 = per_img >> 2;
+    const float4* x4 = reinterpret_cast<const float4*>(xi);
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4;
+         i += (long long)gridDim.x * blockDim.x) {
+      const float4 q = __ldg(x4 + i);
+      const float a = fabsf(q.x), b = fabsf(q.y), cc = fabsf(q.z), d = fabsf(q.w);
+      m = (m < a) ? a : m;
+      m = (m < b) ? b : m;
+      m = (m < cc) ? cc : m;
+      m = (m < d) ? d : m;
+    }
+    i0 = n4 << 2;
+  }
+  for (long long i = i0 + blockIdx.x * (long long)blockDim.x + threadIdx.x; i < per_img;
+       i += (long long)gridDim.x * blockDim.x) {
+    const float v = fabsf(xi[i]);
+    m = (m < v) ? v : m;
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    const float u = __shfl_xor_sync(0xffffffffu, m, o);
+    m = (m < u) ? u : m;
+  }
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    m = threadIdx.x < (blockDim.x >> 5) ? sh[threadIdx.x] : 0.0f;
+    for (int o = 16; o > 0; o >>= 1) {
+      const float u = __shfl_xor_sync(0xffffffffu, m, o);
+      m = (m < u) ? u : m;
+    }
+    if (threadIdx.x == 0) {
+      atomicMax(&maxa[n], __float_as_uint(m));
+      __threadfence();
+      last = (atomicAdd(&done[n], 1u) == gridDim.x - 1) ? 1 : 0;
+    }
+  }
+  __syncthreads();
+  if (!last || threadIdx.x != 0) return;
+  __threadfence();
+  const float mx = __uint_as_float(atomicOr(&maxa[n], 0u));
+  zero[n] = mx < 1e-12f ? 1 : 0;
+  inv[n] = __fdiv_rn(127.0f, mx);
+  sa[n] = __fdiv_rn(mx, 127.0f);
+}
+
+bool conv2d_int8_batch_dev(Call& c, const float* x, int N, int H, int W, int Cin,
+                           const int8_t* wq, const float* wscale, const float* bias, int KH,
+                           int KW, int Cout, int stride, int pad, float* out, int act) {
+  const int OH = (H + 2 * pad - KH) / stride + 1, OW = (W + 2 * pad - KW) / stride + 1;
+  if (OH <= 0 || OW <= 0 || N <= 0) return true;
+  if (N > 65535) {
+    set_error(kInvalid, "%s: at most 65535 images per int8 batch call", c.name());
+    c.fail();
+    return false;
+  }
+  const Int8BLayout lay = int8_b_layout(Cin, KH, KW, stride);
+  unsigned* words = (unsigned*)c.scratch((size_t)N * 2 * 4);  // maxa[N], done[N]
+  float* inv = (float*)c.scratch((size_t)N * 4);
+  float* sa = (float*)c.scratch((size_t)N * 4);
+  int* zero = (int*)c.scratch((size_t)N * 4);
+  int* Sw = (int*)c.scratch((size_t)Cout * 4);
+  int8_t* wk = (int8_t*)c.scratch((size_t)Cout * lay.taps * lay.cpad);
+  if (!words || !inv || !sa || !zero || !Sw || !wk) return false;
+  k_int8_wprep<<<Cout, 128, 0, c.stream()>>>(wq, lay.taps, lay.cin, Cout, lay.cpad, wk, Sw, words,
+                                              2 * N);
+  const long long per = (long long)H * W * Cin;
+  long long bx = per / (4 * 256 * 4);
+  bx = bx < 1 ? 1 : (bx > 64 ? 64 : bx);
+  k_absmax_img<<<dim3((unsigned)bx, (unsigned)N), 256, 0, c.stream()>>>(x, per, words, words + N,
+                                                                        inv, sa, zero);
+  if (!c.launched("int8 per-image params")) return false;
+  const bool wino = is_wino_route(H, W, Cin, KH, KW, Cout, stride, pad);
+  Int8ConvArgs a;
+  a.xf = x;
+  a.img_inv = inv;
+  a.img_sa = sa;
+  a.img_zero = zero;
+  a.qmode = wino ? 1 : 0;
+  a.epi = wino ? Epi::I8_WINO : Epi::F32_AB;
+  a.f0 = wscale;
+  a.f1 = bias;
+  a.i0 = Sw;
   return int8_conv_gemm(c, a, N, H, W, Cin, wq, KH, KW, Cout, stride, pad, out, act, wk);
 }
 

@@ -39,6 +39,13 @@ struct EpiParams {
   int img_rows, Wp, OH, OW;
   // when non-NULL and *zero_flag != 0 every stored value is 0 (int8 router: max|x| < 1e-12)
   const int* zero_flag;
+  // int8 convolution over a batch with one activation scale per image (batch-1 semantics):
+  // image n = r / img_rows (remap or not); F32_AB and I8_WINO then take f0 = per-column
+  // weight scale, f1 = bias (or NULL), i0 = column sums, and derive alpha / beta / wso from
+  // img_sa[n] in the same expressions the single-call router precomputes; img_zero[n]
+  // replaces zero_flag.
+  const float* img_sa;
+  const int* img_zero;
 };
 
 // Implicit convolution (stride 1) over a padded NHWC tensor viewed as A[rows][Cpad]:
@@ -131,7 +138,8 @@ __device__ __forceinline__ void epi_stage_cols(const EpiParams& ep, int col, int
     s.c[lane] = (in && ep.i0) ? ep.i0[col] : 0;
   } else if constexpr (EPI == Epi::F32_AB) {
     s.a[lane] = in ? ep.f0[col] : 0.0f;
-    s.b[lane] = in ? ep.f1[col] : 0.0f;
+    s.b[lane] = (in && ep.f1) ? ep.f1[col] : 0.0f;
+    s.c[lane] = (in && ep.i0) ? ep.i0[col] : 0;
   } else if constexpr (EPI == Epi::F32_BIAS) {
     s.a[lane] = (in && ep.f0) ? ep.f0[col] : 0.0f;
   } else if constexpr (EPI == Epi::I8_WINO) {
@@ -156,7 +164,7 @@ __device__ __forceinline__ void lds32(const T* p, T (&o)[32]) {
 template <Epi EPI>
 __device__ __forceinline__ void epi_store32(const EpiParams& ep, long long orow, int j0, int N,
                                             const uint32_t (&r)[32], const ColSlice& P,
-                                            bool zero) {
+                                            bool zero, float img_sa) {
   // 32 outputs for columns j0..j0+31 of output row `orow`
   const bool full = (j0 + 32 <= N);
   if constexpr (EPI == Epi::S32) {
@@ -203,12 +211,28 @@ __device__ __forceinline__ void epi_store32(const EpiParams& ep, long long orow,
     if constexpr (EPI == Epi::F32_AB) {
       lds32(P.a, p0);
       lds32(P.b, p1);
+      if (ep.img_sa) {
+        // alpha = sa*ws, beta = bias - (alpha*128)*Sw: k_int8_colparams's expressions
+        lds32(P.c, pi);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float a = __fmul_rn(img_sa, p0[i]);
+          p1[i] = __fsub_rn(p1[i], __fmul_rn(__fmul_rn(a, 128.0f), (float)pi[i]));
+          p0[i] = a;
+        }
+      }
     } else if constexpr (EPI == Epi::F32_BIAS) {
       lds32(P.a, p0);
     } else {  // I8_WINO
       lds32(P.a, p0);
       lds32(P.b, p1);
       lds32(P.c, pi);
+      if (ep.img_sa) {
+        // wso = (sa*0.25)*ws (winograd_int8.cpp:155)
+        const float q = __fmul_rn(img_sa, 0.25f);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) p0[i] = __fmul_rn(q, p0[i]);
+      }
     }
     float v[32];
 #pragma unroll
@@ -456,9 +480,15 @@ __global__ void __launch_bounds__(320, 1)
       dev::tc_fence_after();
       if (!ok || *abort_flag) break;
       const int r = m0 + q * 32 + lane;
-      const bool zero_out = ep.zero_flag && *ep.zero_flag;
+      bool zero_out = ep.zero_flag && *ep.zero_flag;
+      float img_sa = 0.0f;
       long long orow = r;
       bool store = r < M;
+      if (ep.img_sa && store) {
+        const int n = r / ep.img_rows;
+        img_sa = ep.img_sa[n];
+        zero_out = ep.img_zero[n] != 0;
+      }
       if (ep.remap && store) {
         const int n = r / ep.img_rows, qq = r - n * ep.img_rows;
         const int oh = qq / ep.Wp, ow = qq - oh * ep.Wp;
@@ -472,7 +502,7 @@ __global__ void __launch_bounds__(320, 1)
         uint32_t v[32];
         dev::tmem_ld32(tmem + buf * BN + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
         dev::tmem_ld_wait();
-        if (store) epi_store32<EPI>(ep, orow, n0 + c0, N, v, my[k], zero_out);
+        if (store) epi_store32<EPI>(ep, orow, n0 + c0, N, v, my[k], zero_out, img_sa);
       }
       dev::tc_fence_before();
       __syncwarp();

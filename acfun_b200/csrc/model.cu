@@ -38,6 +38,8 @@ struct MLayer {
   float* b = nullptr;
   int act = 0;
   int post_relu = 0;
+  int8_t* wq = nullptr;  // int8 mode: per-column quantised conv weights (device)
+  float* wqs = nullptr;  // and their scales
 };
 
 }  // namespace acf
@@ -53,6 +55,8 @@ struct AcfunModel {
   float* buf[2] = {nullptr, nullptr};
   size_t bufcap = 0;         // floats per buffer
   std::mutex mu;
+  bool int8 = false;         // dense convs through the int8 router, one scale per image
+  void* dq = nullptr;        // device allocation of all layers' wq / wqs
 };
 
 namespace acf {
@@ -346,6 +350,17 @@ static bool run_model(Call& c, AcfunModel* m, int n, const float* x, float* y) {
       case 7: {
         const int KH = L.p[0], KW = L.p[1], Cout = L.p[2], st = L.p[3], pd = L.p[4];
         const int groups = L.type == 7 ? L.p[5] : 1;
+        if (m->int8 && L.wq) {
+          // int8 mode: acfun_conv2d_int8 per image (the reference's int8 model harness)
+          ok = conv2d_int8_batch_dev(c, cur, n, H, W, C, L.wq, L.wqs, L.b, KH, KW, Cout, st, pd,
+                                     next, act);
+          H = (H + 2 * pd - KH) / st + 1;
+          W = (W + 2 * pd - KW) / st + 1;
+          C = Cout;
+          cur = next;
+          which ^= 1;
+          break;
+        }
         // Conv -> MaxPool: the pooled output straight from the conv when the pair fuses
         bool fused = false;
         if (groups == 1 && li + 1 < nl && m->layers[li + 1].type == 4) {
@@ -466,6 +481,7 @@ extern "C" void acfun_model_destroy(AcfunModel* m) {
   cudaSetDevice(m->device);
   cudaDeviceSynchronize();
   cudaFree(m->dparams);
+  cudaFree(m->dq);
   cudaFree(m->buf[0]);
   cudaFree(m->buf[1]);
   delete m;
@@ -495,6 +511,65 @@ extern "C" int acfun_model_infer_batch(AcfunModel* m, int n, const float* input,
     return 0;
   }
   return c.finish() ? m->outSize : 0;
+}
+
+// Extension (no counterpart in the reference, whose int8 path has no model format): run every
+// dense convolution of the model through the int8 router with one activation scale per image
+// -- what the reference's per-image harness does with acfun_quantize_weights +
+// acfun_conv2d_int8 -- while FC, pooling, BN and softmax stay fp32.  Weights are quantised
+// here, on the host, from the folded fp32 weights.
+extern "C" int acfun_model_set_int8(AcfunModel* m, int enable) {
+  if (!m) {
+    set_error(kInvalid, "acfun_model_set_int8: NULL model");
+    return kInvalid;
+  }
+  std::lock_guard<std::mutex> g(m->mu);
+  if (!enable) {
+    m->int8 = false;
+    return 0;
+  }
+  if (m->dq) {
+    m->int8 = true;
+    return 0;
+  }
+  // sizes: per dense conv K*Cout bytes of wq + Cout floats of scales (16-byte aligned slots)
+  size_t total = 0;
+  for (auto& L : m->layers) {
+    if (L.type != 1) continue;
+    const size_t cout = (size_t)L.p[2];
+    total += align_up(L.wn, 16) + align_up(cout * 4, 16);
+  }
+  std::vector<unsigned char> host(total);
+  size_t off = 0;
+  std::vector<size_t> offs;
+  for (auto& L : m->layers) {
+    if (L.type != 1) continue;
+    const int cout = L.p[2];
+    const int K = (int)(L.wn / (size_t)cout);
+    int8_t* q = reinterpret_cast<int8_t*>(host.data() + off);
+    float* sc = reinterpret_cast<float*>(host.data() + off + align_up(L.wn, 16));
+    acfun_quantize_weights(L.w_host, K, cout, sc, q);
+    offs.push_back(off);
+    off += align_up(L.wn, 16) + align_up((size_t)cout * 4, 16);
+  }
+  tctx().device = m->device;
+  if (!ACF_CUDA_OK(cudaSetDevice(m->device))) return kCuda;
+  void* d = nullptr;
+  if (total && (!ACF_CUDA_OK(cudaMalloc(&d, total)) ||
+                !ACF_CUDA_OK(cudaMemcpy(d, host.data(), total, cudaMemcpyHostToDevice)))) {
+    cudaFree(d);
+    return kCuda;
+  }
+  size_t k = 0;
+  for (auto& L : m->layers) {
+    if (L.type != 1) continue;
+    unsigned char* base = static_cast<unsigned char*>(d) + offs[k++];
+    L.wq = reinterpret_cast<int8_t*>(base);
+    L.wqs = reinterpret_cast<float*>(base + align_up(L.wn, 16));
+  }
+  m->dq = d;
+  m->int8 = true;
+  return 0;
 }
 
 extern "C" int acfun_model_infer(AcfunModel* m, const float* input, float* output) {

@@ -113,6 +113,14 @@ void acfun_model_input_dims(AcfunModel* m, int* Cin, int* Hin, int* Win); /* acf
  * element count, 0 on error. */
 int acfun_model_infer_batch(AcfunModel* m, int n, const float* input, float* output);
 
+/* int8 mode for a loaded model (no counterpart in the reference, whose int8 path has no
+ * model format): enable != 0 runs every dense convolution through the int8 router
+ * (acfun_quantize_weights of the folded weights + acfun_conv2d_int8) with one activation
+ * scale per image -- the result of the reference harness that calls acfun_conv2d_int8 per
+ * image -- while FC, pooling, BN and softmax stay fp32; 0 switches back to fp32.  Returns
+ * 0 or an error code. */
+int acfun_model_set_int8(AcfunModel* m, int enable);
+
 /* s8 x s8 GEMM with int32 accumulation and a fused requantising epilogue:
  *   C[i,j] = sat_s8(rne(relu?((float)(acc[i,j] + bias[j]) * scale[j])))
  * bias may be NULL.  This is the int8 GEMM the BASELINE int8 config names; the reference

@@ -120,13 +120,27 @@ class OracleModel:
                 out.append(dict(L))
         return out
 
-    def infer(self, x: np.ndarray) -> np.ndarray:
+    def infer(self, x: np.ndarray, int8: bool = False) -> np.ndarray:
+        """One image.  int8=True runs every dense conv as the reference's int8 harness does:
+        acfun_quantize_weights of the folded weights, then acfun_conv2d_int8 on this image
+        (conv_int8.cpp:24-37, :63-148); everything else stays fp32."""
         O = P.oracle()
         H, W, C = self.inH, self.inW, self.inC
         cur = np.ascontiguousarray(x, np.float32).reshape(-1).copy()
         for L in self.layers:
             t = L["type"]
-            if t in (1, 7):
+            if t == 1 and int8:
+                KH, KW, Cout, st, pd = L["KH"], L["KW"], L["Cout"], L["st"], L["pd"]
+                if "wq" not in L:
+                    K = KH * KW * C
+                    L["ws"] = np.empty(Cout, np.float32)
+                    L["wq"] = np.empty((K, Cout), np.int8)
+                    O.orc_quantize_weights(np.ascontiguousarray(L["w"], np.float32), K, Cout, L["ws"], L["wq"])
+                out = P.orc_conv2d_int8(cur, L["wq"], L["ws"], L["b"], 1, H, W, C, KH, KW, Cout, st, pd,
+                                        L["act"])
+                OH, OW = P.conv_out_hw(H, W, KH, KW, st, pd)
+                cur, H, W, C = out.reshape(-1), OH, OW, Cout
+            elif t in (1, 7):
                 KH, KW, Cout, st, pd = L["KH"], L["KW"], L["Cout"], L["st"], L["pd"]
                 groups = L.get("groups", 1) if t == 7 else 1
                 OH, OW = P.conv_out_hw(H, W, KH, KW, st, pd)

@@ -5,7 +5,7 @@ import os
 import numpy as np
 import pytest
 
-from helpers import TOL_F32, max_rel
+from helpers import TOL_F32, assert_bits_equal, max_rel
 
 pytestmark = pytest.mark.gpu
 GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
@@ -95,4 +95,31 @@ def test_model_conv_pool_fusion_vs_oracle(acf, tmp_path):
     om = OracleModel(blob)
     for k in range(5):
         assert max_rel(y[k], om.infer(x[k])) < TOL_F32
+    m.close()
+
+
+@pytest.mark.parametrize("width_div", [8, 4])
+def test_model_int8_mode_vs_oracle(acf, tmp_path, width_div):
+    """acfun_model_set_int8: every dense conv through the int8 router with one activation scale
+    per image (conv1: u8 im2col route, the rest: int8 Winograd route), FC / pool / softmax fp32.
+    Against the oracle's per-image composition (quantize_weights + conv2d_int8 per layer), and
+    a batch must give each image exactly what a single-image call gives."""
+    from acfun_b200 import acfun0
+    from oracle.model_oracle import OracleModel
+    blob = acfun0.vgg11(seed=3, in_hw=64, width_div=width_div, fc_dims=(128, 64, 10)).tobytes()
+    p = tmp_path / "v8.acfun"
+    p.write_bytes(blob)
+    m = acf.Model(str(p))
+    m.set_int8(True)
+    g = np.random.default_rng(41)
+    x = g.uniform(0, 1, (3, 64, 64, 3)).astype(np.float32)
+    x[1] *= 7.0                     # images with different activation ranges
+    x[2] -= 0.5
+    y = m.infer_batch(x)
+    om = OracleModel(blob)
+    for k in range(3):
+        assert max_rel(y[k], om.infer(x[k], int8=True)) < TOL_F32
+        assert_bits_equal(m.infer_batch(np.ascontiguousarray(x[k:k + 1]))[0], y[k], f"image {k} alone")
+    m.set_int8(False)
+    assert max_rel(m.infer_batch(x)[0], om.infer(x[0])) < TOL_F32
     m.close()
