@@ -395,6 +395,38 @@ def measure_configs(acf, torch, stream, flush, steps, with_cpu=True, cfg_filter=
                                                       "kind": "reference",
                                                       "sample": "2 sequential acfun_model_infer calls (batch-1 API)"}
         m.close()
+
+    if want("cfg5_vgg11_int8_b256"):
+        # the survey's cfg5 int8 variant: every dense conv via quantize_weights + conv2d_int8 per
+        # image (one activation scale per image), FC / pool / softmax fp32
+        import tempfile
+
+        from acfun_b200 import acfun0
+        from oracle.model_oracle import OracleModel
+        path = os.path.join(tempfile.gettempdir(), "acfun_vgg11_seed5.acfun")
+        if not os.path.exists(path):
+            acfun0.vgg11(seed=5).save(path)
+        m = acf.Model(path)
+        m.set_int8(True)
+        n = vgg_images
+        x = g.uniform(0, 1, (n, 224, 224, 3)).astype(np.float32)
+        dx, dy = dev(x), torch.empty((n, 1000), device="cuda")
+        t = timeit(lambda: L.acfun_model_infer_batch(m.h, n, dx.data_ptr(), dy.data_ptr()), max(2, steps // 4))
+        cv = None
+        if R is not None:
+            om = OracleModel(open(path, "rb").read())
+            x0 = np.ascontiguousarray(x[0])
+            cv = cpu(lambda: [om.ref_infer(R, x0, int8=True) for _ in range(2)], 2, 1.0)
+        gf = 15.218e9
+        record("cfg5_vgg11_int8_b256", t, n * gf, 1e12, "int8", None, "",
+               {"img_per_s": round(n / t, 1), "gop_per_img": 15.218, "images": n,
+                "note": "conv ops on the int8 tensor pipe, FC (0.25 GFLOP/img) in 3xBF16"})
+        if cv is not None:
+            out["cfg5_vgg11_int8_b256"]["cpu_baseline"] = {
+                "value": round(cv, 3), "unit": "img/s", "cores": cores, "kind": "reference",
+                "sample": "2 images through the reference's int8 layer API (quantize_weights + conv2d_int8 "
+                          "per conv, fc / maxpool / softmax), the composition its int8 path needs"}
+        m.close()
     return out
 
 

@@ -169,3 +169,54 @@ class OracleModel:
                 O.orc_batchnorm(cur, cur.size, ch, mean, var, gamma.ctypes.data, beta.ctypes.data,
                                 np.float32(1e-5))
         return cur
+
+    def ref_infer(self, R, x: np.ndarray, int8: bool = False) -> np.ndarray:
+        """One image through the reference library itself (R = pyoracle.ref()), layer by layer
+        over this fused list: the harness composition the reference needs for an int8 model
+        (it has no int8 model format), or its fp32 layer API.  CPU-baseline timing only."""
+        H, W, C = self.inH, self.inW, self.inC
+        cur = np.ascontiguousarray(x, np.float32).reshape(-1).copy()
+        for L in self.layers:
+            t = L["type"]
+            if t in (1, 7):
+                KH, KW, Cout, st, pd = L["KH"], L["KW"], L["Cout"], L["st"], L["pd"]
+                OH, OW = P.conv_out_hw(H, W, KH, KW, st, pd)
+                out = np.empty(OH * OW * Cout, np.float32)
+                b = L["b"].ctypes.data
+                if t == 1 and int8:
+                    if "ref_wq" not in L:
+                        K = KH * KW * C
+                        L["ref_ws"] = np.empty(Cout, np.float32)
+                        L["ref_wq"] = np.empty((K, Cout), np.int8)
+                        R.acfun_quantize_weights(np.ascontiguousarray(L["w"], np.float32), K, Cout,
+                                                 L["ref_ws"], L["ref_wq"])
+                    R.acfun_conv2d_int8(cur, 1, H, W, C, L["ref_wq"], L["ref_ws"], b, KH, KW, Cout, st, pd,
+                                        0.0, out, L["act"])
+                else:
+                    groups = L.get("groups", 1) if t == 7 else 1
+                    R.acfun_conv2d_g(cur, 1, H, W, C, np.ascontiguousarray(L["w"], np.float32), b, KH, KW,
+                                     Cout, st, pd, groups, out, L["act"])
+                cur, H, W, C = out, OH, OW, Cout
+            elif t == 2:
+                out = np.empty(L["Cout"], np.float32)
+                fn = R.acfun_fc_relu if L["act"] else R.acfun_fc
+                fn(cur, 1, H * W * C, np.ascontiguousarray(L["w"], np.float32), L["b"].ctypes.data, L["Cout"], out)
+                cur, H, W, C = out, 1, 1, L["Cout"]
+            elif t == 3:
+                R.acfun_relu(cur, cur.size)
+            elif t == 4:
+                OH, OW = P.conv_out_hw(H, W, L["pool"], L["pool"], L["st"], L["pd"])
+                out = np.empty(OH * OW * C, np.float32)
+                fn = R.acfun_maxpool_relu if L["post_relu"] else R.acfun_maxpool
+                fn(cur, 1, H, W, C, L["pool"], L["st"], L["pd"], out)
+                cur, H, W = out, OH, OW
+            elif t == 5:
+                out = np.empty_like(cur)
+                R.acfun_softmax(cur, 1, cur.size, out)
+                cur = out
+            elif t == 6:
+                ch = L["ch"]
+                mean, var, gamma, beta = (np.ascontiguousarray(s) for s in L["stats"])
+                R.acfun_batchnorm(cur, cur.size, ch, mean, var, gamma.ctypes.data, beta.ctypes.data,
+                                  np.float32(1e-5))
+        return cur

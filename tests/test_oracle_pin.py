@@ -220,3 +220,29 @@ def test_oracle_model_vs_reference_vgg_small(orc, tmp_path):
     R.acfun_model_destroy(h)
     y = OracleModel(blob).infer(x)
     assert max_rel(y, o) < TOL_F32
+
+
+@ref_only
+def test_int8_model_composition_oracle_vs_reference(tmp_path):
+    """The int8 VGG composition (quantize_weights + conv2d_int8 per dense conv, per image) in
+    the oracle equals the same composition run on the reference library, bit for bit; the
+    fp32 harness equals the reference's own acfun_model_infer."""
+    from acfun_b200 import acfun0
+    from oracle import pyoracle as P
+    from oracle.model_oracle import OracleModel
+    R = P.ref()
+    blob = acfun0.vgg11(seed=3, in_hw=32, width_div=16, fc_dims=(64, 32, 10)).tobytes()
+    path = tmp_path / "v.acfun"
+    path.write_bytes(blob)
+    om = OracleModel(blob)
+    h = R.acfun_model_load(str(path).encode())
+    try:
+        for seed in (1, 2):
+            x = np.random.default_rng(seed).uniform(-1, 2, (32, 32, 3)).astype(np.float32)
+            o = np.empty(10, np.float32)
+            R.acfun_model_infer(h, x, o)
+            np.testing.assert_array_equal(om.ref_infer(R, x), o)
+            np.testing.assert_array_equal(om.infer(x, int8=True).view(np.int32),
+                                          om.ref_infer(R, x, int8=True).view(np.int32))
+    finally:
+        R.acfun_model_destroy(h)
