@@ -323,6 +323,65 @@ __global__ void k_im2col_u8(const uint8_t* __restrict__ xq, int N, int H, int W,
   }
 }
 
+// k_im2col_u8 with one thread per (output pixel, 16 K bytes): 32-bit index math, the tap /
+// channel position advanced incrementally, one 16-byte store (Kpad is a multiple of 16).
+__global__ void k_im2col_u8_16(const uint8_t* __restrict__ xq, int H, int W, int Cin, int KH,
+                               int KW, int stride, int pad, int OH, int OW, int K16,
+                               unsigned total, uint4* __restrict__ dst) {
+  const int K = KH * KW * Cin;
+  for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const unsigned g = i % K16, m = i / K16;
+    const unsigned ow = m % OW, r = m / OW, oh = r % OH, n = r / OH;
+    int k = (int)g * 16;
+    int tap = k / Cin, c = k - tap * Cin;
+    int kh = tap / KW, kw = tap - kh * KW;
+    const uint8_t* img = xq + (size_t)n * H * W * Cin;
+    uint32_t wv[4] = {0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u};
+#pragma unroll
+    for (int e = 0; e < 16; ++e, ++k) {
+      if (k < K) {
+        const int ih = (int)oh * stride - pad + kh, iw = (int)ow * stride - pad + kw;
+        if (ih >= 0 && ih < H && iw >= 0 && iw < W) {
+          const uint32_t q = img[((size_t)ih * W + iw) * Cin + c];
+          wv[e >> 2] = (wv[e >> 2] & ~(0xFFu << (8 * (e & 3)))) | (q << (8 * (e & 3)));
+        }
+        if (++c == Cin) {
+          c = 0;
+          if (++kw == KW) {
+            kw = 0;
+            ++kh;
+          }
+        }
+      }
+    }
+    dst[i] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+  }
+}
+
+// Dense (unpadded) u8 quantisation of a whole NHWC tensor, 4 elements per thread (float4 in,
+// one 32-bit store): the same rounding as k_quant_pad_u8 (vector lanes = channels below
+// Cin & ~15 in mode 1), one scale per image when img_inv is given.
+template <int MODE>
+__global__ void k_quant_u8_flat4(const float4* __restrict__ x, unsigned n4, int Cin,
+                                 unsigned per_img, const Int8Scalars* s, float inv_host,
+                                 const float* __restrict__ img_inv, uint32_t* __restrict__ dst) {
+  const float inv_all = s ? s->inv_s : inv_host;
+  const int cvec = Cin & ~15;
+  for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += gridDim.x * blockDim.x) {
+    const float4 v = __ldg(x + i);
+    const float xv[4] = {v.x, v.y, v.z, v.w};
+    uint32_t w = 0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const unsigned idx = i * 4 + e;
+      const float inv_s = img_inv ? img_inv[idx / per_img] : inv_all;
+      const int c = (int)(idx % (unsigned)Cin);
+      w |= (uint32_t)quant_one(xv[e], inv_s, MODE, c < cvec) << (8 * e);
+    }
+    dst[i] = w;
+  }
+}
+
 // s8 weights [taps*Cin][Cout] -> K-major [Cout][taps*Cpad] (row n holds output channel n's
 // taps, each tap's Cin weights followed by zeros up to Cpad).  One thread per 4 K bytes.
 __global__ void k_weights_s8k(const int8_t* __restrict__ w, int taps, int Cin, int Cout, int Cpad,
@@ -489,10 +548,21 @@ static bool int8_conv_gemm(Call& c, const Int8ConvArgs& a, int N, int H, int W, 
   // explicit im2col over the quantised input
   const uint8_t* src = a.xq;
   if (a.xf) {
-    xq_dense = (uint8_t*)c.scratch((size_t)N * H * W * Cin);
+    const long long nel = (long long)N * H * W * Cin;
+    xq_dense = (uint8_t*)c.scratch((size_t)nel);
     if (!xq_dense) return false;
-    k_quant_pad_u8<<<grid_n(c, (long long)N * H * W * Cin), 256, 0, c.stream()>>>(
-        a.xf, N, H, W, Cin, 0, H, W, Cin, a.s, a.inv_host, a.img_inv, a.qmode, xq_dense);
+    if (nel % 4 == 0 && nel < (1LL << 32) && aligned16(a.xf)) {
+      const unsigned n4 = (unsigned)(nel / 4), per = (unsigned)((long long)H * W * Cin);
+      if (a.qmode == 0)
+        k_quant_u8_flat4<0><<<grid_n(c, n4), 256, 0, c.stream()>>>(
+            (const float4*)a.xf, n4, Cin, per, a.s, a.inv_host, a.img_inv, (uint32_t*)xq_dense);
+      else
+        k_quant_u8_flat4<1><<<grid_n(c, n4), 256, 0, c.stream()>>>(
+            (const float4*)a.xf, n4, Cin, per, a.s, a.inv_host, a.img_inv, (uint32_t*)xq_dense);
+    } else {
+      k_quant_pad_u8<<<grid_n(c, nel), 256, 0, c.stream()>>>(
+          a.xf, N, H, W, Cin, 0, H, W, Cin, a.s, a.inv_host, a.img_inv, a.qmode, xq_dense);
+    }
     src = xq_dense;
   }
   const long long M = (long long)N * OH * OW;
@@ -500,8 +570,14 @@ static bool int8_conv_gemm(Call& c, const Int8ConvArgs& a, int N, int H, int W, 
   uint8_t* A = (uint8_t*)c.scratch((size_t)M * Kpad);
   int8_t* B = wk ? const_cast<int8_t*>(wk) : (int8_t*)c.scratch((size_t)Cout * Kpad);
   if (!A || !B) return false;
-  k_im2col_u8<<<grid_n(c, M * Kpad), 256, 0, c.stream()>>>(src, N, H, W, Cin, KH, KW, stride, pad,
-                                                           OH, OW, Kpad, A);
+  if (M * (Kpad / 16) < (1LL << 31) && (long long)H * W * Cin < (1LL << 31)) {
+    const unsigned tot16 = (unsigned)(M * (Kpad / 16));
+    k_im2col_u8_16<<<grid_n(c, tot16), 256, 0, c.stream()>>>(src, H, W, Cin, KH, KW, stride, pad,
+                                                              OH, OW, Kpad / 16, tot16, (uint4*)A);
+  } else {
+    k_im2col_u8<<<grid_n(c, M * Kpad), 256, 0, c.stream()>>>(src, N, H, W, Cin, KH, KW, stride,
+                                                             pad, OH, OW, Kpad, A);
+  }
   if (!wk)
     k_weights_s8k<<<grid_n(c, (long long)Cout * Kpad / 4), 256, 0, c.stream()>>>(wq, 1, K, Cout,
                                                                                 Kpad, B);
