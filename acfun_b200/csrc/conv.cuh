@@ -42,6 +42,14 @@ bool conv2d_int8_batch_dev(Call& c, const float* x, int N, int H, int W, int Cin
                            const int8_t* wq, const float* wscale, const float* bias, int KH,
                            int KW, int Cout, int stride, int pad, float* out, int act);
 
+// conv2d_int8_batch_dev immediately followed by max-pool(2, 2, 0, post_relu), fused for small-K
+// non-Winograd routes (sets *handled; otherwise nothing is launched).  Bit-identical to the two
+// layers run in turn.
+bool conv_int8_pool_dev(Call& c, const float* x, int N, int H, int W, int Cin, const int8_t* wq,
+                        const float* wscale, const float* bias, int KH, int KW, int Cout,
+                        int stride, int pad, int act, int pool, int pst, int ppd, int post_relu,
+                        float* out, bool* handled);
+
 // int8 conv router (conv_int8.cpp:63-148) on device pointers.
 bool conv2d_int8_dev(Call& c, const float* x, int N, int H, int W, int Cin, const int8_t* wq,
                      const float* wscale, const float* bias, int KH, int KW, int Cout, int stride,

@@ -639,7 +639,9 @@ bool conv2d_int8_dev(Call& c, const float* x, int N, int H, int W, int Cin, cons
 // (blocks, images); the last block of image n derives inv[n] = 127/max, sa[n] = max/127 and
 // zero[n].  maxa[] and done[] are cleared by k_int8_wprep.
 __global__ void k_absmax_img(const float* __restrict__ x, long long per_img, unsigned* maxa,
-                             unsigned* done, float* inv, float* sa, int* zero) {
+                             unsigned* done, float* inv, float* sa, int* zero,
+                             const float* __restrict__ wscale, const float* __restrict__ bias,
+                             const int* __restrict__ Sw, int Cout, float* __restrict__ ab) {
   __shared__ float sh[32];
   __shared__ int last;
   const int n = blockIdx.y;
@@ -684,12 +686,24 @@ __global__ void k_absmax_img(const float* __restrict__ x, long long per_img, uns
     }
   }
   __syncthreads();
-  if (!last || threadIdx.x != 0) return;
+  if (!last) return;
   __threadfence();
   const float mx = __uint_as_float(atomicOr(&maxa[n], 0u));
-  zero[n] = mx < 1e-12f ? 1 : 0;
-  inv[n] = __fdiv_rn(127.0f, mx);
-  sa[n] = __fdiv_rn(mx, 127.0f);
+  const float s_a = __fdiv_rn(mx, 127.0f);
+  if (threadIdx.x == 0) {
+    zero[n] = mx < 1e-12f ? 1 : 0;
+    inv[n] = __fdiv_rn(127.0f, mx);
+    sa[n] = s_a;
+  }
+  // optional per-image alpha / beta table ab[n][0..Cout) / [Cout..2Cout): the expressions of
+  // k_int8_colparams (alpha = sa*ws, beta = bias - (alpha*128)*Sw)
+  if (ab)
+    for (int j = threadIdx.x; j < Cout; j += blockDim.x) {
+      const float a = __fmul_rn(s_a, wscale[j]);
+      ab[(size_t)n * 2 * Cout + j] = a;
+      ab[(size_t)n * 2 * Cout + Cout + j] =
+          __fsub_rn(bias ? bias[j] : 0.0f, __fmul_rn(__fmul_rn(a, 128.0f), (float)Sw[j]));
+    }
 }
 
 bool conv2d_int8_batch_dev(Call& c, const float* x, int N, int H, int W, int Cin,
@@ -715,8 +729,8 @@ bool conv2d_int8_batch_dev(Call& c, const float* x, int N, int H, int W, int Cin
   const long long per = (long long)H * W * Cin;
   long long bx = per / (4 * 256 * 4);
   bx = bx < 1 ? 1 : (bx > 64 ? 64 : bx);
-  k_absmax_img<<<dim3((unsigned)bx, (unsigned)N), 256, 0, c.stream()>>>(x, per, words, words + N,
-                                                                        inv, sa, zero);
+  k_absmax_img<<<dim3((unsigned)bx, (unsigned)N), 256, 0, c.stream()>>>(
+      x, per, words, words + N, inv, sa, zero, nullptr, nullptr, nullptr, 0, nullptr);
   if (!c.launched("int8 per-image params")) return false;
   const bool wino = is_wino_route(H, W, Cin, KH, KW, Cout, stride, pad);
   Int8ConvArgs a;
@@ -730,6 +744,234 @@ bool conv2d_int8_batch_dev(Call& c, const float* x, int N, int H, int W, int Cin
   a.f1 = bias;
   a.i0 = Sw;
   return int8_conv_gemm(c, a, N, H, W, Cin, wq, KH, KW, Cout, stride, pad, out, act, wk);
+}
+
+// s8 weights [taps*Cin][Cout] -> 4-byte words wpk[tap][cw][Cout] (channels 4cw..4cw+3 of a
+// tap, zero past Cin) for k_conv_int8_pool, and the column sums Sw (one block per output
+// channel); block 0 also clears the nclear words k_absmax_img accumulates into.
+__global__ void k_int8_pool_wpack(const int8_t* __restrict__ wq, int taps, int Cin, int CW,
+                                  int Cout, uint32_t* __restrict__ wpk, int* __restrict__ Sw,
+                                  unsigned* __restrict__ clear, int nclear) {
+  __shared__ int red[32];
+  const int j = blockIdx.x;
+  if (j == 0)
+    for (int i = threadIdx.x; i < nclear; i += blockDim.x) clear[i] = 0u;
+  int sum = 0;
+  for (int r = threadIdx.x; r < taps * CW; r += blockDim.x) {
+    const int tap = r / CW, cw = r - tap * CW;
+    uint32_t wv = 0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int c = cw * 4 + e;
+      if (c < Cin) {
+        const int8_t v = wq[(size_t)(tap * Cin + c) * Cout + j];
+        sum += v;
+        wv |= (uint32_t)(uint8_t)v << (8 * e);
+      }
+    }
+    wpk[(size_t)r * Cout + j] = wv;
+  }
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sum;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int t = 0;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t += red[i];
+    Sw[j] = t;
+  }
+}
+
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+// Small-K int8 convolution (non-Winograd route) fused with the 2x2 / stride-2 / pad-0 max-pool
+// that follows it, for the per-image int8 model path.  A block owns one pooled row of one image:
+// it quantises the input rows that row needs straight from fp32 (RNE, the image's inv_s, zero
+// point 128 -- also outside the image, as the reference's u8 im2col pads) into a padded tile of
+// 4-byte pixel words (channels c..c+3 of a pixel, CW words per pixel) and stages the s8 weights
+// packed in matching words [tap][cw][Cout] (k_int8_pool_wpack) and this image's alpha / beta
+// (k_absmax_img).  One thread per
+// (16-channel block, pooled pixel) then accumulates the exact integer correlation of its four
+// conv pixels with dp4a, dequantises as the F32_AB epilogue does ((float)acc*alpha then +
+// beta), applies act and the pool (start -1e30, window
+// order (0,0) (0,1) (1,0) (1,1)), then the pool's post-ReLU.  Integer sums do not depend on the
+// order, so the output equals the unfused im2col GEMM + max-pool bit for bit.
+template <int CW>
+__global__ void __launch_bounds__(128) k_conv_int8_pool(
+    const float* __restrict__ x, int H, int W, int Cin, const uint32_t* __restrict__ wpk,
+    const float* __restrict__ ab, int Cout, int KH, int KW, int stride, int pad, int PH, int PW,
+    const float* __restrict__ img_inv, const int* __restrict__ img_zero, float* __restrict__ out,
+    int act, int post_relu) {
+  extern __shared__ uint4 ip_sm4[];
+  const int taps = KH * KW;
+  const int Wp = W + 2 * pad, ROWS = stride + KH;
+  uint32_t* wsm = reinterpret_cast<uint32_t*>(ip_sm4);  // [taps][CW][Cout]
+  float* alpha = reinterpret_cast<float*>(wsm + taps * CW * Cout);
+  float* beta = alpha + Cout;
+  uint32_t* tile = reinterpret_cast<uint32_t*>(beta + Cout);  // [ROWS][Wp][CW]
+  const int n = blockIdx.x / PH, ph = blockIdx.x - n * PH;
+  const float inv_s = img_inv[n];
+  const bool zero = img_zero[n] != 0;
+  // packed weights and this image's alpha / beta: all of a thread's loads before its stores
+  {
+    constexpr int U = 8;
+    const int nw = taps * CW * Cout, na = 2 * Cout;
+    const float* abn = ab + (size_t)n * 2 * Cout;
+    for (int b0 = threadIdx.x; b0 < nw + na; b0 += U * blockDim.x) {
+      uint32_t v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = b0 + u * blockDim.x;
+        v[u] = 0u;
+        if (i < nw) v[u] = __ldg(wpk + i);
+        else if (i < nw + na) v[u] = __float_as_uint(__ldg(abn + (i - nw)));
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = b0 + u * blockDim.x;
+        if (i < nw + na) wsm[i] = v[u];  // alpha / beta follow the weights in smem
+      }
+    }
+  }
+  const int r0 = 2 * ph * stride - pad;  // input row of tile row 0
+  const float* img = x + (size_t)n * H * W * Cin;
+  {
+    constexpr int U = 4;
+    const int nt = ROWS * Wp * CW;
+    for (int b0 = threadIdx.x; b0 < nt; b0 += U * blockDim.x) {
+      float v[U][4];
+      bool in[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = b0 + u * blockDim.x;
+        const int cw = i % CW, rc = i / CW, pc = rc % Wp, tr = rc / Wp;
+        const int ih = r0 + tr, iw = pc - pad;
+        in[u] = i < nt && ih >= 0 && ih < H && iw >= 0 && iw < W;
+        const float* src = in[u] ? img + ((size_t)ih * W + iw) * Cin : img;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int c = cw * 4 + e;
+          v[u][e] = (in[u] && c < Cin) ? __ldg(src + c) : 0.0f;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = b0 + u * blockDim.x;
+        if (i >= nt) continue;
+        const int cw = i % CW;
+        uint32_t wv = 0x80808080u;
+        if (in[u]) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const uint32_t q = (cw * 4 + e < Cin) ? quant_one(v[u][e], inv_s, 0, true) : 128u;
+            wv = (wv & ~(0xFFu << (8 * e))) | (q << (8 * e));
+          }
+        }
+        tile[i] = wv;
+      }
+    }
+  }
+  __syncthreads();
+  const int nb = Cout / 16, items = PW * nb;
+  for (int it = threadIdx.x; it < items; it += blockDim.x) {
+    const int cb = it / PW, pw = it - cb * PW;
+    int acc[4][16];
+#pragma unroll
+    for (int p = 0; p < 4; ++p)
+#pragma unroll
+      for (int j = 0; j < 16; ++j) acc[p][j] = 0;
+    for (int kh = 0; kh < KH; ++kh)
+      for (int kw = 0; kw < KW; ++kw)
+#pragma unroll
+        for (int cw = 0; cw < CW; ++cw) {
+          const uint4* wr = reinterpret_cast<const uint4*>(wsm + ((kh * KW + kw) * CW + cw) * Cout + cb * 16);
+          uint32_t wv[16];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint4 t = wr[q];
+            wv[4 * q] = t.x; wv[4 * q + 1] = t.y; wv[4 * q + 2] = t.z; wv[4 * q + 3] = t.w;
+          }
+#pragma unroll
+          for (int p = 0; p < 4; ++p) {
+            const int tr = (p >> 1) * stride + kh;              // conv row 2ph + dy
+            const int pc = (2 * pw + (p & 1)) * stride + kw;    // padded column
+            const uint32_t xv = tile[(tr * Wp + pc) * CW + cw];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) acc[p][j] = dp4a_us(xv, wv[j], acc[p][j]);
+          }
+        }
+    float m[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) m[j] = -1e30f;
+#pragma unroll
+    for (int p = 0; p < 4; ++p)
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        float v = __fadd_rn(__fmul_rn(__int2float_rn(acc[p][j]), alpha[cb * 16 + j]), beta[cb * 16 + j]);
+        v = act ? (v > 0.0f ? v : 0.0f) : v;
+        v = zero ? 0.0f : v;
+        m[j] = m[j] > v ? m[j] : v;
+      }
+    float* dst = out + (((size_t)n * PH + ph) * PW + pw) * Cout + cb * 16;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float4 r = make_float4(m[4 * q], m[4 * q + 1], m[4 * q + 2], m[4 * q + 3]);
+      if (post_relu) {
+        r.x = r.x > 0.f ? r.x : 0.f; r.y = r.y > 0.f ? r.y : 0.f;
+        r.z = r.z > 0.f ? r.z : 0.f; r.w = r.w > 0.f ? r.w : 0.f;
+      }
+      reinterpret_cast<float4*>(dst)[q] = r;
+    }
+  }
+}
+
+
+bool conv_int8_pool_dev(Call& c, const float* x, int N, int H, int W, int Cin, const int8_t* wq,
+                        const float* wscale, const float* bias, int KH, int KW, int Cout,
+                        int stride, int pad, int act, int pool, int pst, int ppd, int post_relu,
+                        float* out, bool* handled) {
+  *handled = false;
+  const int OH = (H + 2 * pad - KH) / stride + 1, OW = (W + 2 * pad - KW) / stride + 1;
+  if (pool != 2 || pst != 2 || ppd != 0 || OH < 2 || OW < 2 || N <= 0 || N > 65535) return true;
+  // the Winograd route quantises half-away and dequantises differently: not fused here
+  if (is_wino_route(H, W, Cin, KH, KW, Cout, stride, pad)) return true;
+  const int taps = KH * KW, K = taps * Cin, CW = (Cin + 3) / 4;
+  if (K > 64 || Cin > 16 || Cout % 16 != 0 || Cout > 64 || !aligned16(out)) return true;
+  const int PH = (OH - 2) / 2 + 1, PW = (OW - 2) / 2 + 1;
+  const long long Wp = (long long)W + 2 * pad, ROWS = stride + KH;
+  const long long smem = ((long long)taps * CW * Cout + 2LL * Cout + ROWS * Wp * CW) * 4;
+  if (smem > 48 * 1024 || (long long)N * PH >= (1LL << 31)) return true;
+  unsigned* words = (unsigned*)c.scratch((size_t)N * 2 * 4);  // maxa[N], done[N]
+  float* inv = (float*)c.scratch((size_t)N * 4);
+  float* sa = (float*)c.scratch((size_t)N * 4);
+  int* zero = (int*)c.scratch((size_t)N * 4);
+  int* Sw = (int*)c.scratch((size_t)Cout * 4);
+  uint32_t* wpk = (uint32_t*)c.scratch((size_t)taps * CW * Cout * 4);
+  float* ab = (float*)c.scratch((size_t)N * 2 * Cout * 4);
+  if (!words || !inv || !sa || !zero || !Sw || !wpk || !ab) return false;
+  k_int8_pool_wpack<<<Cout, 64, 0, c.stream()>>>(wq, taps, Cin, CW, Cout, wpk, Sw, words, 2 * N);
+  const long long per = (long long)H * W * Cin;
+  long long bx = per / (4 * 256 * 4);
+  bx = bx < 1 ? 1 : (bx > 64 ? 64 : bx);
+  k_absmax_img<<<dim3((unsigned)bx, (unsigned)N), 256, 0, c.stream()>>>(
+      x, per, words, words + N, inv, sa, zero, wscale, bias, Sw, Cout, ab);
+#define ACF_I8POOL(CWV)                                                                        \
+  k_conv_int8_pool<CWV><<<N * PH, 128, (size_t)smem, c.stream()>>>(                            \
+      x, H, W, Cin, wpk, ab, Cout, KH, KW, stride, pad, PH, PW, inv, zero, out, act, post_relu)
+  if (CW == 1)
+    ACF_I8POOL(1);
+  else if (CW == 2)
+    ACF_I8POOL(2);
+  else if (CW == 3)
+    ACF_I8POOL(3);
+  else
+    ACF_I8POOL(4);
+#undef ACF_I8POOL
+  *handled = true;
+  return c.launched("k_conv_int8_pool");
 }
 
 }  // namespace acf

@@ -351,9 +351,27 @@ static bool run_model(Call& c, AcfunModel* m, int n, const float* x, float* y) {
         const int KH = L.p[0], KW = L.p[1], Cout = L.p[2], st = L.p[3], pd = L.p[4];
         const int groups = L.type == 7 ? L.p[5] : 1;
         if (m->int8 && L.wq) {
-          // int8 mode: acfun_conv2d_int8 per image (the reference's int8 model harness)
-          ok = conv2d_int8_batch_dev(c, cur, n, H, W, C, L.wq, L.wqs, L.b, KH, KW, Cout, st, pd,
-                                     next, act);
+          // int8 mode: acfun_conv2d_int8 per image (the reference's int8 model harness); a
+          // small-K conv followed by MaxPool(2, 2, 0) runs fused
+          if (li + 1 < nl && m->layers[li + 1].type == 4) {
+            const auto& P = m->layers[li + 1];
+            bool fused = false;
+            ok = conv_int8_pool_dev(c, cur, n, H, W, C, L.wq, L.wqs, L.b, KH, KW, Cout, st, pd, act,
+                                    P.p[0], P.p[1], P.p[2], P.post_relu, next, &fused);
+            if (ok && fused) {
+              H = (H + 2 * pd - KH) / st + 1;
+              W = (W + 2 * pd - KW) / st + 1;
+              H = (H + 2 * P.p[2] - P.p[0]) / P.p[1] + 1;
+              W = (W + 2 * P.p[2] - P.p[0]) / P.p[1] + 1;
+              C = Cout;
+              cur = next;
+              which ^= 1;
+              ++li;
+              break;
+            }
+          }
+          ok = ok && conv2d_int8_batch_dev(c, cur, n, H, W, C, L.wq, L.wqs, L.b, KH, KW, Cout, st,
+                                           pd, next, act);
           H = (H + 2 * pd - KH) / st + 1;
           W = (W + 2 * pd - KW) / st + 1;
           C = Cout;

@@ -123,3 +123,31 @@ def test_model_int8_mode_vs_oracle(acf, tmp_path, width_div):
     m.set_int8(False)
     assert max_rel(m.infer_batch(x)[0], om.infer(x[0])) < TOL_F32
     m.close()
+
+
+@pytest.mark.parametrize("st,post_relu,cin", [(1, False, 3), (2, True, 3), (1, True, 7)])
+def test_model_int8_conv_pool_fusion_bit_exact(acf, tmp_path, st, post_relu, cin):
+    """int8 mode, Conv -> MaxPool(2,2,0) with nothing after it: the fused small-K int8 conv +
+    pool kernel must equal the oracle's conv2d_int8 + maxpool bit for bit (odd sizes, borders,
+    per-image scales, an all-zero image)."""
+    from acfun_b200.acfun0 import Acfun0Writer, bn_params
+    from oracle.model_oracle import OracleModel
+    g = np.random.default_rng(100 + st + cin)
+    u = lambda *s: g.uniform(-0.3, 0.3, size=s).astype(np.float32)
+    Wr = Acfun0Writer(cin, 37, 29)
+    Wr.conv(u(9 * cin, 32), u(32), 3, 3, 32, st, 1).bn(*bn_params(g, 32)).relu().maxpool(2, 2, 0)
+    if post_relu:
+        Wr.relu()
+    blob = Wr.tobytes()
+    p = tmp_path / "cp8.acfun"
+    p.write_bytes(blob)
+    m = acf.Model(str(p))
+    m.set_int8(True)
+    x = np.random.default_rng(7).uniform(-1, 1, (4, 37, 29, cin)).astype(np.float32)
+    x[1] *= 50.0
+    x[3] = 0.0                       # max|x| < 1e-12: the conv writes zeros
+    y = m.infer_batch(x)
+    om = OracleModel(blob)
+    for k in range(4):
+        assert_bits_equal(y[k], om.infer(x[k], int8=True), f"image {k}")
+    m.close()
