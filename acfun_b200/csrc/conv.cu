@@ -289,7 +289,7 @@ template <int CIN, int CB>
 __global__ void __launch_bounds__(128) k_conv_pool_3x3s1(
     const float* __restrict__ x, int H, int W, const float* __restrict__ w,
     const float* __restrict__ bias, int Cout, int PH, int PW, float* __restrict__ out, int act,
-    int post_relu) {
+    int post_relu, void* out_split, long long split_plane, int sHp, int sWp, int spad) {
   constexpr int KH = 3, KW = 3, K = KH * KW * CIN, ROWS = 1 + KH;  // stride 1, pad 1
   extern __shared__ float4 cf_sm4[];
   float* ws = reinterpret_cast<float*>(cf_sm4);  // [K][Cout]
@@ -395,22 +395,42 @@ __global__ void __launch_bounds__(128) k_conv_pool_3x3s1(
         v = act ? (v > 0.0f ? v : 0.0f) : v;
         m[j] = m[j] > v ? m[j] : v;
       }
-    float* dst = out + (((size_t)n * PH + ph) * PW + pw) * Cout + cb * CB;
+    if (post_relu) {
 #pragma unroll
-    for (int q = 0; q < CB / 4; ++q) {
-      float4 r = make_float4(m[4 * q], m[4 * q + 1], m[4 * q + 2], m[4 * q + 3]);
-      if (post_relu) {
-        r.x = r.x > 0.f ? r.x : 0.f; r.y = r.y > 0.f ? r.y : 0.f;
-        r.z = r.z > 0.f ? r.z : 0.f; r.w = r.w > 0.f ? r.w : 0.f;
+      for (int j = 0; j < CB; ++j) m[j] = m[j] > 0.f ? m[j] : 0.f;
+    }
+    if (out_split) {
+      // the next convolution's split input (hi = bf16(v), lo = bf16(v - hi): k_pad_split4's
+      // split), CB channels per plane in 16-byte stores
+      uint32_t ph2[CB / 2], pl2[CB / 2];
+#pragma unroll
+      for (int j = 0; j < CB; j += 2) {
+        const uint16_t h0 = nx_bf16_rne(m[j]), h1 = nx_bf16_rne(m[j + 1]);
+        ph2[j / 2] = (uint32_t)h0 | ((uint32_t)h1 << 16);
+        pl2[j / 2] = (uint32_t)nx_bf16_rne(m[j] - nx_bf16_val(h0)) |
+                     ((uint32_t)nx_bf16_rne(m[j + 1] - nx_bf16_val(h1)) << 16);
       }
-      reinterpret_cast<float4*>(dst)[q] = r;
+      uint16_t* hi = reinterpret_cast<uint16_t*>(out_split) +
+                     (((size_t)n * sHp + ph + spad) * sWp + pw + spad) * Cout + cb * CB;
+      uint16_t* lo = hi + split_plane;
+#pragma unroll
+      for (int q = 0; q < CB / 8; ++q) {
+        reinterpret_cast<uint4*>(hi)[q] = make_uint4(ph2[4 * q], ph2[4 * q + 1], ph2[4 * q + 2], ph2[4 * q + 3]);
+        reinterpret_cast<uint4*>(lo)[q] = make_uint4(pl2[4 * q], pl2[4 * q + 1], pl2[4 * q + 2], pl2[4 * q + 3]);
+      }
+    } else {
+      float* dst = out + (((size_t)n * PH + ph) * PW + pw) * Cout + cb * CB;
+#pragma unroll
+      for (int q = 0; q < CB / 4; ++q)
+        reinterpret_cast<float4*>(dst)[q] = make_float4(m[4 * q], m[4 * q + 1], m[4 * q + 2], m[4 * q + 3]);
     }
   }
 }
 
 bool conv_pool_dev(Call& c, const float* x, int N, int H, int W, int Cin, const float* w,
                    const float* bias, int KH, int KW, int Cout, int stride, int pad, int act,
-                   int pool, int pst, int ppd, int post_relu, float* out, bool* handled) {
+                   int pool, int pst, int ppd, int post_relu, float* out, bool* handled,
+                   const SplitAct* os) {
   *handled = false;
   const int OH = (H + 2 * pad - KH) / stride + 1, OW = (W + 2 * pad - KW) / stride + 1;
   if (pool != 2 || pst != 2 || ppd != 0 || OH < 2 || OW < 2 || Cout % 16 != 0) return true;
@@ -422,11 +442,14 @@ bool conv_pool_dev(Call& c, const float* x, int N, int H, int W, int Cin, const 
     const long long smem3 = ((long long)K * Cout + ((Cout + 3) & ~3) + 4LL * 2 * ((W + 1) / 2) * 3) * 4;
     if (smem3 <= 48 * 1024 && (long long)4 * W * 3 < (1LL << 31)) {
       k_conv_pool_3x3s1<3, 16><<<N * PH, 128, (size_t)smem3, c.stream()>>>(
-          x, H, W, w, bias, Cout, PH, PW, out, act, post_relu);
+          x, H, W, w, bias, Cout, PH, PW, out, act, post_relu, os ? os->base : nullptr,
+          os ? os->plane : 0, os ? os->H + 2 * os->pad : 0, os ? os->W + 2 * os->pad : 0,
+          os ? os->pad : 0);
       *handled = true;
       return c.launched("k_conv_pool_3x3s1");
     }
   }
+  if (os) return true;  // split output only from the 3x3 / Cin 3 kernel
   const long long rows_in = std::min<long long>(H, (long long)stride + KH);
   const long long smem = ((long long)K * Cout + ((Cout + 3) & ~3) + rows_in * W * Cin) * 4;
   // same cases as conv_simt (K <= 64, Cout <= 64), so the fused result equals conv + pool
@@ -533,6 +556,126 @@ static bool conv_tc(Call& c, const float* x, int N, int H, int W, int Cs, int co
   B.ld = Np;
   B.op_stride = (long long)K * Np;
   return gemm_launch(c, kind, Epi::F32_BIAS, A, B, (int)M, Cout_g, K, ep);
+}
+
+// ------------------------------------------------------------------ split activations
+bool conv_split_ok(int H, int W, int Cin, int KH, int KW, int Cout, int stride, int pad) {
+  if (fp32_math(Fp32Use::Conv) != Fp32Math::BF16X3) return false;
+  if (stride != 1 || Cin % 64 != 0 || Cout % 64 != 0 || KH <= 0 || KW <= 0 || pad < 0) return false;
+  const int OH = H + 2 * pad - KH + 1, OW = W + 2 * pad - KW + 1;
+  if (OH <= 0 || OW <= 0) return false;
+  // the CUDA-core route takes narrow layers (conv_simt's condition)
+  const int K = KH * KW * Cin;
+  const bool narrow = (KH == 1 && KW == 1 && pad == 0) || K <= 64;
+  if (narrow && Cout <= 64) return false;
+  return true;
+}
+
+// one thread per (border pixel, 8 channels) of each plane
+__global__ void k_split_border(uint4* __restrict__ base, long long plane8, int N, int Hp, int Wp,
+                               int C8, int pad, long long total) {
+  const int bw = 2 * pad * Wp + 2 * pad * (Hp - 2 * pad);  // border pixels per image
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int c8 = (int)(i % C8);
+    long long r = i / C8;
+    const int b = (int)(r % bw);
+    r /= bw;
+    const int n = (int)(r % N), p = (int)(r / N);
+    int hp, wp;
+    if (b < pad * Wp) {
+      hp = b / Wp;
+      wp = b % Wp;
+    } else if (b < 2 * pad * Wp) {
+      hp = Hp - pad + (b - pad * Wp) / Wp;
+      wp = (b - pad * Wp) % Wp;
+    } else {
+      const int q = b - 2 * pad * Wp, side = q % (2 * pad);
+      hp = pad + q / (2 * pad);
+      wp = side < pad ? side : Wp - 2 * pad + side;
+    }
+    base[p * plane8 + (((long long)n * Hp + hp) * Wp + wp) * C8 + c8] = make_uint4(0, 0, 0, 0);
+  }
+}
+
+bool split_border_dev(Call& c, const SplitAct& a) {
+  if (a.pad == 0) return true;
+  const int Hp = a.H + 2 * a.pad, Wp = a.W + 2 * a.pad, C8 = a.C / 8;
+  const long long bw = 2LL * a.pad * Wp + 2LL * a.pad * (Hp - 2 * a.pad);
+  const long long total = 2 * (long long)a.N * bw * C8;
+  k_split_border<<<grid_ew(c, total), 256, 0, c.stream()>>>((uint4*)a.base, a.plane / 8, a.N, Hp, Wp,
+                                                             C8, a.pad, total);
+  return c.launched("k_split_border");
+}
+
+long long split_weight_bytes(int taps, int Cin, int Cout) {
+  return 2LL * 2 * taps * Cin * (long long)align_up((size_t)Cout, 8);
+}
+
+bool split_weights_dev(Call& c, const float* w, int taps, int Cin, int Cout, void* dst) {
+  const int Np = (int)align_up((size_t)Cout, 8);
+  k_weights_split<true><<<grid_ew(c, (long long)taps * Cin * Np), 256, 0, c.stream()>>>(
+      w, taps, Cin, Cout, Cout, Cin, Np, dst, (long long)taps * Cin * Np);
+  return c.launched("k_weights_split");
+}
+
+bool conv_tc_split_dev(Call& c, const float* x, const SplitAct* xs, int N, int H, int W,
+                       int Cin, const float* w, const void* ws, const float* bias, int KH,
+                       int KW, int Cout, int pad, float* out, const SplitAct* os, int act) {
+  const int OH = H + 2 * pad - KH + 1, OW = W + 2 * pad - KW + 1;
+  const int taps = KH * KW, Hp = H + 2 * pad, Wp = W + 2 * pad, Cpad = Cin;
+  const int Np = (int)align_up((size_t)Cout, 8);
+  const long long rows = (long long)N * Hp * Wp;
+  if (rows >= (1LL << 31) || rows * (Cpad / 4) >= (1LL << 32) || (xs && xs->pad != pad)) {
+    set_error(kInvalid, "%s: split conv geometry", c.name());
+    c.fail();
+    return false;
+  }
+  const void* a = xs ? xs->base : nullptr;
+  long long plane = xs ? xs->plane : rows * Cpad;
+  if (!a) {
+    void* s = c.scratch((size_t)2 * rows * Cpad * 2);
+    if (!s) return false;
+    const long long groups4 = rows * (Cpad / 4);
+    const int vec_in = aligned16(x);
+    k_pad_split4<true><<<grid_ew(c, groups4), 256, 0, c.stream()>>>(
+        x, H, W, Cin, 0, Cin, pad, Hp, Wp, Cpad / 4, (unsigned)groups4, vec_in, s, (size_t)plane);
+    a = s;
+  }
+  if (!ws) {
+    void* s = c.scratch((size_t)split_weight_bytes(taps, Cin, Cout));
+    if (!s || !split_weights_dev(c, w, taps, Cin, Cout, s)) return false;
+    ws = s;
+  }
+  if (!c.launched("split conv prep")) return false;
+  EpiParams ep{};
+  ep.C = out;
+  ep.ldc = Cout;
+  ep.f0 = bias;
+  ep.act = act;
+  ep.remap = 1;
+  ep.img_rows = Hp * Wp;
+  ep.Wp = Wp;
+  ep.OH = OH;
+  ep.OW = OW;
+  if (os) {
+    ep.split_out = os->base;
+    ep.split_plane = os->plane;
+    ep.sHp = os->H + 2 * os->pad;
+    ep.sWp = os->W + 2 * os->pad;
+    ep.spad = os->pad;
+    ep.sC = os->C;
+    ep.ldc = os->C;
+  }
+  Operand A, B;
+  A.p = a;
+  A.ld = Cpad;
+  A.op_stride = plane;
+  B.p = ws;
+  B.ld = Np;
+  B.op_stride = (long long)taps * Cpad * Np;
+  ConvGeom cg{1, Cpad / 64, KW, Wp, Cpad, taps};
+  return gemm_launch(c, GemmKind::BF16X3, Epi::F32_BIAS, A, B, (int)rows, Cout, taps * Cpad, ep, cg);
 }
 
 bool conv_f32_dev(Call& c, const float* x, int N, int H, int W, int Cs, int coff, int Cg,

@@ -29,12 +29,44 @@ bool conv_f32_dev(Call& c, const float* x, int N, int H, int W, int Cs, int coff
                   const float* w, long long ldw, const float* bias, int KH, int KW, int Cout_g,
                   int stride, int pad, float* out, long long ldc, int act);
 
+// An activation held as the zero-padded bf16 hi / lo planes a 3xBF16 implicit convolution
+// reads: [2][N][H + 2*pad][W + 2*pad][C] (C a multiple of 64), the lo plane `plane` elements
+// after the hi plane.  Borders are zero.
+struct SplitAct {
+  void* base = nullptr;
+  long long plane = 0;
+  int N = 0, H = 0, W = 0, C = 0, pad = 0;
+};
+// Bytes such an activation takes.
+inline long long split_act_bytes(int N, int H, int W, int C, int pad) {
+  return 2LL * 2 * N * (H + 2LL * pad) * (W + 2LL * pad) * C;
+}
+// Whether a dense convolution runs as the 3xBF16 implicit GEMM that split activations feed:
+// the model executor then keeps its input (and, when the next layer is one too, its output)
+// in split form.
+bool conv_split_ok(int H, int W, int Cin, int KH, int KW, int Cout, int stride, int pad);
+// Zero the padding border of `a` (both planes).
+bool split_border_dev(Call& c, const SplitAct& a);
+// fp32 weights [taps*Cin][Cout] -> the [2][taps*Cin][Np] bf16 split the implicit GEMM takes
+// (Np = Cout rounded up to 8).  `dst` holds split_weight_bytes.
+long long split_weight_bytes(int taps, int Cin, int Cout);
+bool split_weights_dev(Call& c, const float* w, int taps, int Cin, int Cout, void* dst);
+// conv_split_ok convolution from fp32 x (padded + split here) or the split activation xs
+// (xs->pad == pad), with pre-split weights ws (or NULL: split here), into fp32 out or, when
+// os is given, the next convolution's split input.
+bool conv_tc_split_dev(Call& c, const float* x, const SplitAct* xs, int N, int H, int W,
+                       int Cin, const float* w, const void* ws, const float* bias, int KH,
+                       int KW, int Cout, int pad, float* out, const SplitAct* os, int act);
+
 // Dense conv (groups 1) immediately followed by max-pool(pool, pst, ppd, post_relu), fused when
 // the conv takes the CUDA-core small-K route and the pool is 2x2 / stride 2 / pad 0 (sets
 // *handled; otherwise nothing is launched).  Same result as the two layers run in turn.
+// os != NULL: write the pooled result as the next convolution's split input (3x3 / Cin 3 /
+// stride 1 / pad 1 kernel only; otherwise nothing is launched).
 bool conv_pool_dev(Call& c, const float* x, int N, int H, int W, int Cin, const float* w,
                    const float* bias, int KH, int KW, int Cout, int stride, int pad, int act,
-                   int pool, int pst, int ppd, int post_relu, float* out, bool* handled);
+                   int pool, int pst, int ppd, int post_relu, float* out, bool* handled,
+                   const SplitAct* os = nullptr);
 
 // The same router over a batch with one activation scale per image, i.e. N separate
 // calls of acfun_conv2d_int8 (the reference's per-image model harness) in one pass.

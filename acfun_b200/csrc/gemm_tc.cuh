@@ -19,6 +19,7 @@
 // is output pixel r when remap is off; otherwise r indexes the padded grid and only rows
 // that land on a real output pixel are stored.
 #pragma once
+#include "numerics.cuh"
 #include "ptx.cuh"
 
 namespace acf {
@@ -46,6 +47,14 @@ struct EpiParams {
   // replaces zero_flag.
   const float* img_sa;
   const int* img_zero;
+  // F32_BIAS with split_out (implicit convolution only): the result is written as its bf16
+  // hi / lo split -- the 3xBF16 operand of the next convolution -- into that convolution's
+  // zero-padded input planes instead of C: output pixel (n, oh, ow), channel j at element
+  // ((n*sHp + oh + spad)*sWp + ow + spad)*sC + j of the hi plane; the lo plane follows
+  // split_plane elements later.
+  void* split_out;
+  long long split_plane;
+  int sHp, sWp, spad, sC;
 };
 
 // Implicit convolution (stride 1) over a padded NHWC tensor viewed as A[rows][Cpad]:
@@ -248,6 +257,36 @@ __device__ __forceinline__ void epi_store32(const EpiParams& ep, long long orow,
       }
       if (ep.act) x = relu_max(x);
       v[i] = zero ? 0.0f : x;
+    }
+    if constexpr (EPI == Epi::F32_BIAS) {
+      if (ep.split_out) {
+        // hi = bf16(v), lo = bf16(v - hi): the split k_pad_split4 makes of an fp32 input
+        uint16_t* hi = reinterpret_cast<uint16_t*>(ep.split_out) + orow * ep.ldc + j0;
+        uint16_t* lo = hi + ep.split_plane;
+        uint32_t ph[16], pl[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const uint16_t h0 = nx_bf16_rne(v[i]), h1 = nx_bf16_rne(v[i + 1]);
+          const uint16_t l0 = nx_bf16_rne(v[i] - nx_bf16_val(h0));
+          const uint16_t l1 = nx_bf16_rne(v[i + 1] - nx_bf16_val(h1));
+          ph[i / 2] = (uint32_t)h0 | ((uint32_t)h1 << 16);
+          pl[i / 2] = (uint32_t)l0 | ((uint32_t)l1 << 16);
+        }
+        if (full) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            reinterpret_cast<uint4*>(hi)[q] = make_uint4(ph[4 * q], ph[4 * q + 1], ph[4 * q + 2], ph[4 * q + 3]);
+            reinterpret_cast<uint4*>(lo)[q] = make_uint4(pl[4 * q], pl[4 * q + 1], pl[4 * q + 2], pl[4 * q + 3]);
+          }
+        } else {
+          for (int i = 0; i < 32; ++i)
+            if (j0 + i < N) {
+              hi[i] = (uint16_t)(ph[i / 2] >> (16 * (i & 1)));
+              lo[i] = (uint16_t)(pl[i / 2] >> (16 * (i & 1)));
+            }
+        }
+        return;
+      }
     }
     float* dst = reinterpret_cast<float*>(ep.C) + orow * ep.ldc + j0;
     if (full && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
@@ -493,7 +532,8 @@ __global__ void __launch_bounds__(320, 1)
         const int n = r / ep.img_rows, qq = r - n * ep.img_rows;
         const int oh = qq / ep.Wp, ow = qq - oh * ep.Wp;
         store = (oh < ep.OH) && (ow < ep.OW);
-        orow = ((long long)n * ep.OH + oh) * ep.OW + ow;
+        orow = ep.split_out ? ((long long)n * ep.sHp + oh + ep.spad) * ep.sWp + ow + ep.spad
+                            : ((long long)n * ep.OH + oh) * ep.OW + ow;
       }
 #pragma unroll 1
       for (int k = 0; k < S::CHUNKS_PER_WARP; ++k) {

@@ -12,6 +12,7 @@
 // NULL with error code 5 instead of reading past the blob), weights live on the GPU, and
 // acfun_model_infer_batch runs n images through each layer at once (batch-1 semantics per
 // image, Softmax per image).
+#include <algorithm>
 #include <math.h>
 #include <stdio.h>
 #include <string.h>
@@ -40,6 +41,7 @@ struct MLayer {
   int post_relu = 0;
   int8_t* wq = nullptr;  // int8 mode: per-column quantised conv weights (device)
   float* wqs = nullptr;  // and their scales
+  void* wsplit = nullptr;  // bf16 hi / lo split of w for the split-activation conv route
 };
 
 }  // namespace acf
@@ -308,7 +310,13 @@ static size_t max_activation(const AcfunModel* m) {
       H = (H + 2 * L.p[2] - L.p[0]) / L.p[1] + 1;
       W = (W + 2 * L.p[2] - L.p[0]) / L.p[1] + 1;
     }
-    const size_t a = (size_t)H * W * C;
+    size_t a = (size_t)H * W * C;
+    // room for the zero-padded split form when a convolution reads this output
+    const size_t li = (size_t)(&L - m->layers.data());
+    if (li + 1 < m->layers.size() && m->layers[li + 1].type == 1) {
+      const int p = m->layers[li + 1].p[4];
+      a = std::max(a, (size_t)(H + 2 * p) * (W + 2 * p) * C);
+    }
     if (a > mx) mx = a;
   }
   return mx;
@@ -334,6 +342,24 @@ static bool run_model(Call& c, AcfunModel* m, int n, const float* x, float* y) {
   const float* cur = x;
   int which = 0;
   const size_t nl = m->layers.size();
+  // The current activation may be held in split form (cs): the zero-padded bf16 hi / lo planes
+  // the next convolution's 3xBF16 implicit GEMM reads, written directly by the layer that
+  // produced it.  Only a layer whose consumer is such a convolution produces it.
+  SplitAct cs;
+  bool in_split = false;
+  auto split_target = [&](size_t j, int Hn, int Wn, int Cn, float* buf, SplitAct& os) -> bool {
+    if (m->int8 || j >= nl || m->layers[j].type != 1) return false;
+    const auto& Nx = m->layers[j];
+    if (!conv_split_ok(Hn, Wn, Cn, Nx.p[0], Nx.p[1], Nx.p[2], Nx.p[3], Nx.p[4])) return false;
+    os.base = buf;
+    os.N = n;
+    os.H = Hn;
+    os.W = Wn;
+    os.C = Cn;
+    os.pad = Nx.p[4];
+    os.plane = (long long)n * (Hn + 2 * os.pad) * (Wn + 2 * os.pad) * Cn;
+    return true;
+  };
   for (size_t li = 0; li < nl; ++li) {
     auto& L = m->layers[li];
     float* next = m->buf[which];
@@ -379,23 +405,59 @@ static bool run_model(Call& c, AcfunModel* m, int n, const float* x, float* y) {
           which ^= 1;
           break;
         }
+        const int OHc = (H + 2 * pd - KH) / st + 1, OWc = (W + 2 * pd - KW) / st + 1;
         // Conv -> MaxPool: the pooled output straight from the conv when the pair fuses
-        bool fused = false;
-        if (groups == 1 && li + 1 < nl && m->layers[li + 1].type == 4) {
+        // (written in split form when the layer after the pool is a split convolution)
+        if (!in_split && groups == 1 && li + 1 < nl && m->layers[li + 1].type == 4) {
           const auto& P = m->layers[li + 1];
-          ok = conv_pool_dev(c, cur, n, H, W, C, L.w, L.b, KH, KW, Cout, st, pd, act, P.p[0], P.p[1],
-                             P.p[2], P.post_relu, next, &fused);
+          const int PH = (OHc + 2 * P.p[2] - P.p[0]) / P.p[1] + 1;
+          const int PW = (OWc + 2 * P.p[2] - P.p[0]) / P.p[1] + 1;
+          SplitAct os;
+          bool fused = false, as_split = false;
+          if (split_target(li + 2, PH, PW, Cout, next, os)) {
+            ok = split_border_dev(c, os) &&
+                 conv_pool_dev(c, cur, n, H, W, C, L.w, L.b, KH, KW, Cout, st, pd, act, P.p[0],
+                               P.p[1], P.p[2], P.post_relu, next, &fused, &os);
+            as_split = fused;
+          }
+          if (ok && !fused)
+            ok = conv_pool_dev(c, cur, n, H, W, C, L.w, L.b, KH, KW, Cout, st, pd, act, P.p[0],
+                               P.p[1], P.p[2], P.post_relu, next, &fused);
           if (ok && fused) {
-            H = (H + 2 * pd - KH) / st + 1;
-            W = (W + 2 * pd - KW) / st + 1;
-            H = (H + 2 * P.p[2] - P.p[0]) / P.p[1] + 1;
-            W = (W + 2 * P.p[2] - P.p[0]) / P.p[1] + 1;
+            H = PH;
+            W = PW;
             C = Cout;
             cur = next;
             which ^= 1;
+            in_split = as_split;
+            if (as_split) cs = os;
             ++li;
             break;
           }
+        }
+        // 3xBF16 implicit GEMM from / to split activations, weights split once per model
+        if (ok && groups == 1 && (in_split || conv_split_ok(H, W, C, KH, KW, Cout, st, pd))) {
+          if (!L.wsplit) {
+            if (!ACF_CUDA_OK(cudaMalloc(&L.wsplit, (size_t)split_weight_bytes(KH * KW, C, Cout))) ||
+                !split_weights_dev(c, L.w, KH * KW, C, Cout, L.wsplit)) {
+              c.fail();
+              return false;
+            }
+          }
+          SplitAct os;
+          const bool want = split_target(li + 1, OHc, OWc, Cout, next, os);
+          if (want) ok = split_border_dev(c, os);
+          ok = ok && conv_tc_split_dev(c, in_split ? nullptr : cur, in_split ? &cs : nullptr, n, H, W,
+                                       C, L.w, L.wsplit, L.b, KH, KW, Cout, pd, next,
+                                       want ? &os : nullptr, act);
+          H = OHc;
+          W = OWc;
+          C = Cout;
+          cur = next;
+          which ^= 1;
+          in_split = want;
+          if (want) cs = os;
+          break;
         }
         ok = ok && conv2d_dev(c, cur, n, H, W, C, L.w, L.b, KH, KW, Cout, st, pd, groups, next, act);
         H = (H + 2 * pd - KH) / st + 1;
@@ -425,11 +487,18 @@ static bool run_model(Call& c, AcfunModel* m, int n, const float* x, float* y) {
         break;
       case 4: {
         const int pool = L.p[0], st = L.p[1], pd = L.p[2];
-        ok = maxpool_dev(c, cur, n, H, W, C, pool, st, pd, next, L.post_relu);
-        H = (H + 2 * pd - pool) / st + 1;
-        W = (W + 2 * pd - pool) / st + 1;
+        const int PH = (H + 2 * pd - pool) / st + 1, PW = (W + 2 * pd - pool) / st + 1;
+        SplitAct os;
+        const bool want = C % 16 == 0 && split_target(li + 1, PH, PW, C, next, os);
+        if (want) ok = split_border_dev(c, os);
+        ok = ok && maxpool_dev(c, cur, n, H, W, C, pool, st, pd, next, L.post_relu,
+                               want ? &os : nullptr);
+        H = PH;
+        W = PW;
         cur = next;
         which ^= 1;
+        in_split = want;
+        if (want) cs = os;
         break;
       }
       case 5:
@@ -500,6 +569,7 @@ extern "C" void acfun_model_destroy(AcfunModel* m) {
   cudaDeviceSynchronize();
   cudaFree(m->dparams);
   cudaFree(m->dq);
+  for (auto& L : m->layers) cudaFree(L.wsplit);
   cudaFree(m->buf[0]);
   cudaFree(m->buf[1]);
   delete m;

@@ -14,6 +14,8 @@
 #include <float.h>
 
 #include "api_export.cuh"
+#include "conv.cuh"
+#include "numerics.cuh"
 #include "ops.cuh"
 #include "runtime.cuh"
 
@@ -81,9 +83,13 @@ __global__ void k_maxpool(const float* __restrict__ in, int N, int H, int W, int
 }
 
 // float4 variant for whole vector-lane channel groups (C % 4 == 0, all lanes vectorised).
+// out_split != NULL: the result goes, split into bf16 hi / lo, into the next convolution's
+// zero-padded input planes (pixel (n, oh, ow) at ((n*sHp + oh + spad)*sWp + ow + spad)) instead
+// of `out`; nx_store_split4 is the split k_pad_split4 makes, so the next layer reads the same.
 __global__ void k_maxpool4(const float4* __restrict__ in, int N, int H, int W, int C4, int pool,
                            int stride, int pad, int OH, int OW, float4* __restrict__ out,
-                           int post_relu) {
+                           int post_relu, void* out_split, long long split_plane, int sHp,
+                           int sWp, int spad) {
   const long long total = (long long)N * OH * OW * C4;
   GRID_STRIDE(idx, total) {
     const int c = (int)(idx % C4);
@@ -112,12 +118,18 @@ __global__ void k_maxpool4(const float4* __restrict__ in, int N, int H, int W, i
       m.z = m.z > 0.f ? m.z : 0.f;
       m.w = m.w > 0.f ? m.w : 0.f;
     }
-    out[idx] = m;
+    if (out_split) {
+      const float v[4] = {m.x, m.y, m.z, m.w};
+      const size_t i4 = (((size_t)n * sHp + oh + spad) * sWp + ow + spad) * C4 + c;
+      nx_store_split4<true>(out_split, i4, (size_t)split_plane, v);
+    } else {
+      out[idx] = m;
+    }
   }
 }
 
 bool maxpool_dev(Call& c, const float* in, int N, int H, int W, int C, int pool, int stride,
-                 int pad, float* out, int post_relu) {
+                 int pad, float* out, int post_relu, const SplitAct* os) {
   const int OH = (H + 2 * pad - pool) / stride + 1, OW = (W + 2 * pad - pool) / stride + 1;
   if (OH <= 0 || OW <= 0 || N <= 0 || C <= 0) return true;
   // lanes handled by the reference's vector kernels (maxpool_impl, layers.cpp:250-258)
@@ -125,8 +137,15 @@ bool maxpool_dev(Call& c, const float* in, int N, int H, int W, int C, int pool,
   if (cfull == C && C % 4 == 0 && aligned16(in) && aligned16(out)) {
     const long long total = (long long)N * OH * OW * (C / 4);
     k_maxpool4<<<grid_for(c, total), 256, 0, c.stream()>>>(
-        (const float4*)in, N, H, W, C / 4, pool, stride, pad, OH, OW, (float4*)out, post_relu);
+        (const float4*)in, N, H, W, C / 4, pool, stride, pad, OH, OW, (float4*)out, post_relu,
+        os ? os->base : nullptr, os ? os->plane : 0, os ? os->H + 2 * os->pad : 0,
+        os ? os->W + 2 * os->pad : 0, os ? os->pad : 0);
     return c.launched("k_maxpool4");
+  }
+  if (os) {
+    set_error(kInvalid, "%s: split max-pool output needs whole 16-channel groups", c.name());
+    c.fail();
+    return false;
   }
   const long long total = (long long)N * OH * OW * C;
   k_maxpool<<<grid_for(c, total), 256, 0, c.stream()>>>(in, N, H, W, C, pool, stride, pad, OH,

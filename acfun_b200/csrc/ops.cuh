@@ -5,8 +5,10 @@
 
 namespace acf {
 bool relu_dev(Call& c, float* d, long long n, int six);
+struct SplitAct;
+// os != NULL: write the result as the next convolution's split input (C % 16 == 0)
 bool maxpool_dev(Call& c, const float* in, int N, int H, int W, int C, int pool, int stride,
-                 int pad, float* out, int post_relu);
+                 int pad, float* out, int post_relu, const SplitAct* os = nullptr);
 bool softmax_dev(Call& c, const float* in, int rows, int cols, float* out);
 bool batchnorm_dev(Call& c, float* d, int size, int channels, const float* mean,
                    const float* var, const float* gamma, const float* beta, float eps);
