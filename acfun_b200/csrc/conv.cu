@@ -328,11 +328,11 @@ __global__ void __launch_bounds__(128) k_conv_pool_3x3s1(
   const int nb = Cout / CB, items = PW * nb;
   for (int it = threadIdx.x; it < items; it += blockDim.x) {
     const int cb = it / PW, pw = it - cb * PW;
-    float acc[4][CB];
+    float2 acc[4][CB / 2];  // channel pairs (2j, 2j+1), one packed fma per pair
 #pragma unroll
     for (int p = 0; p < 4; ++p)
 #pragma unroll
-      for (int j = 0; j < CB; ++j) acc[p][j] = 0.0f;
+      for (int j = 0; j < CB / 2; ++j) acc[p][j] = make_float2(0.0f, 0.0f);
     const bool interior = r0 >= 0 && r0 + ROWS <= H && pw >= 1 && 2 * pw + 2 < W;
     if (interior) {
       // pixel (dy, dx), tap (kh, kw): tile row dy + kh, column 2pw + dx - 1 + kw
@@ -345,19 +345,21 @@ __global__ void __launch_bounds__(128) k_conv_pool_3x3s1(
           for (int ic = 0; ic < CIN; ++ic) {
             const int k = (kh * KW + kw) * CIN + ic;
             const float4* wr = reinterpret_cast<const float4*>(ws + k * Cout + cb * CB);
-            float wv[CB];
+            float2 wv[CB / 2];
 #pragma unroll
             for (int q = 0; q < CB / 4; ++q) {
               const float4 t = wr[q];
-              wv[4 * q] = t.x; wv[4 * q + 1] = t.y; wv[4 * q + 2] = t.z; wv[4 * q + 3] = t.w;
+              wv[2 * q] = make_float2(t.x, t.y);
+              wv[2 * q + 1] = make_float2(t.z, t.w);
             }
 #pragma unroll
             for (int p = 0; p < 4; ++p) {
               const int dy = p >> 1, dx = p & 1;
               const int col = 2 + dx - 1 + kw;  // column relative to 2*(pw-1)
               const float xv = tb[((dy + kh) * 2 + (col & 1)) * plane + (col >> 1) * CIN + ic];
+              const float2 x2 = make_float2(xv, xv);
 #pragma unroll
-              for (int j = 0; j < CB; ++j) acc[p][j] = __fmaf_rn(xv, wv[j], acc[p][j]);
+              for (int j = 0; j < CB / 2; ++j) acc[p][j] = nx_ffma2(x2, wv[j], acc[p][j]);
             }
           }
     } else {
@@ -367,11 +369,12 @@ __global__ void __launch_bounds__(128) k_conv_pool_3x3s1(
           for (int ic = 0; ic < CIN; ++ic) {
             const int k = (kh * KW + kw) * CIN + ic;
             const float4* wr = reinterpret_cast<const float4*>(ws + k * Cout + cb * CB);
-            float wv[CB];
+            float2 wv[CB / 2];
 #pragma unroll
             for (int q = 0; q < CB / 4; ++q) {
               const float4 t = wr[q];
-              wv[4 * q] = t.x; wv[4 * q + 1] = t.y; wv[4 * q + 2] = t.z; wv[4 * q + 3] = t.w;
+              wv[2 * q] = make_float2(t.x, t.y);
+              wv[2 * q + 1] = make_float2(t.z, t.w);
             }
 #pragma unroll
             for (int p = 0; p < 4; ++p) {
@@ -379,8 +382,9 @@ __global__ void __launch_bounds__(128) k_conv_pool_3x3s1(
               const int ih = 2 * ph + dy - 1 + kh, iw = 2 * pw + dx - 1 + kw;
               if (ih < 0 || ih >= H || iw < 0 || iw >= W) continue;
               const float xv = tile[((ih - r0) * 2 + (iw & 1)) * plane + (iw >> 1) * CIN + ic];
+              const float2 x2 = make_float2(xv, xv);
 #pragma unroll
-              for (int j = 0; j < CB; ++j) acc[p][j] = __fmaf_rn(xv, wv[j], acc[p][j]);
+              for (int j = 0; j < CB / 2; ++j) acc[p][j] = nx_ffma2(x2, wv[j], acc[p][j]);
             }
           }
     }
@@ -391,7 +395,7 @@ __global__ void __launch_bounds__(128) k_conv_pool_3x3s1(
     for (int p = 0; p < 4; ++p)
 #pragma unroll
       for (int j = 0; j < CB; ++j) {
-        float v = __fadd_rn(acc[p][j], bs[cb * CB + j]);
+        float v = __fadd_rn((j & 1) ? acc[p][j / 2].y : acc[p][j / 2].x, bs[cb * CB + j]);
         v = act ? (v > 0.0f ? v : 0.0f) : v;
         m[j] = m[j] > v ? m[j] : v;
       }

@@ -70,4 +70,14 @@ static __device__ __forceinline__ void nx_store_split1(void* dst, size_t i, size
   }
 }
 
+// Two independent IEEE fma.rn in one instruction (sm_100 packed f32x2): lane k of the result
+// is fmaf(a_k, b_k, c_k), bit-identical to __fmaf_rn on each lane.
+static __device__ __forceinline__ float2 nx_ffma2(float2 a, float2 b, float2 c) {
+  unsigned long long d = __builtin_bit_cast(unsigned long long, c);
+  asm("fma.rn.f32x2 %0, %1, %2, %0;"
+      : "+l"(d)
+      : "l"(__builtin_bit_cast(unsigned long long, a)), "l"(__builtin_bit_cast(unsigned long long, b)));
+  return __builtin_bit_cast(float2, d);
+}
+
 }  // namespace acf

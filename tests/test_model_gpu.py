@@ -151,3 +151,24 @@ def test_model_int8_conv_pool_fusion_bit_exact(acf, tmp_path, st, post_relu, cin
     for k in range(4):
         assert_bits_equal(y[k], om.infer(x[k], int8=True), f"image {k}")
     m.close()
+
+
+@pytest.mark.parametrize("hw", [(224, 224), (37, 29)])
+def test_fused_conv1_pool_bit_exact_vs_separate_calls(acf, tmp_path, hw):
+    """The fused 3x3 / Cin 3 conv + 2x2 pool kernel (packed f32x2 FMAs) against acfun_conv2d
+    (CUDA-core route, scalar fma chain) followed by acfun_maxpool: identical bits."""
+    from acfun_b200.acfun0 import Acfun0Writer
+    H, W = hw
+    g = np.random.default_rng(H)
+    w = g.uniform(-0.5, 0.5, (27, 64)).astype(np.float32)
+    b = g.uniform(-0.1, 0.1, 64).astype(np.float32)
+    Wr = Acfun0Writer(3, H, W)
+    Wr.conv(w, b, 3, 3, 64, 1, 1).maxpool(2, 2, 0)
+    p = tmp_path / "c1.acfun"
+    p.write_bytes(Wr.tobytes())
+    m = acf.Model(str(p))
+    x = g.uniform(-1, 1, (2, H, W, 3)).astype(np.float32)
+    y = m.infer_batch(x)
+    ref = acf.maxpool(acf.conv2d(x, w, b, 3, 3, 64, 1, 1, 0), 2, 2, 0)
+    assert_bits_equal(y, ref.reshape(y.shape), "fused conv1 + pool")
+    m.close()
