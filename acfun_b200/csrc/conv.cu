@@ -142,16 +142,26 @@ __global__ void __launch_bounds__(128) k_conv_simt(const float* __restrict__ x, 
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
               const float* wr = wt + (k + u) * NB;
+              const float2 x2 = make_float2(xv[u], xv[u]);
 #pragma unroll
-              for (int j = 0; j < NB; ++j) acc[j] = __fmaf_rn(xv[u], wr[j], acc[j]);
+              for (int j = 0; j < NB; j += 2) {
+                const float2 r2 = nx_ffma2(x2, make_float2(wr[j], wr[j + 1]), make_float2(acc[j], acc[j + 1]));
+                acc[j] = r2.x;
+                acc[j + 1] = r2.y;
+              }
             }
           }
         }
         for (; k < Cin; ++k) {
           const float xv = src[k];
           const float* wr = wt + k * NB;
+          const float2 x2 = make_float2(xv, xv);
 #pragma unroll
-          for (int j = 0; j < NB; ++j) acc[j] = __fmaf_rn(xv, wr[j], acc[j]);
+          for (int j = 0; j < NB; j += 2) {
+            const float2 r2 = nx_ffma2(x2, make_float2(wr[j], wr[j + 1]), make_float2(acc[j], acc[j + 1]));
+            acc[j] = r2.x;
+            acc[j + 1] = r2.y;
+          }
         }
       }
     }

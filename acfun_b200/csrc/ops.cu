@@ -409,10 +409,12 @@ __global__ void k_dw_strip(const float* __restrict__ in, int H, int W, int C,
         for (int t = 0; t < TW; ++t) {
           if (!((ok >> (t * STRIDE + kw)) & 1u)) continue;
           const float4 x = xc[t * STRIDE + kw];
-          acc[t].x = __fmaf_rn(x.x, wv.x, acc[t].x);
-          acc[t].y = __fmaf_rn(x.y, wv.y, acc[t].y);
-          acc[t].z = __fmaf_rn(x.z, wv.z, acc[t].z);
-          acc[t].w = __fmaf_rn(x.w, wv.w, acc[t].w);
+          // two packed fmas (lanes x,y and z,w): bit-identical to four __fmaf_rn
+          const float2 lo = nx_ffma2(make_float2(x.x, x.y), make_float2(wv.x, wv.y),
+                                     make_float2(acc[t].x, acc[t].y));
+          const float2 hi = nx_ffma2(make_float2(x.z, x.w), make_float2(wv.z, wv.w),
+                                     make_float2(acc[t].z, acc[t].w));
+          acc[t] = make_float4(lo.x, lo.y, hi.x, hi.y);
         }
       }
     }
