@@ -1,7 +1,7 @@
 // gemm.cu — GEMM-family entry points and the tcgen05 GEMM launcher.
 //
 // Entry points (reference behaviour in brackets, hit-droid/Acfun paths):
-//   acfun_gemm / acfun_gemm_epi   fp32, 3xTF32 on kind::tf32  [gemm.cpp:90-99,138-148]
+//   acfun_gemm / acfun_gemm_epi   fp32, 3xBF16 (or 3xTF32)     [gemm.cpp:90-99,138-148]
 //   acfun_gemm_bf16               bf16 RNE operands, f32 acc   [gemm_bf16_avx512.cpp:171-232]
 //   acfun_gemm_int8               u8 x s8 -> s32, exact        [gemm_int8.cpp:45-50]
 //   acfun_gemm_int8_epi           + (float)acc*alpha + beta    [gemm_int8.cpp:69-75]
@@ -185,11 +185,15 @@ __global__ void k_to_bf16x2(const float* __restrict__ src, long long lds, int ro
   }
 }
 
-Operand to_bf16x2(Call& c, const float* src, int rows, int cols, long long lds) {
+long long bf16x2_bytes(int rows, int cols) {
+  return 2LL * rows * (long long)align_up((size_t)cols, 8) * 2;
+}
+
+Operand to_bf16x2(Call& c, const float* src, int rows, int cols, long long lds, void* into) {
   Operand o;
   if (!c.ok()) return o;
   const long long ldp = (long long)align_up((size_t)cols, 8);
-  uint16_t* d = (uint16_t*)c.scratch((size_t)2 * rows * ldp * 2);
+  uint16_t* d = into ? (uint16_t*)into : (uint16_t*)c.scratch((size_t)2 * rows * ldp * 2);
   if (!d) return o;
   k_to_bf16x2<<<ew_grid(c, rows * (ldp / 4)), 256, 0, c.stream()>>>(src, lds, rows, cols, d, ldp,
                                                                       (long long)rows * ldp);
@@ -396,10 +400,12 @@ bool gemm_launch(Call& c, GemmKind kind, Epi epi, const Operand& A, const Operan
 
 // fp32 GEMM (+bias, +ReLU) on device operands, used by GEMM, FC and conv routes.
 bool gemm_f32(Call& c, const float* dA, long long lda, const float* dB, long long ldb, int M,
-              int N, int K, float* dC, long long ldc, const float* dbias, int act, Fp32Use use) {
+              int N, int K, float* dC, long long ldc, const float* dbias, int act, Fp32Use use,
+              const Operand* b_split) {
   const bool bf = fp32_math(use) == Fp32Math::BF16X3;
   Operand a = bf ? to_bf16x2(c, dA, M, K, lda) : to_tf32x2(c, dA, M, K, lda);
-  Operand b = bf ? to_bf16x2(c, dB, K, N, ldb) : to_tf32x2(c, dB, K, N, ldb);
+  Operand b = (bf && b_split) ? *b_split
+                              : bf ? to_bf16x2(c, dB, K, N, ldb) : to_tf32x2(c, dB, K, N, ldb);
   EpiParams ep{};
   ep.C = dC;
   ep.ldc = ldc;
@@ -430,7 +436,7 @@ extern "C" void acfun_gemm_epi(int M, int N, int K, const float* A, const float*
   const float* db = bias ? (const float*)c.in(bias, (size_t)N * 4) : nullptr;
   float* dC = (float*)c.out(C, (size_t)M * N * 4);
   if (!c.ok()) return;
-  gemm_f32(c, dA, K, dB, N, M, N, K, dC, N, db, act ? 1 : 0, Fp32Use::GemmApi);
+  gemm_f32(c, dA, K, dB, N, M, N, K, dC, N, db, act ? 1 : 0, Fp32Use::GemmApi, nullptr);
   c.finish();
 }
 

@@ -38,8 +38,11 @@ enum class GemmKind { I8U, I8S, BF16, TF32X3, BF16X3 };
 enum class Fp32Math { TF32X3, BF16X3 };
 enum class Fp32Use { GemmApi, Conv };
 Fp32Math fp32_math(Fp32Use use);
-// fp32 -> [2][rows][ldp] bf16 (hi, lo) for 3xBF16, ldp a multiple of 8.
-Operand to_bf16x2(Call& c, const float* src_dev, int rows, int cols, long long lds);
+// fp32 -> [2][rows][ldp] bf16 (hi, lo) for 3xBF16, ldp a multiple of 8; into scratch, or into
+// `into` (bf16x2_bytes(rows, cols) bytes) when given, e.g. a model's cached weight split.
+Operand to_bf16x2(Call& c, const float* src_dev, int rows, int cols, long long lds,
+                  void* into = nullptr);
+long long bf16x2_bytes(int rows, int cols);
 
 // C-tile launch: chooses the tile width from the problem size and the SM count.
 // With cg.enabled, A is a padded NHWC tensor [rows][cpad] and B the weights

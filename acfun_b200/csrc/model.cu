@@ -469,7 +469,24 @@ static bool run_model(Call& c, AcfunModel* m, int n, const float* x, float* y) {
       }
       case 2: {
         const int Cout = L.p[0], inDim = H * W * C;
-        ok = gemm_f32(c, cur, inDim, L.w, Cout, n, Cout, inDim, next, Cout, L.b, act, Fp32Use::Conv);
+        // the weights' 3xBF16 split is made once and cached with the layer
+        Operand bs;
+        const Operand* bsp = nullptr;
+        if (fp32_math(Fp32Use::Conv) == Fp32Math::BF16X3) {
+          if (!L.wsplit) {
+            if (!ACF_CUDA_OK(cudaMalloc(&L.wsplit, (size_t)bf16x2_bytes(inDim, Cout)))) {
+              c.fail();
+              return false;
+            }
+            to_bf16x2(c, L.w, inDim, Cout, Cout, L.wsplit);
+          }
+          bs.p = L.wsplit;
+          bs.ld = (long long)align_up((size_t)Cout, 8);
+          bs.op_stride = (long long)inDim * bs.ld;
+          bsp = &bs;
+        }
+        ok = c.ok() && gemm_f32(c, cur, inDim, L.w, Cout, n, Cout, inDim, next, Cout, L.b, act,
+                                Fp32Use::Conv, bsp);
         H = W = 1;
         C = Cout;
         cur = next;

@@ -19,7 +19,10 @@ bool group_dev(Call& c, const float* in, int N, int H, int W, int Cin, const flo
                const float* bias, int KH, int KW, int Cout, int stride, int pad, int groups,
                float* out, int act);
 // fp32 GEMM on device operands on tensor cores (3xTF32 or 3xBF16 per fp32_math, gemm.cu)
+// b_split: B already split for 3xBF16 (to_bf16x2), used when that mode is active.
 enum class Fp32Use;
+struct Operand;
 bool gemm_f32(Call& c, const float* dA, long long lda, const float* dB, long long ldb, int M,
-              int N, int K, float* dC, long long ldc, const float* dbias, int act, Fp32Use use);
+              int N, int K, float* dC, long long ldc, const float* dbias, int act, Fp32Use use,
+              const Operand* b_split = nullptr);
 }  // namespace acf
