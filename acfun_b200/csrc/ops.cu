@@ -371,11 +371,31 @@ __global__ void k_dw_strip(const float* __restrict__ in, int H, int W, int C,
   float* wT = reinterpret_cast<float*>(dss4);
   const int K = KH * KW;
   float* bs = wT + K * C;
-  for (int i = threadIdx.x; i < K * C; i += blockDim.x) {
-    const int k = i / C, c = i - k * C;
-    wT[i] = w[c * K + k];
+  {
+    // every thread issues its U loads before its stores: one memory round trip per U
+    // elements instead of one per element
+    constexpr int U = 8;
+    const int tot = K * C + C;
+    for (int b0 = threadIdx.x; b0 < tot; b0 += U * blockDim.x) {
+      float v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = b0 + u * blockDim.x;
+        v[u] = 0.0f;
+        if (i < K * C) {
+          const int k = i / C, c = i - k * C;
+          v[u] = __ldg(w + c * K + k);
+        } else if (i < tot && bias) {
+          v[u] = __ldg(bias + (i - K * C));
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int i = b0 + u * blockDim.x;
+        if (i < tot) wT[i] = v[u];  // bs follows wT
+      }
+    }
   }
-  for (int i = threadIdx.x; i < C; i += blockDim.x) bs[i] = bias ? bias[i] : 0.0f;
   __syncthreads();
   const int n = blockIdx.x / OH, oh = blockIdx.x - n * OH;
   const int C4 = C >> 2, strips = (OW + TW - 1) / TW, items = strips * C4;
@@ -469,10 +489,10 @@ bool dw_dev(Call& c, const float* in, int N, int H, int W, int C, const float* w
                     (long long)N * OH < (1LL << 31) && (long long)H * W * C < (1LL << 31);
   if (rowk && KW == 3 && (stride == 1 || stride == 2)) {
     if (stride == 1)
-      k_dw_strip<4, 3, 1><<<N * OH, 128, smem, c.stream()>>>(in, H, W, C, w, bias, KH, pad, OH, OW,
+      k_dw_strip<4, 3, 1><<<N * OH, 256, smem, c.stream()>>>(in, H, W, C, w, bias, KH, pad, OH, OW,
                                                              out, act);
     else
-      k_dw_strip<4, 3, 2><<<N * OH, 128, smem, c.stream()>>>(in, H, W, C, w, bias, KH, pad, OH, OW,
+      k_dw_strip<4, 3, 2><<<N * OH, 256, smem, c.stream()>>>(in, H, W, C, w, bias, KH, pad, OH, OW,
                                                              out, act);
     return c.launched("k_dw_strip");
   }
