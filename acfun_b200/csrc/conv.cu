@@ -20,6 +20,11 @@
 #include "numerics.cuh"
 #include "ops.cuh"
 
+namespace {
+// im2col bytes per chunk of images on the tensor-core conv + pool route (kept in L2)
+constexpr long long kPoolIm2colChunkBytes = 96LL << 20;
+}  // namespace
+
 namespace acf {
 
 static int grid_ew(Call& c, long long work) {
@@ -418,12 +423,7 @@ __global__ void __launch_bounds__(128) k_conv_pool_3x3s1(
       // split), CB channels per plane in 16-byte stores
       uint32_t ph2[CB / 2], pl2[CB / 2];
 #pragma unroll
-      for (int j = 0; j < CB; j += 2) {
-        const uint16_t h0 = nx_bf16_rne(m[j]), h1 = nx_bf16_rne(m[j + 1]);
-        ph2[j / 2] = (uint32_t)h0 | ((uint32_t)h1 << 16);
-        pl2[j / 2] = (uint32_t)nx_bf16_rne(m[j] - nx_bf16_val(h0)) |
-                     ((uint32_t)nx_bf16_rne(m[j + 1] - nx_bf16_val(h1)) << 16);
-      }
+      for (int j = 0; j < CB; j += 2) nx_split_bf16x2(m[j], m[j + 1], ph2[j / 2], pl2[j / 2]);
       uint16_t* hi = reinterpret_cast<uint16_t*>(out_split) +
                      (((size_t)n * sHp + ph + spad) * sWp + pw + spad) * Cout + cb * CB;
       uint16_t* lo = hi + split_plane;
@@ -441,6 +441,185 @@ __global__ void __launch_bounds__(128) k_conv_pool_3x3s1(
   }
 }
 
+// im2col of a small-K convolution in pooled-window order, as the 3xBF16 split: row
+// ((n*PH + py)*PW + px)*4 + d holds the patch of output pixel (2py + d/2, 2px + d%2), K in
+// (kh, kw, ci) order zero-padded to KP, bf16 hi = bf16(v) and lo = bf16(v - hi) planes
+// (k_pad_split4's split).  The pooling GEMM epilogue then reduces each group of four rows.
+template <int KP>
+__global__ void k_im2col_pool_split(const float* __restrict__ x, int H, int W, int Cin, int KH,
+                                    int KW, int stride, int pad, int PH, int PW, long long rows,
+                                    uint16_t* __restrict__ hi, long long plane) {
+  for (long long r = blockIdx.x * (long long)blockDim.x + threadIdx.x; r < rows;
+       r += (long long)gridDim.x * blockDim.x) {
+    const int d = (int)(r & 3);
+    long long P = r >> 2;
+    const int px = (int)(P % PW);
+    P /= PW;
+    const int py = (int)(P % PH);
+    const long long n = P / PH;
+    const int iy0 = (2 * py + (d >> 1)) * stride - pad, ix0 = (2 * px + (d & 1)) * stride - pad;
+    const float* xn = x + n * H * W * Cin;
+    float v[KP];
+    int kh = 0, kw = 0, ci = 0;
+#pragma unroll
+    for (int k = 0; k < KP; ++k) {
+      float t = 0.0f;
+      if (kh < KH) {
+        const int iy = iy0 + kh, ix = ix0 + kw;
+        if (iy >= 0 && iy < H && ix >= 0 && ix < W) t = xn[((long long)iy * W + ix) * Cin + ci];
+        if (++ci == Cin) {
+          ci = 0;
+          if (++kw == KW) {
+            kw = 0;
+            ++kh;
+          }
+        }
+      }
+      v[k] = t;
+    }
+    uint32_t ph[KP / 2], pl[KP / 2];
+#pragma unroll
+    for (int k = 0; k < KP; k += 2) nx_split_bf16x2(v[k], v[k + 1], ph[k / 2], pl[k / 2]);
+    uint4* dh = reinterpret_cast<uint4*>(hi + r * KP);
+    uint4* dl = reinterpret_cast<uint4*>(hi + plane + r * KP);
+#pragma unroll
+    for (int q = 0; q < KP / 8; ++q) {
+      dh[q] = make_uint4(ph[4 * q], ph[4 * q + 1], ph[4 * q + 2], ph[4 * q + 3]);
+      dl[q] = make_uint4(pl[4 * q], pl[4 * q + 1], pl[4 * q + 2], pl[4 * q + 3]);
+    }
+  }
+}
+
+// k_im2col_pool_split<32> for the 3x3 / stride 1 / pad 1 / 3-channel case.  A block of 64
+// threads takes 64 consecutive pooled pixels, one each: the pixel's 4x4x3 input patch is read
+// once and its window's four rows (256 bytes per plane) go to shared memory; the block's rows
+// are contiguous in both planes, so they leave in coalesced 16-byte stores.
+constexpr int kIm2colPix = 64;
+constexpr int kIm2colRowB = 272;  // 256 bytes per pixel + 16: conflict-free 16-byte writes
+__global__ void __launch_bounds__(kIm2colPix) k_im2col_pool_3x3c3(
+    const float* __restrict__ x, int H, int W, int PH, int PW, long long pooled,
+    uint16_t* __restrict__ hi, long long plane) {
+  __shared__ __align__(16) uint8_t st[2][kIm2colPix * kIm2colRowB];
+  const int t = threadIdx.x;
+  for (long long base = (long long)blockIdx.x * kIm2colPix; base < pooled;
+       base += (long long)gridDim.x * kIm2colPix) {
+    const long long P = base + t;
+    if (P < pooled) {
+      const int px = (int)(P % PW);
+      const long long q = P / PW;
+      const int py = (int)(q % PH);
+      const long long n = q / PH;
+      const int y0 = 2 * py - 1, x0 = 2 * px - 1;
+      const float* xn = x + n * H * W * 3;
+      const bool inside = y0 >= 0 && y0 + 4 <= H && x0 >= 0 && x0 + 4 <= W;
+      float p[4][12];
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int c = 0; c < 12; ++c) {
+          const int iy = y0 + r, ix = x0 + c / 3;
+          p[r][c] = (inside || (iy >= 0 && iy < H && ix >= 0 && ix < W))
+                        ? xn[((long long)iy * W + x0) * 3 + c]
+                        : 0.0f;
+        }
+#pragma unroll
+      for (int d = 0; d < 4; ++d) {
+        const int dy = d >> 1, dx = d & 1;
+        float v[32];
+#pragma unroll
+        for (int k = 0; k < 32; ++k)
+          v[k] = k < 27 ? p[dy + k / 9][(dx + (k / 3) % 3) * 3 + k % 3] : 0.0f;
+        uint32_t ph[16], pl[16];
+#pragma unroll
+        for (int k = 0; k < 32; k += 2) nx_split_bf16x2(v[k], v[k + 1], ph[k / 2], pl[k / 2]);
+        uint4* sh = reinterpret_cast<uint4*>(st[0] + t * kIm2colRowB + d * 64);
+        uint4* sl = reinterpret_cast<uint4*>(st[1] + t * kIm2colRowB + d * 64);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          sh[u] = make_uint4(ph[4 * u], ph[4 * u + 1], ph[4 * u + 2], ph[4 * u + 3]);
+          sl[u] = make_uint4(pl[4 * u], pl[4 * u + 1], pl[4 * u + 2], pl[4 * u + 3]);
+        }
+      }
+    }
+    __syncthreads();
+    const int npix = (int)(pooled - base < kIm2colPix ? pooled - base : kIm2colPix);
+    uint4* gh = reinterpret_cast<uint4*>(hi + base * 4 * 32);
+    uint4* gl = reinterpret_cast<uint4*>(hi + plane + base * 4 * 32);
+    for (int u = t; u < npix * 16; u += kIm2colPix) {
+      const int off = (u >> 4) * kIm2colRowB + (u & 15) * 16;
+      gh[u] = *reinterpret_cast<const uint4*>(st[0] + off);
+      gl[u] = *reinterpret_cast<const uint4*>(st[1] + off);
+    }
+    __syncthreads();
+  }
+}
+
+// Conv (K <= 64) + 2x2/2 max-pool on the tensor cores: pooled-order im2col, then a 3xBF16
+// GEMM whose epilogue takes each window's maximum before bias and activation (max commutes
+// with the per-channel bias add and ReLU, both monotone).  Images go in chunks whose im2col
+// stays in L2 between its producer and the GEMM.
+static bool conv_pool_tc(Call& c, const float* x, int N, int H, int W, int Cin, const float* w,
+                         const float* bias, int KH, int KW, int Cout, int stride, int pad, int act,
+                         int PH, int PW, float* out, const SplitAct* os) {
+  const int K = KH * KW * Cin, KP = K <= 32 ? 32 : 64;
+  const int Np = (int)align_up((size_t)Cout, 8);
+  const long long img_rows = 4LL * PH * PW;
+  const long long img_bytes = img_rows * KP * 2 * 2;
+  const int chunk = (int)std::max<long long>(1, std::min<long long>(N, kPoolIm2colChunkBytes / img_bytes));
+  const long long plane = (long long)chunk * img_rows * KP;
+  uint16_t* a = static_cast<uint16_t*>(c.scratch((size_t)(2 * plane * 2 + split_weight_bytes(1, KP, Cout))));
+  if (!a) return false;
+  void* b = a + 2 * plane;
+  k_weights_split<true><<<grid_ew(c, (long long)KP * Np), 256, 0, c.stream()>>>(
+      w, 1, K, Cout, Cout, KP, Np, b, (long long)KP * Np);
+  if (!c.launched("k_weights_split")) return false;
+  EpiParams ep{};
+  ep.f0 = bias;
+  ep.act = act;
+  ep.pool4 = 1;
+  ep.ph = PH;
+  ep.pw = PW;
+  ep.ldc = Cout;
+  if (os) {
+    ep.split_plane = os->plane;
+    ep.sHp = os->H + 2 * os->pad;
+    ep.sWp = os->W + 2 * os->pad;
+    ep.spad = os->pad;
+    ep.sC = os->C;
+    ep.ldc = os->C;
+  }
+  Operand A, B;
+  A.p = a;
+  A.ld = KP;
+  A.op_stride = plane;
+  B.p = b;
+  B.ld = Np;
+  B.op_stride = (long long)KP * Np;
+  for (int n0 = 0; n0 < N; n0 += chunk) {
+    const int nc = std::min(chunk, N - n0);
+    const long long rows = nc * img_rows;
+    if (KH == 3 && KW == 3 && stride == 1 && pad == 1 && Cin == 3)
+      k_im2col_pool_3x3c3<<<(unsigned)std::min<long long>((rows / 4 + kIm2colPix - 1) / kIm2colPix,
+                                                          64LL * c.sm_count()),
+                            kIm2colPix, 0, c.stream()>>>(
+          x + (long long)n0 * H * W * Cin, H, W, PH, PW, rows / 4, a, plane);
+    else if (KP == 32)
+      k_im2col_pool_split<32><<<grid_ew(c, rows), 256, 0, c.stream()>>>(
+          x + (long long)n0 * H * W * Cin, H, W, Cin, KH, KW, stride, pad, PH, PW, rows, a, plane);
+    else
+      k_im2col_pool_split<64><<<grid_ew(c, rows), 256, 0, c.stream()>>>(
+          x + (long long)n0 * H * W * Cin, H, W, Cin, KH, KW, stride, pad, PH, PW, rows, a, plane);
+    if (!c.launched("k_im2col_pool_split")) return false;
+    if (os)
+      ep.split_out = static_cast<uint16_t*>(os->base) + (long long)n0 * ep.sHp * ep.sWp * ep.sC;
+    else
+      ep.C = out + (long long)n0 * PH * PW * Cout;
+    if (!gemm_launch(c, GemmKind::BF16X3, Epi::F32_BIAS, A, B, (int)rows, Cout, KP, ep))
+      return false;
+  }
+  return true;
+}
+
 bool conv_pool_dev(Call& c, const float* x, int N, int H, int W, int Cin, const float* w,
                    const float* bias, int KH, int KW, int Cout, int stride, int pad, int act,
                    int pool, int pst, int ppd, int post_relu, float* out, bool* handled,
@@ -450,6 +629,13 @@ bool conv_pool_dev(Call& c, const float* x, int N, int H, int W, int Cin, const 
   if (pool != 2 || pst != 2 || ppd != 0 || OH < 2 || OW < 2 || Cout % 16 != 0) return true;
   const int K = KH * KW * Cin;
   const int PH = (OH - 2) / 2 + 1, PW = (OW - 2) / 2 + 1;
+  // tensor-core route once the GEMM fills the GPU (two 128-row sub-tiles per CTA)
+  if (K <= 64 && fp32_math(Fp32Use::Conv) == Fp32Math::BF16X3 &&
+      4LL * N * PH * PW >= 256LL * c.sm_count() && 4LL * PH * PW * 64 * 4 <= kPoolIm2colChunkBytes) {
+    *handled = true;
+    return conv_pool_tc(c, x, N, H, W, Cin, w, bias, KH, KW, Cout, stride, pad, act | post_relu, PH,
+                        PW, out, os);
+  }
   if (K > 64 || Cout > 64 || !aligned16(w) || !aligned16(out) || (long long)N * PH >= (1LL << 31))
     return true;
   if (KH == 3 && KW == 3 && stride == 1 && pad == 1 && Cin == 3) {

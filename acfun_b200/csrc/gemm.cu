@@ -230,10 +230,10 @@ Fp32Math fp32_math(Fp32Use use) {
 
 // ------------------------------------------------------------------ launcher
 template <dev::MmaKind KIND, int BN, int STAGES, int NPASS, Epi EPI, bool AS, int BKB = 128,
-          bool BKM = false>
+          bool BKM = false, int MT = 1>
 static bool launch_one(Call& c, const Operand& A, const Operand& B, int M, int N, int K,
                        const EpiParams& ep, const ConvGeom& cg) {
-  using S = GemmShape<KIND, BN, STAGES, NPASS, BKB, BKM>;
+  using S = GemmShape<KIND, BN, STAGES, NPASS, BKB, BKM, MT>;
   static_assert(S::SMEM <= 232448, "shared memory budget");
   const CUtensorMapDataType dt = (KIND == dev::MmaKind::I8) ? CU_TENSOR_MAP_DATA_TYPE_UINT8
                                  : (KIND == dev::MmaKind::F16) ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
@@ -271,7 +271,7 @@ static bool launch_one(Call& c, const Operand& A, const Operand& B, int M, int N
       return false;
     }
   }
-  auto kern = gemm_tc_kernel<KIND, BN, STAGES, NPASS, EPI, AS, BKB, BKM>;
+  auto kern = gemm_tc_kernel<KIND, BN, STAGES, NPASS, EPI, AS, BKB, BKM, MT>;
   static bool attr_done[64] = {false};
   const int dv = current_device();
   if (dv >= 0 && dv < 64 && !attr_done[dv]) {
@@ -282,7 +282,7 @@ static bool launch_one(Call& c, const Operand& A, const Operand& B, int M, int N
     }
     attr_done[dv] = true;
   }
-  const long long tiles = (long long)((M + 127) / 128) * ((N + BN - 1) / BN);
+  const long long tiles = (long long)((M + S::BM - 1) / S::BM) * ((N + BN - 1) / BN);
   if (tiles >= (1LL << 31)) {
     set_error(kInvalid, "%s: problem too large", c.name());
     c.fail();
@@ -290,12 +290,15 @@ static bool launch_one(Call& c, const Operand& A, const Operand& B, int M, int N
   }
   // persistent: one CTA per SM (1 CTA/SM by shared memory), tiles strided over the grid
   const dim3 grid((unsigned)(tiles < c.sm_count() ? tiles : c.sm_count()));
-  kern<<<grid, S::THREADS, S::SMEM, c.stream()>>>(ta, tb, ep, cg, M, N, K, c.err());
+  // the implicit convolution walks cpad channels per tap in blocks of this variant's BKE
+  ConvGeom g = cg;
+  if (g.enabled) g.cblocks = g.cpad / S::BKE;
+  kern<<<grid, S::THREADS, S::SMEM, c.stream()>>>(ta, tb, ep, g, M, N, K, c.err());
   return c.launched("gemm_tc_kernel");
 }
 
-static long long tiles(int M, int N, int bn) {
-  return (long long)((M + 127) / 128) * ((N + bn - 1) / bn);
+static long long tiles(int M, int N, int bn, int bm = 128) {
+  return (long long)((M + bm - 1) / bm) * ((N + bn - 1) / bn);
 }
 
 int gemm_bke(GemmKind kind) {
@@ -380,8 +383,20 @@ bool gemm_launch(Call& c, GemmKind kind, Epi epi, const Operand& A, const Operan
     }
     case GemmKind::BF16X3: {
       if (epi != Epi::F32_BIAS) break;
+      // 256-column tiles in 64-byte K blocks: a quarter fewer operand bytes per MAC than
+      // 128-column tiles (the 3xBF16 main loop is bound by shared-memory fill from L2)
+      if (N > 128 && tiles(M, N, 256) >= sms)
+        return launch_one<MK::F16, 256, 4, 3, Epi::F32_BIAS, false, 64>(c, A, B, M, N, K, ep, cg);
+      // narrower N: two 128-row sub-tiles per CTA share each B stage, for the same bytes
+      // per MAC as the 256-column tile
+      if (N > 64 && tiles(M, N, 128, 256) >= sms)
+        return launch_one<MK::F16, 128, 4, 3, Epi::F32_BIAS, false, 64, false, 2>(c, A, B, M, N, K,
+                                                                                 ep, cg);
       if (N > 64 && tiles(M, N, 128) >= sms)
         return launch_one<MK::F16, 128, 3, 3, Epi::F32_BIAS, false>(c, A, B, M, N, K, ep, cg);
+      if (N > 32 && tiles(M, N, 64, 256) >= sms)
+        return launch_one<MK::F16, 64, 5, 3, Epi::F32_BIAS, false, 64, false, 2>(c, A, B, M, N, K,
+                                                                                ep, cg);
       return launch_one<MK::F16, 64, 4, 3, Epi::F32_BIAS, false>(c, A, B, M, N, K, ep, cg);
     }
     case GemmKind::TF32X3: {

@@ -55,6 +55,11 @@ struct EpiParams {
   void* split_out;
   long long split_plane;
   int sHp, sWp, spad, sC;
+  // F32_BIAS with pool4 (plain GEMM rows, no remap): rows come in groups of four, the 2x2
+  // window of one pooled pixel; the group's maximum is biased / activated and stored as
+  // pooled row r/4 -- of a ph x pw grid per image when it goes to split_out.
+  int pool4;
+  int ph, pw;
 };
 
 // Implicit convolution (stride 1) over a padded NHWC tensor viewed as A[rows][Cpad]:
@@ -97,21 +102,26 @@ struct KindTraits<dev::MmaKind::TF32> {
 // BKB_ = K bytes per pipeline block (128: SW128 K-major rows; 64: SW64, for operands whose
 // K run per tap is 64 bytes).  B_KMAJ: B is stored [N][K] (K contiguous) and loaded like A as
 // one BN-row tile; otherwise B is [K][N] (MN-major) and loaded in 128-byte N chunks.
-template <dev::MmaKind KIND, int BN, int STAGES, int NPASS, int BKB_ = 128, bool B_KMAJ = false>
+// MT: 128-row sub-tiles per CTA tile (BM = 128*MT); they share every B stage, each with its
+// own TMEM accumulator (MT*BN columns), which divides the B bytes per MAC by MT.
+template <dev::MmaKind KIND, int BN, int STAGES, int NPASS, int BKB_ = 128, bool B_KMAJ = false,
+          int MT_ = 1>
 struct GemmShape {
   static constexpr int ELEM = KindTraits<KIND>::ELEM;
-  static constexpr int BM = 128;
+  static constexpr int MT = MT_;
+  static constexpr int BM = 128 * MT;
   static constexpr int BKB = BKB_;                     // K bytes per block
   static constexpr int BKE = BKB / ELEM;               // K elements per block
   static constexpr int KSTEPS = BKB / 32;              // 32-byte MMA K-steps per block
   static constexpr int NOPS = (NPASS == 3) ? 2 : 1;    // hi/lo operand copies
-  static constexpr int A_TILE = BM * BKB;
+  static constexpr int A_TILE = 128 * BKB;             // one sub-tile
+  static constexpr int A_OP = MT * A_TILE;               // all sub-tiles of one operand copy
   static constexpr uint32_t K_LAYOUT = (BKB == 128) ? dev::UMMA_SW128 : dev::UMMA_SW64;
   static constexpr int K_SBO = 8 * BKB;                // 8-row core-matrix group stride
   static constexpr int NCHUNK = B_KMAJ ? 1 : BN * ELEM / 128;  // TMA boxes per B tile
   static constexpr int CHUNK_B = B_KMAJ ? BN * BKB : BKE * 128;
   static constexpr int B_TILE = NCHUNK * CHUNK_B;
-  static constexpr int STAGE = NOPS * (A_TILE + B_TILE);
+  static constexpr int STAGE = NOPS * (A_OP + B_TILE);
   // B descriptor advance per MMA K-step
   static constexpr int KSTEP_B = B_KMAJ ? 32 : (32 / ELEM) * 128;
   // MN-major 32-bit (tf32) operands only exist in the 128B swizzle with 32-byte atoms
@@ -121,7 +131,8 @@ struct GemmShape {
       B_KMAJ ? K_LAYOUT : (ELEM == 4) ? dev::UMMA_SW128_B32 : dev::UMMA_SW128;
   static constexpr int B_SBO = B_KMAJ ? K_SBO : (ELEM == 4) ? 512 : 1024;
   static constexpr int B_LBO = B_KMAJ ? 16 : CHUNK_B;
-  static constexpr int TMEM_COLS = 2 * BN;  // double-buffered accumulator
+  static constexpr int ACC_COLS = MT * BN;   // one accumulator buffer
+  static constexpr int TMEM_COLS = 2 * ACC_COLS;  // double-buffered
   // warps 0 (TMA) and 1 (MMA / TMEM), then EPI_WARPS epilogue warps: two per TMEM lane
   // quadrant, splitting the tile's 32-column chunks between them (even / odd chunks)
   static constexpr int EPI_WARPS = 8;
@@ -131,9 +142,11 @@ struct GemmShape {
   static constexpr int BAR_BYTES = ((2 * STAGES + 5) * 8 + 8 + 15) / 16 * 16;
   static constexpr int PARAM_BYTES = EPI_WARPS * CHUNKS_PER_WARP * (int)sizeof(ColSlice);
   static constexpr int SMEM = 1024 + STAGES * STAGE + BAR_BYTES + PARAM_BYTES;
-  static_assert(BKB == 128 || (BKB == 64 && B_KMAJ && NPASS == 1), "64-byte K blocks: K-major B");
+  static_assert(BKB == 128 || (BKB == 64 && (B_KMAJ ? NPASS == 1 : ELEM == 2)),
+                "64-byte K blocks: K-major int8 B or MN-major bf16 B");
   static_assert(B_KMAJ || BN * ELEM % 128 == 0, "B tile must be whole 128-byte chunks");
   static_assert(BN == 32 || BN == 64 || BN == 128 || BN == 256, "TMEM columns");
+  static_assert((MT == 1 || MT == 2 || MT == 4) && TMEM_COLS <= 512, "TMEM capacity");
 };
 
 __device__ __forceinline__ float relu_max(float v) { return v > 0.0f ? v : 0.0f; }
@@ -265,13 +278,7 @@ __device__ __forceinline__ void epi_store32(const EpiParams& ep, long long orow,
         uint16_t* lo = hi + ep.split_plane;
         uint32_t ph[16], pl[16];
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const uint16_t h0 = nx_bf16_rne(v[i]), h1 = nx_bf16_rne(v[i + 1]);
-          const uint16_t l0 = nx_bf16_rne(v[i] - nx_bf16_val(h0));
-          const uint16_t l1 = nx_bf16_rne(v[i + 1] - nx_bf16_val(h1));
-          ph[i / 2] = (uint32_t)h0 | ((uint32_t)h1 << 16);
-          pl[i / 2] = (uint32_t)l0 | ((uint32_t)l1 << 16);
-        }
+        for (int i = 0; i < 32; i += 2) nx_split_bf16x2(v[i], v[i + 1], ph[i / 2], pl[i / 2]);
         if (full) {
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
@@ -300,16 +307,55 @@ __device__ __forceinline__ void epi_store32(const EpiParams& ep, long long orow,
   }
 }
 
+// F32_BIAS with pool4: eight pooled columns j0..j0+7 of pooled row `orow` (their bias at
+// P.a[cs..cs+7]): bias, activation, fp32 or split-bf16 store.
+__device__ __forceinline__ void epi_store_pool8(const EpiParams& ep, long long orow, int j0, int N,
+                                                const float (&m)[8], const ColSlice& P, int cs) {
+  float v[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float x = __fadd_rn(m[i], P.a[cs + i]);
+    v[i] = ep.act ? relu_max(x) : x;
+  }
+  const bool full = j0 + 8 <= N;
+  if (ep.split_out) {
+    uint16_t* hi = reinterpret_cast<uint16_t*>(ep.split_out) + orow * ep.ldc + j0;
+    uint16_t* lo = hi + ep.split_plane;
+    uint32_t ph[4], pl[4];
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) nx_split_bf16x2(v[i], v[i + 1], ph[i / 2], pl[i / 2]);
+    if (full && ((reinterpret_cast<uintptr_t>(hi) | reinterpret_cast<uintptr_t>(lo)) & 15) == 0) {
+      *reinterpret_cast<uint4*>(hi) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
+      *reinterpret_cast<uint4*>(lo) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
+    } else {
+      for (int i = 0; i < 8; ++i)
+        if (j0 + i < N) {
+          hi[i] = (uint16_t)(ph[i / 2] >> (16 * (i & 1)));
+          lo[i] = (uint16_t)(pl[i / 2] >> (16 * (i & 1)));
+        }
+    }
+    return;
+  }
+  float* dst = reinterpret_cast<float*>(ep.C) + orow * ep.ldc + j0;
+  if (full && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+    reinterpret_cast<float4*>(dst)[0] = make_float4(v[0], v[1], v[2], v[3]);
+    reinterpret_cast<float4*>(dst)[1] = make_float4(v[4], v[5], v[6], v[7]);
+  } else {
+    for (int i = 0; i < 8; ++i)
+      if (j0 + i < N) dst[i] = v[i];
+  }
+}
+
 // Persistent kernel: grid = min(#tiles, #SMs); CTA b walks tiles b, b+grid, ...  The smem
 // ring runs continuously across tiles, and the accumulator is double-buffered in TMEM
 // (2 x BN columns): the UMMA warp fills buffer i&1 while the epilogue warps drain the
 // other, so a tile's epilogue overlaps the next tile's MMAs.
 template <dev::MmaKind KIND, int BN, int STAGES, int NPASS, Epi EPI, bool A_SIGNED, int BKB = 128,
-          bool B_KMAJ = false>
+          bool B_KMAJ = false, int MT = 1>
 __global__ void __launch_bounds__(320, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    EpiParams ep, ConvGeom cg, int M, int N, int K, unsigned* err) {
-  using S = GemmShape<KIND, BN, STAGES, NPASS, BKB, B_KMAJ>;
+  using S = GemmShape<KIND, BN, STAGES, NPASS, BKB, B_KMAJ, MT>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -394,19 +440,25 @@ __global__ void __launch_bounds__(320, 1)
         }
 #pragma unroll
         for (int op = 0; op < S::NOPS; ++op) {
-          uint8_t* a_dst = st + op * S::A_TILE;
-          uint8_t* b_dst = st + S::NOPS * S::A_TILE + op * S::B_TILE;
+          uint8_t* a_dst = st + op * S::A_OP;
+          uint8_t* b_dst = st + S::NOPS * S::A_OP + op * S::B_TILE;
           if constexpr (B_KMAJ) {
-            dev::tma_load_2d(a_dst, &tmA, &full_bar[s], kx, ay);
+#pragma unroll
+            for (int i = 0; i < MT; ++i)
+              dev::tma_load_2d(a_dst + i * S::A_TILE, &tmA, &full_bar[s], kx, ay + 128 * i);
             dev::tma_load_2d(b_dst, &tmB, &full_bar[s], by, n0);
           } else if constexpr (S::NOPS == 1) {
-            dev::tma_load_2d(a_dst, &tmA, &full_bar[s], kx, ay);
+#pragma unroll
+            for (int i = 0; i < MT; ++i)
+              dev::tma_load_2d(a_dst + i * S::A_TILE, &tmA, &full_bar[s], kx, ay + 128 * i);
 #pragma unroll
             for (int c = 0; c < S::NCHUNK; ++c)
               dev::tma_load_2d(b_dst + c * S::CHUNK_B, &tmB, &full_bar[s],
                                n0 + c * (128 / S::ELEM), by);
           } else {
-            dev::tma_load_3d(a_dst, &tmA, &full_bar[s], kx, ay, op);
+#pragma unroll
+            for (int i = 0; i < MT; ++i)
+              dev::tma_load_3d(a_dst + i * S::A_TILE, &tmA, &full_bar[s], kx, ay + 128 * i, op);
 #pragma unroll
             for (int c = 0; c < S::NCHUNK; ++c)
               dev::tma_load_3d(b_dst + c * S::CHUNK_B, &tmB, &full_bar[s],
@@ -439,7 +491,7 @@ __global__ void __launch_bounds__(320, 1)
     // to the 14-bit start-address field (addresses are below 256 KB, so it never carries).
     const uint32_t smem_base = dev::smem_u32(smem);
     const uint64_t a_desc0 = dev::umma_sdesc(smem_base, 16, S::K_SBO, S::K_LAYOUT);
-    const uint64_t b_desc0 = dev::umma_sdesc(smem_base + S::NOPS * S::A_TILE, S::B_LBO, S::B_SBO,
+    const uint64_t b_desc0 = dev::umma_sdesc(smem_base + S::NOPS * S::A_OP, S::B_LBO, S::B_SBO,
                                              S::B_LAYOUT);
     bool ok = true;
     uint32_t it = 0, local = 0;
@@ -451,7 +503,7 @@ __global__ void __launch_bounds__(320, 1)
         break;
       }
       dev::tc_fence_after();
-      const uint32_t d_tmem = tmem + buf * BN;
+      const uint32_t d_tmem = tmem + buf * S::ACC_COLS;
       for (int kb = 0; kb < nkb; ++kb, ++it) {
         if (!dev::mbar_wait(&full_bar[s], ph, err)) {
           ok = false;
@@ -461,20 +513,23 @@ __global__ void __launch_bounds__(320, 1)
         const uint64_t soff = (uint64_t)((s * (uint32_t)S::STAGE) >> 4);
 #pragma unroll
         for (int ks = 0; ks < S::KSTEPS; ++ks) {
-          if constexpr (NPASS == 1) {
-            const uint64_t ad = a_desc0 + soff + (uint64_t)(ks * 32 / 16);
-            const uint64_t bd = b_desc0 + soff + (uint64_t)(ks * S::KSTEP_B / 16);
-            dev::umma<KIND>(d_tmem, ad, bd, idesc, (kb | ks) != 0);
-          } else {
-            // (a_op, b_op): lo*hi, hi*lo, hi*hi
-            const int aop[3] = {1, 0, 0}, bop[3] = {0, 1, 0};
 #pragma unroll
-            for (int p = 0; p < 3; ++p) {
-              const uint64_t ad =
-                  a_desc0 + soff + (uint64_t)((aop[p] * S::A_TILE + ks * 32) / 16);
-              const uint64_t bd =
-                  b_desc0 + soff + (uint64_t)((bop[p] * S::B_TILE + ks * S::KSTEP_B) / 16);
-              dev::umma<KIND>(d_tmem, ad, bd, idesc, (kb | ks | p) != 0);
+          for (int i = 0; i < MT; ++i) {
+            if constexpr (NPASS == 1) {
+              const uint64_t ad = a_desc0 + soff + (uint64_t)((i * S::A_TILE + ks * 32) / 16);
+              const uint64_t bd = b_desc0 + soff + (uint64_t)(ks * S::KSTEP_B / 16);
+              dev::umma<KIND>(d_tmem + i * BN, ad, bd, idesc, (kb | ks) != 0);
+            } else {
+              // (a_op, b_op): lo*hi, hi*lo, hi*hi
+              const int aop[3] = {1, 0, 0}, bop[3] = {0, 1, 0};
+#pragma unroll
+              for (int p = 0; p < 3; ++p) {
+                const uint64_t ad = a_desc0 + soff +
+                                    (uint64_t)((aop[p] * S::A_OP + i * S::A_TILE + ks * 32) / 16);
+                const uint64_t bd =
+                    b_desc0 + soff + (uint64_t)((bop[p] * S::B_TILE + ks * S::KSTEP_B) / 16);
+                dev::umma<KIND>(d_tmem + i * BN, ad, bd, idesc, (kb | ks | p) != 0);
+              }
             }
           }
         }
@@ -518,31 +573,66 @@ __global__ void __launch_bounds__(320, 1)
       const bool ok = dev::mbar_wait(&tfull_bar[buf], use & 1, err);
       dev::tc_fence_after();
       if (!ok || *abort_flag) break;
-      const int r = m0 + q * 32 + lane;
-      bool zero_out = ep.zero_flag && *ep.zero_flag;
-      float img_sa = 0.0f;
-      long long orow = r;
-      bool store = r < M;
-      if (ep.img_sa && store) {
-        const int n = r / ep.img_rows;
-        img_sa = ep.img_sa[n];
-        zero_out = ep.img_zero[n] != 0;
-      }
-      if (ep.remap && store) {
-        const int n = r / ep.img_rows, qq = r - n * ep.img_rows;
-        const int oh = qq / ep.Wp, ow = qq - oh * ep.Wp;
-        store = (oh < ep.OH) && (ow < ep.OW);
-        orow = ep.split_out ? ((long long)n * ep.sHp + oh + ep.spad) * ep.sWp + ow + ep.spad
-                            : ((long long)n * ep.OH + oh) * ep.OW + ow;
-      }
 #pragma unroll 1
-      for (int k = 0; k < S::CHUNKS_PER_WARP; ++k) {
-        const int c0 = h * 32 + 64 * k;
-        if (c0 >= BN || n0 + c0 >= N) break;  // warp-uniform
-        uint32_t v[32];
-        dev::tmem_ld32(tmem + buf * BN + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
-        dev::tmem_ld_wait();
-        if (store) epi_store32<EPI>(ep, orow, n0 + c0, N, v, my[k], zero_out, img_sa);
+      for (int i = 0; i < MT; ++i) {  // 128-row sub-tiles
+        const int r = m0 + 128 * i + q * 32 + lane;
+        bool zero_out = ep.zero_flag && *ep.zero_flag;
+        float img_sa = 0.0f;
+        long long orow = r;
+        bool store = r < M;
+        if (ep.img_sa && store) {
+          const int n = r / ep.img_rows;
+          img_sa = ep.img_sa[n];
+          zero_out = ep.img_zero[n] != 0;
+        }
+        if (ep.remap && store) {
+          const int n = r / ep.img_rows, qq = r - n * ep.img_rows;
+          const int oh = qq / ep.Wp, ow = qq - oh * ep.Wp;
+          store = (oh < ep.OH) && (ow < ep.OW);
+          orow = ep.split_out ? ((long long)n * ep.sHp + oh + ep.spad) * ep.sWp + ow + ep.spad
+                              : ((long long)n * ep.OH + oh) * ep.OW + ow;
+        }
+        if (ep.pool4) {
+          const int P = r >> 2;
+          orow = P;
+          if (ep.split_out) {
+            const int per = ep.ph * ep.pw, n = P / per, rem = P - n * per, py = rem / ep.pw;
+            orow = ((long long)n * ep.sHp + py + ep.spad) * ep.sWp + (rem - py * ep.pw) + ep.spad;
+          }
+        }
+#pragma unroll 1
+        for (int k = 0; k < S::CHUNKS_PER_WARP; ++k) {
+          const int c0 = h * 32 + 64 * k;
+          if (c0 >= BN || n0 + c0 >= N) break;  // warp-uniform
+          uint32_t v[32];
+          dev::tmem_ld32(
+              tmem + buf * S::ACC_COLS + (uint32_t)(i * BN + c0) + ((uint32_t)(q * 32) << 16), v);
+          dev::tmem_ld_wait();
+          if constexpr (EPI == Epi::F32_BIAS) {
+            if (ep.pool4) {
+              // warp-uniform.  The window's four rows are lanes 4g..4g+3: a reduce-scatter
+              // over them leaves lane 4g+s with the maxima of columns 8s..8s+7.
+              const int s4 = lane & 3;
+              const bool up = (s4 & 2) != 0, odd = (s4 & 1) != 0;
+              float k16[16], m8[8];
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const float send = __uint_as_float(up ? v[j] : v[16 + j]);
+                const float keep = __uint_as_float(up ? v[16 + j] : v[j]);
+                k16[j] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, 2));
+              }
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const float send = odd ? k16[j] : k16[8 + j];
+                const float keep = odd ? k16[8 + j] : k16[j];
+                m8[j] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, 1));
+              }
+              if (store) epi_store_pool8(ep, orow, n0 + c0 + 8 * s4, N, m8, my[k], 8 * s4);
+              continue;
+            }
+          }
+          if (store) epi_store32<EPI>(ep, orow, n0 + c0, N, v, my[k], zero_out, img_sa);
+        }
       }
       dev::tc_fence_before();
       __syncwarp();

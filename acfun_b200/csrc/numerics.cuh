@@ -24,23 +24,28 @@ static __device__ __forceinline__ float nx_bf16_val(uint16_t h) {
   return __uint_as_float((uint32_t)h << 16);
 }
 
+// 3xBF16 split of a pair on the hardware converter (cvt.rn.bf16x2.f32 rounds to nearest
+// even, the same bits as nx_bf16_rne for every non-NaN input): hi = bf16(a) | bf16(b) << 16,
+// lo = the bf16 of the exact remainders a - hi, b - hi in the same packing.
+static __device__ __forceinline__ void nx_split_bf16x2(float a, float b, uint32_t& hi,
+                                                       uint32_t& lo) {
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(hi) : "f"(b), "f"(a));
+  const float ra = a - __uint_as_float(hi << 16), rb = b - __uint_as_float(hi & 0xffff0000u);
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(lo) : "f"(rb), "f"(ra));
+}
+
 // Store the split of 4 consecutive values at element index 4*i of the hi plane and the same
 // index of the lo plane (op_stride elements further).
 template <bool BF>
 static __device__ __forceinline__ void nx_store_split4(void* dst, size_t i4, size_t op_stride,
                                                        const float (&v)[4]) {
   if constexpr (BF) {
-    uint16_t h[4], l[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      h[k] = nx_bf16_rne(v[k]);
-      l[k] = nx_bf16_rne(v[k] - nx_bf16_val(h[k]));
-    }
+    uint32_t h0, l0, h1, l1;
+    nx_split_bf16x2(v[0], v[1], h0, l0);
+    nx_split_bf16x2(v[2], v[3], h1, l1);
     uint16_t* d = reinterpret_cast<uint16_t*>(dst) + 4 * i4;
-    *reinterpret_cast<uint2*>(d) =
-        make_uint2((uint32_t)h[0] | ((uint32_t)h[1] << 16), (uint32_t)h[2] | ((uint32_t)h[3] << 16));
-    *reinterpret_cast<uint2*>(d + op_stride) =
-        make_uint2((uint32_t)l[0] | ((uint32_t)l[1] << 16), (uint32_t)l[2] | ((uint32_t)l[3] << 16));
+    *reinterpret_cast<uint2*>(d) = make_uint2(h0, h1);
+    *reinterpret_cast<uint2*>(d + op_stride) = make_uint2(l0, l1);
   } else {
     float h[4], l[4];
 #pragma unroll

@@ -170,3 +170,38 @@ def test_conv_f32_last_wave_images(acf, orc):
     orc.oracle().orc_conv2d(np.ascontiguousarray(x[N - 3:]), 3, H, W, Cin, w, b.ctypes.data, 3, 3, Cout, 1, 1,
                             1, ref, 1)
     assert max_rel(got[N - 3:], ref) < TOL_F32, max_rel(got[N - 3:], ref)
+
+
+def test_conv_f32_wide_tiles_vs_oracle(acf, orc):
+    """16 x 28 x 28, 96 -> 320: 226 implicit-GEMM tiles of 128 x 256 in 64-byte K blocks
+    (Cin padded to 128, Cout ragged in the second column tile); first and last images."""
+    N, H, W, Cin, Cout = 16, 28, 28, 96, 320
+    g = np.random.default_rng(320)
+    x = g.uniform(0, 1, (N, H, W, Cin)).astype(np.float32)
+    w = he(g, (9 * Cin, Cout), 9 * Cin)
+    b = g.uniform(-0.1, 0.1, Cout).astype(np.float32)
+    got = acf.conv2d(x, w, b, 3, 3, Cout, 1, 1, 1)
+    for sl in (slice(0, 2), slice(N - 2, N)):
+        ref = np.empty((2, H, W, Cout), np.float32)
+        orc.oracle().orc_conv2d(np.ascontiguousarray(x[sl]), 2, H, W, Cin, w, b.ctypes.data, 3, 3, Cout, 1,
+                                1, 1, ref, 1)
+        assert max_rel(got[sl], ref) < TOL_F32, max_rel(got[sl], ref)
+
+
+@pytest.mark.parametrize("N,H,W,Cout", [(12, 56, 56, 96), (14, 50, 50, 48)])
+def test_conv_f32_paired_subtiles_vs_oracle(acf, orc, N, H, W, Cout):
+    """Implicit GEMMs with two 128-row sub-tiles per CTA sharing each weight stage (Cout 96
+    on 128-column tiles, 48 on 64-column tiles); the last images sit in the second wave, and
+    at 14 x 52 x 52 padded rows the last tile's second sub-tile is past the end."""
+    Cin = 64
+    g = np.random.default_rng(N * 1000 + Cout)
+    x = g.uniform(0, 1, (N, H, W, Cin)).astype(np.float32)
+    w = he(g, (9 * Cin, Cout), 9 * Cin)
+    b = g.uniform(-0.1, 0.1, Cout).astype(np.float32)
+    got = acf.conv2d(x, w, b, 3, 3, Cout, 1, 1, 1)
+    for sl in (slice(0, 1), slice(N - 2, N)):
+        n = sl.stop - sl.start
+        ref = np.empty((n, H, W, Cout), np.float32)
+        orc.oracle().orc_conv2d(np.ascontiguousarray(x[sl]), n, H, W, Cin, w, b.ctypes.data, 3, 3, Cout, 1,
+                                1, 1, ref, 1)
+        assert max_rel(got[sl], ref) < TOL_F32, max_rel(got[sl], ref)

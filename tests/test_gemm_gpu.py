@@ -100,7 +100,10 @@ def test_gemm_s8_requant_full_size_sampled(acf, orc, M, N, K):
 
 
 @pytest.mark.parametrize("M,N,K", [(64, 64, 64), (100, 100, 100), (255, 255, 255), (1024, 1024, 1024),
-                                   (33, 47, 129), (300, 24, 144), (1, 1000, 4096), (512, 17, 64)])
+                                   (33, 47, 129), (300, 24, 144), (1, 1000, 4096), (512, 17, 64),
+                                   (10240, 300, 200),    # 256-column tiles, ragged N and K
+                                   (40000, 100, 136),    # two 128-row sub-tiles per CTA, N 128
+                                   (37856, 40, 72)])     # the same at N 64; last sub-tile empty
 def test_gemm_f32_tolerance(acf, orc, M, N, K):
     g = np.random.default_rng(M + N + K)
     A = g.uniform(-1, 1, (M, K)).astype(np.float32)

@@ -155,7 +155,8 @@ def test_model_int8_conv_pool_fusion_bit_exact(acf, tmp_path, st, post_relu, cin
 
 @pytest.mark.parametrize("hw", [(224, 224), (37, 29)])
 def test_fused_conv1_pool_bit_exact_vs_separate_calls(acf, tmp_path, hw):
-    """The fused 3x3 / Cin 3 conv + 2x2 pool kernel (packed f32x2 FMAs) against acfun_conv2d
+    """The fused CUDA-core 3x3 / Cin 3 conv + 2x2 pool kernel (packed f32x2 FMAs; the route
+    in 3xTF32 mode, where the tensor-core conv + pool route is off) against acfun_conv2d
     (CUDA-core route, scalar fma chain) followed by acfun_maxpool: identical bits."""
     from acfun_b200.acfun0 import Acfun0Writer
     H, W = hw
@@ -166,9 +167,40 @@ def test_fused_conv1_pool_bit_exact_vs_separate_calls(acf, tmp_path, hw):
     Wr.conv(w, b, 3, 3, 64, 1, 1).maxpool(2, 2, 0)
     p = tmp_path / "c1.acfun"
     p.write_bytes(Wr.tobytes())
+    L = acf.lib()
+    assert L.acfun_set_fp32_math(1) == 0
+    try:
+        m = acf.Model(str(p))
+        x = g.uniform(-1, 1, (2, H, W, 3)).astype(np.float32)
+        y = m.infer_batch(x)
+        ref = acf.maxpool(acf.conv2d(x, w, b, 3, 3, 64, 1, 1, 0), 2, 2, 0)
+        assert_bits_equal(y, ref.reshape(y.shape), "fused conv1 + pool")
+        m.close()
+    finally:
+        L.acfun_set_fp32_math(0)
+
+
+@pytest.mark.parametrize("hw,nxt", [((224, 224), False), ((224, 224), True), ((223, 221), True)])
+def test_conv1_pool_tensor_route_vs_oracle(acf, tmp_path, hw, nxt):
+    """Conv (K = 27) + 2x2 pool on the tensor cores: pooled-order im2col and a 3xBF16 GEMM
+    that pools in its epilogue, writing fp32 or (nxt) the next conv's split input; odd sizes
+    drop the last row / column like the pool."""
+    from acfun_b200.acfun0 import Acfun0Writer
+    from oracle.model_oracle import OracleModel
+    H, W = hw
+    g = np.random.default_rng(H + W + nxt)
+    u = lambda *s: g.uniform(-0.5, 0.5, size=s).astype(np.float32)
+    Wr = Acfun0Writer(3, H, W)
+    Wr.conv(u(27, 64), u(64), 3, 3, 64, 1, 1).relu().maxpool(2, 2, 0)
+    if nxt:
+        Wr.conv(u(576, 64) * 0.2, u(64), 3, 3, 64, 1, 1).relu()
+    blob = Wr.tobytes()
+    p = tmp_path / "c1t.acfun"
+    p.write_bytes(blob)
     m = acf.Model(str(p))
-    x = g.uniform(-1, 1, (2, H, W, 3)).astype(np.float32)
+    x = g.uniform(0, 1, (2, H, W, 3)).astype(np.float32)
     y = m.infer_batch(x)
-    ref = acf.maxpool(acf.conv2d(x, w, b, 3, 3, 64, 1, 1, 0), 2, 2, 0)
-    assert_bits_equal(y, ref.reshape(y.shape), "fused conv1 + pool")
+    om = OracleModel(blob)
+    for k in range(2):
+        assert max_rel(y[k], om.infer(x[k]).reshape(y[k].shape)) < TOL_F32
     m.close()
