@@ -70,9 +70,13 @@ bool conv_pool_dev(Call& c, const float* x, int N, int H, int W, int Cin, const 
 
 // The same router over a batch with one activation scale per image, i.e. N separate
 // calls of acfun_conv2d_int8 (the reference's per-image model harness) in one pass.
+// in_max: the input's per-image max |x| already accumulated by its producer (skips the absmax
+// pass); out_max: accumulate the output's per-image max |y| (zeroed by the caller) for the next
+// int8 layer.
 bool conv2d_int8_batch_dev(Call& c, const float* x, int N, int H, int W, int Cin,
                            const int8_t* wq, const float* wscale, const float* bias, int KH,
-                           int KW, int Cout, int stride, int pad, float* out, int act);
+                           int KW, int Cout, int stride, int pad, float* out, int act,
+                           const unsigned* in_max = nullptr, unsigned* out_max = nullptr);
 
 // conv2d_int8_batch_dev immediately followed by max-pool(2, 2, 0, post_relu), fused for small-K
 // non-Winograd routes (sets *handled; otherwise nothing is launched).  Bit-identical to the two
@@ -80,7 +84,7 @@ bool conv2d_int8_batch_dev(Call& c, const float* x, int N, int H, int W, int Cin
 bool conv_int8_pool_dev(Call& c, const float* x, int N, int H, int W, int Cin, const int8_t* wq,
                         const float* wscale, const float* bias, int KH, int KW, int Cout,
                         int stride, int pad, int act, int pool, int pst, int ppd, int post_relu,
-                        float* out, bool* handled);
+                        float* out, bool* handled, unsigned* out_max = nullptr);
 
 // int8 conv router (conv_int8.cpp:63-148) on device pointers.
 bool conv2d_int8_dev(Call& c, const float* x, int N, int H, int W, int Cin, const int8_t* wq,

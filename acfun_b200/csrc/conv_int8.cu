@@ -459,6 +459,8 @@ struct Int8ConvArgs {
   const float* img_inv = nullptr;
   const float* img_sa = nullptr;
   const int* img_zero = nullptr;
+  // per-image max |output| accumulator for the next int8 layer (EpiParams::img_absmax)
+  unsigned* out_max = nullptr;
 };
 
 // K-major weight layout a convolution's GEMM uses: implicit route (stride 1, Cin >= 32):
@@ -501,6 +503,7 @@ static bool int8_conv_gemm(Call& c, const Int8ConvArgs& a, int N, int H, int W, 
   ep.zero_flag = a.zero_flag;
   ep.img_sa = a.img_sa;
   ep.img_zero = a.img_zero;
+  ep.img_absmax = a.out_max;
   uint8_t* xq_dense = nullptr;  // unpadded u8 input for the gather path
   const Int8BLayout lay = int8_b_layout(Cin, KH, KW, stride);
   if (lay.implicit) {
@@ -706,9 +709,22 @@ __global__ void k_absmax_img(const float* __restrict__ x, long long per_img, uns
     }
 }
 
+// k_absmax_img's per-image derivation from a maximum its producer already accumulated
+// (EpiParams::img_absmax, k_maxpool4, k_conv_int8_pool): the same expressions.
+__global__ void k_int8_img_scalars(const unsigned* __restrict__ maxa, int N, float* inv, float* sa,
+                                   int* zero) {
+  for (int n = blockIdx.x * blockDim.x + threadIdx.x; n < N; n += gridDim.x * blockDim.x) {
+    const float mx = __uint_as_float(maxa[n]);
+    zero[n] = mx < 1e-12f ? 1 : 0;
+    inv[n] = __fdiv_rn(127.0f, mx);
+    sa[n] = __fdiv_rn(mx, 127.0f);
+  }
+}
+
 bool conv2d_int8_batch_dev(Call& c, const float* x, int N, int H, int W, int Cin,
                            const int8_t* wq, const float* wscale, const float* bias, int KH,
-                           int KW, int Cout, int stride, int pad, float* out, int act) {
+                           int KW, int Cout, int stride, int pad, float* out, int act,
+                           const unsigned* in_max, unsigned* out_max) {
   const int OH = (H + 2 * pad - KH) / stride + 1, OW = (W + 2 * pad - KW) / stride + 1;
   if (OH <= 0 || OW <= 0 || N <= 0) return true;
   if (N > 65535) {
@@ -726,11 +742,15 @@ bool conv2d_int8_batch_dev(Call& c, const float* x, int N, int H, int W, int Cin
   if (!words || !inv || !sa || !zero || !Sw || !wk) return false;
   k_int8_wprep<<<Cout, 128, 0, c.stream()>>>(wq, lay.taps, lay.cin, Cout, lay.cpad, wk, Sw, words,
                                               2 * N);
-  const long long per = (long long)H * W * Cin;
-  long long bx = per / (4 * 256 * 4);
-  bx = bx < 1 ? 1 : (bx > 64 ? 64 : bx);
-  k_absmax_img<<<dim3((unsigned)bx, (unsigned)N), 256, 0, c.stream()>>>(
-      x, per, words, words + N, inv, sa, zero, nullptr, nullptr, nullptr, 0, nullptr);
+  if (in_max) {
+    k_int8_img_scalars<<<(N + 127) / 128, 128, 0, c.stream()>>>(in_max, N, inv, sa, zero);
+  } else {
+    const long long per = (long long)H * W * Cin;
+    long long bx = per / (4 * 256 * 4);
+    bx = bx < 1 ? 1 : (bx > 64 ? 64 : bx);
+    k_absmax_img<<<dim3((unsigned)bx, (unsigned)N), 256, 0, c.stream()>>>(
+        x, per, words, words + N, inv, sa, zero, nullptr, nullptr, nullptr, 0, nullptr);
+  }
   if (!c.launched("int8 per-image params")) return false;
   const bool wino = is_wino_route(H, W, Cin, KH, KW, Cout, stride, pad);
   Int8ConvArgs a;
@@ -743,6 +763,7 @@ bool conv2d_int8_batch_dev(Call& c, const float* x, int N, int H, int W, int Cin
   a.f0 = wscale;
   a.f1 = bias;
   a.i0 = Sw;
+  a.out_max = out_max;
   return int8_conv_gemm(c, a, N, H, W, Cin, wq, KH, KW, Cout, stride, pad, out, act, wk);
 }
 
@@ -804,8 +825,10 @@ __global__ void __launch_bounds__(128) k_conv_int8_pool(
     const float* __restrict__ x, int H, int W, int Cin, const uint32_t* __restrict__ wpk,
     const float* __restrict__ ab, int Cout, int KH, int KW, int stride, int pad, int PH, int PW,
     const float* __restrict__ img_inv, const int* __restrict__ img_zero, float* __restrict__ out,
-    int act, int post_relu) {
+    int act, int post_relu, unsigned* __restrict__ out_max) {
   extern __shared__ uint4 ip_sm4[];
+  __shared__ float am_red[4];
+  float am = 0.0f;  // max |stored value| of this block (one image): out_max
   const int taps = KH * KW;
   const int Wp = W + 2 * pad, ROWS = stride + KH;
   uint32_t* wsm = reinterpret_cast<uint32_t*>(ip_sm4);  // [taps][CW][Cout]
@@ -924,6 +947,23 @@ __global__ void __launch_bounds__(128) k_conv_int8_pool(
         r.z = r.z > 0.f ? r.z : 0.f; r.w = r.w > 0.f ? r.w : 0.f;
       }
       reinterpret_cast<float4*>(dst)[q] = r;
+      amax_acc(am, r.x);
+      amax_acc(am, r.y);
+      amax_acc(am, r.z);
+      amax_acc(am, r.w);
+    }
+  }
+  if (out_max) {  // block-uniform
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float u = __shfl_xor_sync(0xffffffffu, am, o);
+      am = (am < u) ? u : am;
+    }
+    if ((threadIdx.x & 31) == 0) am_red[threadIdx.x >> 5] = am;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      for (int w = 1; w < (int)(blockDim.x >> 5); ++w) am = (am < am_red[w]) ? am_red[w] : am;
+      if (am > 0.0f) atomicMax(&out_max[n], __float_as_uint(am));
     }
   }
 }
@@ -932,7 +972,7 @@ __global__ void __launch_bounds__(128) k_conv_int8_pool(
 bool conv_int8_pool_dev(Call& c, const float* x, int N, int H, int W, int Cin, const int8_t* wq,
                         const float* wscale, const float* bias, int KH, int KW, int Cout,
                         int stride, int pad, int act, int pool, int pst, int ppd, int post_relu,
-                        float* out, bool* handled) {
+                        float* out, bool* handled, unsigned* out_max) {
   *handled = false;
   const int OH = (H + 2 * pad - KH) / stride + 1, OW = (W + 2 * pad - KW) / stride + 1;
   if (pool != 2 || pst != 2 || ppd != 0 || OH < 2 || OW < 2 || N <= 0 || N > 65535) return true;
@@ -960,7 +1000,8 @@ bool conv_int8_pool_dev(Call& c, const float* x, int N, int H, int W, int Cin, c
       x, per, words, words + N, inv, sa, zero, wscale, bias, Sw, Cout, ab);
 #define ACF_I8POOL(CWV)                                                                        \
   k_conv_int8_pool<CWV><<<N * PH, 128, (size_t)smem, c.stream()>>>(                            \
-      x, H, W, Cin, wpk, ab, Cout, KH, KW, stride, pad, PH, PW, inv, zero, out, act, post_relu)
+      x, H, W, Cin, wpk, ab, Cout, KH, KW, stride, pad, PH, PW, inv, zero, out, act, post_relu,  \
+      out_max)
   if (CW == 1)
     ACF_I8POOL(1);
   else if (CW == 2)

@@ -60,6 +60,10 @@ struct EpiParams {
   // pooled row r/4 -- of a ph x pw grid per image when it goes to split_out.
   int pool4;
   int ph, pw;
+  // when non-NULL (float epilogues): img_absmax[n] = max(img_absmax[n], max |stored value| of
+  // image n = r / img_rows), an atomicMax on the bits of a non-negative float -- the next int8
+  // convolution's per-image activation maximum, folded into the producer.
+  unsigned* img_absmax;
 };
 
 // Implicit convolution (stride 1) over a padded NHWC tensor viewed as A[rows][Cpad]:
@@ -183,10 +187,26 @@ __device__ __forceinline__ void lds32(const T* p, T (&o)[32]) {
   }
 }
 
+// Fold one warp's row maxima (lane's image n, or -1 for a row it does not store) into
+// img_absmax: one atomic per warp when the rows share an image.
+__device__ __forceinline__ void amax_flush(unsigned* img_absmax, int n, float am) {
+  const int n0 = __shfl_sync(0xffffffffu, n, 0);
+  if (__all_sync(0xffffffffu, n == n0 || n < 0)) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float u = __shfl_xor_sync(0xffffffffu, am, o);
+      am = (am < u) ? u : am;
+    }
+    if ((threadIdx.x & 31) == 0 && n0 >= 0 && am > 0.0f) atomicMax(&img_absmax[n0], __float_as_uint(am));
+  } else if (n >= 0 && am > 0.0f) {
+    atomicMax(&img_absmax[n], __float_as_uint(am));
+  }
+}
+
 template <Epi EPI>
 __device__ __forceinline__ void epi_store32(const EpiParams& ep, long long orow, int j0, int N,
                                             const uint32_t (&r)[32], const ColSlice& P,
-                                            bool zero, float img_sa) {
+                                            bool zero, float img_sa, float& am) {
   // 32 outputs for columns j0..j0+31 of output row `orow`
   const bool full = (j0 + 32 <= N);
   if constexpr (EPI == Epi::S32) {
@@ -271,6 +291,11 @@ __device__ __forceinline__ void epi_store32(const EpiParams& ep, long long orow,
       if (ep.act) x = relu_max(x);
       v[i] = zero ? 0.0f : x;
     }
+    if (ep.img_absmax) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (j0 + i < N) amax_acc(am, v[i]);
+    }
     if constexpr (EPI == Epi::F32_BIAS) {
       if (ep.split_out) {
         // hi = bf16(v), lo = bf16(v - hi): the split k_pad_split4 makes of an fp32 input
@@ -310,12 +335,18 @@ __device__ __forceinline__ void epi_store32(const EpiParams& ep, long long orow,
 // F32_BIAS with pool4: eight pooled columns j0..j0+7 of pooled row `orow` (their bias at
 // P.a[cs..cs+7]): bias, activation, fp32 or split-bf16 store.
 __device__ __forceinline__ void epi_store_pool8(const EpiParams& ep, long long orow, int j0, int N,
-                                                const float (&m)[8], const ColSlice& P, int cs) {
+                                                const float (&m)[8], const ColSlice& P, int cs,
+                                                float& am) {
   float v[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const float x = __fadd_rn(m[i], P.a[cs + i]);
     v[i] = ep.act ? relu_max(x) : x;
+  }
+  if (ep.img_absmax) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (j0 + i < N) amax_acc(am, v[i]);
   }
   const bool full = j0 + 8 <= N;
   if (ep.split_out) {
@@ -600,6 +631,8 @@ __global__ void __launch_bounds__(320, 1)
             orow = ((long long)n * ep.sHp + py + ep.spad) * ep.sWp + (rem - py * ep.pw) + ep.spad;
           }
         }
+        float am = 0.0f;  // this row's max |stored value| (img_absmax)
+        const int nimg = (ep.img_absmax && store) ? r / ep.img_rows : -1;
 #pragma unroll 1
         for (int k = 0; k < S::CHUNKS_PER_WARP; ++k) {
           const int c0 = h * 32 + 64 * k;
@@ -627,12 +660,13 @@ __global__ void __launch_bounds__(320, 1)
                 const float keep = odd ? k16[8 + j] : k16[j];
                 m8[j] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, 1));
               }
-              if (store) epi_store_pool8(ep, orow, n0 + c0 + 8 * s4, N, m8, my[k], 8 * s4);
+              if (store) epi_store_pool8(ep, orow, n0 + c0 + 8 * s4, N, m8, my[k], 8 * s4, am);
               continue;
             }
           }
-          if (store) epi_store32<EPI>(ep, orow, n0 + c0, N, v, my[k], zero_out, img_sa);
+          if (store) epi_store32<EPI>(ep, orow, n0 + c0, N, v, my[k], zero_out, img_sa, am);
         }
+        if (ep.img_absmax) amax_flush(ep.img_absmax, nimg, am);  // warp-uniform
       }
       dev::tc_fence_before();
       __syncwarp();

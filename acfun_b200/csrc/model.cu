@@ -360,10 +360,31 @@ static bool run_model(Call& c, AcfunModel* m, int n, const float* x, float* y) {
     os.plane = (long long)n * (Hn + 2 * os.pad) * (Wn + 2 * os.pad) * Cn;
     return true;
   };
+  // int8 mode: a conv whose output feeds a dense int8 conv directly accumulates that output's
+  // per-image max |y| (the next conv's activation scale) in its epilogue as it stores it, so
+  // the next conv skips its absmax pass; cur_max is the maximum of `cur` when its producer did
+  // so.  (A max-pool producer does not: per-image reductions in its grid-stride order cost
+  // more than the absmax pass they save.)
+  unsigned* imax[2] = {nullptr, nullptr};
+  const unsigned* cur_max = nullptr;
+  int mwhich = 0;
+  if (m->int8) {
+    imax[0] = static_cast<unsigned*>(c.scratch((size_t)n * 4));
+    imax[1] = static_cast<unsigned*>(c.scratch((size_t)n * 4));
+    if (!imax[0] || !imax[1]) return false;
+  }
+  auto max_for = [&](size_t j) -> unsigned* {
+    if (!m->int8 || j >= nl || m->layers[j].type != 1 || !m->layers[j].wq) return nullptr;
+    unsigned* d = imax[mwhich];
+    mwhich ^= 1;
+    return ACF_CUDA_OK(cudaMemsetAsync(d, 0, (size_t)n * 4, c.stream())) ? d : nullptr;
+  };
   for (size_t li = 0; li < nl; ++li) {
     auto& L = m->layers[li];
     float* next = m->buf[which];
     bool ok = true;
+    const unsigned* in_max = cur_max;
+    cur_max = nullptr;
     // A standalone ReLU right after a Conv / FC (the loader keeps Conv->BN->ReLU's ReLU
     // separate, model.cpp:211-226) is applied in that layer's epilogue instead of a pass.
     int act = L.act;
@@ -382,8 +403,10 @@ static bool run_model(Call& c, AcfunModel* m, int n, const float* x, float* y) {
           if (li + 1 < nl && m->layers[li + 1].type == 4) {
             const auto& P = m->layers[li + 1];
             bool fused = false;
+            unsigned* om = max_for(li + 2);
             ok = conv_int8_pool_dev(c, cur, n, H, W, C, L.wq, L.wqs, L.b, KH, KW, Cout, st, pd, act,
-                                    P.p[0], P.p[1], P.p[2], P.post_relu, next, &fused);
+                                    P.p[0], P.p[1], P.p[2], P.post_relu, next, &fused, om);
+            if (ok && fused) cur_max = om;
             if (ok && fused) {
               H = (H + 2 * pd - KH) / st + 1;
               W = (W + 2 * pd - KW) / st + 1;
@@ -396,8 +419,10 @@ static bool run_model(Call& c, AcfunModel* m, int n, const float* x, float* y) {
               break;
             }
           }
+          unsigned* om = ok ? max_for(li + 1) : nullptr;
           ok = ok && conv2d_int8_batch_dev(c, cur, n, H, W, C, L.wq, L.wqs, L.b, KH, KW, Cout, st,
-                                           pd, next, act);
+                                           pd, next, act, in_max, om);
+          cur_max = om;
           H = (H + 2 * pd - KH) / st + 1;
           W = (W + 2 * pd - KW) / st + 1;
           C = Cout;

@@ -24,6 +24,13 @@ static __device__ __forceinline__ float nx_bf16_val(uint16_t h) {
   return __uint_as_float((uint32_t)h << 16);
 }
 
+// Running maximum of |v| as the int8 router's absmax accumulates it (k_absmax_img: a NaN never
+// replaces the running value).
+static __device__ __forceinline__ void amax_acc(float& am, float v) {
+  const float a = fabsf(v);
+  am = (am < a) ? a : am;
+}
+
 // 3xBF16 split of a pair on the hardware converter (cvt.rn.bf16x2.f32 rounds to nearest
 // even, the same bits as nx_bf16_rne for every non-NaN input): hi = bf16(a) | bf16(b) << 16,
 // lo = the bf16 of the exact remainders a - hi, b - hi in the same packing.
