@@ -819,9 +819,24 @@ bool split_weights_dev(Call& c, const float* w, int taps, int Cin, int Cout, voi
   return c.launched("k_weights_split");
 }
 
+long long pair_geometry(ConvGeom& cg, int N, int Hp, int OH, int OW) {
+  if (Hp % 2 != 0 || OH < 2 || OW < 2) return 0;
+  int bxl = 1;
+  while ((1 << bxl) < OW && bxl < 7) ++bxl;
+  cg.pair = 1;
+  cg.bxl = bxl;
+  cg.by = 128 >> bxl;
+  cg.xb = (OW + (1 << bxl) - 1) >> bxl;
+  cg.hp2 = Hp / 2;
+  cg.npr = N * (Hp / 2);
+  const long long pb = (cg.npr + cg.by - 1) / cg.by;
+  return pb * cg.xb * 256;
+}
+
 bool conv_tc_split_dev(Call& c, const float* x, const SplitAct* xs, int N, int H, int W,
                        int Cin, const float* w, const void* ws, const float* bias, int KH,
-                       int KW, int Cout, int pad, float* out, const SplitAct* os, int act) {
+                       int KW, int Cout, int pad, float* out, const SplitAct* os, int act,
+                       bool pool) {
   const int OH = H + 2 * pad - KH + 1, OW = W + 2 * pad - KW + 1;
   const int taps = KH * KW, Hp = H + 2 * pad, Wp = W + 2 * pad, Cpad = Cin;
   const int Np = (int)align_up((size_t)Cout, 8);
@@ -875,7 +890,21 @@ bool conv_tc_split_dev(Call& c, const float* x, const SplitAct* xs, int N, int H
   B.ld = Np;
   B.op_stride = (long long)taps * Cpad * Np;
   ConvGeom cg{1, Cpad / 64, KW, Wp, Cpad, taps};
-  return gemm_launch(c, GemmKind::BF16X3, Epi::F32_BIAS, A, B, (int)rows, Cout, taps * Cpad, ep, cg);
+  long long M = rows;
+  if (pool) {
+    // the 2x2 / stride-2 max-pool in the epilogue: output (N, OH/2, OW/2, Cout), fp32 `out`
+    // or the split planes `os` of that size
+    M = pair_geometry(cg, N, Hp, OH, OW);
+    if (M <= 0 || M >= (1LL << 31)) {
+      set_error(kInvalid, "%s: pooled split conv geometry", c.name());
+      c.fail();
+      return false;
+    }
+    ep.remap = 0;
+    ep.ph = OH / 2;
+    ep.pw = OW / 2;
+  }
+  return gemm_launch(c, GemmKind::BF16X3, Epi::F32_BIAS, A, B, (int)M, Cout, taps * Cpad, ep, cg);
 }
 
 bool conv_f32_dev(Call& c, const float* x, int N, int H, int W, int Cs, int coff, int Cg,

@@ -5,6 +5,8 @@
 
 namespace acf {
 
+struct ConvGeom;
+
 enum ConvRoute {
   kRouteDepthwise = 1,
   kRouteGroupedDirect = 2,
@@ -50,13 +52,22 @@ bool split_border_dev(Call& c, const SplitAct& a);
 // fp32 weights [taps*Cin][Cout] -> the [2][taps*Cin][Np] bf16 split the implicit GEMM takes
 // (Np = Cout rounded up to 8).  `dst` holds split_weight_bytes.
 long long split_weight_bytes(int taps, int Cin, int Cout);
+
+// Row-pair tiling of a stride-1 implicit convolution over N images of padded height Hp whose
+// OH x OW output is max-pooled 2x2 / stride 2 (ConvGeom::pair): fills cg's pair fields and
+// returns the GEMM's virtual row count (256 per tile), or 0 when the shape does not qualify
+// (odd Hp, output narrower than 2).
+long long pair_geometry(ConvGeom& cg, int N, int Hp, int OH, int OW);
 bool split_weights_dev(Call& c, const float* w, int taps, int Cin, int Cout, void* dst);
 // conv_split_ok convolution from fp32 x (padded + split here) or the split activation xs
 // (xs->pad == pad), with pre-split weights ws (or NULL: split here), into fp32 out or, when
-// os is given, the next convolution's split input.
+// os is given, the next convolution's split input.  pool: the 2x2 / stride-2 / pad-0 max-pool
+// that follows runs in the epilogue (output (OH/2) x (OW/2); needs H + 2*pad even), its
+// post-ReLU folded into act.
 bool conv_tc_split_dev(Call& c, const float* x, const SplitAct* xs, int N, int H, int W,
                        int Cin, const float* w, const void* ws, const float* bias, int KH,
-                       int KW, int Cout, int pad, float* out, const SplitAct* os, int act);
+                       int KW, int Cout, int pad, float* out, const SplitAct* os, int act,
+                       bool pool = false);
 
 // Dense conv (groups 1) immediately followed by max-pool(pool, pst, ppd, post_relu), fused when
 // the conv takes the CUDA-core small-K route and the pool is 2x2 / stride 2 / pad 0 (sets
@@ -73,10 +84,14 @@ bool conv_pool_dev(Call& c, const float* x, int N, int H, int W, int Cin, const 
 // in_max: the input's per-image max |x| already accumulated by its producer (skips the absmax
 // pass); out_max: accumulate the output's per-image max |y| (zeroed by the caller) for the next
 // int8 layer.
+// pool: the 2x2 / stride-2 / pad-0 max-pool that follows runs in the GEMM epilogue (output
+// (OH/2) x (OW/2)) when int8_pool_ok holds for the shape; its post-ReLU folded into act.
 bool conv2d_int8_batch_dev(Call& c, const float* x, int N, int H, int W, int Cin,
                            const int8_t* wq, const float* wscale, const float* bias, int KH,
                            int KW, int Cout, int stride, int pad, float* out, int act,
-                           const unsigned* in_max = nullptr, unsigned* out_max = nullptr);
+                           const unsigned* in_max = nullptr, unsigned* out_max = nullptr,
+                           bool pool = false);
+bool int8_pool_ok(int H, int W, int Cin, int KH, int KW, int Cout, int stride, int pad);
 
 // conv2d_int8_batch_dev immediately followed by max-pool(2, 2, 0, post_relu), fused for small-K
 // non-Winograd routes (sets *handled; otherwise nothing is launched).  Bit-identical to the two

@@ -489,7 +489,7 @@ static Int8BLayout int8_b_layout(int Cin, int KH, int KW, int stride) {
 // wk: weights already in int8_b_layout's K-major form (else prepared here from wq)
 static bool int8_conv_gemm(Call& c, const Int8ConvArgs& a, int N, int H, int W, int Cin,
                            const int8_t* wq, int KH, int KW, int Cout, int stride, int pad,
-                           float* out, int act, const int8_t* wk = nullptr) {
+                           float* out, int act, const int8_t* wk = nullptr, bool pool = false) {
   const int OH = (H + 2 * pad - KH) / stride + 1, OW = (W + 2 * pad - KW) / stride + 1;
   if (OH <= 0 || OW <= 0) return true;
   const int taps = KH * KW;
@@ -546,7 +546,24 @@ static bool int8_conv_gemm(Call& c, const Int8ConvArgs& a, int N, int H, int W, 
     ep.OH = OH;
     ep.OW = OW;
     ConvGeom cg{1, Cpad / bkb, KW, Wp, Cpad, taps};
-    return gemm_launch_i8k(c, a.epi, Ao, Bo, (int)rows, Cout, taps * Cpad, ep, cg, bkb);
+    long long M = rows;
+    if (pool) {  // 2x2 / stride-2 max-pool in the epilogue (int8_pool_ok)
+      M = pair_geometry(cg, N, Hp, OH, OW);
+      if (M <= 0 || M >= (1LL << 31)) {
+        set_error(kInvalid, "%s: pooled int8 conv geometry", c.name());
+        c.fail();
+        return false;
+      }
+      ep.remap = 0;
+      ep.ph = OH / 2;
+      ep.pw = OW / 2;
+    }
+    return gemm_launch_i8k(c, a.epi, Ao, Bo, (int)M, Cout, taps * Cpad, ep, cg, bkb);
+  }
+  if (pool) {
+    set_error(kInvalid, "%s: pooled int8 conv needs the implicit route", c.name());
+    c.fail();
+    return false;
   }
   // explicit im2col over the quantised input
   const uint8_t* src = a.xq;
@@ -721,10 +738,16 @@ __global__ void k_int8_img_scalars(const unsigned* __restrict__ maxa, int N, flo
   }
 }
 
+bool int8_pool_ok(int H, int W, int Cin, int KH, int KW, int Cout, int stride, int pad) {
+  const int OH = (H + 2 * pad - KH) / stride + 1, OW = (W + 2 * pad - KW) / stride + 1;
+  return int8_b_layout(Cin, KH, KW, stride).implicit && Cout > 64 && (H + 2 * pad) % 2 == 0 &&
+         OH >= 2 && OW >= 2;
+}
+
 bool conv2d_int8_batch_dev(Call& c, const float* x, int N, int H, int W, int Cin,
                            const int8_t* wq, const float* wscale, const float* bias, int KH,
                            int KW, int Cout, int stride, int pad, float* out, int act,
-                           const unsigned* in_max, unsigned* out_max) {
+                           const unsigned* in_max, unsigned* out_max, bool pool) {
   const int OH = (H + 2 * pad - KH) / stride + 1, OW = (W + 2 * pad - KW) / stride + 1;
   if (OH <= 0 || OW <= 0 || N <= 0) return true;
   if (N > 65535) {
@@ -764,7 +787,7 @@ bool conv2d_int8_batch_dev(Call& c, const float* x, int N, int H, int W, int Cin
   a.f1 = bias;
   a.i0 = Sw;
   a.out_max = out_max;
-  return int8_conv_gemm(c, a, N, H, W, Cin, wq, KH, KW, Cout, stride, pad, out, act, wk);
+  return int8_conv_gemm(c, a, N, H, W, Cin, wq, KH, KW, Cout, stride, pad, out, act, wk, pool);
 }
 
 // s8 weights [taps*Cin][Cout] -> 4-byte words wpk[tap][cw][Cout] (channels 4cw..4cw+3 of a

@@ -245,7 +245,38 @@ static bool launch_one(Call& c, const Operand& A, const Operand& B, int M, int N
   const CUtensorMapSwizzle bswz = BKM ? kswz
                                   : (S::ELEM == 4) ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
                                                    : CU_TENSOR_MAP_SWIZZLE_128B;
-  if (NPASS == 1) {
+  if (MT == 2 && cg.enabled && cg.pair) {
+    // row-pair view of the padded activation [pairs][2][Wp][cpad] (+ the hi / lo copy):
+    // box = 1 parity x `by` pairs x 2^bxl columns x BKE channels = 128 rows
+    const uint64_t C = (uint64_t)A.ld, Wp = (uint64_t)cg.Wp;
+    const uint64_t dA[5] = {C, Wp, 2, (uint64_t)cg.npr, 2};
+    const uint64_t sA[4] = {C * E, Wp * C * E, 2 * Wp * C * E, (uint64_t)A.op_stride * E};
+    const uint32_t bA[5] = {(uint32_t)S::BKE, 1u << cg.bxl, 1u, (uint32_t)cg.by, 1u};
+    const int rank = NPASS == 1 ? 4 : 5;
+    if ((1 << cg.bxl) * cg.by != 128 || !encode_tmap(&ta, dt, rank, A.p, dA, sA, bA, kswz)) {
+      set_error(kInvalid, "%s: row-pair tensor map", c.name());
+      c.fail();
+      return false;
+    }
+    if (NPASS == 1) {
+      const uint64_t dB[2] = {BKM ? (uint64_t)K : (uint64_t)N, BKM ? (uint64_t)N : (uint64_t)K};
+      const uint64_t sB[1] = {(uint64_t)B.ld * E};
+      const uint32_t bB[2] = {BKM ? (uint32_t)S::BKE : (uint32_t)(128 / S::ELEM),
+                              BKM ? (uint32_t)BN : (uint32_t)S::BKE};
+      if (!encode_tmap(&tb, dt, 2, B.p, dB, sB, bB, bswz)) {
+        c.fail();
+        return false;
+      }
+    } else {
+      const uint64_t dB[3] = {(uint64_t)N, (uint64_t)K, 2};
+      const uint64_t sB[2] = {(uint64_t)B.ld * E, (uint64_t)B.op_stride * E};
+      const uint32_t bB[3] = {(uint32_t)(128 / S::ELEM), (uint32_t)S::BKE, 1u};
+      if (!encode_tmap(&tb, dt, 3, B.p, dB, sB, bB, bswz)) {
+        c.fail();
+        return false;
+      }
+    }
+  } else if (NPASS == 1) {
     const uint64_t dA[2] = {(uint64_t)K, (uint64_t)M}, sA[1] = {(uint64_t)A.ld * E};
     const uint32_t bA[2] = {(uint32_t)S::BKE, 128u};
     // K-major B: [N][K] rows, one BN-row box; MN-major B: [K][N], 128-byte N chunks
@@ -322,17 +353,34 @@ static bool launch_i8k(Call& c, const Operand& A, const Operand& B, int M, int N
   return launch_one<MK::I8, 256, 4, 1, EPI, false, 128, true>(c, A, B, M, N, K, ep, cg);
 }
 
+// Row-pair (pooled) implicit convolutions: two 128-row sub-tiles of 128 columns per CTA.
+template <Epi EPI>
+static bool launch_i8k_pair(Call& c, const Operand& A, const Operand& B, int M, int N, int K,
+                            const EpiParams& ep, const ConvGeom& cg, int bkb) {
+  using MK = dev::MmaKind;
+  if (bkb == 64)
+    return launch_one<MK::I8, 128, 8, 1, EPI, false, 64, true, 2>(c, A, B, M, N, K, ep, cg);
+  return launch_one<MK::I8, 128, 4, 1, EPI, false, 128, true, 2>(c, A, B, M, N, K, ep, cg);
+}
+
 bool gemm_launch_i8k(Call& c, Epi epi, const Operand& A, const Operand& B, int M, int N, int K,
                      const EpiParams& ep, const ConvGeom& cg, int bkb) {
   if (!c.ok() || !A.p || !B.p || (bkb != 64 && bkb != 128)) {
     c.fail();
     return false;
   }
+  if (cg.enabled && cg.pair && N <= 64) {
+    set_error(kInvalid, "%s: row-pair int8 convolution needs more than 64 output channels", c.name());
+    c.fail();
+    return false;
+  }
   switch (epi) {
     case Epi::F32_AB:
-      return launch_i8k<Epi::F32_AB>(c, A, B, M, N, K, ep, cg, bkb);
+      return cg.pair ? launch_i8k_pair<Epi::F32_AB>(c, A, B, M, N, K, ep, cg, bkb)
+                     : launch_i8k<Epi::F32_AB>(c, A, B, M, N, K, ep, cg, bkb);
     case Epi::I8_WINO:
-      return launch_i8k<Epi::I8_WINO>(c, A, B, M, N, K, ep, cg, bkb);
+      return cg.pair ? launch_i8k_pair<Epi::I8_WINO>(c, A, B, M, N, K, ep, cg, bkb)
+                     : launch_i8k<Epi::I8_WINO>(c, A, B, M, N, K, ep, cg, bkb);
     default:
       set_error(kInvalid, "%s: unsupported int8 epilogue", c.name());
       c.fail();
@@ -383,6 +431,11 @@ bool gemm_launch(Call& c, GemmKind kind, Epi epi, const Operand& A, const Operan
     }
     case GemmKind::BF16X3: {
       if (epi != Epi::F32_BIAS) break;
+      if (cg.enabled && cg.pair)  // row-pair (pooled) convolution: two sub-tiles per CTA
+        return N > 64 ? launch_one<MK::F16, 128, 4, 3, Epi::F32_BIAS, false, 64, false, 2>(
+                            c, A, B, M, N, K, ep, cg)
+                      : launch_one<MK::F16, 64, 5, 3, Epi::F32_BIAS, false, 64, false, 2>(
+                            c, A, B, M, N, K, ep, cg);
       // 256-column tiles in 64-byte K blocks: a quarter fewer operand bytes per MAC than
       // 128-column tiles (the 3xBF16 main loop is bound by shared-memory fill from L2)
       if (N > 128 && tiles(M, N, 256) >= sms)

@@ -76,6 +76,12 @@ struct ConvGeom {
   int Wp;
   int cpad;     // channels per tap in B
   int taps;
+  // Row-pair tiling (MT = 2; a convolution followed by a 2x2 / stride-2 max-pool): A is viewed
+  // as [pairs][2][Wp][cpad] (padded rows 2p, 2p+1; the hi / lo copy outermost for 3xBF16) and
+  // a tile is `by` pairs x 2^bxl columns of output pixels, sub-tile i holding the rows of
+  // parity i, so each 2x2 window sits in lanes (l, l^1) of the two sub-tiles.  xb = column
+  // blocks per pair block, hp2 = pairs per image (Hp / 2), npr = pairs in the tensor.
+  int pair, bxl, by, xb, hp2, npr;
 };
 
 // Per-column epilogue parameters of one 32-column chunk, staged in the epilogue warp's own
@@ -332,47 +338,82 @@ __device__ __forceinline__ void epi_store32(const EpiParams& ep, long long orow,
   }
 }
 
-// F32_BIAS with pool4: eight pooled columns j0..j0+7 of pooled row `orow` (their bias at
-// P.a[cs..cs+7]): bias, activation, fp32 or split-bf16 store.
-__device__ __forceinline__ void epi_store_pool8(const EpiParams& ep, long long orow, int j0, int N,
-                                                const float (&m)[8], const ColSlice& P, int cs,
-                                                float& am) {
-  float v[8];
+// Window maximum of two accumulator words: fp32 (F32_BIAS) or int32 (F32_AB, I8_WINO, whose
+// dequantisation is non-decreasing in the accumulator -- every scale is >= 0 -- so the maximum
+// may be taken before it; bias and ReLU are monotone too).
+template <Epi EPI>
+__device__ __forceinline__ uint32_t acc_max(uint32_t a, uint32_t b) {
+  if constexpr (EPI == Epi::F32_BIAS)
+    return __float_as_uint(fmaxf(__uint_as_float(a), __uint_as_float(b)));
+  else
+    return (int32_t)a > (int32_t)b ? a : b;
+}
+
+// Pooled epilogue: NC columns j0..j0+NC-1 of pooled row `orow` from window maxima m (accumulator
+// words), the columns' parameters at P.{a,b,c}[cs..cs+NC); epi_store32's arithmetic per EPI.
+template <Epi EPI, int NC>
+__device__ __forceinline__ void epi_store_pool(const EpiParams& ep, long long orow, int j0, int N,
+                                               const uint32_t (&m)[NC], const ColSlice& P, int cs,
+                                               bool zero, float img_sa, float& am) {
+  static_assert(EPI == Epi::F32_BIAS || EPI == Epi::F32_AB || EPI == Epi::I8_WINO, "float out");
+  float v[NC];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float x = __fadd_rn(m[i], P.a[cs + i]);
-    v[i] = ep.act ? relu_max(x) : x;
+  for (int i = 0; i < NC; ++i) {
+    float x;
+    if constexpr (EPI == Epi::F32_BIAS) {
+      x = __fadd_rn(__uint_as_float(m[i]), P.a[cs + i]);
+    } else if constexpr (EPI == Epi::F32_AB) {
+      float a = P.a[cs + i], b = P.b[cs + i];
+      if (ep.img_sa) {
+        a = __fmul_rn(img_sa, a);
+        b = __fsub_rn(b, __fmul_rn(__fmul_rn(a, 128.0f), (float)P.c[cs + i]));
+      }
+      x = __fadd_rn(__fmul_rn(__int2float_rn((int32_t)m[i]), a), b);
+    } else {
+      float w = P.a[cs + i];
+      if (ep.img_sa) w = __fmul_rn(__fmul_rn(img_sa, 0.25f), w);
+      const int32_t c = (int32_t)m[i] - 128 * P.c[cs + i];
+      x = __fmaf_rn(__fmul_rn(4.0f, __int2float_rn(c)), w, P.b[cs + i]);
+    }
+    if (ep.act) x = relu_max(x);
+    v[i] = zero ? 0.0f : x;
   }
   if (ep.img_absmax) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
+    for (int i = 0; i < NC; ++i)
       if (j0 + i < N) amax_acc(am, v[i]);
   }
-  const bool full = j0 + 8 <= N;
-  if (ep.split_out) {
-    uint16_t* hi = reinterpret_cast<uint16_t*>(ep.split_out) + orow * ep.ldc + j0;
-    uint16_t* lo = hi + ep.split_plane;
-    uint32_t ph[4], pl[4];
+  const bool full = j0 + NC <= N;
+  if constexpr (EPI == Epi::F32_BIAS) {
+    if (ep.split_out) {
+      uint16_t* hi = reinterpret_cast<uint16_t*>(ep.split_out) + orow * ep.ldc + j0;
+      uint16_t* lo = hi + ep.split_plane;
+      uint32_t ph[NC / 2], pl[NC / 2];
 #pragma unroll
-    for (int i = 0; i < 8; i += 2) nx_split_bf16x2(v[i], v[i + 1], ph[i / 2], pl[i / 2]);
-    if (full && ((reinterpret_cast<uintptr_t>(hi) | reinterpret_cast<uintptr_t>(lo)) & 15) == 0) {
-      *reinterpret_cast<uint4*>(hi) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
-      *reinterpret_cast<uint4*>(lo) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
-    } else {
-      for (int i = 0; i < 8; ++i)
-        if (j0 + i < N) {
-          hi[i] = (uint16_t)(ph[i / 2] >> (16 * (i & 1)));
-          lo[i] = (uint16_t)(pl[i / 2] >> (16 * (i & 1)));
+      for (int i = 0; i < NC; i += 2) nx_split_bf16x2(v[i], v[i + 1], ph[i / 2], pl[i / 2]);
+      if (full && ((reinterpret_cast<uintptr_t>(hi) | reinterpret_cast<uintptr_t>(lo)) & 15) == 0) {
+#pragma unroll
+        for (int q = 0; q < NC / 8; ++q) {
+          reinterpret_cast<uint4*>(hi)[q] = make_uint4(ph[4 * q], ph[4 * q + 1], ph[4 * q + 2], ph[4 * q + 3]);
+          reinterpret_cast<uint4*>(lo)[q] = make_uint4(pl[4 * q], pl[4 * q + 1], pl[4 * q + 2], pl[4 * q + 3]);
         }
+      } else {
+        for (int i = 0; i < NC; ++i)
+          if (j0 + i < N) {
+            hi[i] = (uint16_t)(ph[i / 2] >> (16 * (i & 1)));
+            lo[i] = (uint16_t)(pl[i / 2] >> (16 * (i & 1)));
+          }
+      }
+      return;
     }
-    return;
   }
   float* dst = reinterpret_cast<float*>(ep.C) + orow * ep.ldc + j0;
   if (full && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-    reinterpret_cast<float4*>(dst)[0] = make_float4(v[0], v[1], v[2], v[3]);
-    reinterpret_cast<float4*>(dst)[1] = make_float4(v[4], v[5], v[6], v[7]);
+#pragma unroll
+    for (int q = 0; q < NC / 4; ++q)
+      reinterpret_cast<float4*>(dst)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
   } else {
-    for (int i = 0; i < 8; ++i)
+    for (int i = 0; i < NC; ++i)
       if (j0 + i < N) dst[i] = v[i];
   }
 }
@@ -441,7 +482,14 @@ __global__ void __launch_bounds__(320, 1)
     for (int t = blockIdx.x; t < num_tiles && !stop; t += gridDim.x) {
       if (*abort_flag) break;
       const int m0 = (t / tiles_n) * S::BM, n0 = (t % tiles_n) * BN;
-      int cb = 0, kw = 0, row_off = 0, tap_k = 0;  // conv: channel block, kw, A row shift, B k
+      // conv: channel block, kw, kh, A row shift, B k
+      int cb = 0, kw = 0, kh = 0, row_off = 0, tap_k = 0;
+      int pr0 = 0, px0 = 0;  // row-pair tiling: first pair and first column of the tile
+      if (MT == 2 && cg.pair) {
+        const int tm = t / tiles_n, pb = tm / cg.xb;
+        pr0 = pb * cg.by;
+        px0 = (tm - pb * cg.xb) << cg.bxl;
+      }
       for (int kb = 0; kb < nkb; ++kb) {
         if (!dev::mbar_wait(&empty_bar[s], ph ^ 1, err)) {
           *abort_flag = 1;
@@ -451,6 +499,7 @@ __global__ void __launch_bounds__(320, 1)
         uint8_t* st = smem + s * S::STAGE;
         dev::mbar_arrive_expect_tx(&full_bar[s], S::STAGE);
         int kx, ay, by;
+        const int akw = kw, akh = kh;  // this block's tap
         if (cg.enabled) {
           kx = cb * S::BKE;
           ay = m0 + row_off;
@@ -461,6 +510,7 @@ __global__ void __launch_bounds__(320, 1)
             ++row_off;
             if (++kw == cg.KW) {
               kw = 0;
+              ++kh;
               row_off += cg.Wp - cg.KW;
             }
           }
@@ -473,23 +523,46 @@ __global__ void __launch_bounds__(320, 1)
         for (int op = 0; op < S::NOPS; ++op) {
           uint8_t* a_dst = st + op * S::A_OP;
           uint8_t* b_dst = st + S::NOPS * S::A_OP + op * S::B_TILE;
-          if constexpr (B_KMAJ) {
+          bool a_done = false;
+          if constexpr (MT == 2) {
+            if (cg.pair) {
+              // output rows 2p + i read padded rows 2p + i + kh: pair p + (i+kh)/2, parity (i+kh)&1
 #pragma unroll
-            for (int i = 0; i < MT; ++i)
-              dev::tma_load_2d(a_dst + i * S::A_TILE, &tmA, &full_bar[s], kx, ay + 128 * i);
+              for (int i = 0; i < 2; ++i) {
+                const int pi = i + akh;
+                if constexpr (S::NOPS == 1)
+                  dev::tma_load_4d(a_dst + i * S::A_TILE, &tmA, &full_bar[s], kx, px0 + akw,
+                                   pi & 1, pr0 + (pi >> 1));
+                else
+                  dev::tma_load_5d(a_dst + i * S::A_TILE, &tmA, &full_bar[s], kx, px0 + akw,
+                                   pi & 1, pr0 + (pi >> 1), op);
+              }
+              a_done = true;
+            }
+          }
+          if constexpr (B_KMAJ) {
+            if (!a_done) {
+#pragma unroll
+              for (int i = 0; i < MT; ++i)
+                dev::tma_load_2d(a_dst + i * S::A_TILE, &tmA, &full_bar[s], kx, ay + 128 * i);
+            }
             dev::tma_load_2d(b_dst, &tmB, &full_bar[s], by, n0);
           } else if constexpr (S::NOPS == 1) {
+            if (!a_done) {
 #pragma unroll
-            for (int i = 0; i < MT; ++i)
-              dev::tma_load_2d(a_dst + i * S::A_TILE, &tmA, &full_bar[s], kx, ay + 128 * i);
+              for (int i = 0; i < MT; ++i)
+                dev::tma_load_2d(a_dst + i * S::A_TILE, &tmA, &full_bar[s], kx, ay + 128 * i);
+            }
 #pragma unroll
             for (int c = 0; c < S::NCHUNK; ++c)
               dev::tma_load_2d(b_dst + c * S::CHUNK_B, &tmB, &full_bar[s],
                                n0 + c * (128 / S::ELEM), by);
           } else {
+            if (!a_done) {
 #pragma unroll
-            for (int i = 0; i < MT; ++i)
-              dev::tma_load_3d(a_dst + i * S::A_TILE, &tmA, &full_bar[s], kx, ay + 128 * i, op);
+              for (int i = 0; i < MT; ++i)
+                dev::tma_load_3d(a_dst + i * S::A_TILE, &tmA, &full_bar[s], kx, ay + 128 * i, op);
+            }
 #pragma unroll
             for (int c = 0; c < S::NCHUNK; ++c)
               dev::tma_load_3d(b_dst + c * S::CHUNK_B, &tmB, &full_bar[s],
@@ -604,6 +677,57 @@ __global__ void __launch_bounds__(320, 1)
       const bool ok = dev::mbar_wait(&tfull_bar[buf], use & 1, err);
       dev::tc_fence_after();
       if (!ok || *abort_flag) break;
+      if constexpr (MT == 2 && (EPI == Epi::F32_BIAS || EPI == Epi::F32_AB ||
+                                EPI == Epi::I8_WINO)) {
+        if (cg.pair) {
+          // Row-pair tile: lane l of both sub-tiles is output pixel (2*pr + i, x) with pr =
+          // pr0 + l / 2^bxl, x = x0 + l % 2^bxl; the 2x2 window of pooled pixel (pr, x/2) is
+          // lanes (l, l^1) of the two sub-tiles.
+          const int tm = t / tiles_n, pb = tm / cg.xb;
+          const int l = q * 32 + lane, lby = l >> cg.bxl;
+          const int pr = pb * cg.by + lby;
+          const int xx = ((tm - pb * cg.xb) << cg.bxl) + (l & ((1 << cg.bxl) - 1));
+          const int n = pr / cg.hp2, py = pr - n * cg.hp2, px = xx >> 1;
+          const bool store = lby < cg.by && pr < cg.npr && py < ep.ph && px < ep.pw;
+          const long long orow = ep.split_out
+                                     ? ((long long)n * ep.sHp + py + ep.spad) * ep.sWp + px + ep.spad
+                                     : ((long long)n * ep.ph + py) * ep.pw + px;
+          bool zero_out = ep.zero_flag && *ep.zero_flag;
+          float img_sa = 0.0f;
+          if (ep.img_sa && store) {
+            img_sa = ep.img_sa[n];
+            zero_out = ep.img_zero[n] != 0;
+          }
+          float am = 0.0f;
+          const int hs = lane & 1;  // this lane keeps columns 16*hs..16*hs+15 of each chunk
+#pragma unroll 1
+          for (int k = 0; k < S::CHUNKS_PER_WARP; ++k) {
+            const int c0 = h * 32 + 64 * k;
+            if (c0 >= BN || n0 + c0 >= N) break;  // warp-uniform
+            uint32_t v0[32], v1[32];
+            const uint32_t ta = tmem + buf * S::ACC_COLS + (uint32_t)c0 + ((uint32_t)(q * 32) << 16);
+            dev::tmem_ld32(ta, v0);
+            dev::tmem_ld32(ta + BN, v1);
+            dev::tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v0[j] = acc_max<EPI>(v0[j], v1[j]);
+            uint32_t m16[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const uint32_t send = hs ? v0[j] : v0[16 + j], keep = hs ? v0[16 + j] : v0[j];
+              m16[j] = acc_max<EPI>(keep, __shfl_xor_sync(0xffffffffu, send, 1));
+            }
+            if (store)
+              epi_store_pool<EPI, 16>(ep, orow, n0 + c0 + 16 * hs, N, m16, my[k], 16 * hs, zero_out,
+                                      img_sa, am);
+          }
+          if (ep.img_absmax) amax_flush(ep.img_absmax, store ? n : -1, am);  // warp-uniform
+          dev::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) dev::mbar_arrive(&tempty_bar[buf]);
+          continue;
+        }
+      }
 #pragma unroll 1
       for (int i = 0; i < MT; ++i) {  // 128-row sub-tiles
         const int r = m0 + 128 * i + q * 32 + lane;
@@ -641,26 +765,26 @@ __global__ void __launch_bounds__(320, 1)
           dev::tmem_ld32(
               tmem + buf * S::ACC_COLS + (uint32_t)(i * BN + c0) + ((uint32_t)(q * 32) << 16), v);
           dev::tmem_ld_wait();
-          if constexpr (EPI == Epi::F32_BIAS) {
+          if constexpr (EPI == Epi::F32_BIAS || EPI == Epi::F32_AB || EPI == Epi::I8_WINO) {
             if (ep.pool4) {
               // warp-uniform.  The window's four rows are lanes 4g..4g+3: a reduce-scatter
               // over them leaves lane 4g+s with the maxima of columns 8s..8s+7.
               const int s4 = lane & 3;
               const bool up = (s4 & 2) != 0, odd = (s4 & 1) != 0;
-              float k16[16], m8[8];
+              uint32_t k16[16], m8[8];
 #pragma unroll
               for (int j = 0; j < 16; ++j) {
-                const float send = __uint_as_float(up ? v[j] : v[16 + j]);
-                const float keep = __uint_as_float(up ? v[16 + j] : v[j]);
-                k16[j] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, 2));
+                const uint32_t send = up ? v[j] : v[16 + j], keep = up ? v[16 + j] : v[j];
+                k16[j] = acc_max<EPI>(keep, __shfl_xor_sync(0xffffffffu, send, 2));
               }
 #pragma unroll
               for (int j = 0; j < 8; ++j) {
-                const float send = odd ? k16[j] : k16[8 + j];
-                const float keep = odd ? k16[8 + j] : k16[j];
-                m8[j] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, 1));
+                const uint32_t send = odd ? k16[j] : k16[8 + j], keep = odd ? k16[8 + j] : k16[j];
+                m8[j] = acc_max<EPI>(keep, __shfl_xor_sync(0xffffffffu, send, 1));
               }
-              if (store) epi_store_pool8(ep, orow, n0 + c0 + 8 * s4, N, m8, my[k], 8 * s4, am);
+              if (store)
+                epi_store_pool<EPI, 8>(ep, orow, n0 + c0 + 8 * s4, N, m8, my[k], 8 * s4, zero_out,
+                                       img_sa, am);
               continue;
             }
           }

@@ -373,6 +373,11 @@ static bool run_model(Call& c, AcfunModel* m, int n, const float* x, float* y) {
     imax[1] = static_cast<unsigned*>(c.scratch((size_t)n * 4));
     if (!imax[0] || !imax[1]) return false;
   }
+  auto pool2_follows = [&](size_t j) -> bool {  // layer j + 1 is MaxPool(2, 2, 0)
+    if (j + 1 >= nl || m->layers[j + 1].type != 4) return false;
+    const auto& P = m->layers[j + 1];
+    return P.p[0] == 2 && P.p[1] == 2 && P.p[2] == 0;
+  };
   auto max_for = [&](size_t j) -> unsigned* {
     if (!m->int8 || j >= nl || m->layers[j].type != 1 || !m->layers[j].wq) return nullptr;
     unsigned* d = imax[mwhich];
@@ -400,13 +405,15 @@ static bool run_model(Call& c, AcfunModel* m, int n, const float* x, float* y) {
         if (m->int8 && L.wq) {
           // int8 mode: acfun_conv2d_int8 per image (the reference's int8 model harness); a
           // small-K conv followed by MaxPool(2, 2, 0) runs fused
-          if (li + 1 < nl && m->layers[li + 1].type == 4) {
+          // (one max_for per layer: a second call would hand out the array in_max points at)
+          const bool pool_next = li + 1 < nl && m->layers[li + 1].type == 4;
+          unsigned* om_pool = pool_next ? max_for(li + 2) : nullptr;  // the pool's consumer
+          if (pool_next) {
             const auto& P = m->layers[li + 1];
             bool fused = false;
-            unsigned* om = max_for(li + 2);
             ok = conv_int8_pool_dev(c, cur, n, H, W, C, L.wq, L.wqs, L.b, KH, KW, Cout, st, pd, act,
-                                    P.p[0], P.p[1], P.p[2], P.post_relu, next, &fused, om);
-            if (ok && fused) cur_max = om;
+                                    P.p[0], P.p[1], P.p[2], P.post_relu, next, &fused, om_pool);
+            if (ok && fused) cur_max = om_pool;
             if (ok && fused) {
               H = (H + 2 * pd - KH) / st + 1;
               W = (W + 2 * pd - KW) / st + 1;
@@ -419,12 +426,20 @@ static bool run_model(Call& c, AcfunModel* m, int n, const float* x, float* y) {
               break;
             }
           }
-          unsigned* om = ok ? max_for(li + 1) : nullptr;
+          // a following MaxPool(2, 2, 0) runs in the GEMM epilogue when the route allows
+          const bool pooled = pool2_follows(li) && int8_pool_ok(H, W, C, KH, KW, Cout, st, pd);
+          unsigned* om = pooled ? om_pool : (ok && !pool_next ? max_for(li + 1) : nullptr);
           ok = ok && conv2d_int8_batch_dev(c, cur, n, H, W, C, L.wq, L.wqs, L.b, KH, KW, Cout, st,
-                                           pd, next, act, in_max, om);
+                                           pd, next, pooled ? (act | m->layers[li + 1].post_relu) : act,
+                                           in_max, om, pooled);
           cur_max = om;
           H = (H + 2 * pd - KH) / st + 1;
           W = (W + 2 * pd - KW) / st + 1;
+          if (pooled) {
+            H /= 2;
+            W /= 2;
+            ++li;
+          }
           C = Cout;
           cur = next;
           which ^= 1;
@@ -469,14 +484,20 @@ static bool run_model(Call& c, AcfunModel* m, int n, const float* x, float* y) {
               return false;
             }
           }
+          // a following MaxPool(2, 2, 0) runs in the conv's epilogue (row-pair tiles)
+          const bool pooled = pool2_follows(li) && st == 1 && (H + 2 * pd) % 2 == 0 && OHc >= 2 &&
+                              OWc >= 2;
+          const int oh = pooled ? OHc / 2 : OHc, ow = pooled ? OWc / 2 : OWc;
           SplitAct os;
-          const bool want = split_target(li + 1, OHc, OWc, Cout, next, os);
+          const bool want = split_target(li + (pooled ? 2 : 1), oh, ow, Cout, next, os);
           if (want) ok = split_border_dev(c, os);
           ok = ok && conv_tc_split_dev(c, in_split ? nullptr : cur, in_split ? &cs : nullptr, n, H, W,
                                        C, L.w, L.wsplit, L.b, KH, KW, Cout, pd, next,
-                                       want ? &os : nullptr, act);
-          H = OHc;
-          W = OWc;
+                                       want ? &os : nullptr,
+                                       pooled ? (act | m->layers[li + 1].post_relu) : act, pooled);
+          if (pooled) ++li;
+          H = oh;
+          W = ow;
           C = Cout;
           cur = next;
           which ^= 1;

@@ -26,7 +26,9 @@ def test_model_demo_golden(acf, tmp_path):
     m.close()
 
 
-@pytest.mark.parametrize("width_div", [8, 4])   # 4: conv1 has 16 channels -> fused conv + pool
+# 4: conv1 has 16 channels -> fused conv + pool; 2: conv2..conv8 run their max-pool in the
+# GEMM epilogue (row-pair tiles 32, 16, 8 and 4 columns wide)
+@pytest.mark.parametrize("width_div", [8, 4, 2])
 def test_model_vgg_small_vs_oracle(acf, tmp_path, width_div):
     from acfun_b200 import acfun0
     from oracle.model_oracle import OracleModel
@@ -98,7 +100,7 @@ def test_model_conv_pool_fusion_vs_oracle(acf, tmp_path):
     m.close()
 
 
-@pytest.mark.parametrize("width_div", [8, 4])
+@pytest.mark.parametrize("width_div", [8, 4, 2])   # 2: pooled int8 GEMM epilogues (Cout > 64)
 def test_model_int8_mode_vs_oracle(acf, tmp_path, width_div):
     """acfun_model_set_int8: every dense conv through the int8 router with one activation scale
     per image (conv1: u8 im2col route, the rest: int8 Winograd route), FC / pool / softmax fp32.
@@ -203,4 +205,39 @@ def test_conv1_pool_tensor_route_vs_oracle(acf, tmp_path, hw, nxt):
     om = OracleModel(blob)
     for k in range(2):
         assert max_rel(y[k], om.infer(x[k]).reshape(y[k].shape)) < TOL_F32
+    m.close()
+
+
+@pytest.mark.parametrize("hw,cin,c2,k2,nimg", [((112, 112), 64, 128, 3, 2),  # 128- then 64-wide
+                                               ((56, 58), 64, 192, 1, 2),    # 1x1; 64 then 32, odd
+                                               ((30, 29), 64, 128, 3, 3),    # 32-wide, odd OW
+                                               ((14, 14), 128, 128, 3, 3)])  # 16-wide
+def test_model_pooled_conv_vs_oracle(acf, tmp_path, hw, cin, c2, k2, nimg):
+    """Conv -> MaxPool(2, 2, 0) as one implicit GEMM with row-pair tiles (the pool in the
+    epilogue), fp32 (3xBF16; the pooled output written as the next conv's split input and as
+    fp32) and int8 (Winograd and 1x1 routes, per-image scales; bit-exact) against the oracle."""
+    from acfun_b200.acfun0 import Acfun0Writer, bn_params
+    from oracle.model_oracle import OracleModel
+    H, W = hw
+    g = np.random.default_rng(H * 7 + c2)
+    u = lambda s, *d: g.uniform(-s, s, size=d).astype(np.float32)
+    Wr = Acfun0Writer(cin, H, W)
+    Wr.conv(u(0.1, k2 * k2 * cin, c2), u(0.1, c2), k2, k2, c2, 1, k2 // 2).bn(*bn_params(g, c2)).relu()
+    Wr.maxpool(2, 2, 0)
+    Wr.conv(u(0.05, 9 * c2, 128), u(0.1, 128), 3, 3, 128, 1, 1).relu().maxpool(2, 2, 0).relu()
+    blob = Wr.tobytes()
+    p = tmp_path / "pc.acfun"
+    p.write_bytes(blob)
+    m = acf.Model(str(p))
+    x = np.random.default_rng(5).uniform(0, 1, (nimg, H, W, cin)).astype(np.float32)
+    x[-1] *= 9.0
+    om = OracleModel(blob)
+    y = m.infer_batch(x)
+    for k in range(nimg):
+        assert max_rel(y[k], om.infer(x[k]).reshape(y[k].shape)) < TOL_F32, k
+    m.set_int8(True)
+    y8 = m.infer_batch(x)
+    for k in range(nimg):
+        assert_bits_equal(y8[k], om.infer(x[k], int8=True).reshape(y8[k].shape), f"int8 image {k}")
+    assert_bits_equal(m.infer_batch(np.ascontiguousarray(x[-1:]))[0], y8[-1], "int8 last image alone")
     m.close()
