@@ -142,14 +142,17 @@ struct GemmShape {
   static constexpr int B_SBO = B_KMAJ ? K_SBO : (ELEM == 4) ? 512 : 1024;
   static constexpr int B_LBO = B_KMAJ ? 16 : CHUNK_B;
   static constexpr int ACC_COLS = MT * BN;   // one accumulator buffer
-  static constexpr int TMEM_COLS = 2 * ACC_COLS;  // double-buffered
+  // accumulator buffers in TMEM: 4 when they fit (short-K tiles then keep the MMA several
+  // tiles ahead of the epilogue), else 2
+  static constexpr int NBUF = ACC_COLS <= 128 ? 4 : 2;
+  static constexpr int TMEM_COLS = NBUF * ACC_COLS;
   // warps 0 (TMA) and 1 (MMA / TMEM), then EPI_WARPS epilogue warps: two per TMEM lane
   // quadrant, splitting the tile's 32-column chunks between them (even / odd chunks)
   static constexpr int EPI_WARPS = 8;
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
   static constexpr int CHUNKS_PER_WARP = (BN / 32 + 1) / 2;
   // full/empty per stage, tfull[2], tempty[2], drain; TMEM slot; abort flag
-  static constexpr int BAR_BYTES = ((2 * STAGES + 5) * 8 + 8 + 15) / 16 * 16;
+  static constexpr int BAR_BYTES = ((2 * STAGES + 2 * NBUF + 1) * 8 + 8 + 15) / 16 * 16;
   static constexpr int PARAM_BYTES = EPI_WARPS * CHUNKS_PER_WARP * (int)sizeof(ColSlice);
   static constexpr int SMEM = 1024 + STAGES * STAGE + BAR_BYTES + PARAM_BYTES;
   static_assert(BKB == 128 || (BKB == 64 && (B_KMAJ ? NPASS == 1 : ELEM == 2)),
@@ -419,9 +422,9 @@ __device__ __forceinline__ void epi_store_pool(const EpiParams& ep, long long or
 }
 
 // Persistent kernel: grid = min(#tiles, #SMs); CTA b walks tiles b, b+grid, ...  The smem
-// ring runs continuously across tiles, and the accumulator is double-buffered in TMEM
-// (2 x BN columns): the UMMA warp fills buffer i&1 while the epilogue warps drain the
-// other, so a tile's epilogue overlaps the next tile's MMAs.
+// ring runs continuously across tiles, and the accumulator has NBUF buffers in TMEM
+// (NBUF x MT*BN columns): the UMMA warp fills buffer i % NBUF while the epilogue warps drain
+// the earlier ones, so a tile's epilogue overlaps the next tiles' MMAs.
 template <dev::MmaKind KIND, int BN, int STAGES, int NPASS, Epi EPI, bool A_SIGNED, int BKB = 128,
           bool B_KMAJ = false, int MT = 1>
 __global__ void __launch_bounds__(320, 1)
@@ -433,9 +436,9 @@ __global__ void __launch_bounds__(320, 1)
                                              ~uintptr_t(1023));
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * S::STAGE);
   uint64_t* empty_bar = full_bar + STAGES;
-  uint64_t* tfull_bar = empty_bar + STAGES;   // [2] accumulator buffer ready for the epilogue
-  uint64_t* tempty_bar = tfull_bar + 2;       // [2] accumulator buffer drained
-  uint64_t* drain_bar = tempty_bar + 2;       // error-path MMA drain
+  uint64_t* tfull_bar = empty_bar + STAGES;     // [NBUF] accumulator ready for the epilogue
+  uint64_t* tempty_bar = tfull_bar + S::NBUF;   // [NBUF] accumulator drained
+  uint64_t* drain_bar = tempty_bar + S::NBUF;   // error-path MMA drain
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   ColSlice* col_slices = reinterpret_cast<ColSlice*>(smem + STAGES * S::STAGE + S::BAR_BYTES);
@@ -453,7 +456,7 @@ __global__ void __launch_bounds__(320, 1)
       dev::mbar_init(&full_bar[s], 1);
       dev::mbar_init(&empty_bar[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < S::NBUF; ++b) {
       dev::mbar_init(&tfull_bar[b], 1);
       dev::mbar_init(&tempty_bar[b], S::EPI_WARPS);  // one arrive per epilogue warp
     }
@@ -601,7 +604,7 @@ __global__ void __launch_bounds__(320, 1)
     uint32_t it = 0, local = 0;
     uint32_t s = 0, ph = 0;
     for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local) {
-      const uint32_t buf = local & 1, use = local >> 1;
+      const uint32_t buf = local % S::NBUF, use = local / S::NBUF;
       if (*abort_flag || !dev::mbar_wait(&tempty_bar[buf], (use & 1) ^ 1, err)) {
         ok = false;
         break;
@@ -649,8 +652,8 @@ __global__ void __launch_bounds__(320, 1)
       *abort_flag = 1;
       dev::umma_commit(drain_bar);
       dev::mbar_wait(drain_bar, 0, nullptr, 200000000ull);
-      dev::mbar_arrive(&tfull_bar[0]);  // release epilogue warps (they see abort_flag)
-      dev::mbar_arrive(&tfull_bar[1]);
+      for (int b = 0; b < S::NBUF; ++b)
+        dev::mbar_arrive(&tfull_bar[b]);  // release epilogue warps (they see abort_flag)
     }
   } else if (warp >= 2) {
     // ---------------- epilogue
@@ -660,7 +663,7 @@ __global__ void __launch_bounds__(320, 1)
     uint32_t local = 0;
     int staged_n0 = -1;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
-      const uint32_t buf = local & 1, use = local >> 1;
+      const uint32_t buf = local % S::NBUF, use = local / S::NBUF;
       const int m0 = (t / tiles_n) * S::BM, n0 = (t % tiles_n) * BN;
       if constexpr (EPI != Epi::S32) {
         // per-column parameters of this tile's chunks, loaded before the accumulator is
@@ -765,7 +768,7 @@ __global__ void __launch_bounds__(320, 1)
           dev::tmem_ld32(
               tmem + buf * S::ACC_COLS + (uint32_t)(i * BN + c0) + ((uint32_t)(q * 32) << 16), v);
           dev::tmem_ld_wait();
-          if constexpr (EPI == Epi::F32_BIAS || EPI == Epi::F32_AB || EPI == Epi::I8_WINO) {
+          if constexpr (EPI == Epi::F32_BIAS) {
             if (ep.pool4) {
               // warp-uniform.  The window's four rows are lanes 4g..4g+3: a reduce-scatter
               // over them leaves lane 4g+s with the maxima of columns 8s..8s+7.
