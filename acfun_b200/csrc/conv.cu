@@ -108,7 +108,9 @@ __global__ void k_weights_split(const float* __restrict__ w, int taps, int Cg, i
 // thread per output pixel keeps NB fp32 accumulators and the weights [taps*Cin][Cout] sit in
 // shared memory as warp-wide broadcasts.  out = relu?(sum_taps,k x*w + bias[j]) with an fp32
 // FMA chain (taps outside the image are skipped).
-template <int NB>
+// S threads share a pixel, each owning NB/S of its output channels (more warps in flight for
+// layers with few pixels per SM).
+template <int NB, int S>
 __global__ void __launch_bounds__(128) k_conv_simt(const float* __restrict__ x, int H, int W,
                                                    int Cs, int coff, int Cin,
                                                    const float* __restrict__ w, long long ldw,
@@ -120,17 +122,20 @@ __global__ void __launch_bounds__(128) k_conv_simt(const float* __restrict__ x, 
   float* ws = reinterpret_cast<float*>(cs_sm4);  // [taps*Cin][NB]
   const int K = KH * KW * Cin;
   float* bs = ws + K * NB;
-  for (int i = threadIdx.x; i < K * NB; i += blockDim.x) {
+  stage_block<16>(ws, K * NB, [&](int i) {
     const int k = i / NB, j = i - k * NB;
-    ws[i] = (j < Cout) ? w[(long long)k * ldw + j] : 0.0f;
-  }
+    return (j < Cout) ? __ldg(w + (long long)k * ldw + j) : 0.0f;
+  });
   for (int j = threadIdx.x; j < NB; j += blockDim.x) bs[j] = (bias && j < Cout) ? bias[j] : 0.0f;
   __syncthreads();
-  for (unsigned m = blockIdx.x * blockDim.x + threadIdx.x; m < M; m += gridDim.x * blockDim.x) {
+  constexpr int NBT = NB / S;  // accumulators per thread
+  static_assert(NBT % 4 == 0, "16-byte weight broadcasts");
+  for (unsigned q = blockIdx.x * blockDim.x + threadIdx.x; q < M * S; q += gridDim.x * blockDim.x) {
+    const unsigned m = q / S, g0 = (q % S) * NBT;
     const unsigned ow = m % OW, t = m / OW, oh = t % OH, n = t / OH;
-    float acc[NB];
+    float acc[NBT];
 #pragma unroll
-    for (int j = 0; j < NB; ++j) acc[j] = 0.0f;
+    for (int j = 0; j < NBT; ++j) acc[j] = 0.0f;
     for (int kh = 0; kh < KH; ++kh) {
       const int ih = (int)oh * stride - pad + kh;
       if (ih < 0 || ih >= H) continue;
@@ -138,7 +143,7 @@ __global__ void __launch_bounds__(128) k_conv_simt(const float* __restrict__ x, 
         const int iw = (int)ow * stride - pad + kw;
         if (iw < 0 || iw >= W) continue;
         const float* src = x + (((size_t)n * H + ih) * W + iw) * Cs + coff;
-        const float* wt = ws + (kh * KW + kw) * Cin * NB;
+        const float* wt = ws + (kh * KW + kw) * Cin * NB + g0;
         int k = 0;
         if (vec_in) {
           for (; k + 4 <= Cin; k += 4) {
@@ -146,13 +151,18 @@ __global__ void __launch_bounds__(128) k_conv_simt(const float* __restrict__ x, 
             const float xv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
-              const float* wr = wt + (k + u) * NB;
+              // weight rows are NB (a multiple of 4) floats: 16-byte broadcasts feed two FMA2s
+              const float4* wr4 = reinterpret_cast<const float4*>(wt + (k + u) * NB);
               const float2 x2 = make_float2(xv[u], xv[u]);
 #pragma unroll
-              for (int j = 0; j < NB; j += 2) {
-                const float2 r2 = nx_ffma2(x2, make_float2(wr[j], wr[j + 1]), make_float2(acc[j], acc[j + 1]));
-                acc[j] = r2.x;
-                acc[j + 1] = r2.y;
+              for (int j = 0; j < NBT; j += 4) {
+                const float4 w4 = wr4[j / 4];
+                const float2 r0 = nx_ffma2(x2, make_float2(w4.x, w4.y), make_float2(acc[j], acc[j + 1]));
+                const float2 r1 = nx_ffma2(x2, make_float2(w4.z, w4.w), make_float2(acc[j + 2], acc[j + 3]));
+                acc[j] = r0.x;
+                acc[j + 1] = r0.y;
+                acc[j + 2] = r1.x;
+                acc[j + 3] = r1.y;
               }
             }
           }
@@ -162,7 +172,7 @@ __global__ void __launch_bounds__(128) k_conv_simt(const float* __restrict__ x, 
           const float* wr = wt + k * NB;
           const float2 x2 = make_float2(xv, xv);
 #pragma unroll
-          for (int j = 0; j < NB; j += 2) {
+          for (int j = 0; j < NBT; j += 2) {
             const float2 r2 = nx_ffma2(x2, make_float2(wr[j], wr[j + 1]), make_float2(acc[j], acc[j + 1]));
             acc[j] = r2.x;
             acc[j + 1] = r2.y;
@@ -170,21 +180,21 @@ __global__ void __launch_bounds__(128) k_conv_simt(const float* __restrict__ x, 
         }
       }
     }
-    float* dst = out + (size_t)m * ldc;
+    float* dst = out + (size_t)m * ldc + g0;
 #pragma unroll
-    for (int j = 0; j < NB; ++j) {
-      const float v = __fadd_rn(acc[j], bs[j]);
+    for (int j = 0; j < NBT; ++j) {
+      const float v = __fadd_rn(acc[j], bs[g0 + j]);
       acc[j] = act ? (v > 0.0f ? v : 0.0f) : v;
     }
     if (vec_out) {
 #pragma unroll
-      for (int j = 0; j < NB; j += 4)
-        if (j < Cout)
+      for (int j = 0; j < NBT; j += 4)
+        if ((int)g0 + j < Cout)
           *reinterpret_cast<float4*>(dst + j) = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
     } else {
 #pragma unroll
-      for (int j = 0; j < NB; ++j)
-        if (j < Cout) dst[j] = acc[j];
+      for (int j = 0; j < NBT; ++j)
+        if ((int)g0 + j < Cout) dst[j] = acc[j];
     }
   }
 }
@@ -669,21 +679,27 @@ static bool conv_simt(Call& c, const float* x, int N, int H, int W, int Cs, int 
   const long long M = (long long)N * OH * OW;
   const int K = KH * KW * Cg;
   const bool narrow = (KH == 1 && KW == 1 && pad == 0) || K <= 64;
-  const int NB = Cout <= 16 ? 16 : (Cout <= 32 ? 32 : 64);
+  const int NB = Cout <= 16 ? 16 : Cout <= 24 ? 24 : Cout <= 32 ? 32 : Cout <= 48 ? 48 : 64;
   const size_t smem = ((size_t)K * NB + NB) * 4;
-  if (!narrow || Cout > 64 || smem > 48 * 1024 || M >= (1LL << 31)) return true;
+  if (!narrow || Cout > 64 || smem > 48 * 1024 || M >= (1LL << 30)) return true;
   *handled = true;
   const int vec_in = (Cs % 4 == 0) && (coff % 4 == 0) && aligned16(x);
   const int vec_out = (Cout % 4 == 0) && (ldc % 4 == 0) && aligned16(out);
-  const int grid = grid_ew(c, 2 * M);  // ceil(M / 128) blocks of 128 threads, capped
+  // a few resident blocks per SM, each walking many pixels: the weight staging is paid once
+  // per block
+  const int grid = (int)std::min<long long>((2 * M + 127) / 128, 8LL * c.sm_count());
 #define ACF_CONV_SIMT(NBV)                                                                      \
-  k_conv_simt<NBV><<<grid, 128, smem, c.stream()>>>(x, H, W, Cs, coff, Cg, w, ldw, bias, Cout, KH, \
-                                                    KW, stride, pad, OH, OW, (unsigned)M, out,   \
-                                                    ldc, act, vec_in, vec_out)
+  k_conv_simt<NBV, 2><<<grid, 128, smem, c.stream()>>>(x, H, W, Cs, coff, Cg, w, ldw, bias, Cout,  \
+                                                       KH, KW, stride, pad, OH, OW, (unsigned)M, \
+                                                       out, ldc, act, vec_in, vec_out)
   if (NB == 16)
     ACF_CONV_SIMT(16);
+  else if (NB == 24)
+    ACF_CONV_SIMT(24);
   else if (NB == 32)
     ACF_CONV_SIMT(32);
+  else if (NB == 48)
+    ACF_CONV_SIMT(48);
   else
     ACF_CONV_SIMT(64);
 #undef ACF_CONV_SIMT

@@ -24,6 +24,26 @@ static __device__ __forceinline__ float nx_bf16_val(uint16_t h) {
   return __uint_as_float((uint32_t)h << 16);
 }
 
+// Block-wide copy into shared memory, dst[i] = f(i) for i < n, each thread issuing its U
+// loads before its U stores: one memory round trip per U*blockDim elements rather than one
+// per blockDim.
+template <int U, typename F>
+static __device__ __forceinline__ void stage_block(float* dst, int n, F f) {
+  for (int b0 = threadIdx.x; b0 < n; b0 += U * blockDim.x) {
+    float v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = b0 + u * blockDim.x;
+      v[u] = i < n ? f(i) : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = b0 + u * blockDim.x;
+      if (i < n) dst[i] = v[u];
+    }
+  }
+}
+
 // Running maximum of |v| as the int8 router's absmax accumulates it (k_absmax_img: a NaN never
 // replaces the running value).
 static __device__ __forceinline__ void amax_acc(float& am, float v) {

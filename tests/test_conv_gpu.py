@@ -48,6 +48,7 @@ def he(g, shape, fan_in):
     ("vgg_l1", 2, 224, 224, 3, 3, 3, 64, 1, 1),          # im2col route (Cin=3 < 4)
     ("odd", 3, 17, 23, 40, 3, 3, 72, 1, 1),
     ("k5s2", 2, 19, 21, 12, 5, 5, 20, 2, 2),
+    ("pw_c40", 4, 20, 22, 72, 1, 1, 40, 1, 0),         # CUDA-core route, 48-wide accumulators
 ])
 def test_conv_f32_configs_vs_oracle(acf, orc, cfg):
     tag, N, H, W, Cin, KH, KW, Cout, st, pd = cfg
