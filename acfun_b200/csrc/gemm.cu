@@ -313,7 +313,8 @@ static bool launch_one(Call& c, const Operand& A, const Operand& B, int M, int N
     }
     attr_done[dv] = true;
   }
-  const long long tiles = (long long)((M + S::BM - 1) / S::BM) * ((N + BN - 1) / BN);
+  const long long tiles = (long long)((M + S::BM - 1) / S::BM) * ((N + BN - 1) / BN) *
+                          ((!cg.enabled && cg.ksplit > 1) ? cg.ksplit : 1);
   if (tiles >= (1LL << 31)) {
     set_error(kInvalid, "%s: problem too large", c.name());
     c.fail();
@@ -330,6 +331,74 @@ static bool launch_one(Call& c, const Operand& A, const Operand& B, int M, int N
 
 static long long tiles(int M, int N, int bn, int bm = 128) {
   return (long long)((M + bm - 1) / bm) * ((N + bn - 1) / bn);
+}
+
+// Split-K partial sums [S][M][N] -> out = act(sum_s part[s] + bias), summed in split order;
+// VEC: 4 consecutive columns per thread (N and ldc multiples of 4, 16-byte aligned buffers).
+template <bool VEC>
+__global__ void k_splitk_reduce(const float* __restrict__ part, int S, int M, int N,
+                                const float* __restrict__ bias, int act, float* __restrict__ out,
+                                long long ldc) {
+  const long long mn = (long long)M * N;
+  constexpr int V = VEC ? 4 : 1;
+  for (long long i = (blockIdx.x * (long long)blockDim.x + threadIdx.x) * V; i < mn;
+       i += (long long)gridDim.x * blockDim.x * V) {
+    const int m = (int)(i / N), n = (int)(i - (long long)m * N);
+    float v[V];
+    if constexpr (VEC) {
+      const float4 p = *reinterpret_cast<const float4*>(part + i);
+      v[0] = p.x; v[1] = p.y; v[2] = p.z; v[3] = p.w;
+      for (int s = 1; s < S; ++s) {
+        const float4 q = *reinterpret_cast<const float4*>(part + s * mn + i);
+        v[0] = __fadd_rn(v[0], q.x); v[1] = __fadd_rn(v[1], q.y);
+        v[2] = __fadd_rn(v[2], q.z); v[3] = __fadd_rn(v[3], q.w);
+      }
+    } else {
+      v[0] = part[i];
+      for (int s = 1; s < S; ++s) v[0] = __fadd_rn(v[0], part[s * mn + i]);
+    }
+#pragma unroll
+    for (int u = 0; u < V; ++u) {
+      const float x = __fadd_rn(v[u], bias ? bias[n + u] : 0.0f);
+      v[u] = act ? (x > 0.0f ? x : 0.0f) : x;
+    }
+    float* o = out + (long long)m * ldc + n;
+    if constexpr (VEC)
+      *reinterpret_cast<float4*>(o) = make_float4(v[0], v[1], v[2], v[3]);
+    else
+      o[0] = v[0];
+  }
+}
+
+// 3xBF16 GEMMs with few output tiles and a long K (FC layers at small batch): K is split over
+// 256x128 tiles so every SM streams a K range; fp32 partials, then k_splitk_reduce.
+static bool gemm_bf16x3_splitk(Call& c, const Operand& A, const Operand& B, int M, int N, int K,
+                               const EpiParams& ep, int tiles_mn) {
+  using MK = dev::MmaKind;
+  const int nkb = (K + 31) / 32;  // 64-byte bf16 K blocks
+  int S = std::max(2, std::min(std::min(c.sm_count() / std::max(1, tiles_mn), nkb / 8), 16));
+  const int per = (nkb + S - 1) / S;
+  S = (nkb + per - 1) / per;  // no empty split
+  float* part = static_cast<float*>(c.scratch((size_t)S * M * N * 4));
+  if (!part) return false;
+  EpiParams pe{};
+  pe.C = part;
+  pe.ldc = N;
+  ConvGeom g{};
+  g.ksplit = S;
+  if (!launch_one<MK::F16, 128, 4, 3, Epi::F32_BIAS, false, 64, false, 2>(c, A, B, M, N, K, pe, g))
+    return false;
+  const long long mn = (long long)M * N;
+  const bool vec = N % 4 == 0 && ep.ldc % 4 == 0 && aligned16(ep.C);
+  const unsigned grid =
+      (unsigned)std::min<long long>((mn / (vec ? 4 : 1) + 255) / 256, 16LL * c.sm_count());
+  if (vec)
+    k_splitk_reduce<true><<<grid, 256, 0, c.stream()>>>(part, S, M, N, ep.f0, ep.act,
+                                                        static_cast<float*>(ep.C), ep.ldc);
+  else
+    k_splitk_reduce<false><<<grid, 256, 0, c.stream()>>>(part, S, M, N, ep.f0, ep.act,
+                                                         static_cast<float*>(ep.C), ep.ldc);
+  return c.launched("k_splitk_reduce");
 }
 
 int gemm_bke(GemmKind kind) {
@@ -431,6 +500,9 @@ bool gemm_launch(Call& c, GemmKind kind, Epi epi, const Operand& A, const Operan
     }
     case GemmKind::BF16X3: {
       if (epi != Epi::F32_BIAS) break;
+      if (!cg.enabled && !ep.remap && !ep.split_out && !ep.pool4 && !ep.img_absmax && K >= 2048 &&
+          2 * tiles(M, N, 128, 256) <= sms && (long long)M * N < (1LL << 31))
+        return gemm_bf16x3_splitk(c, A, B, M, N, K, ep, (int)tiles(M, N, 128, 256));
       if (cg.enabled && cg.pair)  // row-pair (pooled) convolution: two sub-tiles per CTA
         return N > 64 ? launch_one<MK::F16, 128, 4, 3, Epi::F32_BIAS, false, 64, false, 2>(
                             c, A, B, M, N, K, ep, cg)

@@ -82,6 +82,9 @@ struct ConvGeom {
   // parity i, so each 2x2 window sits in lanes (l, l^1) of the two sub-tiles.  xb = column
   // blocks per pair block, hp2 = pairs per image (Hp / 2), npr = pairs in the tensor.
   int pair, bxl, by, xb, hp2, npr;
+  // Split-K (plain GEMMs only): tile t covers K blocks of split t / (tiles_m*tiles_n), whose
+  // raw accumulator goes to rows ks*M + r of C (partials [ksplit][M][ldc], summed by the caller)
+  int ksplit;
 };
 
 // Per-column epilogue parameters of one 32-column chunk, staged in the epilogue warp's own
@@ -448,8 +451,11 @@ __global__ void __launch_bounds__(320, 1)
   const int lane = threadIdx.x & 31;
   const int tiles_m = (M + S::BM - 1) / S::BM;
   const int tiles_n = (N + BN - 1) / BN;
-  const int num_tiles = tiles_m * tiles_n;
-  const int nkb = cg.enabled ? cg.taps * cg.cblocks : (K + S::BKE - 1) / S::BKE;
+  const int tiles_mn = tiles_m * tiles_n;
+  const int ksplit = (!cg.enabled && cg.ksplit > 1) ? cg.ksplit : 1;
+  const int num_tiles = tiles_mn * ksplit;
+  const int nkb_all = cg.enabled ? cg.taps * cg.cblocks : (K + S::BKE - 1) / S::BKE;
+  const int nkb_s = (nkb_all + ksplit - 1) / ksplit;  // K blocks per split
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -484,16 +490,18 @@ __global__ void __launch_bounds__(320, 1)
     bool stop = false;
     for (int t = blockIdx.x; t < num_tiles && !stop; t += gridDim.x) {
       if (*abort_flag) break;
-      const int m0 = (t / tiles_n) * S::BM, n0 = (t % tiles_n) * BN;
+      const int tt = t % tiles_mn, ks = t / tiles_mn;
+      const int m0 = (tt / tiles_n) * S::BM, n0 = (tt % tiles_n) * BN;
+      const int kb0 = ks * nkb_s, nkb = min(nkb_all, kb0 + nkb_s);
       // conv: channel block, kw, kh, A row shift, B k
       int cb = 0, kw = 0, kh = 0, row_off = 0, tap_k = 0;
       int pr0 = 0, px0 = 0;  // row-pair tiling: first pair and first column of the tile
       if (MT == 2 && cg.pair) {
-        const int tm = t / tiles_n, pb = tm / cg.xb;
+        const int tm = tt / tiles_n, pb = tm / cg.xb;
         pr0 = pb * cg.by;
         px0 = (tm - pb * cg.xb) << cg.bxl;
       }
-      for (int kb = 0; kb < nkb; ++kb) {
+      for (int kb = kb0; kb < nkb; ++kb) {
         if (!dev::mbar_wait(&empty_bar[s], ph ^ 1, err)) {
           *abort_flag = 1;
           stop = true;
@@ -611,7 +619,8 @@ __global__ void __launch_bounds__(320, 1)
       }
       dev::tc_fence_after();
       const uint32_t d_tmem = tmem + buf * S::ACC_COLS;
-      for (int kb = 0; kb < nkb; ++kb, ++it) {
+      const int kb0 = (t / tiles_mn) * nkb_s, nkb = min(nkb_all, kb0 + nkb_s);
+      for (int kb = kb0; kb < nkb; ++kb, ++it) {
         if (!dev::mbar_wait(&full_bar[s], ph, err)) {
           ok = false;
           break;
@@ -625,7 +634,7 @@ __global__ void __launch_bounds__(320, 1)
             if constexpr (NPASS == 1) {
               const uint64_t ad = a_desc0 + soff + (uint64_t)((i * S::A_TILE + ks * 32) / 16);
               const uint64_t bd = b_desc0 + soff + (uint64_t)(ks * S::KSTEP_B / 16);
-              dev::umma<KIND>(d_tmem + i * BN, ad, bd, idesc, (kb | ks) != 0);
+              dev::umma<KIND>(d_tmem + i * BN, ad, bd, idesc, ((kb - kb0) | ks) != 0);
             } else {
               // (a_op, b_op): lo*hi, hi*lo, hi*hi
               const int aop[3] = {1, 0, 0}, bop[3] = {0, 1, 0};
@@ -635,7 +644,7 @@ __global__ void __launch_bounds__(320, 1)
                                     (uint64_t)((aop[p] * S::A_OP + i * S::A_TILE + ks * 32) / 16);
                 const uint64_t bd =
                     b_desc0 + soff + (uint64_t)((bop[p] * S::B_TILE + ks * S::KSTEP_B) / 16);
-                dev::umma<KIND>(d_tmem + i * BN, ad, bd, idesc, (kb | ks | p) != 0);
+                dev::umma<KIND>(d_tmem + i * BN, ad, bd, idesc, ((kb - kb0) | ks | p) != 0);
               }
             }
           }
@@ -664,7 +673,8 @@ __global__ void __launch_bounds__(320, 1)
     int staged_n0 = -1;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
       const uint32_t buf = local % S::NBUF, use = local / S::NBUF;
-      const int m0 = (t / tiles_n) * S::BM, n0 = (t % tiles_n) * BN;
+      const int tt = t % tiles_mn, ksp = t / tiles_mn;
+      const int m0 = (tt / tiles_n) * S::BM, n0 = (tt % tiles_n) * BN;
       if constexpr (EPI != Epi::S32) {
         // per-column parameters of this tile's chunks, loaded before the accumulator is
         // ready (and only when the column block changes)
@@ -686,7 +696,7 @@ __global__ void __launch_bounds__(320, 1)
           // Row-pair tile: lane l of both sub-tiles is output pixel (2*pr + i, x) with pr =
           // pr0 + l / 2^bxl, x = x0 + l % 2^bxl; the 2x2 window of pooled pixel (pr, x/2) is
           // lanes (l, l^1) of the two sub-tiles.
-          const int tm = t / tiles_n, pb = tm / cg.xb;
+          const int tm = tt / tiles_n, pb = tm / cg.xb;
           const int l = q * 32 + lane, lby = l >> cg.bxl;
           const int pr = pb * cg.by + lby;
           const int xx = ((tm - pb * cg.xb) << cg.bxl) + (l & ((1 << cg.bxl) - 1));
@@ -736,7 +746,7 @@ __global__ void __launch_bounds__(320, 1)
         const int r = m0 + 128 * i + q * 32 + lane;
         bool zero_out = ep.zero_flag && *ep.zero_flag;
         float img_sa = 0.0f;
-        long long orow = r;
+        long long orow = r + (long long)ksp * M;  // split-K partial rows
         bool store = r < M;
         if (ep.img_sa && store) {
           const int n = r / ep.img_rows;

@@ -103,7 +103,9 @@ def test_gemm_s8_requant_full_size_sampled(acf, orc, M, N, K):
                                    (33, 47, 129), (300, 24, 144), (1, 1000, 4096), (512, 17, 64),
                                    (10240, 300, 200),    # 256-column tiles, ragged N and K
                                    (40000, 100, 136),    # two 128-row sub-tiles per CTA, N 128
-                                   (37856, 40, 72)])     # the same at N 64; last sub-tile empty
+                                   (37856, 40, 72),      # the same at N 64; last sub-tile empty
+                                   (300, 520, 5000),     # split-K over 14 K ranges, K tail
+                                   (256, 4096, 25088)])  # VGG FC1 shape (split-K)
 def test_gemm_f32_tolerance(acf, orc, M, N, K):
     g = np.random.default_rng(M + N + K)
     A = g.uniform(-1, 1, (M, K)).astype(np.float32)
