@@ -912,7 +912,7 @@ __global__ void __launch_bounds__(128) k_conv_int8_pool(
         if (in[u]) {
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const uint32_t q = (cw * 4 + e < Cin) ? quant_one(v[u][e], inv_s, 0, true) : 128u;
+            const uint32_t q = (cw * 4 + e < Cin) ? quant_fast<0>(v[u][e], inv_s) : 128u;
             wv = (wv & ~(0xFFu << (8 * e))) | (q << (8 * e));
           }
         }
@@ -950,17 +950,28 @@ __global__ void __launch_bounds__(128) k_conv_int8_pool(
           }
         }
     float m[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) m[j] = -1e30f;
-#pragma unroll
-    for (int p = 0; p < 4; ++p)
+    if (act) {
+      // the window maximum of the int32 sums, then one dequantisation: (float)acc*alpha + beta
+      // is non-decreasing in acc (alpha = sa*ws >= 0) and ReLU maps both zeros to +0, so this
+      // is the maximum of the four dequantised, activated values bit for bit
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
-        float v = __fadd_rn(__fmul_rn(__int2float_rn(acc[p][j]), alpha[cb * 16 + j]), beta[cb * 16 + j]);
-        v = act ? (v > 0.0f ? v : 0.0f) : v;
-        v = zero ? 0.0f : v;
-        m[j] = m[j] > v ? m[j] : v;
+        const int a = max(max(acc[0][j], acc[1][j]), max(acc[2][j], acc[3][j]));
+        const float v = __fadd_rn(__fmul_rn(__int2float_rn(a), alpha[cb * 16 + j]), beta[cb * 16 + j]);
+        m[j] = zero ? 0.0f : (v > 0.0f ? v : 0.0f);
       }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) m[j] = -1e30f;
+#pragma unroll
+      for (int p = 0; p < 4; ++p)
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          float v = __fadd_rn(__fmul_rn(__int2float_rn(acc[p][j]), alpha[cb * 16 + j]), beta[cb * 16 + j]);
+          v = zero ? 0.0f : v;
+          m[j] = m[j] > v ? m[j] : v;
+        }
+    }
     float* dst = out + (((size_t)n * PH + ph) * PW + pw) * Cout + cb * 16;
 #pragma unroll
     for (int q = 0; q < 4; ++q) {

@@ -127,8 +127,9 @@ def test_model_int8_mode_vs_oracle(acf, tmp_path, width_div):
     m.close()
 
 
-@pytest.mark.parametrize("st,post_relu,cin", [(1, False, 3), (2, True, 3), (1, True, 7)])
-def test_model_int8_conv_pool_fusion_bit_exact(acf, tmp_path, st, post_relu, cin):
+@pytest.mark.parametrize("st,post_relu,cin,relu", [(1, False, 3, True), (2, True, 3, True),
+                                                  (1, True, 7, True), (1, False, 3, False)])
+def test_model_int8_conv_pool_fusion_bit_exact(acf, tmp_path, st, post_relu, cin, relu):
     """int8 mode, Conv -> MaxPool(2,2,0) with nothing after it: the fused small-K int8 conv +
     pool kernel must equal the oracle's conv2d_int8 + maxpool bit for bit (odd sizes, borders,
     per-image scales, an all-zero image)."""
@@ -137,7 +138,10 @@ def test_model_int8_conv_pool_fusion_bit_exact(acf, tmp_path, st, post_relu, cin
     g = np.random.default_rng(100 + st + cin)
     u = lambda *s: g.uniform(-0.3, 0.3, size=s).astype(np.float32)
     Wr = Acfun0Writer(cin, 37, 29)
-    Wr.conv(u(9 * cin, 32), u(32), 3, 3, 32, st, 1).bn(*bn_params(g, 32)).relu().maxpool(2, 2, 0)
+    Wr.conv(u(9 * cin, 32), u(32), 3, 3, 32, st, 1).bn(*bn_params(g, 32))
+    if relu:
+        Wr.relu()
+    Wr.maxpool(2, 2, 0)
     if post_relu:
         Wr.relu()
     blob = Wr.tobytes()
