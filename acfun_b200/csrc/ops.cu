@@ -408,18 +408,28 @@ __global__ void k_dw_strip(const float* __restrict__ in, int H, int W, int C,
     const float4 b4 = *reinterpret_cast<const float4*>(bs + c);
 #pragma unroll
     for (int t = 0; t < TW; ++t) acc[t] = b4;
+    // strips whose input columns all lie inside the image take a branch-free body
+    const bool inner = iw0 >= 0 && iw0 + NCOL <= W;
     for (int kh = 0; kh < KH; ++kh) {
       const int ih = oh * stride - pad + kh;
       if (ih < 0 || ih >= H) continue;  // out-of-image taps are skipped, not multiplied by 0
       float4 xc[NCOL];
-      unsigned ok = 0;
+      unsigned ok = (1u << NCOL) - 1u;
+      if (inner) {
+        const float* rowp = img + ((size_t)ih * W + iw0) * C + c;
 #pragma unroll
-      for (int j = 0; j < NCOL; ++j) {
-        const int iw = iw0 + j;
-        xc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (iw >= 0 && iw < W) {
-          xc[j] = __ldg(reinterpret_cast<const float4*>(img + ((size_t)ih * W + iw) * C + c));
-          ok |= 1u << j;
+        for (int j = 0; j < NCOL; ++j)
+          xc[j] = __ldg(reinterpret_cast<const float4*>(rowp + (size_t)j * C));
+      } else {
+        ok = 0;
+#pragma unroll
+        for (int j = 0; j < NCOL; ++j) {
+          const int iw = iw0 + j;
+          xc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (iw >= 0 && iw < W) {
+            xc[j] = __ldg(reinterpret_cast<const float4*>(img + ((size_t)ih * W + iw) * C + c));
+            ok |= 1u << j;
+          }
         }
       }
 #pragma unroll
@@ -427,7 +437,7 @@ __global__ void k_dw_strip(const float* __restrict__ in, int H, int W, int C,
         const float4 wv = *reinterpret_cast<const float4*>(wT + (kh * KW + kw) * C + c);
 #pragma unroll
         for (int t = 0; t < TW; ++t) {
-          if (!((ok >> (t * STRIDE + kw)) & 1u)) continue;
+          if (!inner && !((ok >> (t * STRIDE + kw)) & 1u)) continue;
           const float4 x = xc[t * STRIDE + kw];
           // two packed fmas (lanes x,y and z,w): bit-identical to four __fmaf_rn
           const float2 lo = nx_ffma2(make_float2(x.x, x.y), make_float2(wv.x, wv.y),
