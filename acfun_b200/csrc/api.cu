@@ -18,11 +18,6 @@ extern "C" void acfun_set_threads(int n) { (void)n; }
 // acfun.h:23-24 (gemm.cpp:81-88)
 extern "C" int acfun_backend(void) { return ACFUN_BACKEND_CUDA_SM100A; }
 extern "C" const char* acfun_backend_name(void) { return "CUDA-sm100a"; }
-// acfun.h:29-30 (autotune.cpp:421-430): tile shapes are compile-time; nothing to tune.
-extern "C" void acfun_autotune(void) {}
-extern "C" const char* acfun_tune_status(void) {
-  return "static: tcgen05 tiles 128x{32..256} (TMA SW128, 3-8 stage ring); no CPU KC/NC search";
-}
 // internal.h:111-115,225 (gemm.cpp:19-20,43-67,104-136)
 extern "C" void acfun_set_num_threads_runtime(int n) { g_rt_threads = n > 0 ? n : 1; }
 extern "C" int acfun_get_num_threads_runtime(void) { return g_rt_threads; }

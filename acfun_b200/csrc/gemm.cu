@@ -465,9 +465,16 @@ bool gemm_launch(Call& c, GemmKind kind, Epi epi, const Operand& A, const Operan
   }
   const int sms = c.sm_count();
   using MK = dev::MmaKind;
+  // plain GEMMs may take the tile variant of the measured tile table (gemm.cuh)
+  const bool plain = !cg.enabled && !ep.remap && !ep.split_out && !ep.pool4 && !ep.img_absmax;
+  auto pick = [&](TuneFamily f) {
+    const int v = plain ? tune_variant(c, f, M, N, K) : -1;
+    return (v >= 0 && tune_variant_valid(f, v, M, N, K)) ? v : -1;
+  };
   switch (kind) {
     case GemmKind::I8U: {
-      const bool wide = N > 128 && tiles(M, N, 256) >= sms;
+      const int v = pick(TuneFamily::I8);
+      const bool wide = v >= 0 ? v == 1 : (N > 128 && tiles(M, N, 256) >= sms);
       switch (epi) {
         case Epi::S32:
           return wide ? launch_one<MK::I8, 256, 4, 1, Epi::S32, false>(c, A, B, M, N, K, ep, cg)
@@ -484,7 +491,8 @@ bool gemm_launch(Call& c, GemmKind kind, Epi epi, const Operand& A, const Operan
       break;
     }
     case GemmKind::I8S: {
-      const bool wide = N > 128 && tiles(M, N, 256) >= sms;
+      const int v = pick(TuneFamily::I8);
+      const bool wide = v >= 0 ? v == 1 : (N > 128 && tiles(M, N, 256) >= sms);
       if (epi == Epi::S8_REQ)
         return wide ? launch_one<MK::I8, 256, 4, 1, Epi::S8_REQ, true>(c, A, B, M, N, K, ep, cg)
                     : launch_one<MK::I8, 128, 6, 1, Epi::S8_REQ, true>(c, A, B, M, N, K, ep, cg);
@@ -492,16 +500,34 @@ bool gemm_launch(Call& c, GemmKind kind, Epi epi, const Operand& A, const Operan
     }
     case GemmKind::BF16: {
       if (epi != Epi::F32_BIAS) break;
-      if (N > 128 && tiles(M, N, 256) >= sms)
+      const int v = pick(TuneFamily::BF16);
+      if (v == 2 || (v < 0 && N > 128 && tiles(M, N, 256) >= sms))
         return launch_one<MK::F16, 256, 4, 1, Epi::F32_BIAS, false>(c, A, B, M, N, K, ep, cg);
-      if (N > 64 && tiles(M, N, 128) >= sms)
+      if (v == 1 || (v < 0 && N > 64 && tiles(M, N, 128) >= sms))
         return launch_one<MK::F16, 128, 6, 1, Epi::F32_BIAS, false>(c, A, B, M, N, K, ep, cg);
       return launch_one<MK::F16, 64, 8, 1, Epi::F32_BIAS, false>(c, A, B, M, N, K, ep, cg);
     }
     case GemmKind::BF16X3: {
       if (epi != Epi::F32_BIAS) break;
-      if (!cg.enabled && !ep.remap && !ep.split_out && !ep.pool4 && !ep.img_absmax && K >= 2048 &&
-          2 * tiles(M, N, 128, 256) <= sms && (long long)M * N < (1LL << 31))
+      switch (pick(TuneFamily::F32)) {
+        case 0:
+          return launch_one<MK::F16, 64, 4, 3, Epi::F32_BIAS, false>(c, A, B, M, N, K, ep, cg);
+        case 1:
+          return launch_one<MK::F16, 64, 5, 3, Epi::F32_BIAS, false, 64, false, 2>(c, A, B, M, N,
+                                                                                  K, ep, cg);
+        case 2:
+          return launch_one<MK::F16, 128, 3, 3, Epi::F32_BIAS, false>(c, A, B, M, N, K, ep, cg);
+        case 3:
+          return launch_one<MK::F16, 128, 4, 3, Epi::F32_BIAS, false, 64, false, 2>(c, A, B, M, N,
+                                                                                   K, ep, cg);
+        case 4:
+          return launch_one<MK::F16, 256, 4, 3, Epi::F32_BIAS, false, 64>(c, A, B, M, N, K, ep, cg);
+        case 5:
+          return gemm_bf16x3_splitk(c, A, B, M, N, K, ep, (int)tiles(M, N, 128, 256));
+        default:
+          break;
+      }
+      if (plain && K >= 2048 && 2 * tiles(M, N, 128, 256) <= sms && (long long)M * N < (1LL << 31))
         return gemm_bf16x3_splitk(c, A, B, M, N, K, ep, (int)tiles(M, N, 128, 256));
       if (cg.enabled && cg.pair)  // row-pair (pooled) convolution: two sub-tiles per CTA
         return N > 64 ? launch_one<MK::F16, 128, 4, 3, Epi::F32_BIAS, false, 64, false, 2>(

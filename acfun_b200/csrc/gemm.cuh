@@ -51,6 +51,24 @@ bool gemm_launch(Call& c, GemmKind kind, Epi epi, const Operand& A, const Operan
                  int N, int K, const EpiParams& ep, const ConvGeom& cg = ConvGeom{});
 int gemm_bke(GemmKind kind);  // K elements per pipeline block (128 bytes)
 
+// ---- tile table (acfun_autotune, tune.cu) ----
+// Plain GEMMs (no implicit convolution, no remap / split / pool / maximum epilogue) of three
+// families choose among several tile variants; the built-in choice is a size heuristic, and a
+// table measured on this GPU by acfun_autotune overrides it per shape class (M, N, K rounded
+// up to powers of two).
+enum class TuneFamily : int { F32 = 0, BF16 = 1, I8 = 2 };
+constexpr int kTuneVariants[3] = {6, 3, 2};
+// F32 (3xBF16): 0 BN64 BKB128 | 1 BN64 BKB64 two sub-tiles | 2 BN128 BKB128 |
+//               3 BN128 BKB64 two sub-tiles | 4 BN256 BKB64 | 5 split-K over 256x128 tiles
+// BF16:         0 BN64 | 1 BN128 | 2 BN256
+// I8:           0 BN128 | 1 BN256
+bool tune_variant_valid(TuneFamily f, int v, int M, int N, int K);
+// The table's variant for the shape class (or -1), or the variant the tuner forces on this
+// thread while it measures.  The first lookup loads the table; with ACFUN_AUTOTUNE=1 and no
+// table it measures one first, on the caller's stream.
+int tune_variant(Call& c, TuneFamily f, int M, int N, int K);
+void tune_force(int v);  // tuner only; -1 ends it
+
 // u8 x s8 GEMM with a K-major B ([N][K] rows, ld = row pitch in bytes) and `bkb`-byte K
 // blocks (64 or 128): tiles 64..256 wide, so narrow outputs (N <= 64) waste no MMA work.
 // With cg.enabled, B is [N][taps*cpad] and cg.cblocks counts bkb-byte channel blocks.

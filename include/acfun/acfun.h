@@ -34,13 +34,20 @@ extern "C" {
 void acfun_set_threads(int n);                 /* acfun.h:20 — kept for ABI; CPU thread count has no meaning here */
 int acfun_backend(void);                       /* acfun.h:23 — returns 4 (ACFUN_BACKEND_CUDA_SM100A) */
 const char* acfun_backend_name(void);          /* acfun.h:24 — "CUDA-sm100a" */
-void acfun_autotune(void);                     /* acfun.h:29 — tile shapes are compile-time: no-op */
-const char* acfun_tune_status(void);           /* acfun.h:30 — describes the fixed tile configuration */
+/* acfun.h:29 — measures, on the current GPU, the fastest tcgen05 tile variant of the plain
+ * fp32 (3xBF16), bf16 and int8 GEMMs per shape class (M, N, K rounded up to powers of two) and
+ * writes the table to $ACFUN_TUNE_CACHE or ~/.cache/acfun/tile_table_<gpu>.txt; later runs load
+ * it on first use.  Without a table the built-in size heuristics choose.  Results do not
+ * depend on the table (it only picks among tested kernels). */
+void acfun_autotune(void);
+/* acfun.h:30 — "tuned: <n> shape classes ..." or "static heuristics: ..." */
+const char* acfun_tune_status(void);
 
 #define ACFUN_BACKEND_CUDA_SM100A 4
 
 /* ---- GEMM (reference acfun.h:33-51) ---- */
-/* acfun.h:33 — fp32 C = A*B; computed as 3xTF32 on tcgen05 tensor cores (fp32-class error) */
+/* acfun.h:33 — fp32 C = A*B; computed as 3xBF16 on tcgen05 tensor cores (3xTF32 with
+ * acfun_set_fp32_math(1)), fp32-class error */
 void acfun_gemm(int M, int N, int K, const float* A, const float* B, float* C);
 /* acfun.h:43 — C = A*B + bias[j] (bias may be NULL), then ReLU if act==1 */
 void acfun_gemm_epi(int M, int N, int K, const float* A, const float* B, float* C,
