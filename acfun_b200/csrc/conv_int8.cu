@@ -950,27 +950,28 @@ __global__ void __launch_bounds__(128) k_conv_int8_pool(
           }
         }
     float m[16];
-    if (act) {
-      // the window maximum of the int32 sums, then one dequantisation: (float)acc*alpha + beta
-      // is non-decreasing in acc (alpha = sa*ws >= 0) and ReLU maps both zeros to +0, so this
-      // is the maximum of the four dequantised, activated values bit for bit
+    // The window maximum of the int32 sums, then one dequantisation: (float)acc*alpha + beta
+    // is non-decreasing in acc (alpha = sa*ws >= 0) and so is ReLU, so this is the maximum of
+    // the four dequantised values bit for bit -- except that with alpha == 0 and beta == +-0
+    // the four values are zeros whose signs follow the sums' signs; such a channel (only
+    // without ReLU, which maps both zeros to +0) takes the per-pixel maximum.
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
+    for (int j = 0; j < 16; ++j) {
+      const float al = alpha[cb * 16 + j], be = beta[cb * 16 + j];
+      float v;
+      if (act || al > 0.0f || be != 0.0f) {
         const int a = max(max(acc[0][j], acc[1][j]), max(acc[2][j], acc[3][j]));
-        const float v = __fadd_rn(__fmul_rn(__int2float_rn(a), alpha[cb * 16 + j]), beta[cb * 16 + j]);
-        m[j] = zero ? 0.0f : (v > 0.0f ? v : 0.0f);
-      }
-    } else {
+        v = __fadd_rn(__fmul_rn(__int2float_rn(a), al), be);
+        if (act) v = v > 0.0f ? v : 0.0f;
+      } else {
+        v = -1e30f;
 #pragma unroll
-      for (int j = 0; j < 16; ++j) m[j] = -1e30f;
-#pragma unroll
-      for (int p = 0; p < 4; ++p)
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          float v = __fadd_rn(__fmul_rn(__int2float_rn(acc[p][j]), alpha[cb * 16 + j]), beta[cb * 16 + j]);
-          v = zero ? 0.0f : v;
-          m[j] = m[j] > v ? m[j] : v;
+        for (int p = 0; p < 4; ++p) {
+          const float u = __fadd_rn(__fmul_rn(__int2float_rn(acc[p][j]), al), be);
+          v = v > u ? v : u;
         }
+      }
+      m[j] = zero ? 0.0f : v;
     }
     float* dst = out + (((size_t)n * PH + ph) * PW + pw) * Cout + cb * 16;
 #pragma unroll
