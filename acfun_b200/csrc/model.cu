@@ -192,7 +192,12 @@ static AcfunModel* load_blob(std::vector<unsigned char>&& blob) {
     }
     raw.push_back(L);
   }
-  // ---- fusion (model.cpp:198-247)
+  // ---- fusion (model.cpp:198-247).  ACFUN_PARITY_STRICT=0 corrects the reference's two
+  // order quirks instead of reproducing them: a ReLU right before a MaxPool is kept, and
+  // Conv -> ReLU -> BN keeps the BN as its own layer after the activation (the reference
+  // folds it into the conv, i.e. applies BN before ReLU).
+  const char* strict_env = getenv("ACFUN_PARITY_STRICT");
+  const bool strict = !(strict_env && strict_env[0] == '0' && strict_env[1] == 0);
   const int n = (int)raw.size();
   std::vector<char> consumed(n, 0);
   for (int i = 0; i < n; ++i) {
@@ -204,17 +209,17 @@ static AcfunModel* load_blob(std::vector<unsigned char>&& blob) {
       const int Cout = L.type == 2 ? L.p[0] : L.p[2];
       int j = i + 1, relu_idx = -1;
       if (j < n && raw[j].type == 3) relu_idx = j++;
-      if (j < n && raw[j].type == 6 && raw[j].p[0] == Cout) {
+      if (j < n && raw[j].type == 6 && raw[j].p[0] == Cout && (strict || relu_idx < 0)) {
         fold_bn(F, raw[j], Cout, m.get());
         consumed[j] = 1;
       }
       if (relu_idx >= 0) {
         consumed[relu_idx] = 1;
-        F.act = (j < n && raw[j].type == 4) ? 0 : 1;
+        F.act = (strict && j < n && raw[j].type == 4) ? 0 : 1;
       }
       m->layers.push_back(F);
     } else if (L.type == 3) {
-      if (i + 1 < n && raw[i + 1].type == 4) {
+      if (strict && i + 1 < n && raw[i + 1].type == 4) {
         consumed[i] = 1;
         continue;
       }

@@ -245,3 +245,35 @@ def test_model_pooled_conv_vs_oracle(acf, tmp_path, hw, cin, c2, k2, nimg):
         assert_bits_equal(y8[k], om.infer(x[k], int8=True).reshape(y8[k].shape), f"int8 image {k}")
     assert_bits_equal(m.infer_batch(np.ascontiguousarray(x[-1:]))[0], y8[-1], "int8 last image alone")
     m.close()
+
+
+def test_parity_strict_off_corrects_the_loader_quirks(acf, tmp_path, monkeypatch):
+    """ACFUN_PARITY_STRICT=0: a ReLU before MaxPool is kept (the reference drops it), and
+    Conv -> ReLU -> BN applies BN after the activation (the reference folds BN into the conv)."""
+    from acfun_b200.acfun0 import Acfun0Writer, bn_params
+    g = np.random.default_rng(21)
+    w = g.uniform(-0.3, 0.3, (36, 8)).astype(np.float32)
+    b = np.where(np.arange(8) % 2 == 0, -10.0, 0.2).astype(np.float32)  # all-negative channels
+    x = g.uniform(0, 1, (2, 10, 10, 4)).astype(np.float32)
+
+    def run(Wr, name):
+        p = tmp_path / name
+        p.write_bytes(Wr.tobytes())
+        m = acf.Model(str(p))
+        y = m.infer_batch(x)
+        m.close()
+        return y
+
+    pool_model = lambda: Acfun0Writer(4, 10, 10).conv(w, b, 3, 3, 8, 1, 1).relu().maxpool(2, 2, 0)
+    y_strict = run(pool_model(), "a.acfun")
+    assert (y_strict < 0).any()                       # the dropped ReLU: pooled negatives
+    monkeypatch.setenv("ACFUN_PARITY_STRICT", "0")
+    y_fixed = run(pool_model(), "b.acfun")
+    assert_bits_equal(y_fixed, np.maximum(y_strict, 0.0), "ReLU kept before MaxPool")
+
+    mean, var, gamma, beta = bn_params(g, 8)
+    y_bn = run(Acfun0Writer(4, 10, 10).conv(w, b, 3, 3, 8, 1, 1).relu().bn(mean, var, gamma, beta),
+               "c.acfun")
+    conv = acf.conv2d(x, w, b, 3, 3, 8, 1, 1, 1).reshape(2, 10, 10, 8)   # ReLU'd conv
+    ref = ((conv - mean) / np.sqrt(var + 1e-5) * gamma + beta).reshape(y_bn.shape)  # then BN
+    assert max_rel(y_bn, ref) < TOL_F32, max_rel(y_bn, ref)
