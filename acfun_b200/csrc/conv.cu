@@ -837,12 +837,28 @@ bool split_weights_dev(Call& c, const float* w, int taps, int Cin, int Cout, voi
 
 long long pair_geometry(ConvGeom& cg, int N, int Hp, int OH, int OW) {
   if (Hp % 2 != 0 || OH < 2 || OW < 2) return 0;
-  int bxl = 1;
-  while ((1 << bxl) < OW && bxl < 7) ++bxl;
+  // Tile width 2^bxl: the widest whose column blocks cover the 2*(OW/2) pooled columns with
+  // at most 3 % padding (every padding column is MMA work for a discarded lane), else the
+  // least padded; e.g. OW 112 -> 16 (7 blocks), 56 -> 8, 28 -> 4, 14 -> 2.
+  const int used = 2 * (OW / 2);
+  int bxl = 0;
+  double best = -1.0;
+  for (int l = 7; l >= 1; --l) {
+    const int bx = 1 << l, blocks = (used + bx - 1) / bx;
+    const double util = (double)used / ((double)blocks * bx);
+    if (util >= 0.97) {
+      bxl = l;
+      break;
+    }
+    if (util > best) {
+      best = util;
+      bxl = l;
+    }
+  }
   cg.pair = 1;
   cg.bxl = bxl;
   cg.by = 128 >> bxl;
-  cg.xb = (OW + (1 << bxl) - 1) >> bxl;
+  cg.xb = (used + (1 << bxl) - 1) >> bxl;
   cg.hp2 = Hp / 2;
   cg.npr = N * (Hp / 2);
   const long long pb = (cg.npr + cg.by - 1) / cg.by;
