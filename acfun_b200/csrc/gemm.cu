@@ -144,44 +144,45 @@ Operand to_tf32x2(Call& c, const float* src, int rows, int cols, long long lds) 
   return o;
 }
 
-// Round-to-nearest-even fp32 -> bf16 with NaN kept quiet (for the 3xBF16 split; the
-// bf16 GEMM entry point keeps the reference's bit trick, bf16_bits_ref).
-__device__ __forceinline__ uint16_t bf16_rne(float f) {
-  const uint32_t x = __float_as_uint(f);
-  if ((x & 0x7f800000u) == 0x7f800000u) return (uint16_t)((x >> 16) | ((x & 0xffffu) ? 0x40u : 0u));
-  return (uint16_t)((x + 0x7fffu + ((x >> 16) & 1u)) >> 16);
-}
-__device__ __forceinline__ float bf16_val(uint16_t h) { return __uint_as_float((uint32_t)h << 16); }
-
 // 3xBF16 split: x = hi + lo + r with hi = bf16(x), lo = bf16(x - hi), |r| <= 2^-18 |x|;
-// fp32 [rows][cols] -> [2][rows][ldp] bf16, zero padding (ldp a multiple of 8).
-__global__ void k_to_bf16x2(const float* __restrict__ src, long long lds, int rows, int cols,
-                            uint16_t* __restrict__ dst, long long ldp, long long op_stride) {
-  const long long groups = ldp / 4;
-  const long long total = (long long)rows * groups;
-  for (long long g = blockIdx.x * (long long)blockDim.x + threadIdx.x; g < total;
+// fp32 [rows][cols] -> [2][rows][ldp] bf16, zero padding (ldp a multiple of 8).  One launch
+// splits one or two matrices (job 1's 4-column groups follow job 0's).
+struct Bf16x2Job {
+  const float* src;
+  long long lds;
+  int rows, cols;
+  uint16_t* dst;
+  long long ldp, op_stride;
+};
+__global__ void k_to_bf16x2(Bf16x2Job j0, Bf16x2Job j1, long long g0, long long gt) {
+  for (long long g = blockIdx.x * (long long)blockDim.x + threadIdx.x; g < gt;
        g += (long long)gridDim.x * blockDim.x) {
-    const long long r = g / groups;
-    const int j = (int)(g - r * groups) * 4;
-    const float* s = src + r * lds;
-    uint32_t hi2[2], lo2[2];
+    const bool sec = g >= g0;
+    const float* src = sec ? j1.src : j0.src;
+    const long long lds = sec ? j1.lds : j0.lds, ldp = sec ? j1.ldp : j0.ldp;
+    const int cols = sec ? j1.cols : j0.cols;
+    uint16_t* dst = sec ? j1.dst : j0.dst;
+    const long long ops = sec ? j1.op_stride : j0.op_stride;
+    const long long gg = sec ? g - g0 : g, groups = ldp / 4;
+    const long long r = gg / groups;
+    const int j = (int)(gg - r * groups) * 4;
+    const float* s = src + r * lds + j;
+    float v[4];
+    if (j + 4 <= cols && (reinterpret_cast<uintptr_t>(s) & 15) == 0) {
+      const float4 q = __ldg(reinterpret_cast<const float4*>(s));
+      v[0] = q.x;
+      v[1] = q.y;
+      v[2] = q.z;
+      v[3] = q.w;
+    } else {
 #pragma unroll
-    for (int t = 0; t < 2; ++t) {
-      uint32_t hp = 0, lp = 0;
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int jj = j + 2 * t + u;
-        const float x = jj < cols ? s[jj] : 0.0f;
-        const uint16_t h = bf16_rne(x);
-        const uint16_t l = bf16_rne(x - bf16_val(h));
-        hp |= (uint32_t)h << (16 * u);
-        lp |= (uint32_t)l << (16 * u);
-      }
-      hi2[t] = hp;
-      lo2[t] = lp;
+      for (int u = 0; u < 4; ++u) v[u] = j + u < cols ? s[u] : 0.0f;
     }
-    *reinterpret_cast<uint2*>(dst + r * ldp + j) = make_uint2(hi2[0], hi2[1]);
-    *reinterpret_cast<uint2*>(dst + op_stride + r * ldp + j) = make_uint2(lo2[0], lo2[1]);
+    uint32_t h0, l0, h1, l1;
+    nx_split_bf16x2(v[0], v[1], h0, l0);
+    nx_split_bf16x2(v[2], v[3], h1, l1);
+    *reinterpret_cast<uint2*>(dst + r * ldp + j) = make_uint2(h0, h1);
+    *reinterpret_cast<uint2*>(dst + ops + r * ldp + j) = make_uint2(l0, l1);
   }
 }
 
@@ -189,19 +190,38 @@ long long bf16x2_bytes(int rows, int cols) {
   return 2LL * rows * (long long)align_up((size_t)cols, 8) * 2;
 }
 
-Operand to_bf16x2(Call& c, const float* src, int rows, int cols, long long lds, void* into) {
-  Operand o;
-  if (!c.ok()) return o;
+static bool bf16x2_job(Call& c, const float* src, int rows, int cols, long long lds, void* into,
+                       Bf16x2Job& j, Operand& o) {
   const long long ldp = (long long)align_up((size_t)cols, 8);
   uint16_t* d = into ? (uint16_t*)into : (uint16_t*)c.scratch((size_t)2 * rows * ldp * 2);
-  if (!d) return o;
-  k_to_bf16x2<<<ew_grid(c, rows * (ldp / 4)), 256, 0, c.stream()>>>(src, lds, rows, cols, d, ldp,
-                                                                      (long long)rows * ldp);
-  if (!c.launched("k_to_bf16x2")) return o;
+  if (!d) return false;
+  j = Bf16x2Job{src, lds, rows, cols, d, ldp, (long long)rows * ldp};
   o.p = d;
   o.ld = ldp;
   o.op_stride = (long long)rows * ldp;
+  return true;
+}
+
+Operand to_bf16x2(Call& c, const float* src, int rows, int cols, long long lds, void* into) {
+  Operand o;
+  Bf16x2Job j{};
+  if (!c.ok() || !bf16x2_job(c, src, rows, cols, lds, into, j, o)) return Operand{};
+  const long long g = (long long)rows * (j.ldp / 4);
+  k_to_bf16x2<<<ew_grid(c, g), 256, 0, c.stream()>>>(j, j, g, g);
+  if (!c.launched("k_to_bf16x2")) return Operand{};
   return o;
+}
+
+// Both operands of a 3xBF16 GEMM in one launch.
+static bool to_bf16x2_pair(Call& c, const float* a, int ar, int ac, long long lda, const float* b,
+                           int br, int bc, long long ldb, Operand& oa, Operand& ob) {
+  Bf16x2Job ja{}, jb{};
+  if (!c.ok() || !bf16x2_job(c, a, ar, ac, lda, nullptr, ja, oa) ||
+      !bf16x2_job(c, b, br, bc, ldb, nullptr, jb, ob))
+    return false;
+  const long long g0 = (long long)ar * (ja.ldp / 4), gt = g0 + (long long)br * (jb.ldp / 4);
+  k_to_bf16x2<<<ew_grid(c, gt), 256, 0, c.stream()>>>(ja, jb, g0, gt);
+  return c.launched("k_to_bf16x2");
 }
 
 // 0 (default) and 2: 3xBF16 everywhere; 1: 3xTF32 everywhere.  Initialised from
@@ -569,9 +589,14 @@ bool gemm_f32(Call& c, const float* dA, long long lda, const float* dB, long lon
               int N, int K, float* dC, long long ldc, const float* dbias, int act, Fp32Use use,
               const Operand* b_split) {
   const bool bf = fp32_math(use) == Fp32Math::BF16X3;
-  Operand a = bf ? to_bf16x2(c, dA, M, K, lda) : to_tf32x2(c, dA, M, K, lda);
-  Operand b = (bf && b_split) ? *b_split
-                              : bf ? to_bf16x2(c, dB, K, N, ldb) : to_tf32x2(c, dB, K, N, ldb);
+  Operand a, b;
+  if (bf && !b_split) {
+    if (!to_bf16x2_pair(c, dA, M, K, lda, dB, K, N, ldb, a, b)) return false;
+  } else {
+    a = bf ? to_bf16x2(c, dA, M, K, lda) : to_tf32x2(c, dA, M, K, lda);
+    b = (bf && b_split) ? *b_split
+                        : bf ? to_bf16x2(c, dB, K, N, ldb) : to_tf32x2(c, dB, K, N, ldb);
+  }
   EpiParams ep{};
   ep.C = dC;
   ep.ldc = ldc;
