@@ -55,27 +55,6 @@ __device__ __forceinline__ float tf32_rne(float x) {
   return __uint_as_float(u & 0xffffe000u);
 }
 
-__global__ void k_to_bf16(const float* __restrict__ src, long long lds, int rows, int cols,
-                          uint16_t* __restrict__ dst, long long ldp) {
-  const long long groups = ldp / 8;
-  const long long total = (long long)rows * groups;
-  for (long long g = blockIdx.x * (long long)blockDim.x + threadIdx.x; g < total;
-       g += (long long)gridDim.x * blockDim.x) {
-    const long long r = g / groups;
-    const int j = (int)(g - r * groups) * 8;
-    const float* s = src + r * lds;
-    uint32_t w[4];
-#pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      const int j0 = j + 2 * t, j1 = j0 + 1;
-      const uint16_t lo = j0 < cols ? bf16_bits_ref(s[j0]) : 0;
-      const uint16_t hi = j1 < cols ? bf16_bits_ref(s[j1]) : 0;
-      w[t] = (uint32_t)lo | ((uint32_t)hi << 16);
-    }
-    *reinterpret_cast<uint4*>(dst + r * ldp + j) = make_uint4(w[0], w[1], w[2], w[3]);
-  }
-}
-
 __global__ void k_to_tf32x2(const float* __restrict__ src, long long lds, int rows, int cols,
                             float* __restrict__ dst, long long ldp, long long op_stride) {
   const long long groups = ldp / 4;
@@ -116,16 +95,63 @@ static int ew_grid(Call& c, long long work) {
   return (int)b;
 }
 
-Operand to_bf16(Call& c, const float* src, int rows, int cols, long long lds) {
-  Operand o;
-  if (!c.ok()) return o;
+// One launch converts one or two fp32 matrices (job 1's 8-column groups follow job 0's).
+struct Bf16Job {
+  const float* src;
+  long long lds;
+  int rows, cols;
+  uint16_t* dst;
+  long long ldp;
+};
+__global__ void k_to_bf16(Bf16Job j0, Bf16Job j1, long long g0, long long gt) {
+  for (long long g = blockIdx.x * (long long)blockDim.x + threadIdx.x; g < gt;
+       g += (long long)gridDim.x * blockDim.x) {
+    const bool sec = g >= g0;
+    const float* src = sec ? j1.src : j0.src;
+    const long long lds = sec ? j1.lds : j0.lds, ldp = sec ? j1.ldp : j0.ldp;
+    const int cols = sec ? j1.cols : j0.cols;
+    uint16_t* dst = sec ? j1.dst : j0.dst;
+    const long long gg = sec ? g - g0 : g, groups = ldp / 8;
+    const long long r = gg / groups;
+    const int j = (int)(gg - r * groups) * 8;
+    const float* s = src + r * lds + j;
+    float v[8];
+    if (j + 8 <= cols && (reinterpret_cast<uintptr_t>(s) & 15) == 0) {
+      const float4 p = __ldg(reinterpret_cast<const float4*>(s));
+      const float4 q = __ldg(reinterpret_cast<const float4*>(s + 4));
+      v[0] = p.x; v[1] = p.y; v[2] = p.z; v[3] = p.w;
+      v[4] = q.x; v[5] = q.y; v[6] = q.z; v[7] = q.w;
+    } else {
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = j + u < cols ? s[u] : 0.0f;
+    }
+    uint32_t w[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const uint16_t lo = j + 2 * t < cols ? bf16_bits_ref(v[2 * t]) : 0;
+      const uint16_t hi = j + 2 * t + 1 < cols ? bf16_bits_ref(v[2 * t + 1]) : 0;
+      w[t] = (uint32_t)lo | ((uint32_t)hi << 16);
+    }
+    *reinterpret_cast<uint4*>(dst + r * ldp + j) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+static bool bf16_job(Call& c, const float* src, int rows, int cols, long long lds, Bf16Job& j,
+                     Operand& o) {
   const long long ldp = (long long)align_up((size_t)cols, 8);
   uint16_t* d = (uint16_t*)c.scratch((size_t)rows * ldp * 2);
-  if (!d) return o;
-  k_to_bf16<<<ew_grid(c, rows * (ldp / 8)), 256, 0, c.stream()>>>(src, lds, rows, cols, d, ldp);
-  if (!c.launched("k_to_bf16")) return o;
+  if (!d) return false;
+  j = Bf16Job{src, lds, rows, cols, d, ldp};
   o.p = d;
   o.ld = ldp;
+  return true;
+}
+Operand to_bf16(Call& c, const float* src, int rows, int cols, long long lds) {
+  Operand o;
+  Bf16Job j{};
+  if (!c.ok() || !bf16_job(c, src, rows, cols, lds, j, o)) return Operand{};
+  const long long g = (long long)rows * (j.ldp / 8);
+  k_to_bf16<<<ew_grid(c, g), 256, 0, c.stream()>>>(j, j, g, g);
+  if (!c.launched("k_to_bf16")) return Operand{};
   return o;
 }
 
@@ -643,8 +669,19 @@ extern "C" void acfun_gemm_bf16(int M, int N, int K, const float* A, const float
   const float* dB = (const float*)c.in(B, (size_t)K * N * 4);
   float* dC = (float*)c.out(C, (size_t)M * N * 4);
   if (!c.ok()) return;
-  Operand a = to_bf16(c, dA, M, K, K);
-  Operand b = to_bf16(c, dB, K, N, N);
+  // both operands converted in one launch
+  Operand a, b;
+  Bf16Job ja{}, jb{};
+  if (!bf16_job(c, dA, M, K, K, ja, a) || !bf16_job(c, dB, K, N, N, jb, b)) {
+    c.finish();
+    return;
+  }
+  const long long g0 = (long long)M * (ja.ldp / 8), gt = g0 + (long long)K * (jb.ldp / 8);
+  k_to_bf16<<<ew_grid(c, gt), 256, 0, c.stream()>>>(ja, jb, g0, gt);
+  if (!c.launched("k_to_bf16")) {
+    c.finish();
+    return;
+  }
   EpiParams ep{};
   ep.C = dC;
   ep.ldc = N;
