@@ -274,6 +274,16 @@ Fp32Math fp32_math(Fp32Use use) {
   return Fp32Math::BF16X3;
 }
 
+// Column split of the persistent walk's last wave (ConvGeom::nsplit): on unless
+// ACFUN_TAIL_SPLIT=0.
+static bool tail_split_on() {
+  static const bool on = [] {
+    const char* e = getenv("ACFUN_TAIL_SPLIT");
+    return !(e && !strcmp(e, "0"));
+  }();
+  return on;
+}
+
 // ------------------------------------------------------------------ launcher
 template <dev::MmaKind KIND, int BN, int STAGES, int NPASS, Epi EPI, bool AS, int BKB = 128,
           bool BKM = false, int MT = 1>
@@ -359,18 +369,34 @@ static bool launch_one(Call& c, const Operand& A, const Operand& B, int M, int N
     }
     attr_done[dv] = true;
   }
-  const long long tiles = (long long)((M + S::BM - 1) / S::BM) * ((N + BN - 1) / BN) *
-                          ((!cg.enabled && cg.ksplit > 1) ? cg.ksplit : 1);
+  const long long tiles_mn = (long long)((M + S::BM - 1) / S::BM) * ((N + BN - 1) / BN);
+  long long tiles = tiles_mn * ((!cg.enabled && cg.ksplit > 1) ? cg.ksplit : 1);
   if (tiles >= (1LL << 31)) {
     set_error(kInvalid, "%s: problem too large", c.name());
     c.fail();
     return false;
   }
-  // persistent: one CTA per SM (1 CTA/SM by shared memory), tiles strided over the grid
-  const dim3 grid((unsigned)(tiles < c.sm_count() ? tiles : c.sm_count()));
   // the implicit convolution walks cpad channels per tap in blocks of this variant's BKE
   ConvGeom g = cg;
   if (g.enabled) g.cblocks = g.cpad / S::BKE;
+  const int sms = c.sm_count();
+  g.nsplit = 0;
+  g.tfull = 0;
+  if (MT == 1 && !BKM && !g.enabled && g.ksplit <= 1 && tail_split_on()) {
+    // the last wave holds rem < sms tiles: run them as rem * ns column parts (whole B
+    // chunks, >= 64 columns each) when those still fit in one wave
+    const long long rem = tiles_mn % sms;
+    int ns = 1;
+    while (ns < 4 && S::NCHUNK % (2 * ns) == 0 && BN / (2 * ns) >= 64 && rem * 2 * ns <= sms)
+      ns *= 2;
+    if (rem > 0 && ns > 1) {
+      g.nsplit = ns;
+      g.tfull = (int)(tiles_mn - rem);
+      tiles = g.tfull + rem * ns;
+    }
+  }
+  // persistent: one CTA per SM (1 CTA/SM by shared memory), tiles strided over the grid
+  const dim3 grid((unsigned)(tiles < sms ? tiles : sms));
   kern<<<grid, S::THREADS, S::SMEM, c.stream()>>>(ta, tb, ep, g, M, N, K, c.err());
   return c.launched("gemm_tc_kernel");
 }

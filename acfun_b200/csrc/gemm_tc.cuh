@@ -85,7 +85,38 @@ struct ConvGeom {
   // Split-K (plain GEMMs only): tile t covers K blocks of split t / (tiles_m*tiles_n), whose
   // raw accumulator goes to rows ks*M + r of C (partials [ksplit][M][ldc], summed by the caller)
   int ksplit;
+  // Column split of the last wave (plain GEMMs, MT = 1, MN-major B): tiles [0, tfull) run
+  // whole; each remaining tile -- the last, partial wave of the persistent walk -- becomes
+  // nsplit units of BN / nsplit columns (the same K loop and MMA per column, so the same
+  // bits), which spreads that wave over up to nsplit times as many SMs.
+  int nsplit, tfull;
 };
+
+// One unit of a CTA's persistent walk: a whole tile, one split-K slice of it, or column part
+// `part` (>= 0) of a last-wave tile; K blocks [kb0, kb1).
+struct TileUnit {
+  int tt, ks, kb0, kb1, part;
+};
+
+__device__ __forceinline__ TileUnit tile_unit(int t, int tiles_mn, int nkb_all, int nkb_s,
+                                              int nsplit, int tfull) {
+  TileUnit u;
+  if (nsplit > 1 && t >= tfull) {
+    const int v = t - tfull;
+    u.tt = tfull + v / nsplit;
+    u.part = v - (u.tt - tfull) * nsplit;
+    u.ks = 0;
+    u.kb0 = 0;
+    u.kb1 = nkb_all;
+  } else {
+    u.tt = t % tiles_mn;
+    u.ks = t / tiles_mn;
+    u.part = -1;
+    u.kb0 = u.ks * nkb_s;
+    u.kb1 = min(nkb_all, u.kb0 + nkb_s);
+  }
+  return u;
+}
 
 // Per-column epilogue parameters of one 32-column chunk, staged in the epilogue warp's own
 // shared-memory slice: pa / pb (float) and pc (int32), 32 entries each, zero past column N.
@@ -453,7 +484,9 @@ __global__ void __launch_bounds__(320, 1)
   const int tiles_n = (N + BN - 1) / BN;
   const int tiles_mn = tiles_m * tiles_n;
   const int ksplit = (!cg.enabled && cg.ksplit > 1) ? cg.ksplit : 1;
-  const int num_tiles = tiles_mn * ksplit;
+  const int nsplit =
+      (MT == 1 && !B_KMAJ && !cg.enabled && ksplit == 1 && cg.nsplit > 1) ? cg.nsplit : 0;
+  const int num_tiles = nsplit ? cg.tfull + (tiles_mn - cg.tfull) * nsplit : tiles_mn * ksplit;
   const int nkb_all = cg.enabled ? cg.taps * cg.cblocks : (K + S::BKE - 1) / S::BKE;
   const int nkb_s = (nkb_all + ksplit - 1) / ksplit;  // K blocks per split
 
@@ -490,9 +523,15 @@ __global__ void __launch_bounds__(320, 1)
     bool stop = false;
     for (int t = blockIdx.x; t < num_tiles && !stop; t += gridDim.x) {
       if (*abort_flag) break;
-      const int tt = t % tiles_mn, ks = t / tiles_mn;
-      const int m0 = (tt / tiles_n) * S::BM, n0 = (tt % tiles_n) * BN;
-      const int kb0 = ks * nkb_s, nkb = min(nkb_all, kb0 + nkb_s);
+      const TileUnit u = tile_unit(t, tiles_mn, nkb_all, nkb_s, nsplit, cg.tfull);
+      const int tt = u.tt;
+      // a column part loads the first NCHUNK / nsplit B chunks of its own column range
+      const int nch = u.part >= 0 ? S::NCHUNK / nsplit : S::NCHUNK;
+      const uint32_t stage_bytes =
+          u.part >= 0 ? (uint32_t)(S::NOPS * (S::A_OP + nch * S::CHUNK_B)) : (uint32_t)S::STAGE;
+      const int m0 = (tt / tiles_n) * S::BM;
+      const int n0 = (tt % tiles_n) * BN + (u.part > 0 ? u.part * (BN / nsplit) : 0);
+      const int kb0 = u.kb0, nkb = u.kb1;
       // conv: channel block, kw, kh, A row shift, B k
       int cb = 0, kw = 0, kh = 0, row_off = 0, tap_k = 0;
       int pr0 = 0, px0 = 0;  // row-pair tiling: first pair and first column of the tile
@@ -508,7 +547,7 @@ __global__ void __launch_bounds__(320, 1)
           break;
         }
         uint8_t* st = smem + s * S::STAGE;
-        dev::mbar_arrive_expect_tx(&full_bar[s], S::STAGE);
+        dev::mbar_arrive_expect_tx(&full_bar[s], stage_bytes);
         int kx, ay, by;
         const int akw = kw, akh = kh;  // this block's tap
         if (cg.enabled) {
@@ -566,8 +605,9 @@ __global__ void __launch_bounds__(320, 1)
             }
 #pragma unroll
             for (int c = 0; c < S::NCHUNK; ++c)
-              dev::tma_load_2d(b_dst + c * S::CHUNK_B, &tmB, &full_bar[s],
-                               n0 + c * (128 / S::ELEM), by);
+              if (c < nch)
+                dev::tma_load_2d(b_dst + c * S::CHUNK_B, &tmB, &full_bar[s],
+                                 n0 + c * (128 / S::ELEM), by);
           } else {
             if (!a_done) {
 #pragma unroll
@@ -576,8 +616,9 @@ __global__ void __launch_bounds__(320, 1)
             }
 #pragma unroll
             for (int c = 0; c < S::NCHUNK; ++c)
-              dev::tma_load_3d(b_dst + c * S::CHUNK_B, &tmB, &full_bar[s],
-                               n0 + c * (128 / S::ELEM), by, op);
+              if (c < nch)
+                dev::tma_load_3d(b_dst + c * S::CHUNK_B, &tmB, &full_bar[s],
+                                 n0 + c * (128 / S::ELEM), by, op);
           }
         }
         ++it;
@@ -600,8 +641,11 @@ __global__ void __launch_bounds__(320, 1)
                                : (KIND == dev::MmaKind::F16) ? 1u : 2u;
     constexpr uint32_t b_fmt = (KIND == dev::MmaKind::I8) ? 1u
                                : (KIND == dev::MmaKind::F16) ? 1u : 2u;
-    constexpr uint32_t idesc =
+    constexpr uint32_t idesc_full =
         dev::umma_idesc(c_fmt, a_fmt, b_fmt, 0u, B_KMAJ ? 0u : 1u, 128u, (uint32_t)BN);
+    const uint32_t idesc_part = nsplit ? dev::umma_idesc(c_fmt, a_fmt, b_fmt, 0u, B_KMAJ ? 0u : 1u,
+                                                         128u, (uint32_t)(BN / nsplit))
+                                       : idesc_full;
     // Shared-memory descriptors are built once; a stage / K-step / operand offset is an add
     // to the 14-bit start-address field (addresses are below 256 KB, so it never carries).
     const uint32_t smem_base = dev::smem_u32(smem);
@@ -619,7 +663,9 @@ __global__ void __launch_bounds__(320, 1)
       }
       dev::tc_fence_after();
       const uint32_t d_tmem = tmem + buf * S::ACC_COLS;
-      const int kb0 = (t / tiles_mn) * nkb_s, nkb = min(nkb_all, kb0 + nkb_s);
+      const TileUnit u = tile_unit(t, tiles_mn, nkb_all, nkb_s, nsplit, cg.tfull);
+      const int kb0 = u.kb0, nkb = u.kb1;
+      const uint32_t idesc = u.part >= 0 ? idesc_part : idesc_full;  // N = this unit's columns
       for (int kb = kb0; kb < nkb; ++kb, ++it) {
         if (!dev::mbar_wait(&full_bar[s], ph, err)) {
           ok = false;
@@ -673,8 +719,11 @@ __global__ void __launch_bounds__(320, 1)
     int staged_n0 = -1;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
       const uint32_t buf = local % S::NBUF, use = local / S::NBUF;
-      const int tt = t % tiles_mn, ksp = t / tiles_mn;
-      const int m0 = (tt / tiles_n) * S::BM, n0 = (tt % tiles_n) * BN;
+      const TileUnit u = tile_unit(t, tiles_mn, nkb_all, nkb_s, nsplit, cg.tfull);
+      const int tt = u.tt, ksp = u.ks;
+      const int nw = u.part >= 0 ? BN / nsplit : BN;  // this unit's columns
+      const int m0 = (tt / tiles_n) * S::BM;
+      const int n0 = (tt % tiles_n) * BN + (u.part > 0 ? u.part * nw : 0);
       if constexpr (EPI != Epi::S32) {
         // per-column parameters of this tile's chunks, loaded before the accumulator is
         // ready (and only when the column block changes)
@@ -773,7 +822,7 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll 1
         for (int k = 0; k < S::CHUNKS_PER_WARP; ++k) {
           const int c0 = h * 32 + 64 * k;
-          if (c0 >= BN || n0 + c0 >= N) break;  // warp-uniform
+          if (c0 >= nw || n0 + c0 >= N) break;  // warp-uniform
           uint32_t v[32];
           dev::tmem_ld32(
               tmem + buf * S::ACC_COLS + (uint32_t)(i * BN + c0) + ((uint32_t)(q * 32) << 16), v);

@@ -202,3 +202,56 @@ def test_s8_requant_two_waves_device(acf, orc):
     orc.oracle().orc_gemm_s8_requant(rows.size, N, K, np.ascontiguousarray(A[rows]), B, bias.ctypes.data,
                                      scale, ref, 1)
     assert_bits_equal(got[rows], ref, "requant two waves")
+
+
+@pytest.mark.parametrize("M,N,K", [(2432, 2000, 700),     # 152 tiles: 4 left, in two halves
+                                   (2560, 2048, 1000)])  # 160 tiles: 12 left, in two halves
+def test_int8_last_wave_column_parts_exact(acf, orc, M, N, K):
+    """The persistent walk's last, partial wave of 128x256 tiles runs as 128-column parts on
+    more SMs (ragged N in the last part): bit-exact against the oracle on the last row
+    blocks, through host and device pointers."""
+    g = np.random.default_rng(M + N + K)
+    A, B = rand_u8s8(g, M, N, K)
+    rows = np.arange(M - 256, M)
+    ref = np.empty((rows.size, N), np.int32)
+    orc.oracle().orc_gemm_int8(rows.size, N, K, np.ascontiguousarray(A[rows]), B, ref)
+    assert_bits_equal(acf.gemm_int8(A, B)[rows], ref, f"last wave {M}x{N}x{K} host")
+    out = acf.gemm_int8(torch_dev(A), torch_dev(B))
+    acf.synchronize()
+    assert_bits_equal(out.cpu().numpy()[rows], ref, f"last wave {M}x{N}x{K} device")
+
+
+@pytest.mark.parametrize("M,N,K", [(2560, 2048, 512), (4096, 4096, 1024)])
+def test_float_last_wave_column_parts(acf, orc, M, N, K):
+    """bf16 and fp32 (3xBF16) GEMMs whose last wave is cut into 64- or 128-column parts:
+    within tolerance of the oracle on the last row blocks."""
+    g = np.random.default_rng(M + K)
+    A = g.uniform(-1, 1, (M, K)).astype(np.float32)
+    B = g.uniform(-1, 1, (K, N)).astype(np.float32)
+    bias = g.uniform(-1, 1, N).astype(np.float32)
+    rows = np.arange(M - 256, M)
+    Ar = np.ascontiguousarray(A[rows])
+    ref = np.empty((rows.size, N), np.float32)
+    orc.oracle().orc_gemm_f32(rows.size, N, K, Ar, B, ref, bias.ctypes.data, 1)
+    got = acf.gemm(A, B, bias, 1)[rows]
+    assert max_rel(got, ref) < TOL_F32, f"fp32 last wave {M}x{N}x{K}: {max_rel(got, ref)}"
+    ref16 = np.empty((rows.size, N), np.float32)
+    orc.oracle().orc_gemm_bf16(rows.size, N, K, Ar, B, ref16)
+    got16 = acf.gemm_bf16(A, B)[rows]
+    assert max_rel(got16, ref16) < 1e-4, f"bf16 last wave {M}x{N}x{K}: {max_rel(got16, ref16)}"
+
+
+def test_int8_full_size_all_elements_vs_fp64(acf):
+    """BASELINE cfg2 shape, u8 x s8 -> s32: every element (444 whole 128x256 tiles, then the
+    68 tiles of the last wave as 136 column halves) equals torch's float64 product on the
+    GPU, exact here because every partial sum is an integer below 2^53."""
+    import torch
+    M = N = K = 4096
+    gen = torch.Generator(device="cuda").manual_seed(7)
+    A = torch.randint(0, 256, (M, K), dtype=torch.uint8, device="cuda", generator=gen)
+    B = torch.randint(-128, 128, (K, N), dtype=torch.int8, device="cuda", generator=gen)
+    out = acf.gemm_int8(A, B)
+    acf.synchronize()
+    ref = (A.double() @ B.double()).to(torch.int32)
+    bad = int((out != ref).sum().item())
+    assert bad == 0, f"{bad} of {M * N} elements differ"
