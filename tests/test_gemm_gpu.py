@@ -255,3 +255,37 @@ def test_int8_full_size_all_elements_vs_fp64(acf):
     ref = (A.double() @ B.double()).to(torch.int32)
     bad = int((out != ref).sum().item())
     assert bad == 0, f"{bad} of {M * N} elements differ"
+
+
+_SPLIT_OFF_CHILD = r"""
+import sys, numpy as np
+import acfun_b200 as acf
+M, N, K = 2560, 2048, 512
+g = np.random.default_rng(11)
+A = g.uniform(-1, 1, (M, K)).astype(np.float32)
+B = g.uniform(-1, 1, (K, N)).astype(np.float32)
+Ai, Bi = g.integers(0, 256, (M, K), dtype=np.uint8), g.integers(-128, 128, (K, N), dtype=np.int8)
+np.savez(sys.argv[1], f32=acf.gemm(A, B), bf16=acf.gemm_bf16(A, B), i8=acf.gemm_int8(Ai, Bi))
+"""
+
+
+def test_last_wave_column_parts_same_bits_as_whole_tiles(acf, tmp_path):
+    """160 tiles on 148 SMs: the 12 last-wave tiles run as column parts by default and as
+    whole tiles with ACFUN_TAIL_SPLIT=0 (a child process); fp32 (3xBF16), bf16 and int8
+    results are bit-identical, because each output column keeps its whole K loop."""
+    import subprocess
+    import sys
+    out = tmp_path / "whole.npz"
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, ACFUN_TAIL_SPLIT="0", PYTHONPATH=root)
+    subprocess.run([sys.executable, "-c", _SPLIT_OFF_CHILD, str(out)], env=env, cwd=root,
+                   check=True, timeout=300)
+    whole = np.load(out)
+    M, N, K = 2560, 2048, 512
+    g = np.random.default_rng(11)
+    A = g.uniform(-1, 1, (M, K)).astype(np.float32)
+    B = g.uniform(-1, 1, (K, N)).astype(np.float32)
+    Ai, Bi = g.integers(0, 256, (M, K), dtype=np.uint8), g.integers(-128, 128, (K, N), dtype=np.int8)
+    assert_bits_equal(acf.gemm(A, B), whole["f32"], "fp32 column parts vs whole tiles")
+    assert_bits_equal(acf.gemm_bf16(A, B), whole["bf16"], "bf16 column parts vs whole tiles")
+    assert_bits_equal(acf.gemm_int8(Ai, Bi), whole["i8"], "int8 column parts vs whole tiles")
