@@ -406,16 +406,14 @@ void orc_conv2d_int8(const float* input, int N, int H, int W, int Cin,
 /* ====================================================== float convolution */
 
 /* Naive direct convolution, accumulation kh -> kw -> ic per output, starting from the
- * bias (the dw / grouped kernels start from the bias: dw.cpp:23, group_conv.cpp:35).
- * Layouts: groups==1 -> [KH*KW*Cin][Cout] (acfun.h:54-58); groups==Cin==Cout -> [C][KH][KW]
- * (acfun.h:72-73); other groups -> [g][KH*KW*Cin_per][Cout_per] (group_conv.cpp:137-139). */
-void orc_conv2d(const float* input, int N, int H, int W, int Cin,
-                const float* weight, const float* bias, int KH, int KW, int Cout,
-                int stride, int pad, int groups, float* output, int act) {
-    if (groups < 1) groups = 1;
+ * bias, one rounding per multiply and per add.  Layouts: groups==1 -> [KH*KW*Cin][Cout]
+ * (acfun.h:54-58); groups==Cin==Cout -> [C][KH][KW] (acfun.h:72-73); other groups ->
+ * [g][KH*KW*Cin_per][Cout_per] (group_conv.cpp:137-139).  The depthwise and grouped-direct
+ * routes go to their exact restatements below. */
+static void conv_naive(const float* input, int N, int H, int W, int Cin,
+                       const float* weight, const float* bias, int KH, int KW, int Cout,
+                       int stride, int pad, int groups, float* output, int act) {
     int OH = (H + 2 * pad - KH) / stride + 1, OW = (W + 2 * pad - KW) / stride + 1;
-    if (OH <= 0 || OW <= 0) return;
-    int dw = (groups > 1 && groups == Cin && groups == Cout);
     int Cin_p = Cin / groups, Cout_p = Cout / groups;
     for (int n = 0; n < N; ++n)
         for (int oh = 0; oh < OH; ++oh)
@@ -431,10 +429,8 @@ void orc_conv2d(const float* input, int N, int H, int W, int Cin,
                             if (iw < 0 || iw >= W) continue;
                             const float* ip = input + (((size_t)n * H + ih) * W + iw) * Cin + (size_t)g * Cin_p;
                             for (int ic = 0; ic < Cin_p; ++ic) {
-                                float wv;
-                                if (dw) wv = weight[((size_t)oc * KH + kh) * KW + kw];
-                                else wv = weight[(size_t)g * KH * KW * Cin_p * Cout_p +
-                                                 ((size_t)(kh * KW + kw) * Cin_p + ic) * Cout_p + ocp];
+                                float wv = weight[(size_t)g * KH * KW * Cin_p * Cout_p +
+                                                  ((size_t)(kh * KW + kw) * Cin_p + ic) * Cout_p + ocp];
                                 s += ip[ic] * wv;
                             }
                         }
@@ -444,26 +440,72 @@ void orc_conv2d(const float* input, int N, int H, int W, int Cin,
                 }
 }
 
-/* dw.cpp:9-39 */
-void orc_conv2d_dw(const float* input, int N, int H, int W, int C, const float* weight,
-                   const float* bias, int KH, int KW, int stride, int pad, float* output, int act) {
-    orc_conv2d(input, N, H, W, C, weight, bias, KH, KW, C, stride, pad, C > 1 ? C : 1, output, act);
-    if (C == 1) { /* groups==1 layout [KH*KW*1][1] equals [1][KH][KW] */ }
+void orc_conv2d(const float* input, int N, int H, int W, int Cin,
+                const float* weight, const float* bias, int KH, int KW, int Cout,
+                int stride, int pad, int groups, float* output, int act) {
+    if (groups < 1) groups = 1;
+    int OH = (H + 2 * pad - KH) / stride + 1, OW = (W + 2 * pad - KW) / stride + 1;
+    if (OH <= 0 || OW <= 0) return;
+    if (groups > 1 && groups == Cin && groups == Cout) {   /* layers.cpp:112-116 */
+        orc_conv2d_dw(input, N, H, W, Cin, weight, bias, KH, KW, stride, pad, output, act);
+        return;
+    }
+    if (groups > 1 && Cin / groups <= 64 && Cout / groups <= 128) {   /* layers.cpp:126-130 */
+        orc_group_conv(input, N, H, W, Cin, weight, bias, KH, KW, Cout, stride, pad, groups,
+                       output, act);
+        return;
+    }
+    conv_naive(input, N, H, W, Cin, weight, bias, KH, KW, Cout, stride, pad, groups, output, act);
 }
 
-/* group_conv.cpp:16-55 */
+/* dw_avx512.cpp:20-74 (the route on an AVX-512 host, dw.cpp:47-58): per output channel the
+ * accumulator starts at the bias and takes one fused multiply-add per tap, kh -> kw, a tap
+ * outside the image contributing fma(0, w, acc); ReLU is max(acc, 0) (vmaxps: acc > 0 ? acc : 0). */
+void orc_conv2d_dw(const float* input, int N, int H, int W, int C, const float* weight,
+                   const float* bias, int KH, int KW, int stride, int pad, float* output, int act) {
+    int OH = (H + 2 * pad - KH) / stride + 1, OW = (W + 2 * pad - KW) / stride + 1;
+    if (OH <= 0 || OW <= 0 || KH <= 0 || KW <= 0) return;
+    for (int n = 0; n < N; ++n)
+        for (int oh = 0; oh < OH; ++oh)
+            for (int ow = 0; ow < OW; ++ow)
+                for (int c = 0; c < C; ++c) {
+                    float acc = bias ? bias[c] : 0.0f;
+                    for (int kh = 0; kh < KH; ++kh)
+                        for (int kw = 0; kw < KW; ++kw) {
+                            int ih = oh * stride - pad + kh, iw = ow * stride - pad + kw;
+                            float v = (ih >= 0 && ih < H && iw >= 0 && iw < W)
+                                          ? input[(((size_t)n * H + ih) * W + iw) * C + c] : 0.0f;
+                            acc = fmaf(v, weight[((size_t)c * KH + kh) * KW + kw], acc);
+                        }
+                    if (act == 1) acc = acc > 0.0f ? acc : 0.0f;
+                    output[(((size_t)n * OH + oh) * OW + ow) * C + c] = acc;
+                }
+}
+
+/* group_conv.cpp:62-79 dispatch on an AVX-512 host: Cout_per >= 16 -> group_conv_avx512.cpp
+ * (every output channel, the masked tail included, one fma per (tap, input channel));
+ * 8 <= Cout_per < 16 -> group_conv_avx2.cpp (whole 8-channel blocks with fma, the remaining
+ * Cout_per % 8 channels in its scalar loop: mul, then add as written); narrower -> the scalar
+ * kernel group_conv.cpp:16-55 (mul, then add).  Taps outside the image are skipped;
+ * accumulation from the bias, kh -> kw -> ic.  Bit-exact against the compiled reference for
+ * Cout_per a multiple of 8, >= 16 or < 8; for the AVX2 tail channels (Cout_per % 8 != 0 below
+ * 16) the compiled reference's rounding depends on how the compiler translated that scalar loop
+ * (measured: matches for Cin_per = 4, not for Cin_per = 5), so such shapes are pinned within
+ * the fp32 tolerance only. */
 void orc_group_conv(const float* input, int N, int H, int W, int Cin, const float* weight,
                     const float* bias, int KH, int KW, int Cout, int stride, int pad,
                     int groups, float* output, int act) {
     int Cin_p = Cin / groups, Cout_p = Cout / groups;
     int OH = (H + 2 * pad - KH) / stride + 1, OW = (W + 2 * pad - KW) / stride + 1;
     if (OH <= 0 || OW <= 0) return;
+    const int fused_below = Cout_p >= 16 ? Cout_p : (Cout_p & ~7);  /* fma channels */
     for (int n = 0; n < N; ++n)
         for (int g = 0; g < groups; ++g)
             for (int oh = 0; oh < OH; ++oh)
                 for (int ow = 0; ow < OW; ++ow)
                     for (int oc = 0; oc < Cout_p; ++oc) {
                         const float* wg = weight + (size_t)g * Cout_p * KH * KW * Cin_p;
+                        const int fused = oc < fused_below;
                         float s = bias ? bias[g * Cout_p + oc] : 0.0f;
                         for (int kh = 0; kh < KH; ++kh) {
                             int ih = oh * stride - pad + kh;
@@ -473,10 +515,13 @@ void orc_group_conv(const float* input, int N, int H, int W, int Cin, const floa
                                 if (iw < 0 || iw >= W) continue;
                                 const float* ip = input + (((size_t)n * H + ih) * W + iw) * Cin + (size_t)g * Cin_p;
                                 const float* wp = wg + (size_t)((kh * KW + kw) * Cin_p) * Cout_p + oc;
-                                for (int ic = 0; ic < Cin_p; ++ic) s += ip[ic] * wp[(size_t)ic * Cout_p];
+                                for (int ic = 0; ic < Cin_p; ++ic) {
+                                    if (fused) s = fmaf(ip[ic], wp[(size_t)ic * Cout_p], s);
+                                    else s += ip[ic] * wp[(size_t)ic * Cout_p];
+                                }
                             }
                         }
-                        if (act == 1 && s < 0.0f) s = 0.0f;
+                        if (act == 1) s = fused ? (s > 0.0f ? s : 0.0f) : (s < 0.0f ? 0.0f : s);
                         output[(((size_t)n * OH + oh) * OW + ow) * Cout + g * Cout_p + oc] = s;
                     }
 }

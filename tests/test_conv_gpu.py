@@ -2,6 +2,7 @@
 C ABI, against the reference's golden vectors and the oracle, plus BASELINE-size cases."""
 import glob
 import os
+import zlib
 
 import numpy as np
 import pytest
@@ -52,17 +53,17 @@ def he(g, shape, fan_in):
 ])
 def test_conv_f32_configs_vs_oracle(acf, orc, cfg):
     tag, N, H, W, Cin, KH, KW, Cout, st, pd = cfg
-    g = np.random.default_rng(abs(hash(tag)) % 2**32)
+    g = np.random.default_rng(zlib.crc32(tag.encode()))
     x = g.uniform(0, 1, (N, H, W, Cin)).astype(np.float32)
     w = he(g, (KH * KW * Cin, Cout), KH * KW * Cin)
     b = g.uniform(-0.1, 0.1, Cout).astype(np.float32)
     got = acf.conv2d(x, w, b, KH, KW, Cout, st, pd, 1)
-    n_chk = min(N, 2)    # the oracle checks the first images (same kernel code path for all)
+    # every image: a persistent kernel's last wave and ragged tiles cover the last images
     OH, OW = orc.conv_out_hw(H, W, KH, KW, st, pd)
-    ref = np.empty((n_chk, OH, OW, Cout), np.float32)
-    orc.oracle().orc_conv2d(np.ascontiguousarray(x[:n_chk]), n_chk, H, W, Cin, w, b.ctypes.data, KH, KW,
-                            Cout, st, pd, 1, ref, 1)
-    assert max_rel(got[:n_chk], ref) < TOL_F32, max_rel(got[:n_chk], ref)
+    ref = np.empty((N, OH, OW, Cout), np.float32)
+    orc.oracle().orc_conv2d(x, N, H, W, Cin, w, b.ctypes.data, KH, KW, Cout, st, pd, 1, ref, 1)
+    for n in range(N):
+        assert max_rel(got[n], ref[n]) < TOL_F32, (n, max_rel(got[n], ref[n]))
     assert np.isfinite(got).all()
 
 
@@ -93,7 +94,7 @@ def test_conv_int8_golden_exact(acf, name):
 ])
 def test_conv_int8_vs_oracle_exact(acf, orc, cfg):
     tag, N, H, W, Cin, KH, KW, Cout, st, pd, act = cfg
-    g = np.random.default_rng(abs(hash(tag)) % 2**32)
+    g = np.random.default_rng(zlib.crc32(tag.encode()))
     x = g.uniform(0, 1, (N, H, W, Cin)).astype(np.float32)
     x[..., ::7] -= 0.5
     w = he(g, (KH * KW * Cin, Cout), KH * KW * Cin)

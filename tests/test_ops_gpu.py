@@ -90,16 +90,33 @@ def test_depthwise_golden_exact(acf, name):
 
 
 def test_depthwise_cfg4_size(acf, orc):
-    """BASELINE cfg4 depthwise: N=32, 56x56x144, 3x3 s1 p1, bias + ReLU."""
+    """BASELINE cfg4 depthwise: N=32, 56x56x144, 3x3 s1 p1, bias + ReLU; every image bit for
+    bit against the oracle (the kernel keeps the reference's per-output fma chain)."""
     g = np.random.default_rng(44)
     N, H, W, C = 32, 56, 56, 144
     x = g.uniform(0, 1, (N, H, W, C)).astype(np.float32)
     w = g.uniform(-np.sqrt(6 / 9), np.sqrt(6 / 9), (C, 3, 3)).astype(np.float32)
     b = g.uniform(-0.1, 0.1, C).astype(np.float32)
     got = acf.conv2d_dw(x, w, b, 3, 3, 1, 1, 1)
-    ref = np.empty_like(x[:2])
-    orc.oracle().orc_conv2d(np.ascontiguousarray(x[:2]), 2, H, W, C, w, b.ctypes.data, 3, 3, C, 1, 1, C, ref, 1)
-    assert max_rel(got[:2], ref) < TOL_F32
+    ref = np.empty_like(x)
+    orc.oracle().orc_conv2d(x, N, H, W, C, w, b.ctypes.data, 3, 3, C, 1, 1, C, ref, 1)
+    assert_bits_equal(got, ref, "cfg4 depthwise")
+
+
+@pytest.mark.parametrize("st", [1, 2])
+def test_grouped_cfg4_size_exact(acf, orc, st):
+    """BASELINE cfg4 grouped conv at its own shape: N=32, 14x14, 24 -> 48, groups 6, 3x3 pad 1,
+    bias + ReLU, He-uniform weights, inputs U[0,1); every image bit for bit against the oracle."""
+    g = np.random.default_rng(600 + st)
+    N, H, W, Cin, Cout, gr = 32, 14, 14, 24, 48, 6
+    x = g.uniform(0, 1, (N, H, W, Cin)).astype(np.float32)
+    fan = 9 * (Cin // gr)
+    w = g.uniform(-np.sqrt(6 / fan), np.sqrt(6 / fan), (gr, fan, Cout // gr)).astype(np.float32)
+    b = g.uniform(-0.1, 0.1, Cout).astype(np.float32)
+    got = acf.conv2d(x, w, b, 3, 3, Cout, st, 1, 1, groups=gr)
+    ref = np.empty_like(got)
+    orc.oracle().orc_conv2d(x, N, H, W, Cin, w, b.ctypes.data, 3, 3, Cout, st, 1, gr, ref, 1)
+    assert_bits_equal(got, ref, f"cfg4 grouped s{st}")
 
 
 @pytest.mark.parametrize("name", ["conv_grp_s1", "conv_grp_s2", "conv_grp_narrow"])

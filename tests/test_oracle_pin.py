@@ -130,6 +130,9 @@ def test_oracle_conv_f32(orc, name):
     orc.oracle().orc_conv2d(d["x"], N, H, W, Cin, np.ascontiguousarray(d["w"]), d["b"].ctypes.data,
                             KH, KW, Cout, st, pd, groups, out, act)
     assert max_rel(out, d["out"]) < TOL_F32, name
+    if orc.oracle().orc_conv2d_route(N, H, W, Cin, KH, KW, Cout, st, pd, groups) in (1, 2):
+        # depthwise and grouped-direct routes: the oracle restates the AVX-512 / AVX2 fma chains
+        assert_bits_equal(out, d["out"], name)
     if name == "conv_f32_wino23":
         o2 = np.empty_like(out)
         orc.oracle().orc_winograd23(d["x"], N, H, W, Cin, d["w"], d["b"].ctypes.data, Cout, o2, act)
@@ -202,6 +205,33 @@ def test_oracle_conv_int8_vs_reference_fresh_seeds(orc, seed):
             a = orc.orc_conv2d_int8(x, wq, ws, b, N, H, W, Cin, KH, KW, Cout, st, pd, act)
             r = orc.ref_conv2d_int8(x, wq, ws, b, N, H, W, Cin, KH, KW, Cout, st, pd, act)
             assert_bits_equal(a, r, f"seed {seed} {(N, H, W, Cin, KH, KW, Cout, st, pd, act)}")
+
+
+@ref_only
+@pytest.mark.parametrize("case", [
+    # (N, H, W, Cin, Cout, groups, K, stride, pad, act): BASELINE cfg4 shapes (fewer images),
+    # plus the AVX-512 masked channel tail (C % 16 != 0) and Cout_per >= 16 / < 8 / = 8
+    (2, 56, 56, 144, 144, 144, 3, 1, 1, 1), (2, 13, 11, 21, 21, 21, 3, 2, 1, 0),
+    (4, 14, 14, 24, 48, 6, 3, 1, 1, 1), (4, 14, 14, 24, 48, 6, 3, 2, 1, 1),
+    (2, 9, 9, 16, 80, 4, 3, 1, 1, 0), (2, 7, 7, 6, 60, 3, 3, 2, 1, 1), (2, 9, 9, 8, 12, 4, 3, 1, 1, 1),
+])
+def test_oracle_dw_grouped_vs_reference_exact(orc, case):
+    """Depthwise and grouped-direct routes: the oracle equals the compiled reference bit for bit
+    (the fma chains of dw_avx512.cpp and group_conv_avx512.cpp / _avx2.cpp)."""
+    N, H, W, Cin, Cout, gr, K, st, pd, act = case
+    g = np.random.default_rng(sum(case))
+    x = g.uniform(-1, 1, (N, H, W, Cin)).astype(np.float32)
+    if gr == Cin == Cout:
+        w = g.uniform(-1, 1, (Cin, K, K)).astype(np.float32)
+    else:
+        w = g.uniform(-1, 1, (gr, K * K * (Cin // gr), Cout // gr)).astype(np.float32)
+    b = g.uniform(-0.1, 0.1, Cout).astype(np.float32)
+    OH, OW = orc.conv_out_hw(H, W, K, K, st, pd)
+    a = np.empty((N, OH, OW, Cout), np.float32)
+    r = np.empty_like(a)
+    orc.oracle().orc_conv2d(x, N, H, W, Cin, w, b.ctypes.data, K, K, Cout, st, pd, gr, a, act)
+    orc.ref().acfun_conv2d_g(x, N, H, W, Cin, w, b.ctypes.data, K, K, Cout, st, pd, gr, r, act)
+    assert_bits_equal(a, r, str(case))
 
 
 @ref_only
