@@ -17,8 +17,9 @@
 //     4 Mi floats = 16 MiB, e.g. any M = N = K <= 1024 problem).  Every GPU that loads the
 //     library holds this array until the process exits.
 //   * The first call on each device resolves the array's device address
-//     (cudaGetSymbolAddress) with that device current; make that first call before any
-//     stream capture.
+//     (cudaGetSymbolAddress) with that device current.
+//   * Every call waits for its stream (cudaStreamSynchronize) to read the device error word,
+//     so it cannot be called while its stream is being captured into a CUDA graph.
 //   * All calls share the one array and it keeps the last call's contents (the split
 //     kernel rewrites every element a call reads, so nothing has to start at zero; the
 //     device error word is cleared by every call).  Calls that overlap on the GPU — on two
@@ -48,7 +49,10 @@ static NoAllocDevice g_na[64];
 static std::mutex g_na_mu;
 
 static NoAllocDevice* noalloc_setup(int device) {
-  if (device < 0 || device >= 64) return nullptr;
+  if (device < 0 || device >= 64) {
+    set_error(kInvalid, "acfun_gemm_epi_noalloc: device index %d out of range", device);
+    return nullptr;
+  }
   NoAllocDevice* d = &g_na[device];
   std::lock_guard<std::mutex> g(g_na_mu);
   if (d->ready) return d;
@@ -96,6 +100,17 @@ static int noalloc_launch(const NoAllocDevice* d, int device, cudaStream_t st, c
   return 0;
 }
 
+// True when p is device (or managed) memory of `device`: a pointer into another GPU's memory
+// would be read by the split kernel and written by the epilogue without peer access.
+static bool on_device(const void* p, int device) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged) && a.device == device;
+}
+
 }  // namespace acf
 
 using namespace acf;
@@ -107,11 +122,12 @@ extern "C" int acfun_gemm_epi_noalloc(int M, int N, int K, const float* A, const
     set_error(kInvalid, "acfun_gemm_epi_noalloc: NULL tensor argument");
     return kInvalid;
   }
-  if (ptr_kind(A) != PtrKind::Device || ptr_kind(B) != PtrKind::Device ||
-      ptr_kind(C) != PtrKind::Device || (bias && ptr_kind(bias) != PtrKind::Device)) {
+  const int device = tctx().device;
+  if (!on_device(A, device) || !on_device(B, device) || !on_device(C, device) ||
+      (bias && !on_device(bias, device))) {
     set_error(kInvalid,
-              "acfun_gemm_epi_noalloc: A, B, C and bias must be device pointers (host memory "
-              "would need staging buffers)");
+              "acfun_gemm_epi_noalloc: A, B, C and bias must be device pointers on the acfun "
+              "device %d (host memory would need staging buffers)", device);
     return kInvalid;
   }
   const long long Kp = (K + 3) / 4 * 4, Np = (N + 3) / 4 * 4;
@@ -123,7 +139,6 @@ extern "C" int acfun_gemm_epi_noalloc(int M, int N, int K, const float* A, const
               M, N, K, need, (unsigned)ACFUN_NOALLOC_SCRATCH_FLOATS);
     return kInvalid;
   }
-  const int device = tctx().device;
   if (!ACF_CUDA_OK(cudaSetDevice(device))) return kCuda;
   NoAllocDevice* d = noalloc_setup(device);
   if (!d) return last_error_code() ? last_error_code() : kCuda;
@@ -156,10 +171,11 @@ extern "C" int acfun_gemm_epi_noalloc(int M, int N, int K, const float* A, const
     rc = noalloc_launch<32, 5>(d, device, st, a, Kp, (long long)M * Kp, b, Np, (long long)K * Np, M,
                                N, K, ep);
   if (rc) return rc;
-  if (!ACF_CUDA_OK(cudaStreamSynchronize(st))) return kCuda;
+  // read the error word on the acfun stream only (no device-wide synchronisation)
   unsigned word = 0;
-  if (!ACF_CUDA_OK(cudaMemcpy(&word, d->err, sizeof(unsigned), cudaMemcpyDeviceToHost)))
+  if (!ACF_CUDA_OK(cudaMemcpyAsync(&word, d->err, sizeof(unsigned), cudaMemcpyDeviceToHost, st)))
     return kCuda;
+  if (!ACF_CUDA_OK(cudaStreamSynchronize(st))) return kCuda;
   if (word) {
     set_error(kTimeout, "acfun_gemm_epi_noalloc: device-side wait timed out (0x%x)", word);
     return kTimeout;

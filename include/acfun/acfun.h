@@ -143,9 +143,10 @@ void acfun_gemm_s8_requant(int M, int N, int K, const int8_t* A, const int8_t* B
  * allocated: the 3xTF32 operand copies live in one
  * fixed 16 MiB device array compiled into the library (held by every GPU that loads it),
  * so 2*(M*K + K*N) must stay <= 4 Mi floats (K, N rounded up to 4).  All tensors must be
- * device pointers.  The first call on a device resolves the array's address; make it
- * before any stream capture.  Calls share the array: calls that overlap on the GPU race.
- * Runs on the acfun stream and returns once it is done: 0, or an error code. */
+ * device pointers on the acfun device.  The first call on a device resolves the array's
+ * address.  Calls share the array: calls that overlap on the GPU race.  Runs on the acfun
+ * stream and synchronises with it before returning (so it cannot be called while that
+ * stream is being captured): returns 0, or an error code. */
 int acfun_gemm_epi_noalloc(int M, int N, int K, const float* A, const float* B, float* C,
                            const float* bias, int act);
 
