@@ -95,11 +95,12 @@ bool int8_pool_ok(int H, int W, int Cin, int KH, int KW, int Cout, int stride, i
 
 // conv2d_int8_batch_dev immediately followed by max-pool(2, 2, 0, post_relu), fused for small-K
 // non-Winograd routes (sets *handled; otherwise nothing is launched).  Bit-identical to the two
-// layers run in turn.
+// layers run in turn.  in_max: the per-image input maximum, given instead of measured.
 bool conv_int8_pool_dev(Call& c, const float* x, int N, int H, int W, int Cin, const int8_t* wq,
                         const float* wscale, const float* bias, int KH, int KW, int Cout,
                         int stride, int pad, int act, int pool, int pst, int ppd, int post_relu,
-                        float* out, bool* handled, unsigned* out_max = nullptr);
+                        float* out, bool* handled, unsigned* out_max = nullptr,
+                        const unsigned* in_max = nullptr);
 
 // int8 conv router (conv_int8.cpp:63-148) on device pointers.
 bool conv2d_int8_dev(Call& c, const float* x, int N, int H, int W, int Cin, const int8_t* wq,

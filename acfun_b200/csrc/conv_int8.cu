@@ -658,10 +658,13 @@ bool conv2d_int8_dev(Call& c, const float* x, int N, int H, int W, int Cin, cons
 // quantises per call, conv_int8.cpp:75-81, and its model harness calls per image): grid
 // (blocks, images); the last block of image n derives inv[n] = 127/max, sa[n] = max/127 and
 // zero[n].  maxa[] and done[] are cleared by k_int8_wprep.
+// preset (optional): a given per-image maximum (the bits of a non-negative float) used instead of
+// reading x -- a model's stored static activation range; launch with per_img = 0 then.
 __global__ void k_absmax_img(const float* __restrict__ x, long long per_img, unsigned* maxa,
                              unsigned* done, float* inv, float* sa, int* zero,
                              const float* __restrict__ wscale, const float* __restrict__ bias,
-                             const int* __restrict__ Sw, int Cout, float* __restrict__ ab) {
+                             const int* __restrict__ Sw, int Cout, float* __restrict__ ab,
+                             const unsigned* __restrict__ preset) {
   __shared__ float sh[32];
   __shared__ int last;
   const int n = blockIdx.y;
@@ -700,7 +703,9 @@ __global__ void k_absmax_img(const float* __restrict__ x, long long per_img, uns
       m = (m < u) ? u : m;
     }
     if (threadIdx.x == 0) {
-      atomicMax(&maxa[n], __float_as_uint(m));
+      unsigned mv = __float_as_uint(m);
+      if (preset) mv = mv < preset[n] ? preset[n] : mv;
+      atomicMax(&maxa[n], mv);
       __threadfence();
       last = (atomicAdd(&done[n], 1u) == gridDim.x - 1) ? 1 : 0;
     }
@@ -772,7 +777,7 @@ bool conv2d_int8_batch_dev(Call& c, const float* x, int N, int H, int W, int Cin
     long long bx = per / (4 * 256 * 4);
     bx = bx < 1 ? 1 : (bx > 64 ? 64 : bx);
     k_absmax_img<<<dim3((unsigned)bx, (unsigned)N), 256, 0, c.stream()>>>(
-        x, per, words, words + N, inv, sa, zero, nullptr, nullptr, nullptr, 0, nullptr);
+        x, per, words, words + N, inv, sa, zero, nullptr, nullptr, nullptr, 0, nullptr, nullptr);
   }
   if (!c.launched("int8 per-image params")) return false;
   const bool wino = is_wino_route(H, W, Cin, KH, KW, Cout, stride, pad);
@@ -1007,7 +1012,7 @@ __global__ void __launch_bounds__(128) k_conv_int8_pool(
 bool conv_int8_pool_dev(Call& c, const float* x, int N, int H, int W, int Cin, const int8_t* wq,
                         const float* wscale, const float* bias, int KH, int KW, int Cout,
                         int stride, int pad, int act, int pool, int pst, int ppd, int post_relu,
-                        float* out, bool* handled, unsigned* out_max) {
+                        float* out, bool* handled, unsigned* out_max, const unsigned* in_max) {
   *handled = false;
   const int OH = (H + 2 * pad - KH) / stride + 1, OW = (W + 2 * pad - KW) / stride + 1;
   if (pool != 2 || pst != 2 || ppd != 0 || OH < 2 || OW < 2 || N <= 0 || N > 65535) return true;
@@ -1028,11 +1033,12 @@ bool conv_int8_pool_dev(Call& c, const float* x, int N, int H, int W, int Cin, c
   float* ab = (float*)c.scratch((size_t)N * 2 * Cout * 4);
   if (!words || !inv || !sa || !zero || !Sw || !wpk || !ab) return false;
   k_int8_pool_wpack<<<Cout, 64, 0, c.stream()>>>(wq, taps, Cin, CW, Cout, wpk, Sw, words, 2 * N);
-  const long long per = (long long)H * W * Cin;
+  // the per-image maximum: measured from x, or given (in_max) without reading x
+  const long long per = in_max ? 0 : (long long)H * W * Cin;
   long long bx = per / (4 * 256 * 4);
   bx = bx < 1 ? 1 : (bx > 64 ? 64 : bx);
   k_absmax_img<<<dim3((unsigned)bx, (unsigned)N), 256, 0, c.stream()>>>(
-      x, per, words, words + N, inv, sa, zero, wscale, bias, Sw, Cout, ab);
+      x, per, words, words + N, inv, sa, zero, wscale, bias, Sw, Cout, ab, in_max);
 #define ACF_I8POOL(CWV)                                                                        \
   k_conv_int8_pool<CWV><<<N * PH, 128, (size_t)smem, c.stream()>>>(                            \
       x, H, W, Cin, wpk, ab, Cout, KH, KW, stride, pad, PH, PW, inv, zero, out, act, post_relu,  \

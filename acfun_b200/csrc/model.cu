@@ -12,6 +12,16 @@
 // NULL with error code 5 instead of reading past the blob), weights live on the GPU, and
 // acfun_model_infer_batch runs n images through each layer at once (batch-1 semantics per
 // image, Softmax per image).
+// Format extension (no counterpart in the reference, whose int8 path has no model format):
+//   8 ConvInt8  u32 KH, KW, Cout, stride, pad | f32 act_max | f32 wscale[Cout] | f32 b[Cout] |
+//               s8 wq[KH*KW*Cin*Cout] | zero bytes to the next multiple of 4
+// an already quantised dense convolution (acfun_quantize_weights output of the BN-folded
+// weights): it runs through the int8 router like a Conv of an int8-mode model, without
+// re-quantising at load.  act_max = 0: one activation scale per image from that image's
+// max|x| (the reference's per-call definition, conv_int8.cpp:75-77); act_max > 0: a stored
+// calibration range used as every image's max|x| (inputs beyond it saturate).  A ReLU after
+// it is fused like a Conv's; a BN after it stays a layer of its own (the stored weights
+// cannot absorb it).
 #include <algorithm>
 #include <math.h>
 #include <stdio.h>
@@ -41,6 +51,9 @@ struct MLayer {
   int post_relu = 0;
   int8_t* wq = nullptr;  // int8 mode: per-column quantised conv weights (device)
   float* wqs = nullptr;  // and their scales
+  const int8_t* wq_host = nullptr;  // ConvInt8 records: the stored wq / scales (into the blob)
+  const float* ws_host = nullptr;
+  float act_max = 0.0f;  // ConvInt8: stored activation range (0: measured per image)
   void* wsplit = nullptr;  // bf16 hi / lo split of w for the split-activation conv route
 };
 
@@ -58,7 +71,9 @@ struct AcfunModel {
   size_t bufcap = 0;         // floats per buffer
   std::mutex mu;
   bool int8 = false;         // dense convs through the int8 router, one scale per image
-  void* dq = nullptr;        // device allocation of all layers' wq / wqs
+  void* dq = nullptr;        // device allocation of all layers' wq / wqs (int8 mode)
+  void* dq8 = nullptr;       // device copies of the ConvInt8 records' wq / wqs
+  bool has_int8_layers = false;
 };
 
 namespace acf {
@@ -155,6 +170,28 @@ static AcfunModel* load_blob(std::vector<unsigned char>&& blob) {
         prevC = (int)v[2];
         break;
       }
+      case 8: {
+        unsigned v[5];
+        for (int k = 0; k < 5; ++k)
+          if (!rd_u32(b, o, v[k])) return bad(i);
+        if (!v[0] || !v[1] || !v[2] || !v[3] || v[0] > 64 || v[1] > 64 || v[2] > (1u << 20))
+          return bad(i);
+        for (int k = 0; k < 5; ++k) L.p[k] = (int)v[k];
+        L.p[5] = 0;
+        const float* am = nullptr;
+        if (!rd_f32(b, o, 1, am) || !(am[0] >= 0.0f) || !(am[0] < 3.0e38f)) return bad(i);
+        L.act_max = am[0];
+        L.wn = (size_t)v[0] * v[1] * prevC * v[2];
+        if (!rd_f32(b, o, v[2], L.ws_host) || !rd_f32(b, o, v[2], L.b_host)) return bad(i);
+        const size_t padded = (L.wn + 3) / 4 * 4;
+        if (o > b.size() || padded > b.size() - o) return bad(i);
+        L.wq_host = reinterpret_cast<const int8_t*>(b.data() + o);
+        o += padded;
+        L.p[6] = prevC;
+        prevC = (int)v[2];
+        m->has_int8_layers = true;
+        break;
+      }
       case 2: {
         unsigned Cout, inDim;
         if (!rd_u32(b, o, Cout) || !rd_u32(b, o, inDim) || !Cout || !inDim) return bad(i);
@@ -203,13 +240,14 @@ static AcfunModel* load_blob(std::vector<unsigned char>&& blob) {
   for (int i = 0; i < n; ++i) {
     if (consumed[i]) continue;
     MLayer& L = raw[i];
-    if (L.type == 1 || L.type == 2 || L.type == 7) {
+    if (L.type == 1 || L.type == 2 || L.type == 7 || L.type == 8) {
       MLayer F = L;
       F.act = 0;
       const int Cout = L.type == 2 ? L.p[0] : L.p[2];
       int j = i + 1, relu_idx = -1;
       if (j < n && raw[j].type == 3) relu_idx = j++;
-      if (j < n && raw[j].type == 6 && raw[j].p[0] == Cout && (strict || relu_idx < 0)) {
+      if (L.type != 8 && j < n && raw[j].type == 6 && raw[j].p[0] == Cout &&
+          (strict || relu_idx < 0)) {
         fold_bn(F, raw[j], Cout, m.get());
         consumed[j] = 1;
       }
@@ -239,7 +277,7 @@ static AcfunModel* load_blob(std::vector<unsigned char>&& blob) {
   int H = m->inH, W = m->inW, C = m->inC;
   size_t total = 0, maxact = (size_t)H * W * C;
   for (auto& L : m->layers) {
-    if (L.type == 1 || L.type == 7) {
+    if (L.type == 1 || L.type == 7 || L.type == 8) {
       if (L.p[6] != C) {
         set_error(kFormat, "acfun_model_load: channel mismatch");
         return nullptr;
@@ -252,7 +290,7 @@ static AcfunModel* load_blob(std::vector<unsigned char>&& blob) {
       H = OH;
       W = OW;
       C = L.p[2];
-      total += L.wn + (size_t)C;
+      total += (L.type == 8 ? 0 : L.wn) + (size_t)C;  // ConvInt8 weights live in dq8
     } else if (L.type == 2) {
       if ((size_t)L.p[1] != (size_t)H * W * C) {
         set_error(kFormat, "acfun_model_load: FC inDim %d != %d", L.p[1], H * W * C);
@@ -283,17 +321,35 @@ static AcfunModel* load_blob(std::vector<unsigned char>&& blob) {
   if (!ACF_CUDA_OK(cudaMalloc(&m->dparams, (total ? total : 1) * 4))) return nullptr;
   size_t off = 0;
   for (auto& L : m->layers) {
-    if (L.wn) {
+    if (L.wn && L.type != 8) {
       L.w = m->dparams + off;
       if (!ACF_CUDA_OK(cudaMemcpy(L.w, L.w_host, L.wn * 4, cudaMemcpyHostToDevice))) return nullptr;
       off += L.wn;
     }
-    if (L.type == 1 || L.type == 7 || L.type == 2) {
+    if (L.type == 1 || L.type == 7 || L.type == 2 || L.type == 8) {
       const int Cout = L.type == 2 ? L.p[0] : L.p[2];
       L.b = m->dparams + off;
       if (!ACF_CUDA_OK(cudaMemcpy(L.b, L.b_host, (size_t)Cout * 4, cudaMemcpyHostToDevice)))
         return nullptr;
       off += Cout;
+    }
+  }
+  // ConvInt8 records: wq and scales, each in a 16-byte aligned slot of one allocation
+  if (m->has_int8_layers) {
+    size_t q = 0;
+    for (auto& L : m->layers)
+      if (L.type == 8) q += align_up(L.wn, 16) + align_up((size_t)L.p[2] * 4, 16);
+    if (!ACF_CUDA_OK(cudaMalloc(&m->dq8, q))) return nullptr;
+    unsigned char* base = static_cast<unsigned char*>(m->dq8);
+    for (auto& L : m->layers) {
+      if (L.type != 8) continue;
+      const size_t cb = (size_t)L.p[2] * 4;
+      L.wq = reinterpret_cast<int8_t*>(base);
+      L.wqs = reinterpret_cast<float*>(base + align_up(L.wn, 16));
+      if (!ACF_CUDA_OK(cudaMemcpy(L.wq, L.wq_host, L.wn, cudaMemcpyHostToDevice)) ||
+          !ACF_CUDA_OK(cudaMemcpy(L.wqs, L.ws_host, cb, cudaMemcpyHostToDevice)))
+        return nullptr;
+      base += align_up(L.wn, 16) + align_up(cb, 16);
     }
   }
   (void)maxact;
@@ -304,7 +360,7 @@ static size_t max_activation(const AcfunModel* m) {
   int H = m->inH, W = m->inW, C = m->inC;
   size_t mx = (size_t)H * W * C;
   for (auto& L : m->layers) {
-    if (L.type == 1 || L.type == 7) {
+    if (L.type == 1 || L.type == 7 || L.type == 8) {
       H = (H + 2 * L.p[4] - L.p[0]) / L.p[3] + 1;
       W = (W + 2 * L.p[4] - L.p[1]) / L.p[3] + 1;
       C = L.p[2];
@@ -371,20 +427,26 @@ static bool run_model(Call& c, AcfunModel* m, int n, const float* x, float* y) {
   // so.  (A max-pool producer does not: per-image reductions in its grid-stride order cost
   // more than the absmax pass they save.)
   unsigned* imax[2] = {nullptr, nullptr};
+  unsigned* smax = nullptr;  // a ConvInt8 layer's stored activation range, per image
   const unsigned* cur_max = nullptr;
   int mwhich = 0;
-  if (m->int8) {
+  if (m->int8 || m->has_int8_layers) {
     imax[0] = static_cast<unsigned*>(c.scratch((size_t)n * 4));
     imax[1] = static_cast<unsigned*>(c.scratch((size_t)n * 4));
-    if (!imax[0] || !imax[1]) return false;
+    smax = static_cast<unsigned*>(c.scratch((size_t)n * 4));
+    if (!imax[0] || !imax[1] || !smax) return false;
   }
+  auto int8_layer = [&](const MLayer& Lj) {  // this layer runs through the int8 router
+    return Lj.wq && ((m->int8 && Lj.type == 1) || Lj.type == 8);
+  };
   auto pool2_follows = [&](size_t j) -> bool {  // layer j + 1 is MaxPool(2, 2, 0)
     if (j + 1 >= nl || m->layers[j + 1].type != 4) return false;
     const auto& P = m->layers[j + 1];
     return P.p[0] == 2 && P.p[1] == 2 && P.p[2] == 0;
   };
   auto max_for = [&](size_t j) -> unsigned* {
-    if (!m->int8 || j >= nl || m->layers[j].type != 1 || !m->layers[j].wq) return nullptr;
+    // (a consumer with a stored activation range needs no measured maximum)
+    if (j >= nl || !int8_layer(m->layers[j]) || m->layers[j].act_max > 0.0f) return nullptr;
     unsigned* d = imax[mwhich];
     mwhich ^= 1;
     return ACF_CUDA_OK(cudaMemsetAsync(d, 0, (size_t)n * 4, c.stream())) ? d : nullptr;
@@ -398,16 +460,25 @@ static bool run_model(Call& c, AcfunModel* m, int n, const float* x, float* y) {
     // A standalone ReLU right after a Conv / FC (the loader keeps Conv->BN->ReLU's ReLU
     // separate, model.cpp:211-226) is applied in that layer's epilogue instead of a pass.
     int act = L.act;
-    if ((L.type == 1 || L.type == 2 || L.type == 7) && li + 1 < nl && m->layers[li + 1].type == 3) {
+    if ((L.type == 1 || L.type == 2 || L.type == 7 || L.type == 8) && li + 1 < nl &&
+        m->layers[li + 1].type == 3) {
       act = 1;
       ++li;
     }
     switch (L.type) {
       case 1:
-      case 7: {
+      case 7:
+      case 8: {
         const int KH = L.p[0], KW = L.p[1], Cout = L.p[2], st = L.p[3], pd = L.p[4];
         const int groups = L.type == 7 ? L.p[5] : 1;
-        if (m->int8 && L.wq) {
+        if (int8_layer(L)) {
+          if (L.act_max > 0.0f) {
+            // a stored activation range: every image's max|x| is that constant
+            unsigned bits;
+            memcpy(&bits, &L.act_max, 4);
+            ok = fill_u32_dev(c, smax, bits, n);
+            in_max = smax;
+          }
           // int8 mode: acfun_conv2d_int8 per image (the reference's int8 model harness); a
           // small-K conv followed by MaxPool(2, 2, 0) runs fused
           // (one max_for per layer: a second call would hand out the array in_max points at)
@@ -416,8 +487,9 @@ static bool run_model(Call& c, AcfunModel* m, int n, const float* x, float* y) {
           if (pool_next) {
             const auto& P = m->layers[li + 1];
             bool fused = false;
-            ok = conv_int8_pool_dev(c, cur, n, H, W, C, L.wq, L.wqs, L.b, KH, KW, Cout, st, pd, act,
-                                    P.p[0], P.p[1], P.p[2], P.post_relu, next, &fused, om_pool);
+            ok = ok && conv_int8_pool_dev(c, cur, n, H, W, C, L.wq, L.wqs, L.b, KH, KW, Cout, st, pd,
+                                          act, P.p[0], P.p[1], P.p[2], P.post_relu, next, &fused,
+                                          om_pool, L.act_max > 0.0f ? smax : nullptr);
             if (ok && fused) cur_max = om_pool;
             if (ok && fused) {
               H = (H + 2 * pd - KH) / st + 1;
@@ -637,6 +709,7 @@ extern "C" void acfun_model_destroy(AcfunModel* m) {
   cudaDeviceSynchronize();
   cudaFree(m->dparams);
   cudaFree(m->dq);
+  cudaFree(m->dq8);
   for (auto& L : m->layers) cudaFree(L.wsplit);
   cudaFree(m->buf[0]);
   cudaFree(m->buf[1]);

@@ -264,6 +264,16 @@ bool quantize_u8_dev(Call& c, const float* in, uint8_t* out, long long n, float 
   return c.launched("k_quantize_u8");
 }
 
+__global__ void k_fill_u32(unsigned* __restrict__ d, unsigned v, long long n) {
+  GRID_STRIDE(i, n) d[i] = v;
+}
+
+bool fill_u32_dev(Call& c, unsigned* d, unsigned v, long long n) {
+  if (n <= 0) return true;
+  k_fill_u32<<<grid_for(c, n), 256, 0, c.stream()>>>(d, v, n);
+  return c.launched("k_fill_u32");
+}
+
 // ------------------------------------------------------------------ depthwise conv
 // One thread per (output pixel, 4 channels): coalesced NHWC float4 reads / writes.
 __global__ void k_dw4(const float* __restrict__ in, int N, int H, int W, int C,

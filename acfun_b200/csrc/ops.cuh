@@ -13,6 +13,8 @@ bool softmax_dev(Call& c, const float* in, int rows, int cols, float* out);
 bool batchnorm_dev(Call& c, float* d, int size, int channels, const float* mean,
                    const float* var, const float* gamma, const float* beta, float eps);
 bool quantize_u8_dev(Call& c, const float* in, uint8_t* out, long long n, float inv_s, int zp);
+// d[0..n) = v
+bool fill_u32_dev(Call& c, unsigned* d, unsigned v, long long n);
 bool dw_dev(Call& c, const float* in, int N, int H, int W, int C, const float* w,
             const float* bias, int KH, int KW, int stride, int pad, float* out, int act);
 bool group_dev(Call& c, const float* in, int N, int H, int W, int Cin, const float* w,
