@@ -41,6 +41,7 @@ OPS = 2.0 * M * N * K
 METRIC = "int8_gemm_tops"
 UNIT = "TOPS"
 WORKLOAD = "cfg2 int8 GEMM 4096^3 s8xs8->s32, fused +bias, *scale, ReLU, requant to s8"
+VGG_CPU_IMAGES = 16   # reference CPU leg of cfg5: images timed one by one, median
 
 
 def make_inputs(seed=1234):
@@ -138,23 +139,59 @@ def ncu_traffic():
     return None
 
 
-def cpu_reference_sample(steps=1, rows=512):
-    """The reference's acfun_gemm_int8 (u8 A = s8 A + 128, the reference's own route for this
-    config) on `rows` rows of the 4096^3 problem, all host threads; returns TOPS and details."""
+_HOST = None
+
+
+def host_info():
+    """What the CPU numbers were measured on: lscpu's model name, nproc, and the reference
+    library's own view (acfun_effective_cores, acfun_backend_name) when it is built."""
+    global _HOST
+    if _HOST is None:
+        model = None
+        try:
+            out = subprocess.run(["lscpu"], capture_output=True, text=True, timeout=10).stdout
+            for ln in out.splitlines():
+                if ln.startswith("Model name:"):
+                    model = ln.split(":", 1)[1].strip()
+        except (OSError, subprocess.TimeoutExpired):
+            pass
+        info = {"cpu_model": model, "nproc": os.cpu_count()}
+        try:
+            from oracle import pyoracle
+            if pyoracle.ref_available():
+                R = pyoracle.ref()
+                info["acfun_effective_cores"] = int(R.acfun_effective_cores())
+                info["acfun_backend_name"] = R.acfun_backend_name().decode()
+        except OSError:
+            pass
+        _HOST = info
+    return dict(_HOST)
+
+
+def cpu_reference_sample(steps=5, rows=512):
+    """The reference's int8 GEMM with its fused epilogue (acfun_gemm_int8_epi on u8 A = s8 A +
+    128: the reference's own route for this config, dequantising alpha * acc + beta with ReLU in
+    the same pass) on `rows` rows of the 4096^3 problem, all host threads, 3 warm-ups and the
+    median of `steps` (>= 5) timed calls (the reference's own method, src/benchmark.cpp:98-111);
+    returns TOPS and details."""
     from oracle import pyoracle
     kind = "reference" if pyoracle.ref_available() else "port"
     A, B, bias, scale = make_inputs()
     cores = os.cpu_count() or 1
+    steps = max(steps, 5)
     Au = (A[:rows].astype(np.int16) + 128).astype(np.uint8)
-    C = np.empty((rows, N), np.int32)
+    C = np.empty((rows, N), np.float32)
+    alpha = scale.copy()
+    beta = (bias.astype(np.float32) * scale).astype(np.float32)
     times = []
     if kind == "reference":
         R = pyoracle.ref()
         pyoracle.ref_set_threads(cores)
-        R.acfun_gemm_int8(rows, N, K, Au, B, C)  # warm-up
+        for _ in range(3):
+            R.acfun_gemm_int8_epi(rows, N, K, Au, B, C, alpha, beta, 1)
         for _ in range(steps):
             t0 = time.perf_counter()
-            R.acfun_gemm_int8(rows, N, K, Au, B, C)
+            R.acfun_gemm_int8_epi(rows, N, K, Au, B, C, alpha, beta, 1)
             times.append(time.perf_counter() - t0)
     else:
         O = pyoracle.oracle()
@@ -163,20 +200,20 @@ def cpu_reference_sample(steps=1, rows=512):
         Au = Au[:r].copy()
         C = C[:r]
         t0 = time.perf_counter()
-        O.orc_gemm_int8(r, N, K, Au, B, C)
+        O.orc_gemm_int8_epi(r, N, K, Au, B, C, alpha, beta, 1)
         times.append(time.perf_counter() - t0)
         rows = r
     t = statistics.median(times)
     return {"value": round(2.0 * rows * N * K / t / 1e12, 4), "unit": UNIT, "cores": cores, "kind": kind,
-            "sample": f"{rows} of {M} rows of the 4096^3 u8xs8 GEMM (acfun_gemm_int8 on A+128), "
-                      f"median of {len(times)}, {cores} threads"}
+            "sample": f"{rows} of {M} rows of the 4096^3 u8xs8 GEMM with its dequant + ReLU epilogue "
+                      f"(acfun_gemm_int8_epi on A+128), 3 warm-ups, median of {len(times)}, {cores} threads",
+            "host": host_info()}
 
 
 def run_reference_arm(args, rank, world):
     if rank != 0:
         return
-    steps = max(args.steps, 1)
-    cb = cpu_reference_sample(steps=steps, rows=args.cpu_rows)
+    cb = cpu_reference_sample(steps=max(args.steps, 5), rows=args.cpu_rows)
     line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8", "data": "synthetic",
@@ -244,13 +281,15 @@ def measure_configs(acf, torch, stream, flush, steps, with_cpu=True, cfg_filter=
         acf.check()
         return sum(s.elapsed_time(e) for s, e in evs) / n / 1e3
 
-    def cpu(fn, units, unit_scale):
-        """median seconds of the reference on `units` (images / rows) -> value per unit."""
+    def cpu(fn, units, unit_scale, warm=3, reps=5):
+        """The reference on `units` (images / rows) per call: `warm` warm-up calls, then the
+        median of `reps` timed calls (src/benchmark.cpp:98-111) -> value per unit."""
         if R is None:
             return None
-        fn()
+        for _ in range(warm):
+            fn()
         ts = []
-        for _ in range(2):
+        for _ in range(reps):
             t0 = time.perf_counter()
             fn()
             ts.append(time.perf_counter() - t0)
@@ -277,7 +316,8 @@ def measure_configs(acf, torch, stream, flush, steps, with_cpu=True, cfg_filter=
                                       "peak_source": peak["hbm"][2]})
         if cpu_val is not None:
             r["cpu_baseline"] = {"value": round(cpu_val, 4), "unit": punit, "cores": cores,
-                                 "kind": "reference", "sample": cpu_sample}
+                                 "kind": "reference", "sample": cpu_sample + ", 3 warm-ups, median of 5",
+                                 "host": host_info()}
         if extra:
             r.update(extra)
         out[name] = r
@@ -384,16 +424,17 @@ def measure_configs(acf, torch, stream, flush, steps, with_cpu=True, cfg_filter=
         if R is not None:
             h = R.acfun_model_load(path.encode())
             o = np.empty(1000, np.float32)
-            x0 = np.ascontiguousarray(x[0])
-            cv = cpu(lambda: [R.acfun_model_infer(h, x0, o) for _ in range(2)], 2, 1.0)
+            imgs = iter([np.ascontiguousarray(x[k]) for k in range(VGG_CPU_IMAGES + 1)])
+            cv = cpu(lambda: R.acfun_model_infer(h, next(imgs), o), 1, 1.0, warm=1, reps=VGG_CPU_IMAGES)
             R.acfun_model_destroy(h)
         gf = 15.218e9
         record("cfg5_vgg11_b256", t, n * gf, 1e12, "f32bf3", None, "",
                {"img_per_s": round(n / t, 1), "gflop_per_img": 15.218, "images": n})
         if cv is not None:
-            out["cfg5_vgg11_b256"]["cpu_baseline"] = {"value": round(cv, 3), "unit": "img/s", "cores": cores,
-                                                      "kind": "reference",
-                                                      "sample": "2 sequential acfun_model_infer calls (batch-1 API)"}
+            out["cfg5_vgg11_b256"]["cpu_baseline"] = {
+                "value": round(cv, 3), "unit": "img/s", "cores": cores, "kind": "reference",
+                "sample": f"acfun_model_infer (batch-1 API) on {VGG_CPU_IMAGES} different images of the batch "
+                          f"after 1 warm-up: 1 / the median per-image time", "host": host_info()}
         m.close()
 
     if want("cfg5_vgg11_int8_b256"):
@@ -415,8 +456,8 @@ def measure_configs(acf, torch, stream, flush, steps, with_cpu=True, cfg_filter=
         cv = None
         if R is not None:
             om = OracleModel(open(path, "rb").read())
-            x0 = np.ascontiguousarray(x[0])
-            cv = cpu(lambda: [om.ref_infer(R, x0, int8=True) for _ in range(2)], 2, 1.0)
+            imgs = iter([np.ascontiguousarray(x[k]) for k in range(VGG_CPU_IMAGES + 1)])
+            cv = cpu(lambda: om.ref_infer(R, next(imgs), int8=True), 1, 1.0, warm=1, reps=VGG_CPU_IMAGES)
         gf = 15.218e9
         record("cfg5_vgg11_int8_b256", t, n * gf, 1e12, "int8", None, "",
                {"img_per_s": round(n / t, 1), "gop_per_img": 15.218, "images": n,
@@ -424,8 +465,10 @@ def measure_configs(acf, torch, stream, flush, steps, with_cpu=True, cfg_filter=
         if cv is not None:
             out["cfg5_vgg11_int8_b256"]["cpu_baseline"] = {
                 "value": round(cv, 3), "unit": "img/s", "cores": cores, "kind": "reference",
-                "sample": "2 images through the reference's int8 layer API (quantize_weights + conv2d_int8 "
-                          "per conv, fc / maxpool / softmax), the composition its int8 path needs"}
+                "sample": f"{VGG_CPU_IMAGES} different images (after 1 warm-up) through the reference's int8 "
+                          "layer API (quantize_weights + conv2d_int8 per conv, fc / maxpool / softmax), the "
+                          "composition its int8 path needs: 1 / the median per-image time",
+                "host": host_info()}
         m.close()
     return out
 
@@ -446,9 +489,13 @@ def vgg_model_path(rank, world, dist):
 
 
 def measure_vgg_sharded(acf, torch, dist, stream, flush, rank, world, steps, n=256):
-    """cfg5 across `world` GPUs: rank r infers its contiguous share of the 256-image batch
-    (acfun_model_infer_batch, device-resident), then the [256, 1000] outputs are all-gathered
-    over NCCL.  Time per step = max over ranks of (inference + gather); img/s = 256 / t."""
+    """cfg5 end to end across `world` GPUs (world = 1 included): every step, rank r copies its
+    contiguous share of the 256-image batch from pinned host memory to its GPU, runs
+    acfun_model_infer_batch on it, the [256, 1000] outputs are all-gathered over NCCL (world >
+    1) and the gathered result is copied back to pinned host memory.  Per step and rank the
+    phases are timed with CUDA events on the launching stream; the step time is the max over
+    ranks; img/s = 256 / that.  After timing, rank 0 infers the whole batch on its own GPU and
+    compares it with the gathered result."""
     from acfun_b200.shard import gather_outputs, shard_bounds
     L = acf.lib()
     path = vgg_model_path(rank, world, dist)
@@ -456,48 +503,84 @@ def measure_vgg_sharded(acf, torch, dist, stream, flush, rank, world, steps, n=2
     b, e = shard_bounds(n, world, rank)
     g = np.random.default_rng(77)
     x_all = g.uniform(0, 1, (n, 224, 224, 3)).astype(np.float32)
-    dx = torch.from_numpy(np.ascontiguousarray(x_all[b:e])).cuda()
+    hx = torch.from_numpy(np.ascontiguousarray(x_all[b:e])).pin_memory()
+    dx = torch.empty(hx.shape, device="cuda")
     dy = torch.empty((e - b, 1000), device="cuda")
+    hy = torch.empty((n, 1000)).pin_memory()
 
-    def step():
+    def step(ev=None):
+        if ev:
+            ev[0].record(stream)
+        dx.copy_(hx, non_blocking=True)
+        if ev:
+            ev[1].record(stream)
         if L.acfun_model_infer_batch(m.h, e - b, dx.data_ptr(), dy.data_ptr()) <= 0:
             acf.check()
-        if world > 1:
-            return gather_outputs(dist, dy, n, world)
-        return dy
+        if ev:
+            ev[2].record(stream)
+        out = gather_outputs(dist, dy, n, world) if world > 1 else dy
+        if ev:
+            ev[3].record(stream)
+        hy.copy_(out, non_blocking=True)
+        if ev:
+            ev[4].record(stream)
+        return out
 
-    for _ in range(2):
+    for _ in range(3):
         step()
     torch.cuda.synchronize()
     acf.check()
-    total = 0.0
+    evs = []
     for _ in range(steps):
         flush.fill_(1)
         if world > 1:
             dist.barrier()
-        s, t = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record(stream)
-        out = step()
-        t.record(stream)
         torch.cuda.synchronize()
-        total += s.elapsed_time(t) / 1e3
-    tt = total / steps
-    if world > 1:
-        tv = torch.tensor([tt], device="cuda")
-        dist.all_reduce(tv, op=dist.ReduceOp.MAX)
-        tt = float(tv[0])
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+        step(ev)
+        torch.cuda.synchronize()
+        evs.append(ev)
     acf.check()
-    ok = bool(torch.isfinite(out).all()) and abs(float(out.sum()) - n) < 1e-2 * n  # softmax rows
+    ph = np.array([[ev[k].elapsed_time(ev[k + 1]) for k in range(4)] for ev in evs]).mean(0) / 1e3
+    tt = float(np.mean([ev[0].elapsed_time(ev[4]) for ev in evs])) / 1e3
+    vals = [tt] + list(ph)
+    if world > 1:
+        tv = torch.tensor(vals, device="cuda", dtype=torch.float64)
+        dist.all_reduce(tv, op=dist.ReduceOp.MAX)
+        vals = [float(v) for v in tv]
+    tt, t_h2d, t_inf, t_gat, t_d2h = vals
+    gathered = hy.numpy().copy()
+    ok = bool(np.isfinite(gathered).all()) and abs(float(gathered.sum()) - n) < 1e-2 * n  # softmax rows
+    parity = None
+    if world > 1:
+        dist.barrier()
+        if rank == 0:
+            # the whole batch on this one GPU (untimed) against the gathered shards
+            dxa = torch.from_numpy(x_all).cuda()
+            dya = torch.empty((n, 1000), device="cuda")
+            if L.acfun_model_infer_batch(m.h, n, dxa.data_ptr(), dya.data_ptr()) <= 0:
+                acf.check()
+            one = dya.cpu().numpy()
+            parity = {"bit_identical_to_1gpu": bool(np.array_equal(one.view(np.int32), gathered.view(np.int32))),
+                      "max_abs_diff": float(np.abs(one - gathered).max())}
+            del dxa, dya
+        dist.barrier()
     m.close()
     bf16, _, src = measured_peaks()
     pk = bf16 / 3
     achieved = n * 15.218e9 / tt / 1e12
     return {"ms": round(tt * 1e3, 3), "value": round(n / tt, 1), "unit": "img/s", "n_gpus": world,
-            "images_per_gpu": e - b, "outputs_valid": ok,
+            "images_per_gpu": e - b, "outputs_valid": ok, "parity_vs_1gpu": parity,
+            "phases_ms_max_over_ranks": {"h2d": round(t_h2d * 1e3, 3), "infer": round(t_inf * 1e3, 3),
+                                         "gather": round(t_gat * 1e3, 3), "d2h": round(t_d2h * 1e3, 3)},
+            "gather_share": round(t_gat / tt, 4),
+            "h2d_bytes_per_step_per_rank": int(hx.numel() * 4), "d2h_bytes_per_step_per_rank": n * 1000 * 4,
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(pk * world, 1),
                          "unit": "TFLOP/s", "frac": round(achieved / (pk * world), 4),
                          "peak_source": f"3xBF16 ceiling = bf16/3 ({src}) x n_gpus"},
-            "collective": "NCCL all-gather of the [256,1000] outputs (1 MB) only" if world > 1 else None}
+            "collective": "NCCL all-gather of the [256,1000] outputs (1 MB) only" if world > 1 else None,
+            "timing": "events on the launching stream around H2D, infer, gather, D2H; mean over steps, "
+                      "max over ranks; L2 flushed before every step"}
 
 
 def main():
@@ -568,10 +651,20 @@ def main():
         L.acfun_gemm_s8_requant(M, N, K, hA.data_ptr(), hB.data_ptr(), hbias.data_ptr(), hscale.data_ptr(),
                                 hC.data_ptr(), 1)
 
-    # correctness spot check before timing (rows vs the oracle's restatement, rank 0 only)
+    # correctness spot check before timing: the first and last 8 rows of C against the CPU
+    # oracle's restatement of the requantising GEMM, bit for bit (test infrastructure used as
+    # the checker only)
     dev_step()
     torch.cuda.synchronize()
     acf.check()
+    from oracle import pyoracle
+    Cd = dC.cpu().numpy()
+    for r0 in (0, M - 8):
+        ref = np.empty((8, N), np.int8)
+        pyoracle.oracle().orc_gemm_s8_requant(8, N, K, np.ascontiguousarray(A[r0:r0 + 8]), B,
+                                              bias.ctypes.data, scale, ref, 1)
+        if not np.array_equal(Cd[r0:r0 + 8], ref):
+            raise SystemExit(f"bench: rows {r0}..{r0 + 7} of the int8 requant GEMM differ from the oracle")
 
     for _ in range(args.warmup):
         dev_step()
@@ -612,7 +705,7 @@ def main():
         dist.barrier()
 
     vgg = None
-    if world > 1 and not args.no_configs:
+    if not args.no_configs:
         vgg = measure_vgg_sharded(acf, torch, dist, stream, flush, rank, world, steps=max(3, min(args.steps, 10)))
 
     if rank == 0:
@@ -652,7 +745,8 @@ def main():
             line["configs"] = measure_configs(acf, torch, stream, flush, steps=max(5, min(args.steps, 20)),
                                               with_cpu=not args.no_cpu_baseline, cfg_filter=filt)
         if vgg is not None:
-            line["configs"] = {"cfg5_vgg11_b256_sharded": vgg}
+            line.setdefault("configs", {})["cfg5_vgg11_b256_sharded"] = vgg
+            line["vgg11_b256_e2e_img_per_s"] = vgg["value"]
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
