@@ -14,6 +14,8 @@
 // that land on real output pixels.  Strided convolutions gather an explicit im2col matrix.
 // Bias and ReLU are fused into the TMEM drain.
 #include <algorithm>
+#include <cstdlib>
+#include <cstring>
 #include "api_export.cuh"
 #include "conv.cuh"
 #include "gemm.cuh"
@@ -722,6 +724,16 @@ static bool conv_tc(Call& c, const float* x, int N, int H, int W, int Cs, int co
   ep.f0 = bias;
   ep.act = act;
   Operand A, B;
+  if constexpr (BF) {
+    // narrow convolutions: resident weights, the activation converted inside the kernel
+    static const bool halo_on = [] {
+      const char* e = getenv("ACFUN_CONV_HALO");
+      return !(e && !strcmp(e, "0"));
+    }();
+    if (halo_on && conv_halo_ok(Cg, KH, KW, Cout_g, stride))
+      return conv_halo_f32_dev(c, x, N, H, W, Cs, coff, Cg, w, ldw, bias, KH, KW, Cout_g, pad, out,
+                               ldc, act);
+  }
   if (stride == 1) {
     const int Hp = H + 2 * pad, Wp = W + 2 * pad;
     const int Cpad = (int)align_up((size_t)Cg, BKE);

@@ -17,6 +17,13 @@ enum ConvRoute {
   kRouteIm2col = 7,
 };
 
+// Narrow stride-1 fp32 convolution (Cin, Cout <= 64, KH*KW <= 9) as one 3xBF16 tcgen05 kernel
+// with resident weights and in-kernel operand conversion (conv_halo.cu).
+bool conv_halo_ok(int Cin, int KH, int KW, int Cout, int stride);
+bool conv_halo_f32_dev(Call& c, const float* x, int N, int H, int W, int Cs, int coff, int Cin,
+                       const float* w, long long ldw, const float* bias, int KH, int KW, int Cout,
+                       int pad, float* out, long long ldc, int act);
+
 // routing of conv2d_impl (layers.cpp:106-195)
 int conv_route(int H, int W, int Cin, int KH, int KW, int Cout, int stride, int pad, int groups);
 size_t conv_weight_elems(int Cin, int KH, int KW, int Cout, int groups);

@@ -473,6 +473,99 @@ __global__ void k_dw_strip(const float* __restrict__ in, int H, int W, int C,
   }
 }
 
+// 3x3 depthwise, persistent: the grid (two blocks per SM) walks every (image, output row, strip
+// of TW outputs, 4 channels) item with the weights staged in shared memory once per block.  A
+// thread loads the 3 x NCOL input float4 of an item before its first FMA, so each thread keeps
+// 3*NCOL loads in flight instead of NCOL.  Per output the arithmetic is k_dw_strip's (bias, then
+// kh outer, kw inner, one fma per in-image tap; taps outside the image skipped).
+template <int TW, int STRIDE>
+__global__ void __launch_bounds__(256) k_dw3_persist(const float* __restrict__ in, int N, int H,
+                                                     int W, int C, const float* __restrict__ w,
+                                                     const float* __restrict__ bias, int pad, int OH,
+                                                     int OW, float* __restrict__ out, int act) {
+  constexpr int NCOL = (TW - 1) * STRIDE + 3;
+  extern __shared__ float4 dp_s4[];
+  float* wT = reinterpret_cast<float*>(dp_s4);  // [9][C]
+  float* bs = wT + 9 * C;
+  stage_block<8>(wT, 9 * C + C, [&](int i) {
+    if (i < 9 * C) {
+      const int k = i / C, c = i - k * C;
+      return __ldg(w + c * 9 + k);
+    }
+    return bias ? __ldg(bias + (i - 9 * C)) : 0.0f;
+  });
+  __syncthreads();
+  const int C4 = C >> 2, strips = (OW + TW - 1) / TW;
+  const long long items = (long long)N * OH * strips * C4;
+  for (long long it = blockIdx.x * (long long)blockDim.x + threadIdx.x; it < items;
+       it += (long long)gridDim.x * blockDim.x) {
+    const int c = (int)(it % C4) * 4;
+    long long r = it / C4;
+    const int s = (int)(r % strips);
+    r /= strips;
+    const int oh = (int)(r % OH), n = (int)(r / OH);
+    const int ow0 = s * TW, iw0 = ow0 * STRIDE - pad;
+    const float* img = in + (size_t)n * H * W * C + c;
+    const bool inner = iw0 >= 0 && iw0 + NCOL <= W;
+    float4 xc[3][NCOL];
+    unsigned rok = 0, cok = (1u << NCOL) - 1u;
+    if (!inner) {
+      cok = 0;
+#pragma unroll
+      for (int j = 0; j < NCOL; ++j)
+        if (iw0 + j >= 0 && iw0 + j < W) cok |= 1u << j;
+    }
+#pragma unroll
+    for (int kh = 0; kh < 3; ++kh) {
+      const int ih = oh * STRIDE - pad + kh;
+      const bool ok = ih >= 0 && ih < H;
+      rok |= ok ? 1u << kh : 0u;
+      const float* rowp = img + ((size_t)(ok ? ih : 0) * W) * C;
+#pragma unroll
+      for (int j = 0; j < NCOL; ++j) {
+        xc[kh][j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (ok && ((cok >> j) & 1u))
+          xc[kh][j] = __ldg(reinterpret_cast<const float4*>(rowp + (size_t)(iw0 + j) * C));
+      }
+    }
+    float4 acc[TW];
+    const float4 b4 = *reinterpret_cast<const float4*>(bs + c);
+#pragma unroll
+    for (int t = 0; t < TW; ++t) acc[t] = b4;
+#pragma unroll
+    for (int kh = 0; kh < 3; ++kh) {
+      if (!((rok >> kh) & 1u)) continue;  // out-of-image rows are skipped
+#pragma unroll
+      for (int kw = 0; kw < 3; ++kw) {
+        const float4 wv = *reinterpret_cast<const float4*>(wT + (kh * 3 + kw) * C + c);
+#pragma unroll
+        for (int t = 0; t < TW; ++t) {
+          if (!((cok >> (t * STRIDE + kw)) & 1u)) continue;
+          const float4 x = xc[kh][t * STRIDE + kw];
+          const float2 lo = nx_ffma2(make_float2(x.x, x.y), make_float2(wv.x, wv.y),
+                                     make_float2(acc[t].x, acc[t].y));
+          const float2 hi = nx_ffma2(make_float2(x.z, x.w), make_float2(wv.z, wv.w),
+                                     make_float2(acc[t].z, acc[t].w));
+          acc[t] = make_float4(lo.x, lo.y, hi.x, hi.y);
+        }
+      }
+    }
+    float* orow = out + ((size_t)n * OH + oh) * OW * C + c;
+#pragma unroll
+    for (int t = 0; t < TW; ++t) {
+      if (ow0 + t >= OW) break;
+      float4 a = acc[t];
+      if (act == 1) {
+        a.x = a.x > 0.f ? a.x : 0.f;
+        a.y = a.y > 0.f ? a.y : 0.f;
+        a.z = a.z > 0.f ? a.z : 0.f;
+        a.w = a.w > 0.f ? a.w : 0.f;
+      }
+      *reinterpret_cast<float4*>(orow + (size_t)(ow0 + t) * C) = a;
+    }
+  }
+}
+
 __global__ void k_dw1(const float* __restrict__ in, int N, int H, int W, int C,
                       const float* __restrict__ w, const float* __restrict__ bias, int KH, int KW,
                       int stride, int pad, int OH, int OW, float* __restrict__ out, int act) {
@@ -507,6 +600,14 @@ bool dw_dev(Call& c, const float* in, int N, int H, int W, int C, const float* w
   const size_t smem = ((size_t)KH * KW * C + C) * 4;
   const bool rowk = C % 4 == 0 && aligned16(in) && aligned16(out) && smem <= 48 * 1024 &&
                     (long long)N * OH < (1LL << 31) && (long long)H * W * C < (1LL << 31);
+  if (rowk && KH == 3 && KW == 3 && (stride == 1 || stride == 2)) {
+    const int grid = 2 * c.sm_count();
+    if (stride == 1)
+      k_dw3_persist<4, 1><<<grid, 256, smem, c.stream()>>>(in, N, H, W, C, w, bias, pad, OH, OW, out, act);
+    else
+      k_dw3_persist<2, 2><<<grid, 256, smem, c.stream()>>>(in, N, H, W, C, w, bias, pad, OH, OW, out, act);
+    return c.launched("k_dw3_persist");
+  }
   if (rowk && KW == 3 && (stride == 1 || stride == 2)) {
     if (stride == 1)
       k_dw_strip<4, 3, 1><<<N * OH, 256, smem, c.stream()>>>(in, H, W, C, w, bias, KH, pad, OH, OW,

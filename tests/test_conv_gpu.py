@@ -50,6 +50,12 @@ def he(g, shape, fan_in):
     ("odd", 3, 17, 23, 40, 3, 3, 72, 1, 1),
     ("k5s2", 2, 19, 21, 12, 5, 5, 20, 2, 2),
     ("pw_c40", 4, 20, 22, 72, 1, 1, 40, 1, 0),         # CUDA-core route, 48-wide accumulators
+    # narrow stride-1 convs (<= 64 -> <= 64 channels): the resident-weight kernel with in-kernel
+    # conversion; channel counts off the vector width, pad 0, many images
+    ("halo_c20_o24", 3, 15, 17, 20, 3, 3, 24, 1, 1),
+    ("halo_c48_o40_p0", 2, 12, 11, 48, 3, 3, 40, 1, 0),
+    ("halo_c16_o64", 5, 40, 37, 16, 3, 3, 64, 1, 1),
+    ("halo_k1x5", 2, 9, 30, 40, 1, 5, 33, 1, 2),
 ])
 def test_conv_f32_configs_vs_oracle(acf, orc, cfg):
     tag, N, H, W, Cin, KH, KW, Cout, st, pd = cfg
