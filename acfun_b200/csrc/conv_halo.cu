@@ -15,8 +15,8 @@
 //     while the MMAs consume the current one.
 //   * One thread issues, per slab, the MMAs of its KW taps: the A operand of tap kw is the
 //     slab's rows kw .. kw + 127, a descriptor whose start is shifted by kw rows, so each
-//     input row is converted and staged once per kernel row instead of once per tap.  3xBF16 per K-step:
-//     lo*hi + hi*lo + hi*hi into the fp32 accumulator in TMEM (four accumulator buffers).
+//     input row is converted and staged once per kernel row instead of once per tap.  3xBF16
+//     per K-step: lo*hi + hi*lo + hi*hi into the fp32 accumulator in TMEM (four buffers).
 //   * Epilogue warps drain TMEM, add the bias, apply ReLU and store the rows that land on
 //     output pixels (the F32_BIAS arithmetic of the general GEMM kernel).
 // Every wait is bounded (ptx.cuh); on expiry the kernel flags the error word and drains.
@@ -37,10 +37,10 @@ constexpr int SLAB_COPY = SLAB_ROWS * ROWB;
 constexpr int SLAB = 2 * SLAB_COPY;             // hi + lo
 constexpr int NSLAB = 2;
 constexpr int NBUF = 4;                         // TMEM accumulator buffers
-constexpr int CONV_WARPS = 8, EPI_WARPS = 4;
+constexpr int CONV_WARPS = 10, EPI_WARPS = 4;
 constexpr int CONV_THREADS = 32 * CONV_WARPS;
 constexpr int THREADS = 64 + 32 * (CONV_WARPS + EPI_WARPS);
-constexpr int UNITS = (SLAB_ROWS * 8 + CONV_THREADS - 1) / CONV_THREADS;  // 16-byte units
+constexpr int UNITS = (SLAB_ROWS * 4 + CONV_THREADS - 1) / CONV_THREADS;  // 16-channel units
 // barriers: b_full, slab_full[2], slab_empty[2], t_full[4], t_empty[4], drain
 constexpr int BAR_BYTES = 16 * 8;
 constexpr int SMEM = 1024 + B_BYTES + NSLAB * SLAB + BAR_BYTES + 16 + BN * 4;
@@ -52,8 +52,8 @@ struct HaloArgs {
   const float* x;        // NHWC input, channels [coff, coff + Cin) of Cs
   int H, W, Cs, coff, Cin;
   int pad, Wp, KH, KW;
-  int img_rows;          // Hp * Wp
-  long long rows;        // N * Hp * Wp
+  unsigned img_rows;     // Hp * Wp
+  unsigned rows;         // N * Hp * Wp (< 2^31)
   float* out;
   long long ldc;
   int act, OH, OW, Cout;
@@ -139,9 +139,12 @@ __global__ void __launch_bounds__(halo::THREADS, 1)
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer
+    // One thread's serial instruction stream: descriptors are built once and advanced by
+    // adding to their 14-bit start-address field (addresses stay below 256 KB, no carry).
     if (lane == 0) {
       constexpr uint32_t idesc = dev::umma_idesc(1u, 1u, 1u, 0u, 1u, 128u, (uint32_t)BN);
-      const uint32_t a0 = dev::smem_u32(sA), b0 = dev::smem_u32(sB);
+      const uint64_t ad0 = halo_desc(dev::smem_u32(sA), 16, 1024);
+      const uint64_t bd0 = halo_desc(dev::smem_u32(sB), TAPB, 1024);
       bool ok = dev::mbar_wait(b_full, 0, err);
       dev::tc_fence_after();
       uint32_t sl = 0, local = 0;
@@ -153,6 +156,7 @@ __global__ void __launch_bounds__(halo::THREADS, 1)
         }
         dev::tc_fence_after();
         const uint32_t d_tmem = tmem + buf * BN;
+        uint64_t bd = bd0;  // tap (kh, kw) of the hi copy
         for (int kh = 0; kh < a.KH; ++kh, ++sl) {
           const uint32_t s = sl & 1, ph = (sl >> 1) & 1;
           if (!dev::mbar_wait(&slab_full[s], ph, err)) {
@@ -160,20 +164,19 @@ __global__ void __launch_bounds__(halo::THREADS, 1)
             break;
           }
           dev::tc_fence_after();
-          for (int kw = 0; kw < a.KW; ++kw) {
-            const int tap = kh * a.KW + kw;
+          uint64_t ad = ad0 + (uint64_t)((s * SLAB) >> 4);  // slab s, hi copy, row 0
+          for (int kw = 0; kw < a.KW; ++kw, ad += ROWB >> 4, bd += TAPB >> 4) {
+            const uint32_t first = (kh | kw) == 0;
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks) {
-              // (a copy, b copy): lo*hi, hi*lo, hi*hi
-#pragma unroll
-              for (int p = 0; p < 3; ++p) {
-                const uint32_t aop = p == 0 ? 1u : 0u, bop = p == 1 ? 1u : 0u;
-                const uint32_t aa = a0 + s * SLAB + aop * SLAB_COPY + kw * ROWB + ks * 32;
-                const uint32_t ba = b0 + bop * B_COPY + tap * TAPB + ks * 16 * ROWB;
-                dev::umma<dev::MmaKind::F16>(d_tmem, halo_desc(aa, 16, 1024),
-                                             halo_desc(ba, TAPB, 1024), idesc,
-                                             (kh | kw | ks | p) != 0);
-              }
+              // lo*hi, hi*lo, hi*hi
+              dev::umma<dev::MmaKind::F16>(d_tmem, ad + ((SLAB_COPY + ks * 32) >> 4),
+                                           bd + ((ks * 16 * ROWB) >> 4), idesc,
+                                           (ks != 0) || !first);
+              dev::umma<dev::MmaKind::F16>(d_tmem, ad + ((ks * 32) >> 4),
+                                           bd + ((B_COPY + ks * 16 * ROWB) >> 4), idesc, 1u);
+              dev::umma<dev::MmaKind::F16>(d_tmem, ad + ((ks * 32) >> 4),
+                                           bd + ((ks * 16 * ROWB) >> 4), idesc, 1u);
             }
           }
           dev::umma_commit(&slab_empty[s]);
@@ -189,66 +192,80 @@ __global__ void __launch_bounds__(halo::THREADS, 1)
     }
   } else if (warp < 2 + CONV_WARPS) {
     // ---------------- converters: fp32 NHWC -> swizzled bf16 hi / lo slab rows
+    // unit = (slab row, 16 channels): 64 contiguous input bytes, two 16-byte chunks per copy.
+    // Slab k of this CTA is (tile blockIdx.x + (k / KH) * gridDim.x, kernel row k % KH); the
+    // loads of slab k + 1 are issued before slab k is stored, so two slabs of loads overlap.
     const int ct = threadIdx.x - 64;
-    const int R = 128 + a.KW - 1;
-    uint32_t sl = 0;
-    bool ok = true;
-    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-      const long long m0 = (long long)t * 128;
-      for (int kh = 0; kh < a.KH; ++kh, ++sl) {
-        if (*abort_flag) {
-          ok = false;
-          break;
-        }
-        const uint32_t s = sl & 1, ph = (sl >> 1) & 1;
-        const long long r0 = m0 + (long long)kh * a.Wp;
-        float v[UNITS][8];
-        // all loads first: one memory round trip per slab
+    const int R = 128 + a.KW - 1, NU = 4 * R;
+    const int my_tiles = num_tiles > (int)blockIdx.x
+                             ? (num_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    const int nslabs = my_tiles * a.KH;
+    auto load_slab = [&](int k, float4 (&v)[UNITS][4]) {
+      const int t = (int)blockIdx.x + (k / a.KH) * (int)gridDim.x, kh = k - (k / a.KH) * a.KH;
+      const unsigned r0 = (unsigned)t * 128u + (unsigned)(kh * a.Wp);
 #pragma unroll
-        for (int u = 0; u < UNITS; ++u) {
-          const int unit = ct + u * CONV_THREADS, row = unit >> 3, ch = (unit & 7) * 8;
+      for (int u = 0; u < UNITS; ++u) {
+        const int idx = ct + u * CONV_THREADS, row = idx >> 2, ch = (idx & 3) * 16;
 #pragma unroll
-          for (int e = 0; e < 8; ++e) v[u][e] = 0.0f;
-          const long long g = r0 + row;
-          if (row < R && g < a.rows && ch < a.Cin) {
-            const int n = (int)(g / a.img_rows), q = (int)(g - (long long)n * a.img_rows);
-            const int hp = q / a.Wp, ih = hp - a.pad, iw = q - hp * a.Wp - a.pad;
-            if (ih >= 0 && ih < a.H && iw >= 0 && iw < a.W) {
-              const float* src = a.x + (((long long)n * a.H + ih) * a.W + iw) * a.Cs + a.coff + ch;
-              if constexpr (VEC) {
-                const float4 p0 = __ldg(reinterpret_cast<const float4*>(src));
-                const float4 p1 = __ldg(reinterpret_cast<const float4*>(src) + 1);
-                v[u][0] = p0.x; v[u][1] = p0.y; v[u][2] = p0.z; v[u][3] = p0.w;
-                v[u][4] = p1.x; v[u][5] = p1.y; v[u][6] = p1.z; v[u][7] = p1.w;
-              } else {
+        for (int e = 0; e < 4; ++e) v[u][e] = make_float4(0.f, 0.f, 0.f, 0.f);
+        const unsigned g = r0 + (unsigned)row;
+        if (idx < NU && g < a.rows && ch < a.Cin) {
+          const unsigned n = g / a.img_rows, q = g - n * a.img_rows;
+          const unsigned hp = q / a.Wp;
+          const int ih = (int)hp - a.pad, iw = (int)(q - hp * a.Wp) - a.pad;
+          if (ih >= 0 && ih < a.H && iw >= 0 && iw < a.W) {
+            const float* src = a.x + (((size_t)n * a.H + ih) * a.W + iw) * a.Cs + a.coff + ch;
+            if constexpr (VEC) {
 #pragma unroll
-                for (int e = 0; e < 8; ++e) v[u][e] = (ch + e < a.Cin) ? __ldg(src + e) : 0.0f;
-              }
+              for (int e = 0; e < 4; ++e)
+                if (ch + 4 * e < a.Cin) v[u][e] = __ldg(reinterpret_cast<const float4*>(src) + e);
+            } else {
+              float* f = reinterpret_cast<float*>(v[u]);
+#pragma unroll
+              for (int e = 0; e < 16; ++e) f[e] = (ch + e < a.Cin) ? __ldg(src + e) : 0.0f;
             }
           }
         }
-        if (!dev::mbar_wait(&slab_empty[s], ph ^ 1, err)) {
-          *abort_flag = 1;
-          ok = false;
-          break;
-        }
-        uint8_t* hi = sA + s * SLAB;
+      }
+    };
+    auto store_slab = [&](int k, const float4 (&v)[UNITS][4]) -> bool {
+      const uint32_t s = (uint32_t)k & 1, ph = ((uint32_t)k >> 1) & 1;
+      if (*abort_flag || !dev::mbar_wait(&slab_empty[s], ph ^ 1, err)) {
+        *abort_flag = 1;
+        return false;
+      }
+      uint8_t* hi = sA + s * SLAB;
 #pragma unroll
-        for (int u = 0; u < UNITS; ++u) {
-          const int unit = ct + u * CONV_THREADS, row = unit >> 3, c16 = unit & 7;
-          if (row < R) {
+      for (int u = 0; u < UNITS; ++u) {
+        const int idx = ct + u * CONV_THREADS, row = idx >> 2, c16 = (idx & 3) * 2;
+        if (idx < NU) {
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            const float4 p0 = v[u][2 * hh], p1 = v[u][2 * hh + 1];
             uint32_t h[4], l[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) nx_split_bf16x2(v[u][2 * e], v[u][2 * e + 1], h[e], l[e]);
-            const int off = row * ROWB + ((c16 ^ (row & 7)) << 4);
+            nx_split_bf16x2(p0.x, p0.y, h[0], l[0]);
+            nx_split_bf16x2(p0.z, p0.w, h[1], l[1]);
+            nx_split_bf16x2(p1.x, p1.y, h[2], l[2]);
+            nx_split_bf16x2(p1.z, p1.w, h[3], l[3]);
+            const int off = row * ROWB + (((c16 + hh) ^ (row & 7)) << 4);
             *reinterpret_cast<uint4*>(hi + off) = make_uint4(h[0], h[1], h[2], h[3]);
             *reinterpret_cast<uint4*>(hi + SLAB_COPY + off) = make_uint4(l[0], l[1], l[2], l[3]);
           }
         }
-        dev::fence_proxy_async_smem();  // generic-proxy stores -> the tensor core's reads
-        __syncwarp();
-        if (lane == 0) dev::mbar_arrive(&slab_full[s]);
       }
+      dev::fence_proxy_async_smem();  // generic-proxy stores -> the tensor core's reads
+      __syncwarp();
+      if (lane == 0) dev::mbar_arrive(&slab_full[s]);
+      return true;
+    };
+    float4 va[UNITS][4], vb[UNITS][4];
+    if (nslabs > 0) load_slab(0, va);
+    for (int k = 0; k < nslabs; k += 2) {
+      if (k + 1 < nslabs) load_slab(k + 1, vb);
+      if (!store_slab(k, va)) break;
+      if (k + 1 >= nslabs) break;
+      if (k + 2 < nslabs) load_slab(k + 2, va);
+      if (!store_slab(k + 1, vb)) break;
     }
   } else {
     // ---------------- epilogue: TMEM -> +bias, ReLU -> output pixels
@@ -259,9 +276,9 @@ __global__ void __launch_bounds__(halo::THREADS, 1)
       const bool ok = dev::mbar_wait(&t_full[buf], use & 1, err);
       dev::tc_fence_after();
       if (!ok || *abort_flag) break;
-      const long long r = (long long)t * 128 + q * 32 + lane;
-      const int n = (int)(r / a.img_rows), qq = (int)(r - (long long)n * a.img_rows);
-      const int oh = qq / a.Wp, ow = qq - oh * a.Wp;
+      const unsigned r = (unsigned)t * 128u + (unsigned)(q * 32 + lane);
+      const unsigned n = r / a.img_rows, qq = r - n * a.img_rows;
+      const int oh = (int)(qq / (unsigned)a.Wp), ow = (int)qq - oh * a.Wp;
       const bool store = r < a.rows && oh < a.OH && ow < a.OW;
       float* dst = a.out + (((long long)n * a.OH + oh) * a.OW + ow) * a.ldc;
 #pragma unroll
@@ -343,15 +360,15 @@ bool conv_halo_f32_dev(Call& c, const float* x, int N, int H, int W, int Cs, int
   a.Wp = Wp;
   a.KH = KH;
   a.KW = KW;
-  a.img_rows = Hp * Wp;
-  a.rows = rows;
+  a.img_rows = (unsigned)(Hp * Wp);
+  a.rows = (unsigned)rows;
   a.out = out;
   a.ldc = ldc;
   a.act = act;
   a.OH = OH;
   a.OW = OW;
   a.Cout = Cout;
-  const bool vec = Cin % 8 == 0 && Cs % 4 == 0 && coff % 4 == 0 && aligned16(x);
+  const bool vec = Cin % 4 == 0 && Cs % 4 == 0 && coff % 4 == 0 && aligned16(x);
   const int tiles = (int)((rows + 127) / 128);
   const int grid = tiles < c.sm_count() ? tiles : c.sm_count();
   static bool attr_done[2][64] = {};
@@ -369,3 +386,4 @@ bool conv_halo_f32_dev(Call& c, const float* x, int N, int H, int W, int Cs, int
 }
 
 }  // namespace acf
+

@@ -473,95 +473,103 @@ __global__ void k_dw_strip(const float* __restrict__ in, int H, int W, int C,
   }
 }
 
-// 3x3 depthwise, persistent: the grid (two blocks per SM) walks every (image, output row, strip
-// of TW outputs, 4 channels) item with the weights staged in shared memory once per block.  A
-// thread loads the 3 x NCOL input float4 of an item before its first FMA, so each thread keeps
-// 3*NCOL loads in flight instead of NCOL.  Per output the arithmetic is k_dw_strip's (bias, then
-// kh outer, kw inner, one fma per in-image tap; taps outside the image skipped).
-template <int TW, int STRIDE>
-__global__ void __launch_bounds__(256) k_dw3_persist(const float* __restrict__ in, int N, int H,
+// 3x3 stride-1 depthwise, rolling window: a thread owns 4 channels of a strip of 4 output
+// columns over TH consecutive output rows and reads each input row of that range once (6 float4
+// columns), folding it into the three output rows it feeds -- kh = 0 of the newest row, 1 of the
+// previous, 2 of the oldest, which is then complete and stored.  Rows are visited in order, so
+// every output still gets bias, then kh = 0, 1, 2 (kw = 0, 1, 2 within each), one fma per
+// in-image tap: k_dw_strip's arithmetic.  The 9 weights and the bias of the 4 channels stay in
+// registers; the next input row is loaded while the current one is folded in.
+template <int TH>
+__global__ void __launch_bounds__(384, 1) k_dw3_roll(const float* __restrict__ in, int N, int H,
                                                      int W, int C, const float* __restrict__ w,
                                                      const float* __restrict__ bias, int pad, int OH,
                                                      int OW, float* __restrict__ out, int act) {
-  constexpr int NCOL = (TW - 1) * STRIDE + 3;
-  extern __shared__ float4 dp_s4[];
-  float* wT = reinterpret_cast<float*>(dp_s4);  // [9][C]
-  float* bs = wT + 9 * C;
-  stage_block<8>(wT, 9 * C + C, [&](int i) {
-    if (i < 9 * C) {
-      const int k = i / C, c = i - k * C;
-      return __ldg(w + c * 9 + k);
-    }
-    return bias ? __ldg(bias + (i - 9 * C)) : 0.0f;
-  });
-  __syncthreads();
-  const int C4 = C >> 2, strips = (OW + TW - 1) / TW;
-  const long long items = (long long)N * OH * strips * C4;
+  const int C4 = C >> 2, strips = (OW + 3) >> 2, segs = (OH + TH - 1) / TH;
+  const long long items = (long long)N * segs * strips * C4;
   for (long long it = blockIdx.x * (long long)blockDim.x + threadIdx.x; it < items;
        it += (long long)gridDim.x * blockDim.x) {
     const int c = (int)(it % C4) * 4;
     long long r = it / C4;
-    const int s = (int)(r % strips);
+    const int st = (int)(r % strips);
     r /= strips;
-    const int oh = (int)(r % OH), n = (int)(r / OH);
-    const int ow0 = s * TW, iw0 = ow0 * STRIDE - pad;
+    const int sg = (int)(r % segs), n = (int)(r / segs);
+    const int oh0 = sg * TH, oh1 = min(oh0 + TH, OH);
+    const int ow0 = st * 4, iw0 = ow0 - pad;
+    unsigned cok = 0;
+#pragma unroll
+    for (int j = 0; j < 6; ++j)
+      if (iw0 + j >= 0 && iw0 + j < W) cok |= 1u << j;
+    float4 wv[9];
+#pragma unroll
+    for (int k = 0; k < 9; ++k)
+      wv[k] = make_float4(__ldg(w + (c + 0) * 9 + k), __ldg(w + (c + 1) * 9 + k),
+                          __ldg(w + (c + 2) * 9 + k), __ldg(w + (c + 3) * 9 + k));
+    const float4 b4 = bias ? __ldg(reinterpret_cast<const float4*>(bias + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
     const float* img = in + (size_t)n * H * W * C + c;
-    const bool inner = iw0 >= 0 && iw0 + NCOL <= W;
-    float4 xc[3][NCOL];
-    unsigned rok = 0, cok = (1u << NCOL) - 1u;
-    if (!inner) {
-      cok = 0;
+    float* obase = out + (size_t)n * OH * OW * C + c;
+    auto load_row = [&](int ih, float4 (&xr)[6]) {
 #pragma unroll
-      for (int j = 0; j < NCOL; ++j)
-        if (iw0 + j >= 0 && iw0 + j < W) cok |= 1u << j;
-    }
-#pragma unroll
-    for (int kh = 0; kh < 3; ++kh) {
-      const int ih = oh * STRIDE - pad + kh;
-      const bool ok = ih >= 0 && ih < H;
-      rok |= ok ? 1u << kh : 0u;
-      const float* rowp = img + ((size_t)(ok ? ih : 0) * W) * C;
-#pragma unroll
-      for (int j = 0; j < NCOL; ++j) {
-        xc[kh][j] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (ok && ((cok >> j) & 1u))
-          xc[kh][j] = __ldg(reinterpret_cast<const float4*>(rowp + (size_t)(iw0 + j) * C));
+      for (int j = 0; j < 6; ++j) {
+        xr[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (ih >= 0 && ih < H && ((cok >> j) & 1u))
+          xr[j] = __ldg(reinterpret_cast<const float4*>(img + ((size_t)ih * W + iw0 + j) * C));
       }
-    }
-    float4 acc[TW];
-    const float4 b4 = *reinterpret_cast<const float4*>(bs + c);
+    };
+    // a0: output row ih + pad - 2 (gets kh = 2, then complete), a1: ih + pad - 1 (kh = 1),
+    // a2: ih + pad (kh = 0, starts from the bias)
+    float4 a0[4], a1[4], a2[4];
+    const int ih_first = oh0 - pad, ih_last = oh1 - 1 - pad + 2;
+    float4 xn[6];
+    load_row(ih_first, xn);
+    for (int ih = ih_first; ih <= ih_last; ++ih) {
+      float4 xr[6];
 #pragma unroll
-    for (int t = 0; t < TW; ++t) acc[t] = b4;
+      for (int j = 0; j < 6; ++j) xr[j] = xn[j];
+      if (ih < ih_last) load_row(ih + 1, xn);  // in flight while this row is folded in
+      const bool row_in = ih >= 0 && ih < H;
 #pragma unroll
-    for (int kh = 0; kh < 3; ++kh) {
-      if (!((rok >> kh) & 1u)) continue;  // out-of-image rows are skipped
+      for (int t = 0; t < 4; ++t) a2[t] = b4;
 #pragma unroll
-      for (int kw = 0; kw < 3; ++kw) {
-        const float4 wv = *reinterpret_cast<const float4*>(wT + (kh * 3 + kw) * C + c);
+      for (int kh = 0; kh < 3; ++kh) {
+        float4* acc = kh == 0 ? a2 : (kh == 1 ? a1 : a0);
+        if (!row_in) break;  // out-of-image rows contribute nothing
 #pragma unroll
-        for (int t = 0; t < TW; ++t) {
-          if (!((cok >> (t * STRIDE + kw)) & 1u)) continue;
-          const float4 x = xc[kh][t * STRIDE + kw];
-          const float2 lo = nx_ffma2(make_float2(x.x, x.y), make_float2(wv.x, wv.y),
-                                     make_float2(acc[t].x, acc[t].y));
-          const float2 hi = nx_ffma2(make_float2(x.z, x.w), make_float2(wv.z, wv.w),
-                                     make_float2(acc[t].z, acc[t].w));
-          acc[t] = make_float4(lo.x, lo.y, hi.x, hi.y);
+        for (int kw = 0; kw < 3; ++kw) {
+          const float4 wk = wv[kh * 3 + kw];
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            if (!((cok >> (t + kw)) & 1u)) continue;
+            const float4 x = xr[t + kw];
+            const float2 lo = nx_ffma2(make_float2(x.x, x.y), make_float2(wk.x, wk.y),
+                                       make_float2(acc[t].x, acc[t].y));
+            const float2 hi = nx_ffma2(make_float2(x.z, x.w), make_float2(wk.z, wk.w),
+                                       make_float2(acc[t].z, acc[t].w));
+            acc[t] = make_float4(lo.x, lo.y, hi.x, hi.y);
+          }
         }
       }
-    }
-    float* orow = out + ((size_t)n * OH + oh) * OW * C + c;
+      const int od = ih + pad - 2;  // complete output row
+      if (od >= oh0 && od < oh1) {
+        float* orow = obase + (size_t)od * OW * C;
 #pragma unroll
-    for (int t = 0; t < TW; ++t) {
-      if (ow0 + t >= OW) break;
-      float4 a = acc[t];
-      if (act == 1) {
-        a.x = a.x > 0.f ? a.x : 0.f;
-        a.y = a.y > 0.f ? a.y : 0.f;
-        a.z = a.z > 0.f ? a.z : 0.f;
-        a.w = a.w > 0.f ? a.w : 0.f;
+        for (int t = 0; t < 4; ++t) {
+          if (ow0 + t >= OW) break;
+          float4 v = a0[t];
+          if (act == 1) {
+            v.x = v.x > 0.f ? v.x : 0.f;
+            v.y = v.y > 0.f ? v.y : 0.f;
+            v.z = v.z > 0.f ? v.z : 0.f;
+            v.w = v.w > 0.f ? v.w : 0.f;
+          }
+          *reinterpret_cast<float4*>(orow + (size_t)(ow0 + t) * C) = v;
+        }
       }
-      *reinterpret_cast<float4*>(orow + (size_t)(ow0 + t) * C) = a;
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        a0[t] = a1[t];
+        a1[t] = a2[t];
+      }
     }
   }
 }
@@ -600,13 +608,19 @@ bool dw_dev(Call& c, const float* in, int N, int H, int W, int C, const float* w
   const size_t smem = ((size_t)KH * KW * C + C) * 4;
   const bool rowk = C % 4 == 0 && aligned16(in) && aligned16(out) && smem <= 48 * 1024 &&
                     (long long)N * OH < (1LL << 31) && (long long)H * W * C < (1LL << 31);
-  if (rowk && KH == 3 && KW == 3 && (stride == 1 || stride == 2)) {
-    const int grid = 2 * c.sm_count();
-    if (stride == 1)
-      k_dw3_persist<4, 1><<<grid, 256, smem, c.stream()>>>(in, N, H, W, C, w, bias, pad, OH, OW, out, act);
-    else
-      k_dw3_persist<2, 2><<<grid, 256, smem, c.stream()>>>(in, N, H, W, C, w, bias, pad, OH, OW, out, act);
-    return c.launched("k_dw3_persist");
+  if (rowk && KH == 3 && KW == 3 && stride == 1 && (!bias || aligned16(bias))) {
+    // rows per item: 8 for tall maps (1.25 row reads per output row), fewer for short ones
+    const long long per8 = (long long)N * ((OH + 7) / 8) * ((OW + 3) / 4) * (C / 4);
+    const long long cap = 384LL * c.sm_count();
+    const int grid = (int)std::min<long long>((per8 + 383) / 384, (long long)c.sm_count());
+    if (OH >= 16) {
+      k_dw3_roll<8><<<grid, 384, 0, c.stream()>>>(in, N, H, W, C, w, bias, pad, OH, OW, out, act);
+    } else {
+      const long long per4 = (long long)N * ((OH + 3) / 4) * ((OW + 3) / 4) * (C / 4);
+      k_dw3_roll<4><<<(int)std::min<long long>((per4 + 383) / 384, cap / 384), 384, 0, c.stream()>>>(
+          in, N, H, W, C, w, bias, pad, OH, OW, out, act);
+    }
+    return c.launched("k_dw3_roll");
   }
   if (rowk && KW == 3 && (stride == 1 || stride == 2)) {
     if (stride == 1)
