@@ -201,6 +201,102 @@ __global__ void __launch_bounds__(128) k_conv_simt(const float* __restrict__ x, 
   }
 }
 
+// 1x1 pad-0 convolution (any stride) with few output channels on CUDA cores, register-tiled over
+// pixels: a thread owns PX consecutive output pixels x NBT output channels (S threads share a
+// pixel group, NB = S*NBT columns), so each 16-byte weight broadcast feeds PX*4 FMAs; the next
+// 4 input channels of its PX pixels are loaded while the current ones are multiplied.  Per
+// output the arithmetic is k_conv_simt's: an fp32 fma chain from 0 over the input channels,
+// then + bias, then ReLU.  Weights [Cin][Cout] (row stride ldw) are staged as [Cin][NB] once per
+// block of a persistent grid.
+template <int NB, int S, int PX>
+__global__ void __launch_bounds__(256, 2) k_pw_simt(const float* __restrict__ x, int H, int W, int Cs,
+                                                 int coff, int Cin, const float* __restrict__ w,
+                                                 long long ldw, const float* __restrict__ bias,
+                                                 int Cout, int stride, int OH, int OW, unsigned M,
+                                                 float* __restrict__ out, long long ldc, int act) {
+  constexpr int NBT = NB / S;
+  static_assert(NBT % 4 == 0, "16-byte weight broadcasts");
+  extern __shared__ float4 pw_sm4[];
+  float* ws = reinterpret_cast<float*>(pw_sm4);  // [Cin][NB]
+  float* bs = ws + Cin * NB;
+  stage_block<16>(ws, Cin * NB, [&](int i) {
+    const int k = i / NB, j = i - k * NB;
+    return (j < Cout) ? __ldg(w + (long long)k * ldw + j) : 0.0f;
+  });
+  for (int j = threadIdx.x; j < NB; j += blockDim.x) bs[j] = (bias && j < Cout) ? bias[j] : 0.0f;
+  __syncthreads();
+  const unsigned groups = (M + PX - 1) / PX;
+  for (unsigned q = blockIdx.x * blockDim.x + threadIdx.x; q < groups * S; q += gridDim.x * blockDim.x) {
+    const unsigned g = q / S, g0 = (q % S) * NBT;
+    const float* src[PX];
+    bool valid[PX];
+#pragma unroll
+    for (int p = 0; p < PX; ++p) {
+      const unsigned m = g * PX + p;
+      valid[p] = m < M;
+      const unsigned mm = valid[p] ? m : 0;
+      const unsigned ow = mm % OW, t = mm / OW, oh = t % OH, n = t / OH;
+      src[p] = x + (((size_t)n * H + oh * stride) * W + ow * stride) * Cs + coff;
+    }
+    float acc[PX][NBT];
+#pragma unroll
+    for (int p = 0; p < PX; ++p)
+#pragma unroll
+      for (int j = 0; j < NBT; ++j) acc[p][j] = 0.0f;
+    float4 xn[PX];
+#pragma unroll
+    for (int p = 0; p < PX; ++p) xn[p] = __ldg(reinterpret_cast<const float4*>(src[p]));
+    for (int k = 0; k < Cin; k += 4) {
+      float4 xc[PX];
+#pragma unroll
+      for (int p = 0; p < PX; ++p) xc[p] = xn[p];
+      if (k + 4 < Cin) {
+#pragma unroll
+        for (int p = 0; p < PX; ++p) xn[p] = __ldg(reinterpret_cast<const float4*>(src[p] + k + 4));
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float4* wr4 = reinterpret_cast<const float4*>(ws + (k + u) * NB + g0);
+#pragma unroll
+        for (int j = 0; j < NBT; j += 4) {
+          const float4 w4 = wr4[j / 4];
+#pragma unroll
+          for (int p = 0; p < PX; ++p) {
+            const float xv = u == 0 ? xc[p].x : (u == 1 ? xc[p].y : (u == 2 ? xc[p].z : xc[p].w));
+            const float2 x2 = make_float2(xv, xv);
+            const float2 r0 = nx_ffma2(x2, make_float2(w4.x, w4.y), make_float2(acc[p][j], acc[p][j + 1]));
+            const float2 r1 = nx_ffma2(x2, make_float2(w4.z, w4.w), make_float2(acc[p][j + 2], acc[p][j + 3]));
+            acc[p][j] = r0.x;
+            acc[p][j + 1] = r0.y;
+            acc[p][j + 2] = r1.x;
+            acc[p][j + 3] = r1.y;
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int p = 0; p < PX; ++p) {
+      if (!valid[p]) continue;
+      float* dst = out + (size_t)(g * PX + p) * ldc + g0;
+#pragma unroll
+      for (int j = 0; j < NBT; j += 4) {
+        float4 v;
+        v.x = __fadd_rn(acc[p][j], bs[g0 + j]);
+        v.y = __fadd_rn(acc[p][j + 1], bs[g0 + j + 1]);
+        v.z = __fadd_rn(acc[p][j + 2], bs[g0 + j + 2]);
+        v.w = __fadd_rn(acc[p][j + 3], bs[g0 + j + 3]);
+        if (act) {
+          v.x = v.x > 0.0f ? v.x : 0.0f;
+          v.y = v.y > 0.0f ? v.y : 0.0f;
+          v.z = v.z > 0.0f ? v.z : 0.0f;
+          v.w = v.w > 0.0f ? v.w : 0.0f;
+        }
+        if ((int)g0 + j < Cout) *reinterpret_cast<float4*>(dst + j) = v;
+      }
+    }
+  }
+}
+
 // Small-K convolution fused with the 2x2 / stride-2 / pad-0 max-pool that follows it (an ACFUN0
 // Conv -> MaxPool pair): a block owns one pooled output row; it stages the conv weights
 // [K][Cout], the bias and the input rows that row needs in shared memory, then one thread per
@@ -687,6 +783,19 @@ static bool conv_simt(Call& c, const float* x, int N, int H, int W, int Cs, int 
   *handled = true;
   const int vec_in = (Cs % 4 == 0) && (coff % 4 == 0) && aligned16(x);
   const int vec_out = (Cout % 4 == 0) && (ldc % 4 == 0) && aligned16(out);
+  if (KH == 1 && KW == 1 && pad == 0 && vec_in && vec_out && Cg % 4 == 0 && Cout % 4 == 0 &&
+      (NB == 24 || NB == 64)) {
+    // 1x1: pixel-tiled kernel (4 pixels per thread)
+    const long long work = (M + 3) / 4 * (NB == 24 ? 2 : 4);
+    const int grid = (int)std::min<long long>((work + 255) / 256, 2LL * c.sm_count());
+    if (NB == 24)
+      k_pw_simt<24, 2, 4><<<grid, 256, smem, c.stream()>>>(x, H, W, Cs, coff, Cg, w, ldw, bias, Cout,
+                                                            stride, OH, OW, (unsigned)M, out, ldc, act);
+    else
+      k_pw_simt<64, 4, 4><<<grid, 256, smem, c.stream()>>>(x, H, W, Cs, coff, Cg, w, ldw, bias, Cout,
+                                                            stride, OH, OW, (unsigned)M, out, ldc, act);
+    return c.launched("k_pw_simt");
+  }
   // a few resident blocks per SM, each walking many pixels: the weight staging is paid once
   // per block
   const int grid = (int)std::min<long long>((2 * M + 127) / 128, 8LL * c.sm_count());

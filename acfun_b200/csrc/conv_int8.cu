@@ -57,10 +57,24 @@ __global__ void k_absmax(const float* __restrict__ x, long long n, Int8Scalars* 
   __shared__ int last;
   float m = 0.0f;
   if ((reinterpret_cast<uintptr_t>(x) & 15) == 0) {
-    const long long n4 = n >> 2;
+    const long long n4 = n >> 2, step = (long long)gridDim.x * blockDim.x;
     const float4* x4 = reinterpret_cast<const float4*>(x);
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4;
-         i += (long long)gridDim.x * blockDim.x) {
+    long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    // four independent 16-byte loads in flight per thread
+    for (; i + 3 * step < n4; i += 4 * step) {
+      float4 q[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) q[u] = __ldg(x4 + i + u * step);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float a = fabsf(q[u].x), b = fabsf(q[u].y), cc = fabsf(q[u].z), d = fabsf(q[u].w);
+        m = (m < a) ? a : m;
+        m = (m < b) ? b : m;
+        m = (m < cc) ? cc : m;
+        m = (m < d) ? d : m;
+      }
+    }
+    for (; i < n4; i += step) {
       const float4 q = __ldg(x4 + i);
       const float a = fabsf(q.x), b = fabsf(q.y), cc = fabsf(q.z), d = fabsf(q.w);
       m = (m < a) ? a : m;
