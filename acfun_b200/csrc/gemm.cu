@@ -565,6 +565,14 @@ bool gemm_launch(Call& c, GemmKind kind, Epi epi, const Operand& A, const Operan
     case GemmKind::I8S: {
       const int v = pick(TuneFamily::I8);
       const bool wide = v >= 0 ? v == 1 : (N > 128 && tiles(M, N, 256) >= sms);
+      // plain requantising GEMMs that fill the GPU with 256 x 256 tiles: the 2-SM MMA
+      static const bool two_sm = [] {
+        const char* e = getenv("ACFUN_GEMM_2SM");
+        return !(e && !strcmp(e, "0"));
+      }();
+      if (epi == Epi::S8_REQ && plain && two_sm && v < 0 && M >= 256 && N >= 256 &&
+          tiles(M, N, 256, 256) * 2 >= sms)
+        return gemm_s8req_2sm(c, A, B, M, N, K, ep);
       if (epi == Epi::S8_REQ)
         return wide ? launch_one<MK::I8, 256, 4, 1, Epi::S8_REQ, true>(c, A, B, M, N, K, ep, cg)
                     : launch_one<MK::I8, 128, 6, 1, Epi::S8_REQ, true>(c, A, B, M, N, K, ep, cg);

@@ -289,3 +289,33 @@ def test_last_wave_column_parts_same_bits_as_whole_tiles(acf, tmp_path):
     assert_bits_equal(acf.gemm(A, B), whole["f32"], "fp32 column parts vs whole tiles")
     assert_bits_equal(acf.gemm_bf16(A, B), whole["bf16"], "bf16 column parts vs whole tiles")
     assert_bits_equal(acf.gemm_int8(Ai, Bi), whole["i8"], "int8 column parts vs whole tiles")
+
+
+def _requant_ref_torch(A, B, bias, scale, act):
+    """sat_s8(rne(relu((float)(acc + bias) * scale))) for every element, on the GPU: the integer
+    product in float64 (exact: every partial sum is an integer below 2^53), then the fp32
+    multiply and round-half-even the kernel's epilogue performs."""
+    import torch
+    acc = (A.double() @ B.double()).to(torch.int64) + bias.to(torch.int64)
+    v = acc.to(torch.int32).to(torch.float32) * scale
+    if act:
+        v = torch.clamp(v, min=0.0)
+    return torch.clamp(torch.round(v), -128, 127).to(torch.int8)
+
+
+@pytest.mark.parametrize("M,N,K,act", [(2304, 2304, 256, 1), (2200, 2450, 333, 0), (4096, 4096, 4096, 1)])
+def test_s8_requant_2sm_every_element(acf, M, N, K, act):
+    """The 2-SM path (tcgen05.mma.cta_group::2, 256 x 256 tiles on CTA pairs; taken when the
+    GEMM has enough such tiles) against an every-element reference: exact multiples, ragged M /
+    N / K (TMA zero fill past the edges, padded operand copies), and the BASELINE cfg2 shape."""
+    import torch
+    gen = torch.Generator(device="cuda").manual_seed(M + N + K)
+    A = torch.randint(-127, 128, (M, K), dtype=torch.int8, device="cuda", generator=gen)
+    B = torch.randint(-127, 128, (K, N), dtype=torch.int8, device="cuda", generator=gen)
+    bias = torch.randint(-1000, 1001, (N,), dtype=torch.int32, device="cuda", generator=gen)
+    scale = (torch.rand(N, device="cuda", generator=gen) * 9e-3 + 1e-3).to(torch.float32)
+    out = acf.gemm_s8_requant(A, B, bias, scale, act)
+    acf.synchronize()
+    ref = _requant_ref_torch(A, B, bias, scale, act)
+    bad = int((out != ref).sum().item())
+    assert bad == 0, f"{bad} of {M * N} elements differ"
