@@ -16,9 +16,11 @@
 //   * One thread issues, per slab, the MMAs of its KW taps: the A operand of tap kw is the
 //     slab's rows kw .. kw + 127, a descriptor whose start is shifted by kw rows, so each
 //     input row is converted and staged once per kernel row instead of once per tap.  3xBF16
-//     per K-step: lo*hi + hi*lo + hi*hi into the fp32 accumulator in TMEM (four buffers).
-//   * Epilogue warps drain TMEM, add the bias, apply ReLU and store the rows that land on
-//     output pixels (the F32_BIAS arithmetic of the general GEMM kernel).
+//     in two MMAs per K-step: hi * [hi | lo] as one 128-column operand (the two weight copies
+//     are the two 64-column chunks of an MN-major B whose chunk stride is one copy) and
+//     lo * hi, into three fp32 partial accumulators in TMEM (two buffers of 256 columns).
+//   * Epilogue warps drain TMEM, sum the partials ((lo*hi + hi*lo) + hi*hi), add the bias,
+//     apply ReLU and store the rows that land on output pixels.
 // Every wait is bounded (ptx.cuh); on expiry the kernel flags the error word and drains.
 #include "conv.cuh"
 #include "gemm.cuh"
@@ -36,7 +38,7 @@ constexpr int B_BYTES = 2 * B_COPY;             // hi + lo weights, resident
 constexpr int SLAB_COPY = SLAB_ROWS * ROWB;
 constexpr int SLAB = 2 * SLAB_COPY;             // hi + lo
 constexpr int NSLAB = 2;
-constexpr int NBUF = 4;                         // TMEM accumulator buffers
+constexpr int NBUF = 2;                         // TMEM buffers of 3 partials (256 columns)
 constexpr int CONV_WARPS = 10, EPI_WARPS = 4;
 constexpr int CONV_THREADS = 32 * CONV_WARPS;
 constexpr int THREADS = 64 + 32 * (CONV_WARPS + EPI_WARPS);
@@ -119,7 +121,7 @@ __global__ void __launch_bounds__(halo::THREADS, 1)
   }
   if (threadIdx.x < BN) sbias[threadIdx.x] = (bias && (int)threadIdx.x < a.Cout) ? bias[threadIdx.x] : 0.0f;
   if (warp == 1) {
-    dev::tmem_alloc(tmem_slot, NBUF * BN);
+    dev::tmem_alloc(tmem_slot, 512);
     dev::tmem_relinquish();
   }
   dev::tc_fence_before();
@@ -143,8 +145,11 @@ __global__ void __launch_bounds__(halo::THREADS, 1)
     // adding to their 14-bit start-address field (addresses stay below 256 KB, no carry).
     if (lane == 0) {
       constexpr uint32_t idesc = dev::umma_idesc(1u, 1u, 1u, 0u, 1u, 128u, (uint32_t)BN);
+      constexpr uint32_t idesc2 = dev::umma_idesc(1u, 1u, 1u, 0u, 1u, 128u, 128u);
       const uint64_t ad0 = halo_desc(dev::smem_u32(sA), 16, 1024);
-      const uint64_t bd0 = halo_desc(dev::smem_u32(sB), TAPB, 1024);
+      // [B_hi | B_lo] as one 128-column MN-major operand: chunk 1 (columns 64..127) sits one
+      // weight copy after chunk 0
+      const uint64_t bd0 = halo_desc(dev::smem_u32(sB), B_COPY, 1024);
       bool ok = dev::mbar_wait(b_full, 0, err);
       dev::tc_fence_after();
       uint32_t sl = 0, local = 0;
@@ -155,7 +160,7 @@ __global__ void __launch_bounds__(halo::THREADS, 1)
           break;
         }
         dev::tc_fence_after();
-        const uint32_t d_tmem = tmem + buf * BN;
+        const uint32_t d_tmem = tmem + buf * 256, d2 = d_tmem + 128;
         uint64_t bd = bd0;  // tap (kh, kw) of the hi copy
         for (int kh = 0; kh < a.KH; ++kh, ++sl) {
           const uint32_t s = sl & 1, ph = (sl >> 1) & 1;
@@ -169,14 +174,11 @@ __global__ void __launch_bounds__(halo::THREADS, 1)
             const uint32_t first = (kh | kw) == 0;
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks) {
-              // lo*hi, hi*lo, hi*hi
-              dev::umma<dev::MmaKind::F16>(d_tmem, ad + ((SLAB_COPY + ks * 32) >> 4),
-                                           bd + ((ks * 16 * ROWB) >> 4), idesc,
-                                           (ks != 0) || !first);
+              // hi * [hi | lo] (128 columns), lo * hi (64 columns)
               dev::umma<dev::MmaKind::F16>(d_tmem, ad + ((ks * 32) >> 4),
-                                           bd + ((B_COPY + ks * 16 * ROWB) >> 4), idesc, 1u);
-              dev::umma<dev::MmaKind::F16>(d_tmem, ad + ((ks * 32) >> 4),
-                                           bd + ((ks * 16 * ROWB) >> 4), idesc, 1u);
+                                           bd + ((ks * 16 * ROWB) >> 4), idesc2, (ks != 0) || !first);
+              dev::umma<dev::MmaKind::F16>(d2, ad + ((SLAB_COPY + ks * 32) >> 4),
+                                           bd + ((ks * 16 * ROWB) >> 4), idesc, (ks != 0) || !first);
             }
           }
           dev::umma_commit(&slab_empty[s]);
@@ -284,9 +286,16 @@ __global__ void __launch_bounds__(halo::THREADS, 1)
 #pragma unroll
       for (int c0 = 0; c0 < BN; c0 += 32) {
         if (c0 >= a.Cout) break;  // warp-uniform
-        uint32_t v[32];
-        dev::tmem_ld32(tmem + buf * BN + (uint32_t)c0 + ((uint32_t)(q * 32) << 16), v);
+        uint32_t v[32], v1[32], v2[32];
+        const uint32_t tb = tmem + buf * 256 + (uint32_t)c0 + ((uint32_t)(q * 32) << 16);
+        dev::tmem_ld32(tb, v);          // hi*hi
+        dev::tmem_ld32(tb + 64, v1);    // hi*lo
+        dev::tmem_ld32(tb + 128, v2);   // lo*hi
         dev::tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          v[i] = __float_as_uint(__fadd_rn(__fadd_rn(__uint_as_float(v2[i]), __uint_as_float(v1[i])),
+                                           __uint_as_float(v[i])));
         if (!store) continue;
         float o[32];
 #pragma unroll
@@ -314,7 +323,7 @@ __global__ void __launch_bounds__(halo::THREADS, 1)
   __syncthreads();
   if (warp == 1) {
     dev::tc_fence_after();
-    dev::tmem_dealloc(tmem, NBUF * BN);
+    dev::tmem_dealloc(tmem, 512);
   }
 }
 
