@@ -143,7 +143,7 @@ def measured_peaks():
 
 def ncu_traffic():
     """DRAM bytes per launch of the GEMM kernel from the committed ncu summary (or None)."""
-    p = os.path.join(ROOT, "profiles", "gemm_tc_int8_requant_4096.json")
+    p = os.path.join(ROOT, "profiles", "gemm_s8req_2sm_4096.json")
     if os.path.exists(p):
         try:
             return json.load(open(p)).get("dram_bytes_per_launch")
