@@ -20,6 +20,13 @@ enum ConvRoute {
 // Narrow stride-1 fp32 convolution (Cin, Cout <= 64, KH*KW <= 9) as one 3xBF16 tcgen05 kernel
 // with resident weights and in-kernel operand conversion (conv_halo.cu).
 bool conv_halo_ok(int Cin, int KH, int KW, int Cout, int stride);
+// Small-K int8 convolution + 2x2/2 max-pool on tensor cores (conv_i8_pool_tc.cu): per-image
+// scales (ab = [N][2][Cout] alpha / beta, img_inv, img_zero from k_absmax_img).
+bool conv_i8_pool_tc_ok(const float* x, int W, int Cin, int KH, int KW, int Cout, int stride, int PW);
+bool conv_i8_pool_tc_dev(Call& c, const float* x, int N, int H, int W, int Cin, const int8_t* wq,
+                         int KH, int KW, int Cout, int pad, int PH, int PW, const float* ab,
+                         const float* img_inv, const int* img_zero, float* out, int act,
+                         int post_relu, unsigned* out_max);
 bool conv_halo_f32_dev(Call& c, const float* x, int N, int H, int W, int Cs, int coff, int Cin,
                        const float* w, long long ldw, const float* bias, int KH, int KW, int Cout,
                        int pad, float* out, long long ldc, int act);

@@ -1,26 +1,25 @@
 // conv_halo.cu — narrow stride-1 fp32 convolutions (at most 64 input and 64 output channels,
 // KH*KW <= 9: the reference's Winograd F(2,3) / F(4,3) routes at the cfg3 shapes,
-// winograd_avx512.cpp:186-250 and winograd43_avx512.cpp:218-280) as one persistent tcgen05
-// kernel in 3xBF16, with no preparation pass over the activation.
+// winograd_avx512.cpp:186-250 and winograd43_avx512.cpp:218-280) as a split pass plus one
+// persistent tcgen05 kernel in 3xBF16.
 //
 // GEMM view: row r = a pixel of the zero-padded input grid (N x Hp x Wp, NHWC), 64 channels
 // per row; output pixel (oh, ow) of image n is row r = (n*Hp + oh)*Wp + ow, and tap (kh, kw)
 // reads row r + kh*Wp + kw.  A tile is 128 consecutive rows x 64 output channels.
+//   * k_halo_split writes the padded grid once as bf16 hi / lo planes ([2][rows][64], zero in
+//     the border and past the channels), a bandwidth pass whose output stays in L2.
 //   * The split weights of every tap ([2][taps][64 channels][64 columns] bf16 hi / lo, 16 KB a
 //     tap) are loaded by TMA once per CTA and stay resident in shared memory.
-//   * For each kernel row kh, converter warps read the tile's 128 + KW - 1 input rows
-//     (a "slab") straight from the fp32 NHWC tensor -- zero outside the image and past the
-//     channels -- split them into bf16 hi / lo and store them in the 128-byte-swizzled
-//     K-major layout the tensor core reads; two slab buffers let the next slab be converted
-//     while the MMAs consume the current one.
-//   * One thread issues, per slab, the MMAs of its KW taps: the A operand of tap kw is the
-//     slab's rows kw .. kw + 127, a descriptor whose start is shifted by kw rows, so each
-//     input row is converted and staged once per kernel row instead of once per tap.  3xBF16
-//     in two MMAs per K-step: hi * [hi | lo] as one 128-column operand (the two weight copies
-//     are the two 64-column chunks of an MN-major B whose chunk stride is one copy) and
-//     lo * hi, into three fp32 partial accumulators in TMEM (two buffers of 256 columns).
-//   * Epilogue warps drain TMEM, sum the partials ((lo*hi + hi*lo) + hi*hi), add the bias,
-//     apply ReLU and store the rows that land on output pixels.
+//   * For each kernel row kh one TMA box brings the tile's 128 + KW - 1 rows of both planes
+//     (a "slab", 128-byte swizzled K-major); the A operand of tap kw is the slab from row kw
+//     on, a descriptor whose start is shifted by kw rows, so a row is staged once per kernel
+//     row instead of once per tap.  3xBF16 in two MMAs per K-step: hi * [hi | lo] as one
+//     128-column operand (the two weight copies are the two 64-column chunks of an MN-major B
+//     whose chunk stride is one copy) and lo * hi, into three fp32 partial accumulators in
+//     TMEM (two buffers of 256 columns).
+//   * Eight epilogue warps (two per TMEM lane quadrant, one 32-column chunk each) sum the
+//     partials ((lo*hi + hi*lo) + hi*hi), add the bias, apply ReLU and store the rows that
+//     land on output pixels.
 // Every wait is bounded (ptx.cuh); on expiry the kernel flags the error word and drains.
 #include "conv.cuh"
 #include "gemm.cuh"
@@ -39,11 +38,9 @@ constexpr int SLAB_COPY = SLAB_ROWS * ROWB;
 constexpr int SLAB = 2 * SLAB_COPY;             // hi + lo
 constexpr int NSLAB = 2;
 constexpr int NBUF = 2;                         // TMEM buffers of 3 partials (256 columns)
-constexpr int CONV_WARPS = 10, EPI_WARPS = 4;
-constexpr int CONV_THREADS = 32 * CONV_WARPS;
-constexpr int THREADS = 64 + 32 * (CONV_WARPS + EPI_WARPS);
-constexpr int UNITS = (SLAB_ROWS * 4 + CONV_THREADS - 1) / CONV_THREADS;  // 16-channel units
-// barriers: b_full, slab_full[2], slab_empty[2], t_full[4], t_empty[4], drain
+constexpr int EPI_WARPS = 8;
+constexpr int THREADS = 64 + 32 * EPI_WARPS;
+// barriers: b_full, slab_full[2], slab_empty[2], t_full[2], t_empty[2], drain
 constexpr int BAR_BYTES = 16 * 8;
 constexpr int SMEM = 1024 + B_BYTES + NSLAB * SLAB + BAR_BYTES + 16 + BN * 4;
 static_assert(SMEM <= 232448, "shared memory");
@@ -51,9 +48,7 @@ static_assert(B_COPY % 1024 == 0 && SLAB_COPY % 1024 == 0, "swizzle-atom alignme
 }  // namespace halo
 
 struct HaloArgs {
-  const float* x;        // NHWC input, channels [coff, coff + Cin) of Cs
-  int H, W, Cs, coff, Cin;
-  int pad, Wp, KH, KW;
+  int KH, KW, Wp;
   unsigned img_rows;     // Hp * Wp
   unsigned rows;         // N * Hp * Wp (< 2^31)
   float* out;
@@ -73,18 +68,50 @@ __global__ void k_halo_wsplit(const float* __restrict__ w, int taps, int Cin, in
   }
 }
 
+// x: NHWC (channel stride Cs, channels [coff, coff + Cin)) -> [2][rows][64] bf16 hi / lo planes of
+// the zero-padded grid; one thread per (grid row, 8 channels): two 16-byte loads, one 16-byte
+// store per plane.
+template <bool VEC>
+__global__ void k_halo_split(const float* __restrict__ x, int H, int W, int Cs, int coff, int Cin,
+                             int pad, int Wp, unsigned img_rows, unsigned total,
+                             uint4* __restrict__ dst, unsigned plane16) {
+  for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const unsigned g = i >> 3, c8 = (i & 7) * 8;
+    const unsigned n = g / img_rows, q = g - n * img_rows;
+    const unsigned hp = q / (unsigned)Wp;
+    const int ih = (int)hp - pad, iw = (int)(q - hp * (unsigned)Wp) - pad;
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if ((int)c8 < Cin && ih >= 0 && ih < H && iw >= 0 && iw < W) {
+      const float* src = x + (((size_t)n * H + ih) * W + iw) * Cs + coff + c8;
+      if (VEC && (int)c8 + 8 <= Cin) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(src));
+        const float4 b = __ldg(reinterpret_cast<const float4*>(src) + 1);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = ((int)c8 + e < Cin) ? __ldg(src + e) : 0.0f;
+      }
+    }
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) nx_split_bf16x2(v[2 * k], v[2 * k + 1], h[k], l[k]);
+    dst[i] = make_uint4(h[0], h[1], h[2], h[3]);
+    dst[i + plane16] = make_uint4(l[0], l[1], l[2], l[3]);
+  }
+}
+
 // 128-byte-swizzle descriptor of a matrix starting at `addr`.  The start may lie on any 128-byte
 // row: the tensor core takes the swizzle phase of each row from the absolute shared-memory address
-// bits, as TMA and the converters wrote it, so the descriptor's base-offset field stays 0 (setting
-// it to the start's phase, (addr >> 7) & 7, measurably reads the wrong rows).
+// bits, as TMA wrote it, so the descriptor's base-offset field stays 0 (setting it to the start's
+// phase, (addr >> 7) & 7, measurably reads the wrong rows).
 __device__ __forceinline__ uint64_t halo_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
   return dev::umma_sdesc(addr, lbo, sbo, dev::UMMA_SW128);
 }
 
-template <bool VEC>
 __global__ void __launch_bounds__(halo::THREADS, 1)
-    conv_halo_kernel(const __grid_constant__ CUtensorMap tmB, HaloArgs a, const float* __restrict__ bias,
-                     int num_tiles, unsigned* err) {
+    conv_halo_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     HaloArgs a, const float* __restrict__ bias, int num_tiles, unsigned* err) {
   using namespace halo;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -96,8 +123,8 @@ __global__ void __launch_bounds__(halo::THREADS, 1)
   uint64_t* slab_full = bars + 1;
   uint64_t* slab_empty = bars + 3;
   uint64_t* t_full = bars + 5;
-  uint64_t* t_empty = bars + 9;
-  uint64_t* drain = bars + 13;
+  uint64_t* t_empty = bars + 7;
+  uint64_t* drain = bars + 9;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + B_BYTES + NSLAB * SLAB + BAR_BYTES);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* sbias = reinterpret_cast<float*>(smem + B_BYTES + NSLAB * SLAB + BAR_BYTES + 16);
@@ -107,7 +134,7 @@ __global__ void __launch_bounds__(halo::THREADS, 1)
   if (threadIdx.x == 0) {
     dev::mbar_init(b_full, 1);
     for (int s = 0; s < NSLAB; ++s) {
-      dev::mbar_init(&slab_full[s], CONV_WARPS);
+      dev::mbar_init(&slab_full[s], 1);
       dev::mbar_init(&slab_empty[s], 1);
     }
     for (int b = 0; b < NBUF; ++b) {
@@ -117,6 +144,7 @@ __global__ void __launch_bounds__(halo::THREADS, 1)
     dev::mbar_init(drain, 1);
     *abort_flag = 0;
     dev::fence_mbar_init();
+    dev::tma_prefetch_desc(&tmA);
     dev::tma_prefetch_desc(&tmB);
   }
   if (threadIdx.x < BN) sbias[threadIdx.x] = (bias && (int)threadIdx.x < a.Cout) ? bias[threadIdx.x] : 0.0f;
@@ -130,14 +158,30 @@ __global__ void __launch_bounds__(halo::THREADS, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // ---------------- resident weights: one TMA box per (copy, tap)
+    // ---------------- TMA producer: resident weights, then one slab per (tile, kernel row)
     if (lane == 0) {
       dev::mbar_arrive_expect_tx(b_full, (uint32_t)(2 * taps * TAPB));
       for (int op = 0; op < 2; ++op)
         for (int t = 0; t < taps; ++t)
           dev::tma_load_3d(sB + op * B_COPY + t * TAPB, &tmB, b_full, 0, t * CP, op);
-      // the copies must land before the CTA can exit
-      dev::mbar_wait(b_full, 0, err);
+      uint32_t it = 0;
+      for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+        for (int kh = 0; kh < a.KH; ++kh, ++it) {
+          const uint32_t s = it & 1, ph = (it >> 1) & 1;
+          if (*abort_flag || !dev::mbar_wait(&slab_empty[s], ph ^ 1, err)) {
+            *abort_flag = 1;
+            break;
+          }
+          dev::mbar_arrive_expect_tx(&slab_full[s], (uint32_t)SLAB);
+          dev::tma_load_3d(sA + s * SLAB, &tmA, &slab_full[s], 0, t * 128 + kh * a.Wp, 0);
+        }
+        if (*abort_flag) break;
+      }
+      // every copy must land before the CTA can release its shared memory
+      dev::mbar_wait(b_full, 0, nullptr, 200000000ull);
+      if (*abort_flag)
+        for (uint32_t k = it > (uint32_t)NSLAB ? it - NSLAB : 0; k < it; ++k)
+          dev::mbar_wait(&slab_full[k & 1], (k >> 1) & 1, nullptr, 200000000ull);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer
@@ -192,86 +236,10 @@ __global__ void __launch_bounds__(halo::THREADS, 1)
         for (int b = 0; b < NBUF; ++b) dev::mbar_arrive(&t_full[b]);
       }
     }
-  } else if (warp < 2 + CONV_WARPS) {
-    // ---------------- converters: fp32 NHWC -> swizzled bf16 hi / lo slab rows
-    // unit = (slab row, 16 channels): 64 contiguous input bytes, two 16-byte chunks per copy.
-    // Slab k of this CTA is (tile blockIdx.x + (k / KH) * gridDim.x, kernel row k % KH); the
-    // loads of slab k + 1 are issued before slab k is stored, so two slabs of loads overlap.
-    const int ct = threadIdx.x - 64;
-    const int R = 128 + a.KW - 1, NU = 4 * R;
-    const int my_tiles = num_tiles > (int)blockIdx.x
-                             ? (num_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-    const int nslabs = my_tiles * a.KH;
-    auto load_slab = [&](int k, float4 (&v)[UNITS][4]) {
-      const int t = (int)blockIdx.x + (k / a.KH) * (int)gridDim.x, kh = k - (k / a.KH) * a.KH;
-      const unsigned r0 = (unsigned)t * 128u + (unsigned)(kh * a.Wp);
-#pragma unroll
-      for (int u = 0; u < UNITS; ++u) {
-        const int idx = ct + u * CONV_THREADS, row = idx >> 2, ch = (idx & 3) * 16;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) v[u][e] = make_float4(0.f, 0.f, 0.f, 0.f);
-        const unsigned g = r0 + (unsigned)row;
-        if (idx < NU && g < a.rows && ch < a.Cin) {
-          const unsigned n = g / a.img_rows, q = g - n * a.img_rows;
-          const unsigned hp = q / a.Wp;
-          const int ih = (int)hp - a.pad, iw = (int)(q - hp * a.Wp) - a.pad;
-          if (ih >= 0 && ih < a.H && iw >= 0 && iw < a.W) {
-            const float* src = a.x + (((size_t)n * a.H + ih) * a.W + iw) * a.Cs + a.coff + ch;
-            if constexpr (VEC) {
-#pragma unroll
-              for (int e = 0; e < 4; ++e)
-                if (ch + 4 * e < a.Cin) v[u][e] = __ldg(reinterpret_cast<const float4*>(src) + e);
-            } else {
-              float* f = reinterpret_cast<float*>(v[u]);
-#pragma unroll
-              for (int e = 0; e < 16; ++e) f[e] = (ch + e < a.Cin) ? __ldg(src + e) : 0.0f;
-            }
-          }
-        }
-      }
-    };
-    auto store_slab = [&](int k, const float4 (&v)[UNITS][4]) -> bool {
-      const uint32_t s = (uint32_t)k & 1, ph = ((uint32_t)k >> 1) & 1;
-      if (*abort_flag || !dev::mbar_wait(&slab_empty[s], ph ^ 1, err)) {
-        *abort_flag = 1;
-        return false;
-      }
-      uint8_t* hi = sA + s * SLAB;
-#pragma unroll
-      for (int u = 0; u < UNITS; ++u) {
-        const int idx = ct + u * CONV_THREADS, row = idx >> 2, c16 = (idx & 3) * 2;
-        if (idx < NU) {
-#pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            const float4 p0 = v[u][2 * hh], p1 = v[u][2 * hh + 1];
-            uint32_t h[4], l[4];
-            nx_split_bf16x2(p0.x, p0.y, h[0], l[0]);
-            nx_split_bf16x2(p0.z, p0.w, h[1], l[1]);
-            nx_split_bf16x2(p1.x, p1.y, h[2], l[2]);
-            nx_split_bf16x2(p1.z, p1.w, h[3], l[3]);
-            const int off = row * ROWB + (((c16 + hh) ^ (row & 7)) << 4);
-            *reinterpret_cast<uint4*>(hi + off) = make_uint4(h[0], h[1], h[2], h[3]);
-            *reinterpret_cast<uint4*>(hi + SLAB_COPY + off) = make_uint4(l[0], l[1], l[2], l[3]);
-          }
-        }
-      }
-      dev::fence_proxy_async_smem();  // generic-proxy stores -> the tensor core's reads
-      __syncwarp();
-      if (lane == 0) dev::mbar_arrive(&slab_full[s]);
-      return true;
-    };
-    float4 va[UNITS][4], vb[UNITS][4];
-    if (nslabs > 0) load_slab(0, va);
-    for (int k = 0; k < nslabs; k += 2) {
-      if (k + 1 < nslabs) load_slab(k + 1, vb);
-      if (!store_slab(k, va)) break;
-      if (k + 1 >= nslabs) break;
-      if (k + 2 < nslabs) load_slab(k + 2, va);
-      if (!store_slab(k + 1, vb)) break;
-    }
   } else {
     // ---------------- epilogue: TMEM -> +bias, ReLU -> output pixels
-    const int q = warp & 3;
+    const int q = warp & 3;                // TMEM lane quadrant this warp may access
+    const int c0 = ((warp - 2) >> 2) * 32;  // this warp's 32 output columns
     uint32_t local = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
       const uint32_t buf = local % NBUF, use = local / NBUF;
@@ -283,34 +251,31 @@ __global__ void __launch_bounds__(halo::THREADS, 1)
       const int oh = (int)(qq / (unsigned)a.Wp), ow = (int)qq - oh * a.Wp;
       const bool store = r < a.rows && oh < a.OH && ow < a.OW;
       float* dst = a.out + (((long long)n * a.OH + oh) * a.OW + ow) * a.ldc;
-#pragma unroll
-      for (int c0 = 0; c0 < BN; c0 += 32) {
-        if (c0 >= a.Cout) break;  // warp-uniform
+      if (c0 < a.Cout) {  // warp-uniform
         uint32_t v[32], v1[32], v2[32];
         const uint32_t tb = tmem + buf * 256 + (uint32_t)c0 + ((uint32_t)(q * 32) << 16);
         dev::tmem_ld32(tb, v);          // hi*hi
         dev::tmem_ld32(tb + 64, v1);    // hi*lo
         dev::tmem_ld32(tb + 128, v2);   // lo*hi
         dev::tmem_ld_wait();
+        if (store) {
+          float o[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          v[i] = __float_as_uint(__fadd_rn(__fadd_rn(__uint_as_float(v2[i]), __uint_as_float(v1[i])),
-                                           __uint_as_float(v[i])));
-        if (!store) continue;
-        float o[32];
+          for (int i = 0; i < 32; ++i) {
+            float y = __fadd_rn(__fadd_rn(__uint_as_float(v2[i]), __uint_as_float(v1[i])),
+                                __uint_as_float(v[i]));
+            y = __fadd_rn(y, sbias[c0 + i]);
+            if (a.act) y = relu_max(y);
+            o[i] = y;
+          }
+          if (c0 + 32 <= a.Cout && (reinterpret_cast<uintptr_t>(dst + c0) & 15) == 0) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float y = __fadd_rn(__uint_as_float(v[i]), sbias[c0 + i]);
-          if (a.act) y = relu_max(y);
-          o[i] = y;
-        }
-        if (c0 + 32 <= a.Cout && (reinterpret_cast<uintptr_t>(dst + c0) & 15) == 0) {
-#pragma unroll
-          for (int i = 0; i < 32; i += 4)
-            *reinterpret_cast<float4*>(dst + c0 + i) = make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
-        } else {
-          for (int i = 0; i < 32; ++i)
-            if (c0 + i < a.Cout) dst[c0 + i] = o[i];
+            for (int i = 0; i < 32; i += 4)
+              *reinterpret_cast<float4*>(dst + c0 + i) = make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
+          } else {
+            for (int i = 0; i < 32; ++i)
+              if (c0 + i < a.Cout) dst[c0 + i] = o[i];
+          }
         }
       }
       dev::tc_fence_before();
@@ -338,37 +303,53 @@ bool conv_halo_f32_dev(Call& c, const float* x, int N, int H, int W, int Cs, int
   const int Hp = H + 2 * pad, Wp = W + 2 * pad, OH = Hp - KH + 1, OW = Wp - KW + 1;
   if (OH <= 0 || OW <= 0 || N <= 0) return true;
   const long long rows = (long long)N * Hp * Wp;
-  if (rows >= (1LL << 31) - 1024 || (long long)Hp * Wp >= (1LL << 31)) {
+  if (rows >= (1LL << 29) || (long long)Hp * Wp >= (1LL << 31)) {
     set_error(kInvalid, "%s: tensor too large", c.name());
     c.fail();
     return false;
   }
   const int taps = KH * KW;
   uint16_t* ws = static_cast<uint16_t*>(c.scratch((size_t)2 * taps * halo::CP * halo::BN * 2));
-  if (!ws) return false;
+  uint4* xs = static_cast<uint4*>(c.scratch((size_t)2 * rows * halo::CP * 2));
+  if (!ws || !xs) return false;
   k_halo_wsplit<<<(taps * halo::CP * halo::BN + 255) / 256, 256, 0, c.stream()>>>(w, taps, Cin, Cout,
                                                                                   ldw, ws);
-  if (!c.launched("k_halo_wsplit")) return false;
-  CUtensorMap tb;
-  const uint64_t dB[3] = {(uint64_t)halo::BN, (uint64_t)taps * halo::CP, 2};
-  const uint64_t sB[2] = {(uint64_t)halo::BN * 2, (uint64_t)taps * halo::CP * halo::BN * 2};
-  const uint32_t bB[3] = {(uint32_t)halo::BN, (uint32_t)halo::CP, 1u};
-  if (!encode_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, ws, dB, sB, bB,
-                   CU_TENSOR_MAP_SWIZZLE_128B)) {
-    c.fail();
-    return false;
+  const unsigned total = (unsigned)(rows * 8);
+  const bool vec = Cin % 4 == 0 && Cs % 4 == 0 && coff % 4 == 0 && aligned16(x);
+  long long gb = (total + 255) / 256, cap = (long long)c.sm_count() * 8;
+  const int grid_s = (int)(gb < cap ? gb : cap);
+  if (vec)
+    k_halo_split<true><<<grid_s, 256, 0, c.stream()>>>(x, H, W, Cs, coff, Cin, pad, Wp,
+                                                       (unsigned)(Hp * Wp), total, xs, total);
+  else
+    k_halo_split<false><<<grid_s, 256, 0, c.stream()>>>(x, H, W, Cs, coff, Cin, pad, Wp,
+                                                        (unsigned)(Hp * Wp), total, xs, total);
+  if (!c.launched("conv halo prep")) return false;
+  CUtensorMap ta, tb;
+  {
+    const uint64_t d[3] = {(uint64_t)halo::CP, (uint64_t)rows, 2};
+    const uint64_t st[2] = {(uint64_t)halo::CP * 2, (uint64_t)rows * halo::CP * 2};
+    const uint32_t bx[3] = {(uint32_t)halo::CP, (uint32_t)halo::SLAB_ROWS, 2u};
+    if (!encode_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, xs, d, st, bx,
+                     CU_TENSOR_MAP_SWIZZLE_128B)) {
+      c.fail();
+      return false;
+    }
+  }
+  {
+    const uint64_t d[3] = {(uint64_t)halo::BN, (uint64_t)taps * halo::CP, 2};
+    const uint64_t st[2] = {(uint64_t)halo::BN * 2, (uint64_t)taps * halo::CP * halo::BN * 2};
+    const uint32_t bx[3] = {(uint32_t)halo::BN, (uint32_t)halo::CP, 1u};
+    if (!encode_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, ws, d, st, bx,
+                     CU_TENSOR_MAP_SWIZZLE_128B)) {
+      c.fail();
+      return false;
+    }
   }
   HaloArgs a;
-  a.x = x;
-  a.H = H;
-  a.W = W;
-  a.Cs = Cs;
-  a.coff = coff;
-  a.Cin = Cin;
-  a.pad = pad;
-  a.Wp = Wp;
   a.KH = KH;
   a.KW = KW;
+  a.Wp = Wp;
   a.img_rows = (unsigned)(Hp * Wp);
   a.rows = (unsigned)rows;
   a.out = out;
@@ -377,22 +358,20 @@ bool conv_halo_f32_dev(Call& c, const float* x, int N, int H, int W, int Cs, int
   a.OH = OH;
   a.OW = OW;
   a.Cout = Cout;
-  const bool vec = Cin % 4 == 0 && Cs % 4 == 0 && coff % 4 == 0 && aligned16(x);
   const int tiles = (int)((rows + 127) / 128);
   const int grid = tiles < c.sm_count() ? tiles : c.sm_count();
-  static bool attr_done[2][64] = {};
+  static bool attr_done[64] = {};
   const int dv = current_device();
-  auto kern = vec ? conv_halo_kernel<true> : conv_halo_kernel<false>;
-  if (dv >= 0 && dv < 64 && !attr_done[vec][dv]) {
-    if (!ACF_CUDA_OK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, halo::SMEM))) {
+  if (dv >= 0 && dv < 64 && !attr_done[dv]) {
+    if (!ACF_CUDA_OK(cudaFuncSetAttribute(conv_halo_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          halo::SMEM))) {
       c.fail();
       return false;
     }
-    attr_done[vec][dv] = true;
+    attr_done[dv] = true;
   }
-  kern<<<grid, halo::THREADS, halo::SMEM, c.stream()>>>(tb, a, bias, tiles, c.err());
+  conv_halo_kernel<<<grid, halo::THREADS, halo::SMEM, c.stream()>>>(ta, tb, a, bias, tiles, c.err());
   return c.launched("conv_halo_kernel");
 }
 
 }  // namespace acf
-

@@ -16,6 +16,8 @@
 // derived on the device so a call never synchronises with the host mid-way.
 #include <float.h>
 #include <math.h>
+#include <stdlib.h>
+#include <string.h>
 
 #include <vector>
 
@@ -27,15 +29,13 @@
 namespace acf {
 
 struct Int8Scalars {
-  unsigned maxa_bits;  // max|x| as float bits (non-negative floats order like unsigned)
-  unsigned done;       // blocks of k_absmax finished (the last one derives the rest)
   float inv_s;         // 127 / maxa
   float sa;            // maxa / 127
   int zero;            // maxa < 1e-12: the reference writes an all-zero output
 };
 
-// Per-output-channel dequantisation factors that k_absmax's last block derives once sa is
-// known (same expressions as k_int8_colparams).
+// Per-output-channel dequantisation factors, derived on the device once sa is known (same
+// expressions as k_int8_colparams).
 struct Int8ColArgs {
   const float* wscale;
   const float* bias;
@@ -51,46 +51,45 @@ static int grid_n(Call& c, long long work) {
   return (int)(b < 1 ? 1 : (b > cap ? cap : b));
 }
 
-// conv_int8.cpp:75-77: maxa = max(maxa, |x|) (std::max keeps maxa when |x| is NaN)
-__global__ void k_absmax(const float* __restrict__ x, long long n, Int8Scalars* s, Int8ColArgs ca) {
-  __shared__ float sh[32];
-  __shared__ int last;
+// conv_int8.cpp:75-77: maxa = max(maxa, |x|) (std::max keeps maxa when |x| is NaN).
+// One block's share of max|x| over x[0, n): grid-stride over float4 with four loads in flight
+// per thread; returns the block maximum (valid in every thread).
+__device__ float block_absmax(const float* __restrict__ x, long long n, int b, int nb) {
+  __shared__ float sh[33];
   float m = 0.0f;
+  const long long step = (long long)nb * blockDim.x;
   if ((reinterpret_cast<uintptr_t>(x) & 15) == 0) {
-    const long long n4 = n >> 2, step = (long long)gridDim.x * blockDim.x;
+    const long long n4 = n >> 2;
     const float4* x4 = reinterpret_cast<const float4*>(x);
-    long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
-    // four independent 16-byte loads in flight per thread
+    long long i = b * (long long)blockDim.x + threadIdx.x;
     for (; i + 3 * step < n4; i += 4 * step) {
       float4 q[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) q[u] = __ldg(x4 + i + u * step);
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        const float a = fabsf(q[u].x), b = fabsf(q[u].y), cc = fabsf(q[u].z), d = fabsf(q[u].w);
+        const float a = fabsf(q[u].x), bb = fabsf(q[u].y), cc = fabsf(q[u].z), d = fabsf(q[u].w);
         m = (m < a) ? a : m;
-        m = (m < b) ? b : m;
+        m = (m < bb) ? bb : m;
         m = (m < cc) ? cc : m;
         m = (m < d) ? d : m;
       }
     }
     for (; i < n4; i += step) {
       const float4 q = __ldg(x4 + i);
-      const float a = fabsf(q.x), b = fabsf(q.y), cc = fabsf(q.z), d = fabsf(q.w);
+      const float a = fabsf(q.x), bb = fabsf(q.y), cc = fabsf(q.z), d = fabsf(q.w);
       m = (m < a) ? a : m;
-      m = (m < b) ? b : m;
+      m = (m < bb) ? bb : m;
       m = (m < cc) ? cc : m;
       m = (m < d) ? d : m;
     }
-    for (long long i = (n4 << 2) + blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
-         i += (long long)gridDim.x * blockDim.x) {
-      const float v = fabsf(x[i]);
+    for (long long k = (n4 << 2) + b * (long long)blockDim.x + threadIdx.x; k < n; k += step) {
+      const float v = fabsf(x[k]);
       m = (m < v) ? v : m;
     }
   } else {
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
-         i += (long long)gridDim.x * blockDim.x) {
-      const float v = fabsf(x[i]);
+    for (long long k = b * (long long)blockDim.x + threadIdx.x; k < n; k += step) {
+      const float v = fabsf(x[k]);
       m = (m < v) ? v : m;
     }
   }
@@ -106,42 +105,126 @@ __global__ void k_absmax(const float* __restrict__ x, long long n, Int8Scalars* 
       const float u = __shfl_xor_sync(0xffffffffu, m, o);
       m = (m < u) ? u : m;
     }
-    if (threadIdx.x == 0) {
-      atomicMax(&s->maxa_bits, __float_as_uint(m));
-      __threadfence();
-      last = (atomicAdd(&s->done, 1u) == gridDim.x - 1) ? 1 : 0;
-    }
+    if (threadIdx.x == 0) sh[32] = m;
   }
   __syncthreads();
-  if (!last) return;
-  // last block to finish: every block's maximum is visible (each fenced before counting)
-  __threadfence();
-  const float maxa = __uint_as_float(atomicOr(&s->maxa_bits, 0u));
-  const float sa = __fdiv_rn(maxa, 127.0f);
-  if (threadIdx.x == 0) {
-    s->zero = maxa < 1e-12f ? 1 : 0;
-    s->inv_s = __fdiv_rn(127.0f, maxa);
-    s->sa = sa;
+  return sh[32];
+}
+
+// Weight preparation for one output channel (a block): s8 [taps*Cin][Cout] -> K-major row n of
+// [Cout][taps*Cpad] (each tap's Cin weights, then zeros up to Cpad) and its column sum Sw[n].
+__device__ void wprep_channel(const int8_t* __restrict__ w, int taps, int Cin, int Cout, int Cpad,
+                              int n, int8_t* __restrict__ dst, int* __restrict__ Sw) {
+  __shared__ int red[32];
+  const int K4 = taps * Cpad / 4;
+  uint32_t* row = reinterpret_cast<uint32_t*>(dst + (size_t)n * taps * Cpad);
+  int sum = 0;
+  for (int i = threadIdx.x; i < K4; i += blockDim.x) {
+    const int k = i * 4, tap = k / Cpad, c0 = k - tap * Cpad;
+    uint32_t packed = 0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int c = c0 + e;
+      const int8_t v = c < Cin ? w[((long long)tap * Cin + c) * Cout + n] : (int8_t)0;
+      sum += v;
+      packed |= (uint32_t)(uint8_t)v << (8 * e);
+    }
+    row[i] = packed;
   }
-  for (int j = threadIdx.x; j < ca.Cout; j += blockDim.x) {
-    if (ca.wino) {
-      ca.f0[j] = __fmul_rn(__fmul_rn(sa, 0.25f), ca.wscale[j]);
-    } else {
-      const float a = __fmul_rn(sa, ca.wscale[j]);
-      const float corr = __fmul_rn(__fmul_rn(a, 128.0f), (float)ca.Sw[j]);
-      ca.f0[j] = a;
-      ca.f1[j] = __fsub_rn(ca.bias ? ca.bias[j] : 0.0f, corr);
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sum;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int t = 0;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t += red[i];
+    Sw[n] = t;
+  }
+}
+
+// First launch of a per-call int8 convolution: blocks [0, Cout) prepare the weights (one
+// output channel each), blocks [Cout, Cout + nparts) write part[b - Cout] = the maximum of
+// |x| over their share.  The partial maxima need no clearing and no counter; the quantiser
+// that runs next reduces them (Int8Derive).
+__global__ void k_int8_prep_absmax(const int8_t* __restrict__ w, int taps, int Cin, int Cout,
+                                   int Cpad, int8_t* __restrict__ wk, int* __restrict__ Sw,
+                                   const float* __restrict__ x, long long n, float* __restrict__ part,
+                                   int nparts) {
+  if ((int)blockIdx.x < Cout) {
+    wprep_channel(w, taps, Cin, Cout, Cpad, blockIdx.x, wk, Sw);
+    return;
+  }
+  const int b = (int)blockIdx.x - Cout;
+  const float m = block_absmax(x, n, b, nparts);
+  if (threadIdx.x == 0) part[b] = m;
+}
+
+// Per-call activation scalars from k_int8_prep_absmax's partial maxima, derived by every block
+// of the kernel that quantises the activation (so no launch waits on a single block):
+// maxa = max(part[]), inv_s = 127/maxa; block 0 also stores inv_s, sa = maxa/127 and the
+// all-zero flag in *s and the per-channel dequantisation factors of ca.
+struct Int8Derive {
+  const float* part = nullptr;
+  int nparts = 0;
+  Int8Scalars* s = nullptr;
+  Int8ColArgs ca{};
+};
+
+__device__ float derive_inv_s(const Int8Derive& d) {
+  __shared__ float sh[33];
+  float m = 0.0f;
+  for (int i = threadIdx.x; i < d.nparts; i += blockDim.x) {
+    const float v = d.part[i];
+    m = (m < v) ? v : m;
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    const float u = __shfl_xor_sync(0xffffffffu, m, o);
+    m = (m < u) ? u : m;
+  }
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    m = threadIdx.x < (blockDim.x >> 5) ? sh[threadIdx.x] : 0.0f;
+    for (int o = 16; o > 0; o >>= 1) {
+      const float u = __shfl_xor_sync(0xffffffffu, m, o);
+      m = (m < u) ? u : m;
+    }
+    if (threadIdx.x == 0) sh[32] = m;
+  }
+  __syncthreads();
+  const float maxa = sh[32];
+  if (blockIdx.x == 0) {
+    const float sa = __fdiv_rn(maxa, 127.0f);
+    if (threadIdx.x == 0) {
+      d.s->zero = maxa < 1e-12f ? 1 : 0;
+      d.s->inv_s = __fdiv_rn(127.0f, maxa);
+      d.s->sa = sa;
+    }
+    const Int8ColArgs& ca = d.ca;
+    for (int j = threadIdx.x; j < ca.Cout; j += blockDim.x) {
+      if (ca.wino) {
+        ca.f0[j] = __fmul_rn(__fmul_rn(sa, 0.25f), ca.wscale[j]);
+      } else {
+        const float a = __fmul_rn(sa, ca.wscale[j]);
+        const float corr = __fmul_rn(__fmul_rn(a, 128.0f), (float)ca.Sw[j]);
+        ca.f0[j] = a;
+        ca.f1[j] = __fsub_rn(ca.bias ? ca.bias[j] : 0.0f, corr);
+      }
     }
   }
+  return __fdiv_rn(127.0f, maxa);
+}
+
+// The activation scale a quantiser uses: derived from partial maxima, else inv_host.
+__device__ __forceinline__ float quant_inv_all(const Int8Derive& d, float inv_host) {
+  return d.part ? derive_inv_s(d) : inv_host;
 }
 
 // Per output channel j (one warp each): Sw = sum_k wq[k][j]; alpha = sa*ws; beta =
 // bias - (alpha*128)*Sw (conv_int8.cpp:100-107, no contraction); wso = (sa*0.25)*ws
-// (winograd_int8.cpp:155).  sa comes from `s` when given, else from `sa_host`.
+// (winograd_int8.cpp:155), for a caller-supplied sa.
 __global__ void k_int8_colparams(const int8_t* __restrict__ wq, int K, int Cout,
                                  const float* __restrict__ wscale, const float* __restrict__ bias,
-                                 const Int8Scalars* s, float sa_host, float* alpha, float* beta,
-                                 float* wso, int* Sw) {
+                                 float sa, float* alpha, float* beta, float* wso, int* Sw) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= Cout) return;
   const int j = warp;
@@ -149,7 +232,6 @@ __global__ void k_int8_colparams(const int8_t* __restrict__ wq, int K, int Cout,
   for (int k = lane; k < K; k += 32) sum += wq[(long long)k * Cout + j];
   for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
   if (lane == 0) {
-    const float sa = s ? s->sa : sa_host;
     const float a = __fmul_rn(sa, wscale[j]);
     const float corr = __fmul_rn(__fmul_rn(a, 128.0f), (float)sum);
     if (alpha) alpha[j] = a;
@@ -177,10 +259,10 @@ __device__ __forceinline__ uint8_t clamp_u8(int v) {
 //   mode 1: channels < Cin&~15: trunc(t + copysign(0.5, t)); tail channels: lroundf(t)
 //           (winograd_int8.cpp:306-325)
 __global__ void k_quant_pad_u8(const float* __restrict__ x, int N, int H, int W, int Cin, int pad,
-                               int Hp, int Wp, int Cpad, const Int8Scalars* s, float inv_host,
+                               int Hp, int Wp, int Cpad, Int8Derive dv, float inv_host,
                                const float* __restrict__ img_inv, int mode,
                                uint8_t* __restrict__ dst) {
-  const float inv_all = s ? s->inv_s : inv_host;
+  const float inv_all = quant_inv_all(dv, inv_host);
   const int cvec = Cin & ~15;
   const long long total = (long long)N * Hp * Wp * Cpad;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
@@ -259,9 +341,9 @@ __device__ __forceinline__ uint32_t quant_fast(float xv, float inv_s) {
 template <int MODE>
 __global__ void k_quant_pad_u8_16(const float* __restrict__ x, int H, int W, int Cin, int pad,
                                   int Hp, int Wp, int C16, unsigned total, int vec_in,
-                                  const Int8Scalars* s, float inv_host,
+                                  Int8Derive dv, float inv_host,
                                   const float* __restrict__ img_inv, uint4* __restrict__ dst) {
-  const float inv_all = s ? s->inv_s : inv_host;
+  const float inv_all = quant_inv_all(dv, inv_host);
   const int cvec = Cin & ~15;
   for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
     const unsigned cg = i % C16, p = i / C16;
@@ -377,9 +459,9 @@ __global__ void k_im2col_u8_16(const uint8_t* __restrict__ xq, int H, int W, int
 // Cin & ~15 in mode 1), one scale per image when img_inv is given.
 template <int MODE>
 __global__ void k_quant_u8_flat4(const float4* __restrict__ x, unsigned n4, int Cin,
-                                 unsigned per_img, const Int8Scalars* s, float inv_host,
+                                 unsigned per_img, Int8Derive dv, float inv_host,
                                  const float* __restrict__ img_inv, uint32_t* __restrict__ dst) {
-  const float inv_all = s ? s->inv_s : inv_host;
+  const float inv_all = quant_inv_all(dv, inv_host);
   const int cvec = Cin & ~15;
   for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += gridDim.x * blockDim.x) {
     const float4 v = __ldg(x + i);
@@ -417,38 +499,14 @@ __global__ void k_weights_s8k(const int8_t* __restrict__ w, int taps, int Cin, i
   }
 }
 
-// k_weights_s8k plus, per output channel (one block each), the column sum Sw[n] of its s8
-// weights; block 0 also clears the nclear words that k_absmax accumulates into.
+// wprep_channel for every output channel (one block each); block 0 also clears the nclear
+// words that k_absmax_img accumulates into.
 __global__ void k_int8_wprep(const int8_t* __restrict__ w, int taps, int Cin, int Cout, int Cpad,
                              int8_t* __restrict__ dst, int* __restrict__ Sw,
                              unsigned* __restrict__ clear, int nclear) {
-  __shared__ int red[32];
-  const int n = blockIdx.x;
-  if (n == 0)
+  if (blockIdx.x == 0)
     for (int i = threadIdx.x; i < nclear; i += blockDim.x) clear[i] = 0u;
-  const int K4 = taps * Cpad / 4;
-  uint32_t* row = reinterpret_cast<uint32_t*>(dst + (size_t)n * taps * Cpad);
-  int sum = 0;
-  for (int i = threadIdx.x; i < K4; i += blockDim.x) {
-    const int k = i * 4, tap = k / Cpad, c0 = k - tap * Cpad;
-    uint32_t packed = 0;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int c = c0 + e;
-      const int8_t v = c < Cin ? w[((long long)tap * Cin + c) * Cout + n] : (int8_t)0;
-      sum += v;
-      packed |= (uint32_t)(uint8_t)v << (8 * e);
-    }
-    row[i] = packed;
-  }
-  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sum;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    int t = 0;
-    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t += red[i];
-    Sw[n] = t;
-  }
+  wprep_channel(w, taps, Cin, Cout, Cpad, blockIdx.x, dst, Sw);
 }
 
 // 64-byte K blocks when they cut the channel padding (Cin mod 128 in 1..64), else 128
@@ -461,7 +519,7 @@ struct Int8ConvArgs {
   const float* xf = nullptr;
   const uint8_t* xq = nullptr;
   int qmode = 0;
-  const Int8Scalars* s = nullptr;
+  Int8Derive dv;       // per-call scalars derived in the quantiser (else inv_host)
   float inv_host = 0.0f;
   Epi epi = Epi::F32_AB;
   const float* f0 = nullptr;  // alpha | wso
@@ -530,18 +588,21 @@ static bool int8_conv_gemm(Call& c, const Int8ConvArgs& a, int N, int H, int W, 
     if (!A || !B) return false;
     if (a.xf && rows * (Cpad / 16) < (1LL << 31)) {
       const long long g16 = rows * (Cpad / 16);
+      // one resident wave when every block first derives the scalars from partial maxima
+      int gq = grid_n(c, g16);
+      if (a.dv.part && gq > 8 * c.sm_count()) gq = 8 * c.sm_count();
       const int vec_in = (Cin % 4 == 0) && aligned16(a.xf);
       if (a.qmode == 0)
-        k_quant_pad_u8_16<0><<<grid_n(c, g16), 256, 0, c.stream()>>>(
-            a.xf, H, W, Cin, pad, Hp, Wp, Cpad / 16, (unsigned)g16, vec_in, a.s, a.inv_host,
+        k_quant_pad_u8_16<0><<<gq, 256, 0, c.stream()>>>(
+            a.xf, H, W, Cin, pad, Hp, Wp, Cpad / 16, (unsigned)g16, vec_in, a.dv, a.inv_host,
             a.img_inv, (uint4*)A);
       else
-        k_quant_pad_u8_16<1><<<grid_n(c, g16), 256, 0, c.stream()>>>(
-            a.xf, H, W, Cin, pad, Hp, Wp, Cpad / 16, (unsigned)g16, vec_in, a.s, a.inv_host,
+        k_quant_pad_u8_16<1><<<gq, 256, 0, c.stream()>>>(
+            a.xf, H, W, Cin, pad, Hp, Wp, Cpad / 16, (unsigned)g16, vec_in, a.dv, a.inv_host,
             a.img_inv, (uint4*)A);
     } else if (a.xf)
       k_quant_pad_u8<<<grid_n(c, rows * Cpad), 256, 0, c.stream()>>>(
-          a.xf, N, H, W, Cin, pad, Hp, Wp, Cpad, a.s, a.inv_host, a.img_inv, a.qmode, A);
+          a.xf, N, H, W, Cin, pad, Hp, Wp, Cpad, a.dv, a.inv_host, a.img_inv, a.qmode, A);
     else
       k_pad_u8<<<grid_n(c, rows * Cpad), 256, 0, c.stream()>>>(a.xq, N, H, W, Cin, pad, Hp, Wp,
                                                                Cpad, A);
@@ -549,6 +610,14 @@ static bool int8_conv_gemm(Call& c, const Int8ConvArgs& a, int N, int H, int W, 
       k_weights_s8k<<<grid_n(c, (long long)Cout * taps * Cpad / 4), 256, 0, c.stream()>>>(
           wq, taps, Cin, Cout, Cpad, B);
     if (!c.launched("int8 implicit prep")) return false;
+    // narrow convolutions: resident weights, one staged slab of input rows per tile
+    static const bool halo_on = [] {
+      const char* e = getenv("ACFUN_CONV_HALO");
+      return !(e && !strcmp(e, "0"));
+    }();
+    if (halo_on && !pool && rows < (1LL << 31) - 4096 &&
+        conv_halo_i8_ok(Cpad, KH, KW, Cout, stride, Wp))
+      return conv_halo_i8_dev(c, a.epi, A, B, N, Hp, Wp, KH, KW, OH, OW, Cout, ep);
     Operand Ao, Bo;
     Ao.p = A;
     Ao.ld = Cpad;
@@ -589,13 +658,13 @@ static bool int8_conv_gemm(Call& c, const Int8ConvArgs& a, int N, int H, int W, 
       const unsigned n4 = (unsigned)(nel / 4), per = (unsigned)((long long)H * W * Cin);
       if (a.qmode == 0)
         k_quant_u8_flat4<0><<<grid_n(c, n4), 256, 0, c.stream()>>>(
-            (const float4*)a.xf, n4, Cin, per, a.s, a.inv_host, a.img_inv, (uint32_t*)xq_dense);
+            (const float4*)a.xf, n4, Cin, per, a.dv, a.inv_host, a.img_inv, (uint32_t*)xq_dense);
       else
         k_quant_u8_flat4<1><<<grid_n(c, n4), 256, 0, c.stream()>>>(
-            (const float4*)a.xf, n4, Cin, per, a.s, a.inv_host, a.img_inv, (uint32_t*)xq_dense);
+            (const float4*)a.xf, n4, Cin, per, a.dv, a.inv_host, a.img_inv, (uint32_t*)xq_dense);
     } else {
       k_quant_pad_u8<<<grid_n(c, nel), 256, 0, c.stream()>>>(
-          a.xf, N, H, W, Cin, 0, H, W, Cin, a.s, a.inv_host, a.img_inv, a.qmode, xq_dense);
+          a.xf, N, H, W, Cin, 0, H, W, Cin, a.dv, a.inv_host, a.img_inv, a.qmode, xq_dense);
     }
     src = xq_dense;
   }
@@ -632,26 +701,32 @@ static bool is_wino_route(int H, int W, int Cin, int KH, int KW, int Cout, int s
 bool conv2d_int8_dev(Call& c, const float* x, int N, int H, int W, int Cin, const int8_t* wq,
                      const float* wscale, const float* bias, int KH, int KW, int Cout, int stride,
                      int pad, float* out, int act) {
-  // 4 launches: weights -> K-major + Sw (+ clear scalars); max|x| whose last block derives
-  // inv_s / sa / per-channel factors; quantise + pad; the integer GEMM with its epilogue.
+  // 3 launches: weights -> K-major + Sw next to the partial maxima of |x|; quantise + pad
+  // (every block derives inv_s from the partials, block 0 also sa and the per-channel
+  // factors); the integer GEMM with its epilogue.
   const Int8BLayout lay = int8_b_layout(Cin, KH, KW, stride);
+  const long long n = (long long)N * H * W * Cin;
+  long long np = (n / 4 + 511) / 512;
+  const long long np_cap = 2LL * c.sm_count();
+  np = np < 1 ? 1 : (np > np_cap ? np_cap : np);
   Int8Scalars* s = (Int8Scalars*)c.scratch(sizeof(Int8Scalars));
+  float* part = (float*)c.scratch((size_t)np * 4);
   float* f0 = (float*)c.scratch((size_t)Cout * 4);
   float* f1 = (float*)c.scratch((size_t)Cout * 4);
   int* Sw = (int*)c.scratch((size_t)Cout * 4);
   int8_t* wk = (int8_t*)c.scratch((size_t)Cout * lay.taps * lay.cpad);
-  if (!s || !f0 || !f1 || !Sw || !wk) return false;
-  k_int8_wprep<<<Cout, 128, 0, c.stream()>>>(wq, lay.taps, lay.cin, Cout, lay.cpad, wk, Sw,
-                                              &s->maxa_bits, 2);
-  const bool wino = is_wino_route(H, W, Cin, KH, KW, Cout, stride, pad);
-  // Winograd: f0 = wso, f1 = bias (or NULL); others: f0 = alpha, f1 = beta
-  const Int8ColArgs ca{wscale, bias, Sw, Cout, wino ? 1 : 0, f0, f1};
-  const long long n = (long long)N * H * W * Cin;
-  k_absmax<<<grid_n(c, n / 4 + 1), 256, 0, c.stream()>>>(x, n, s, ca);
+  if (!s || !part || !f0 || !f1 || !Sw || !wk) return false;
+  k_int8_prep_absmax<<<(unsigned)(Cout + np), 512, 0, c.stream()>>>(
+      wq, lay.taps, lay.cin, Cout, lay.cpad, wk, Sw, x, n, part, (int)np);
   if (!c.launched("int8 params")) return false;
+  const bool wino = is_wino_route(H, W, Cin, KH, KW, Cout, stride, pad);
   Int8ConvArgs a;
   a.xf = x;
-  a.s = s;
+  // Winograd: f0 = wso, f1 = bias (or NULL); others: f0 = alpha, f1 = beta
+  a.dv.part = part;
+  a.dv.nparts = (int)np;
+  a.dv.s = s;
+  a.dv.ca = Int8ColArgs{wscale, bias, Sw, Cout, wino ? 1 : 0, f0, f1};
   a.zero_flag = &s->zero;
   if (wino) {
     a.qmode = 1;
@@ -1053,6 +1128,12 @@ bool conv_int8_pool_dev(Call& c, const float* x, int N, int H, int W, int Cin, c
   bx = bx < 1 ? 1 : (bx > 64 ? 64 : bx);
   k_absmax_img<<<dim3((unsigned)bx, (unsigned)N), 256, 0, c.stream()>>>(
       x, per, words, words + N, inv, sa, zero, wscale, bias, Sw, Cout, ab, in_max);
+  if (conv_i8_pool_tc_ok(x, W, Cin, KH, KW, Cout, stride, PW)) {
+    *handled = true;
+    if (!c.launched("int8 pool params")) return false;
+    return conv_i8_pool_tc_dev(c, x, N, H, W, Cin, wq, KH, KW, Cout, pad, PH, PW, ab, inv, zero, out,
+                               act, post_relu, out_max);
+  }
 #define ACF_I8POOL(CWV)                                                                        \
   k_conv_int8_pool<CWV><<<N * PH, 128, (size_t)smem, c.stream()>>>(                            \
       x, H, W, Cin, wpk, ab, Cout, KH, KW, stride, pad, PH, PW, inv, zero, out, act, post_relu,  \
@@ -1194,7 +1275,7 @@ extern "C" void acfun_winograd_conv3x3_int8(const float* input, int N, int H, in
   int* Sw = (int*)c.scratch((size_t)Cout * 4);
   if (!c.ok()) return;
   k_int8_colparams<<<(Cout * 32 + 255) / 256, 256, 0, c.stream()>>>(
-      dw, 9 * Cin, Cout, ds, db, nullptr, s_in, nullptr, nullptr, wso, Sw);
+      dw, 9 * Cin, Cout, ds, db, s_in, nullptr, nullptr, wso, Sw);
   if (!c.launched("int8 params")) return;
   Int8ConvArgs a;
   a.xf = dx;

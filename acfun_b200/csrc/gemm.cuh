@@ -79,4 +79,9 @@ void tune_force(int v);  // tuner only; -1 ends it
 bool gemm_launch_i8k(Call& c, Epi epi, const Operand& A, const Operand& B, int M, int N, int K,
                      const EpiParams& ep, const ConvGeom& cg, int bkb);
 
+// Narrow stride-1 int8 convolutions (conv_halo_i8.cu): A = the zero-point-padded u8 grid
+// [N*Hp*Wp][64], wk = K-major s8 weights [Cout][KH*KW*64]; F32_AB or I8_WINO epilogue.
+bool conv_halo_i8_ok(int Cpad, int KH, int KW, int Cout, int stride, int Wp);
+bool conv_halo_i8_dev(Call& c, Epi epi, const uint8_t* A, const int8_t* wk, int N, int Hp, int Wp,
+                      int KH, int KW, int OH, int OW, int Cout, const EpiParams& ep);
 }  // namespace acf

@@ -97,12 +97,18 @@ def test_conv_int8_golden_exact(acf, name):
     ("c200_o300", 1, 10, 11, 200, 3, 3, 300, 1, 1, 0),
     ("im2col_k224_o70", 1, 9, 9, 24, 3, 3, 70, 2, 1, 1),
     ("wide_m_o200", 8, 40, 40, 64, 3, 3, 200, 1, 1, 1),
-    # narrow stride-1 convs through the fused kernel (in-kernel weights / quantisation): the
-    # Winograd route with tail channels, the direct route (pad 0), 1x1 and 1x3
+    # narrow stride-1 convs (<= 64 input, <= 128 output channels) through the resident-weight
+    # kernel that stages one slab of input rows per tile: the Winograd route with tail
+    # channels, the direct route (pad 0), 1x1 and 1x3, 128-wide tiles, slabs of three boxes
+    # (wide rows), many images per tile, 25 resident taps
     ("h8_c20_tail", 2, 15, 17, 20, 3, 3, 24, 1, 1, 1),
     ("h8_pad0", 2, 12, 11, 48, 3, 3, 40, 1, 0, 1),
     ("h8_1x1", 2, 20, 20, 64, 1, 1, 48, 1, 0, 0),
     ("h8_k1x3", 2, 9, 30, 40, 1, 3, 33, 1, 0, 1),
+    ("h8_o128", 2, 14, 13, 64, 3, 3, 128, 1, 1, 1),
+    ("h8_o96_wide_rows", 1, 9, 100, 32, 3, 3, 96, 1, 1, 0),
+    ("h8_many_images", 5, 7, 6, 16, 3, 3, 8, 1, 1, 1),
+    ("h8_k5p2", 1, 20, 20, 16, 5, 5, 40, 1, 2, 1),
 ])
 def test_conv_int8_vs_oracle_exact(acf, orc, cfg):
     tag, N, H, W, Cin, KH, KW, Cout, st, pd, act = cfg

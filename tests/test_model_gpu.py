@@ -159,6 +159,65 @@ def test_model_int8_conv_pool_fusion_bit_exact(acf, tmp_path, st, post_relu, cin
     m.close()
 
 
+@pytest.mark.parametrize("cin,k,cout,hw,relu", [(3, 3, 64, (70, 100), True), (3, 3, 48, (33, 65), False),
+                                               (4, 2, 16, (18, 40), True), (1, 3, 32, (64, 64), True)])
+def test_model_int8_conv_pool_tensor_route_bit_exact(acf, tmp_path, cin, k, cout, hw, relu):
+    """int8 mode, small-K stride-1 Conv -> MaxPool(2,2,0) on the tensor-core kernel (K =
+    k*k*cin <= 32, tiles of 2 x 16 pooled pixels: ragged last tiles in both directions, several
+    tiles per image, Cout 16..64), bit for bit against the oracle, with the per-image maxima the
+    next int8 layer would use checked through a second conv."""
+    from acfun_b200.acfun0 import Acfun0Writer, bn_params
+    from oracle.model_oracle import OracleModel
+    g = np.random.default_rng(cin * 100 + k * 10 + cout)
+    H, W = hw
+    Wr = Acfun0Writer(cin, H, W)
+    Wr.conv(g.uniform(-0.3, 0.3, (k * k * cin, cout)).astype(np.float32),
+            g.uniform(-0.1, 0.1, cout).astype(np.float32), k, k, cout, 1, 1).bn(*bn_params(g, cout))
+    if relu:
+        Wr.relu()
+    Wr.maxpool(2, 2, 0)
+    Wr.conv(g.uniform(-0.1, 0.1, (9 * cout, 24)).astype(np.float32), np.zeros(24, np.float32),
+            3, 3, 24, 1, 1)
+    blob = Wr.tobytes()
+    p = tmp_path / "cp8tc.acfun"
+    p.write_bytes(blob)
+    m = acf.Model(str(p))
+    m.set_int8(True)
+    x = np.random.default_rng(11).uniform(-1, 1, (3, H, W, cin)).astype(np.float32)
+    x[1] *= 40.0
+    y = m.infer_batch(x)
+    om = OracleModel(blob)
+    for i in range(3):
+        assert_bits_equal(y[i], om.infer(x[i], int8=True), f"image {i}")
+    m.close()
+
+
+def test_model_int8_conv_pool_tensor_route_exact_slow_channel(acf, tmp_path):
+    """A channel with all-zero weights and zero bias (alpha = 0, beta = 0, no ReLU) sends every
+    tile of the tensor-core conv + pool kernel through its exact per-pixel path; bit for bit."""
+    from acfun_b200.acfun0 import Acfun0Writer
+    from oracle.model_oracle import OracleModel
+    g = np.random.default_rng(77)
+    w = g.uniform(-0.3, 0.3, (27, 64)).astype(np.float32)
+    b = g.uniform(-0.1, 0.1, 64).astype(np.float32)
+    w[:, 5] = 0.0
+    b[5] = 0.0
+    Wr = Acfun0Writer(3, 30, 50)
+    Wr.conv(w, b, 3, 3, 64, 1, 1)
+    Wr.maxpool(2, 2, 0)
+    blob = Wr.tobytes()
+    p = tmp_path / "cp8slow.acfun"
+    p.write_bytes(blob)
+    m = acf.Model(str(p))
+    m.set_int8(True)
+    x = np.random.default_rng(12).uniform(-1, 1, (2, 30, 50, 3)).astype(np.float32)
+    y = m.infer_batch(x)
+    om = OracleModel(blob)
+    for i in range(2):
+        assert_bits_equal(y[i], om.infer(x[i], int8=True), f"image {i}")
+    m.close()
+
+
 @pytest.mark.parametrize("hw", [(224, 224), (37, 29)])
 def test_fused_conv1_pool_bit_exact_vs_separate_calls(acf, tmp_path, hw):
     """The fused CUDA-core 3x3 / Cin 3 conv + 2x2 pool kernel (packed f32x2 FMAs; the route
