@@ -783,6 +783,10 @@ static bool conv_simt(Call& c, const float* x, int N, int H, int W, int Cs, int 
   *handled = true;
   const int vec_in = (Cs % 4 == 0) && (coff % 4 == 0) && aligned16(x);
   const int vec_out = (Cout % 4 == 0) && (ldc % 4 == 0) && aligned16(out);
+  // 1x1 stride 1 over enough pixels to fill the GPU: tensor cores (3xBF16), one read of x
+  if (KH == 1 && KW == 1 && pad == 0 && stride == 1 && fp32_math(Fp32Use::Conv) == Fp32Math::BF16X3 &&
+      conv_pw_tc_ok(x, Cs, coff, Cg, Cout, M))
+    return conv_pw_tc_dev(c, x, M, Cg, w, ldw, bias, Cout, out, ldc, act);
   if (KH == 1 && KW == 1 && pad == 0 && vec_in && vec_out && Cg % 4 == 0 && Cout % 4 == 0 &&
       (NB == 24 || NB == 64)) {
     // 1x1: pixel-tiled kernel (4 pixels per thread)

@@ -20,6 +20,11 @@ enum ConvRoute {
 // Narrow stride-1 fp32 convolution (Cin, Cout <= 64, KH*KW <= 9) as one 3xBF16 tcgen05 kernel
 // with resident weights and in-kernel operand conversion (conv_halo.cu).
 bool conv_halo_ok(int Cin, int KH, int KW, int Cout, int stride);
+// 1x1 stride-1 fp32 convolution (Cin <= 192, a multiple of 4; Cout <= 64) on tensor cores in
+// 3xBF16 (conv_pw_tc.cu); x is [M][Cin] contiguous.
+bool conv_pw_tc_ok(const float* x, int Cs, int coff, int Cin, int Cout, long long M);
+bool conv_pw_tc_dev(Call& c, const float* x, long long M, int Cin, const float* w, long long ldw,
+                    const float* bias, int Cout, float* out, long long ldc, int act);
 // Small-K int8 convolution + 2x2/2 max-pool on tensor cores (conv_i8_pool_tc.cu): per-image
 // scales (ab = [N][2][Cout] alpha / beta, img_inv, img_zero from k_absmax_img).
 bool conv_i8_pool_tc_ok(const float* x, int W, int Cin, int KH, int KW, int Cout, int stride, int PW);

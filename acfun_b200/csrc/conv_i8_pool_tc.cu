@@ -179,10 +179,20 @@ __global__ void __launch_bounds__(i8p::THREADS, 1)
     // ---------------- converters: group g (4 warps) takes the range's tiles g, g+2, ...
     const int cw = warp - 1, g = cw >> 2, ct = threadIdx.x - 32 - 128 * g;  // ct: A row (pooled pixel)
     // resident weights: B[j][k] = wq[k][j] (zero for k >= K and j >= Cout); [64][32] core matrices
-    for (int e = threadIdx.x - 32; e < 64 * MAXK; e += 32 * CONV_WARPS) {
-      const int j = e / MAXK, k = e % MAXK;
-      const int8_t v = (k < a.K && j < a.Cout) ? a.wq[k * a.Cout + j] : (int8_t)0;
-      sB[(j >> 3) * 256 + (k >> 4) * 128 + (j & 7) * 16 + (k & 15)] = (uint8_t)v;
+    {
+      // all of a thread's weight loads in flight at once (one load latency, not eight)
+      constexpr int WU = 64 * MAXK / (32 * CONV_WARPS);
+      int8_t v[WU];
+#pragma unroll
+      for (int u = 0; u < WU; ++u) {
+        const int e = threadIdx.x - 32 + u * 32 * CONV_WARPS, j = e / MAXK, k = e % MAXK;
+        v[u] = (k < a.K && j < a.Cout) ? a.wq[k * a.Cout + j] : (int8_t)0;
+      }
+#pragma unroll
+      for (int u = 0; u < WU; ++u) {
+        const int e = threadIdx.x - 32 + u * 32 * CONV_WARPS, j = e / MAXK, k = e % MAXK;
+        sB[(j >> 3) * 256 + (k >> 4) * 128 + (j & 7) * 16 + (k & 15)] = (uint8_t)v[u];
+      }
     }
     dev::fence_proxy_async_smem();
     __syncwarp();

@@ -50,12 +50,17 @@ def he(g, shape, fan_in):
     ("odd", 3, 17, 23, 40, 3, 3, 72, 1, 1),
     ("k5s2", 2, 19, 21, 12, 5, 5, 20, 2, 2),
     ("pw_c40", 4, 20, 22, 72, 1, 1, 40, 1, 0),         # CUDA-core route, 48-wide accumulators
-    # narrow stride-1 convs (<= 64 -> <= 64 channels): the resident-weight kernel with in-kernel
-    # conversion; channel counts off the vector width, pad 0, many images
+    # narrow stride-1 convs (<= 64 -> <= 64 channels): the split pass + resident-weight slab
+    # kernel; channel counts off the vector width, pad 0, many images
     ("halo_c20_o24", 3, 15, 17, 20, 3, 3, 24, 1, 1),
     ("halo_c48_o40_p0", 2, 12, 11, 48, 3, 3, 40, 1, 0),
     ("halo_c16_o64", 5, 40, 37, 16, 3, 3, 64, 1, 1),
     ("halo_k1x5", 2, 9, 30, 40, 1, 5, 33, 1, 2),
+    # 1x1 stride 1 over >= 148 * 128 pixels: the tensor-core pointwise kernel (ragged last tile,
+    # a partial K block, 1..3 K blocks, Cout padded to 16 / 48 / 64)
+    ("pwtc_c100_o40", 7, 57, 51, 100, 1, 1, 40, 1, 0),
+    ("pwtc_c192_o64", 6, 60, 60, 192, 1, 1, 64, 1, 0),
+    ("pwtc_c12_o8", 5, 66, 61, 12, 1, 1, 8, 1, 0),
 ])
 def test_conv_f32_configs_vs_oracle(acf, orc, cfg):
     tag, N, H, W, Cin, KH, KW, Cout, st, pd = cfg
