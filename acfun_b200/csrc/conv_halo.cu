@@ -7,7 +7,9 @@
 // per row; output pixel (oh, ow) of image n is row r = (n*Hp + oh)*Wp + ow, and tap (kh, kw)
 // reads row r + kh*Wp + kw.  A tile is 128 consecutive rows x 64 output channels.
 //   * k_halo_split writes the padded grid once as bf16 hi / lo planes ([2][rows][64], zero in
-//     the border and past the channels), a bandwidth pass whose output stays in L2.
+//     the border and past the channels), a bandwidth pass whose output stays in L2, and the
+//     split weights; the conv kernel is launched as its programmatic dependent, so its prologue
+//     (barriers, tensor memory) overlaps the pass.
 //   * The split weights of every tap ([2][taps][64 channels][64 columns] bf16 hi / lo, 16 KB a
 //     tap) are loaded by TMA once per CTA and stay resident in shared memory.
 //   * For each kernel row kh one TMA box brings the tile's 128 + KW - 1 rows of both planes
@@ -56,25 +58,24 @@ struct HaloArgs {
   int act, OH, OW, Cout;
 };
 
-// split weights: w [taps*Cin][Cout] (row stride ldw) -> [2][taps*64][64] bf16 hi / lo, zero for
-// channels >= Cin and columns >= Cout
-__global__ void k_halo_wsplit(const float* __restrict__ w, int taps, int Cin, int Cout, long long ldw,
-                              uint16_t* __restrict__ dst) {
-  const int total = taps * halo::CP * halo::BN;
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
-    const int j = i % halo::BN, r = i / halo::BN, tap = r / halo::CP, ch = r % halo::CP;
-    const float v = (ch < Cin && j < Cout) ? w[((long long)tap * Cin + ch) * ldw + j] : 0.0f;
-    nx_store_split1<true>(dst, (size_t)i, (size_t)total, v);
-  }
-}
-
 // x: NHWC (channel stride Cs, channels [coff, coff + Cin)) -> [2][rows][64] bf16 hi / lo planes of
 // the zero-padded grid; one thread per (grid row, 8 channels): two 16-byte loads, one 16-byte
 // store per plane.
+// The same launch splits the weights: w [taps*Cin][Cout] (row stride ldw) -> [2][taps*64][64] bf16
+// hi / lo, zero for channels >= Cin and columns >= Cout.
 template <bool VEC>
 __global__ void k_halo_split(const float* __restrict__ x, int H, int W, int Cs, int coff, int Cin,
                              int pad, int Wp, unsigned img_rows, unsigned total,
-                             uint4* __restrict__ dst, unsigned plane16) {
+                             uint4* __restrict__ dst, unsigned plane16,
+                             const float* __restrict__ w, int taps, int Cout, long long ldw,
+                             uint16_t* __restrict__ wdst) {
+  dev::grid_dep_launch();  // the conv kernel may start its prologue now
+  const int wtotal = taps * halo::CP * halo::BN;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < wtotal; i += gridDim.x * blockDim.x) {
+    const int j = i % halo::BN, r = i / halo::BN, tap = r / halo::CP, ch = r % halo::CP;
+    const float v = (ch < Cin && j < Cout) ? w[((long long)tap * Cin + ch) * ldw + j] : 0.0f;
+    nx_store_split1<true>(wdst, (size_t)i, (size_t)wtotal, v);
+  }
   for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
     const unsigned g = i >> 3, c8 = (i & 7) * 8;
     const unsigned n = g / img_rows, q = g - n * img_rows;
@@ -147,11 +148,13 @@ __global__ void __launch_bounds__(halo::THREADS, 1)
     dev::tma_prefetch_desc(&tmA);
     dev::tma_prefetch_desc(&tmB);
   }
-  if (threadIdx.x < BN) sbias[threadIdx.x] = (bias && (int)threadIdx.x < a.Cout) ? bias[threadIdx.x] : 0.0f;
   if (warp == 1) {
     dev::tmem_alloc(tmem_slot, 512);
     dev::tmem_relinquish();
   }
+  // the prologue above may overlap the split pass; nothing it produced is read before this
+  dev::grid_dep_wait();
+  if (threadIdx.x < BN) sbias[threadIdx.x] = (bias && (int)threadIdx.x < a.Cout) ? bias[threadIdx.x] : 0.0f;
   dev::tc_fence_before();
   __syncthreads();
   dev::tc_fence_after();
@@ -312,18 +315,18 @@ bool conv_halo_f32_dev(Call& c, const float* x, int N, int H, int W, int Cs, int
   uint16_t* ws = static_cast<uint16_t*>(c.scratch((size_t)2 * taps * halo::CP * halo::BN * 2));
   uint4* xs = static_cast<uint4*>(c.scratch((size_t)2 * rows * halo::CP * 2));
   if (!ws || !xs) return false;
-  k_halo_wsplit<<<(taps * halo::CP * halo::BN + 255) / 256, 256, 0, c.stream()>>>(w, taps, Cin, Cout,
-                                                                                  ldw, ws);
   const unsigned total = (unsigned)(rows * 8);
   const bool vec = Cin % 4 == 0 && Cs % 4 == 0 && coff % 4 == 0 && aligned16(x);
   long long gb = (total + 255) / 256, cap = (long long)c.sm_count() * 8;
   const int grid_s = (int)(gb < cap ? gb : cap);
   if (vec)
     k_halo_split<true><<<grid_s, 256, 0, c.stream()>>>(x, H, W, Cs, coff, Cin, pad, Wp,
-                                                       (unsigned)(Hp * Wp), total, xs, total);
+                                                       (unsigned)(Hp * Wp), total, xs, total, w, taps,
+                                                       Cout, ldw, ws);
   else
     k_halo_split<false><<<grid_s, 256, 0, c.stream()>>>(x, H, W, Cs, coff, Cin, pad, Wp,
-                                                        (unsigned)(Hp * Wp), total, xs, total);
+                                                        (unsigned)(Hp * Wp), total, xs, total, w, taps,
+                                                        Cout, ldw, ws);
   if (!c.launched("conv halo prep")) return false;
   CUtensorMap ta, tb;
   {
@@ -370,7 +373,11 @@ bool conv_halo_f32_dev(Call& c, const float* x, int N, int H, int W, int Cs, int
     }
     attr_done[dv] = true;
   }
-  conv_halo_kernel<<<grid, halo::THREADS, halo::SMEM, c.stream()>>>(ta, tb, a, bias, tiles, c.err());
+  if (!ACF_CUDA_OK(launch_pdl(conv_halo_kernel, dim3(grid), dim3(halo::THREADS), halo::SMEM, c.stream(), ta,
+                              tb, a, bias, tiles, c.err()))) {
+    c.fail();
+    return false;
+  }
   return c.launched("conv_halo_kernel");
 }
 

@@ -101,6 +101,8 @@ __global__ void __launch_bounds__(h8::THREADS, 1)
     dev::tmem_alloc(tmem_slot, C::TMEM_COLS);
     dev::tmem_relinquish();
   }
+  // the prologue above may overlap the quantiser; nothing it produced is read before this
+  dev::grid_dep_wait();
   dev::tc_fence_before();
   __syncthreads();
   dev::tc_fence_after();
@@ -265,7 +267,11 @@ static bool launch_h8(Call& c, const CUtensorMap& ta, const CUtensorMap& tb, con
     attr_done[dv] = true;
   }
   const int grid = tiles < c.sm_count() ? tiles : c.sm_count();
-  kern<<<grid, h8::THREADS, smem, c.stream()>>>(ta, tb, ep, g, tiles, c.err());
+  if (!ACF_CUDA_OK(launch_pdl(kern, dim3(grid), dim3(h8::THREADS), (size_t)smem, c.stream(), ta, tb, ep, g,
+                              tiles, c.err()))) {
+    c.fail();
+    return false;
+  }
   return c.launched("conv_halo_i8_kernel");
 }
 

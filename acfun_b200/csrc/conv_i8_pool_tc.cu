@@ -133,6 +133,8 @@ __global__ void __launch_bounds__(i8p::THREADS, 1)
     dev::tmem_alloc(tmem_slot, NBUF * 256);
     dev::tmem_relinquish();
   }
+  // the prologue above may overlap the per-image scalar kernel; nothing it produced is read before this
+  dev::grid_dep_wait();
   dev::tc_fence_before();
   __syncthreads();
   dev::tc_fence_after();
@@ -510,7 +512,11 @@ bool conv_i8_pool_tc_dev(Call& c, const float* x, int N, int H, int W, int Cin, 
     attr_done[dv] = true;
   }
   const int grid = (int)std::min<long long>(tiles, c.sm_count());
-  k_conv_i8_pool_tc<<<grid, i8p::THREADS, i8p::SMEM, c.stream()>>>(tx, a, c.err());
+  if (!ACF_CUDA_OK(launch_pdl(k_conv_i8_pool_tc, dim3(grid), dim3(i8p::THREADS), (size_t)i8p::SMEM, c.stream(),
+                              tx, a, c.err()))) {
+    c.fail();
+    return false;
+  }
   return c.launched("k_conv_i8_pool_tc");
 }
 

@@ -149,6 +149,7 @@ __global__ void k_int8_prep_absmax(const int8_t* __restrict__ w, int taps, int C
                                    int Cpad, int8_t* __restrict__ wk, int* __restrict__ Sw,
                                    const float* __restrict__ x, long long n, float* __restrict__ part,
                                    int nparts) {
+  dev::grid_dep_launch();  // the quantiser may start its prologue now
   if ((int)blockIdx.x < Cout) {
     wprep_channel(w, taps, Cin, Cout, Cpad, blockIdx.x, wk, Sw);
     return;
@@ -343,6 +344,8 @@ __global__ void k_quant_pad_u8_16(const float* __restrict__ x, int H, int W, int
                                   int Hp, int Wp, int C16, unsigned total, int vec_in,
                                   Int8Derive dv, float inv_host,
                                   const float* __restrict__ img_inv, uint4* __restrict__ dst) {
+  dev::grid_dep_wait();    // launched as the dependent of the kernel producing x / the scalars
+  dev::grid_dep_launch();  // and the conv after it may start its prologue
   const float inv_all = quant_inv_all(dv, inv_host);
   const int cvec = Cin & ~15;
   for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
@@ -592,14 +595,16 @@ static bool int8_conv_gemm(Call& c, const Int8ConvArgs& a, int N, int H, int W, 
       int gq = grid_n(c, g16);
       if (a.dv.part && gq > 8 * c.sm_count()) gq = 8 * c.sm_count();
       const int vec_in = (Cin % 4 == 0) && aligned16(a.xf);
-      if (a.qmode == 0)
-        k_quant_pad_u8_16<0><<<gq, 256, 0, c.stream()>>>(
-            a.xf, H, W, Cin, pad, Hp, Wp, Cpad / 16, (unsigned)g16, vec_in, a.dv, a.inv_host,
-            a.img_inv, (uint4*)A);
-      else
-        k_quant_pad_u8_16<1><<<gq, 256, 0, c.stream()>>>(
-            a.xf, H, W, Cin, pad, Hp, Wp, Cpad / 16, (unsigned)g16, vec_in, a.dv, a.inv_host,
-            a.img_inv, (uint4*)A);
+      const cudaError_t e =
+          a.qmode == 0
+              ? launch_pdl(k_quant_pad_u8_16<0>, dim3(gq), dim3(256), 0, c.stream(), a.xf, H, W, Cin, pad,
+                           Hp, Wp, Cpad / 16, (unsigned)g16, vec_in, a.dv, a.inv_host, a.img_inv, (uint4*)A)
+              : launch_pdl(k_quant_pad_u8_16<1>, dim3(gq), dim3(256), 0, c.stream(), a.xf, H, W, Cin, pad,
+                           Hp, Wp, Cpad / 16, (unsigned)g16, vec_in, a.dv, a.inv_host, a.img_inv, (uint4*)A);
+      if (!ACF_CUDA_OK(e)) {
+        c.fail();
+        return false;
+      }
     } else if (a.xf)
       k_quant_pad_u8<<<grid_n(c, rows * Cpad), 256, 0, c.stream()>>>(
           a.xf, N, H, W, Cin, pad, Hp, Wp, Cpad, a.dv, a.inv_host, a.img_inv, a.qmode, A);
@@ -754,6 +759,7 @@ __global__ void k_absmax_img(const float* __restrict__ x, long long per_img, uns
                              const float* __restrict__ wscale, const float* __restrict__ bias,
                              const int* __restrict__ Sw, int Cout, float* __restrict__ ab,
                              const unsigned* __restrict__ preset) {
+  dev::grid_dep_launch();  // a programmatic dependent may start its prologue now
   __shared__ float sh[32];
   __shared__ int last;
   const int n = blockIdx.y;

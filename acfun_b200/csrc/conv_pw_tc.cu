@@ -100,11 +100,13 @@ __global__ void __launch_bounds__(pw::THREADS, 1)
     dev::fence_mbar_init();
     dev::tma_prefetch_desc(&tmX);
   }
-  if (threadIdx.x < MAXNP) sbias[threadIdx.x] = (a.bias && (int)threadIdx.x < a.Cout) ? a.bias[threadIdx.x] : 0.0f;
   if (warp == 1) {
     dev::tmem_alloc(tmem_slot, 512);
     dev::tmem_relinquish();
   }
+  // the prologue above may overlap the weight preparation; nothing it produced is read before this
+  dev::grid_dep_wait();
+  if (threadIdx.x < MAXNP) sbias[threadIdx.x] = (a.bias && (int)threadIdx.x < a.Cout) ? a.bias[threadIdx.x] : 0.0f;
   dev::tc_fence_before();
   __syncthreads();
   dev::tc_fence_after();
@@ -275,6 +277,7 @@ __global__ void __launch_bounds__(pw::THREADS, 1)
 // XOR-swizzled by (row & 7) as the tensor core's 128-byte K-major layout expects.
 __global__ void k_pw_wsplit(const float* __restrict__ w, long long ldw, int Cin, int Cout, int Np, int kb,
                             uint8_t* __restrict__ img) {
+  dev::grid_dep_launch();  // the conv kernel may start its prologue now
   const int rows = 2 * Np, total = kb * rows * pw::BKC;
   for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < total; e += gridDim.x * blockDim.x) {
     const int b = e / (rows * pw::BKC), rem = e - b * rows * pw::BKC;
@@ -333,7 +336,11 @@ bool conv_pw_tc_dev(Call& c, const float* x, long long M, int Cin, const float* 
     attr_done[dv] = true;
   }
   const int grid = std::min(a.num_tiles, c.sm_count());
-  conv_pw_tc_kernel<<<grid, pw::THREADS, smem, c.stream()>>>(tx, a, c.err());
+  if (!ACF_CUDA_OK(launch_pdl(conv_pw_tc_kernel, dim3(grid), dim3(pw::THREADS), (size_t)smem, c.stream(), tx, a,
+                              c.err()))) {
+    c.fail();
+    return false;
+  }
   return c.launched("conv_pw_tc_kernel");
 }
 

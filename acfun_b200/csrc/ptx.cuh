@@ -93,6 +93,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
   }
 }
 
+// ------------------------------------------------------------------ programmatic dependent launch
+// A kernel launched with launch_pdl (runtime.cuh) may start while the previous kernel in the
+// stream is still running; grid_dep_wait() returns once that kernel has completed and its
+// writes are visible.  Every such kernel calls it (all threads) before its first read of data a
+// predecessor produces and before its first global write, so completion stays transitive along
+// the stream.  grid_dep_launch() lets the next kernel start early; both are no-ops otherwise.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ------------------------------------------------------------------ TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");

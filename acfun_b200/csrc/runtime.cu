@@ -223,6 +223,14 @@ void* Call::inout(void* p, size_t bytes) {
   return d;
 }
 
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("ACFUN_PDL");
+    return !(e && !strcmp(e, "0"));
+  }();
+  return on;
+}
+
 bool Call::launched(const char* what) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {

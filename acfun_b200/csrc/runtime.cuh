@@ -9,6 +9,7 @@
 //    device-side error;
 //  * TMA tensor-map encoding through the driver entry point (no libcuda link dependency).
 #pragma once
+#include <utility>
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdarg.h>
@@ -140,6 +141,26 @@ bool check_device_error(DeviceState* d, cudaStream_t s);
 bool encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base,
                  const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
                  CUtensorMapSwizzle swz);
+
+// Launch `k` so that it may start while the previous kernel of `stream` finishes (programmatic
+// stream serialisation); the kernel must call dev::grid_dep_wait() before it reads what that
+// kernel produced or writes global memory.  ACFUN_PDL=0 launches normally.
+bool pdl_enabled();
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...);
+}
 
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
