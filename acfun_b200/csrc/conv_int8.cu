@@ -19,6 +19,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <algorithm>
 #include <vector>
 
 #include "api_export.cuh"
@@ -378,6 +379,41 @@ __global__ void k_quant_pad_u8_16(const float* __restrict__ x, int H, int W, int
   }
 }
 
+// k_quant_pad_u8_16 for 64-channel rows (Cin == Cpad == 64, 16-byte aligned input): a block walks
+// whole padded grid rows (n, hp), so the image / row arithmetic is done once per row and a thread
+// takes (pixel, 16-channel group) = (item >> 2, item & 3) of the row -- no per-item division.
+template <int MODE>
+__global__ void k_quant_pad_rows64(const float* __restrict__ x, int H, int W, int pad, int Hp, int Wp,
+                                   int nrows, Int8Derive dv, float inv_host,
+                                   const float* __restrict__ img_inv, uint4* __restrict__ dst) {
+  dev::grid_dep_wait();    // launched as the dependent of the kernel producing x / the scalars
+  dev::grid_dep_launch();  // and the conv after it may start its prologue
+  const float inv_all = quant_inv_all(dv, inv_host);
+  const int items = Wp * 4;
+  for (int row = blockIdx.x; row < nrows; row += gridDim.x) {
+    const int n = row / Hp, ih = row - n * Hp - pad;
+    const bool row_in = ih >= 0 && ih < H;
+    const float inv_s = img_inv ? img_inv[n] : inv_all;
+    const float* src_row = x + ((size_t)n * H + (row_in ? ih : 0)) * W * 64;
+    uint4* dst_row = dst + (size_t)row * items;
+    for (int it = threadIdx.x; it < items; it += blockDim.x) {
+      const int iw = (it >> 2) - pad, cg = it & 3;
+      uint32_t w[4] = {0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u};
+      if (row_in && iw >= 0 && iw < W) {
+        const float4* src = reinterpret_cast<const float4*>(src_row + (size_t)iw * 64 + cg * 16);
+        float4 q[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) q[k] = __ldg(src + k);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          w[k] = quant_fast<MODE>(q[k].x, inv_s) | (quant_fast<MODE>(q[k].y, inv_s) << 8) |
+                 (quant_fast<MODE>(q[k].z, inv_s) << 16) | (quant_fast<MODE>(q[k].w, inv_s) << 24);
+      }
+      dst_row[it] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+}
+
 // pre-quantised u8 NHWC -> padded [N*Hp*Wp][Cpad] (border = zero point)
 __global__ void k_pad_u8(const uint8_t* __restrict__ xq, int N, int H, int W, int Cin, int pad,
                          int Hp, int Wp, int Cpad, uint8_t* __restrict__ dst) {
@@ -595,8 +631,15 @@ static bool int8_conv_gemm(Call& c, const Int8ConvArgs& a, int N, int H, int W, 
       int gq = grid_n(c, g16);
       if (a.dv.part && gq > 8 * c.sm_count()) gq = 8 * c.sm_count();
       const int vec_in = (Cin % 4 == 0) && aligned16(a.xf);
+      const long long nrows = (long long)N * Hp;
+      const bool rows64 = Cin == 64 && Cpad == 64 && vec_in && a.dv.part && nrows < (1LL << 31);
+      const int gr = (int)std::min<long long>(nrows, 8LL * c.sm_count());
       const cudaError_t e =
-          a.qmode == 0
+          rows64 ? (a.qmode == 0 ? launch_pdl(k_quant_pad_rows64<0>, dim3(gr), dim3(256), 0, c.stream(), a.xf, H, W,
+                                              pad, Hp, Wp, (int)nrows, a.dv, a.inv_host, a.img_inv, (uint4*)A)
+                                 : launch_pdl(k_quant_pad_rows64<1>, dim3(gr), dim3(256), 0, c.stream(), a.xf, H, W,
+                                              pad, Hp, Wp, (int)nrows, a.dv, a.inv_host, a.img_inv, (uint4*)A))
+          : a.qmode == 0
               ? launch_pdl(k_quant_pad_u8_16<0>, dim3(gq), dim3(256), 0, c.stream(), a.xf, H, W, Cin, pad,
                            Hp, Wp, Cpad / 16, (unsigned)g16, vec_in, a.dv, a.inv_host, a.img_inv, (uint4*)A)
               : launch_pdl(k_quant_pad_u8_16<1>, dim3(gq), dim3(256), 0, c.stream(), a.xf, H, W, Cin, pad,
