@@ -246,6 +246,63 @@ __device__ __forceinline__ void amax_flush(unsigned* img_absmax, int n, float am
   }
 }
 
+// The float epilogues' values for 32 columns j0..j0+31 of one row (F32_AB, F32_BIAS, I8_WINO):
+// dequantisation / bias, act, the all-zero override; folds max |value| into am when the
+// per-image maximum is wanted.  epi_store32 stores them; kernels that stage rows in shared
+// memory call it directly.
+template <Epi EPI>
+__device__ __forceinline__ void epi_values32(const EpiParams& ep, int j0, int N, const uint32_t (&r)[32],
+                                             const ColSlice& P, bool zero, float img_sa, float& am,
+                                             float (&v)[32]) {
+  float p0[32], p1[32];
+  int32_t pi[32];
+  if constexpr (EPI == Epi::F32_AB) {
+    lds32(P.a, p0);
+    lds32(P.b, p1);
+    if (ep.img_sa) {
+      // alpha = sa*ws, beta = bias - (alpha*128)*Sw: k_int8_colparams's expressions
+      lds32(P.c, pi);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float a = __fmul_rn(img_sa, p0[i]);
+        p1[i] = __fsub_rn(p1[i], __fmul_rn(__fmul_rn(a, 128.0f), (float)pi[i]));
+        p0[i] = a;
+      }
+    }
+  } else if constexpr (EPI == Epi::F32_BIAS) {
+    lds32(P.a, p0);
+  } else {  // I8_WINO
+    lds32(P.a, p0);
+    lds32(P.b, p1);
+    lds32(P.c, pi);
+    if (ep.img_sa) {
+      // wso = (sa*0.25)*ws (winograd_int8.cpp:155)
+      const float q = __fmul_rn(img_sa, 0.25f);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) p0[i] = __fmul_rn(q, p0[i]);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    float x;
+    if constexpr (EPI == Epi::F32_AB) {
+      x = __fadd_rn(__fmul_rn(__int2float_rn((int32_t)r[i]), p0[i]), p1[i]);
+    } else if constexpr (EPI == Epi::F32_BIAS) {
+      x = __fadd_rn(__uint_as_float(r[i]), p0[i]);
+    } else {  // I8_WINO
+      const int32_t c = (int32_t)r[i] - 128 * pi[i];
+      x = __fmaf_rn(__fmul_rn(4.0f, __int2float_rn(c)), p0[i], p1[i]);
+    }
+    if (ep.act) x = relu_max(x);
+    v[i] = zero ? 0.0f : x;
+  }
+  if (ep.img_absmax) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (j0 + i < N) amax_acc(am, v[i]);
+  }
+}
+
 template <Epi EPI>
 __device__ __forceinline__ void epi_store32(const EpiParams& ep, long long orow, int j0, int N,
                                             const uint32_t (&r)[32], const ColSlice& P,
@@ -291,54 +348,8 @@ __device__ __forceinline__ void epi_store32(const EpiParams& ep, long long orow,
         if (j0 + i < N) dst[i] = (int8_t)((packed[i / 4] >> (8 * (i % 4))) & 0xFF);
     }
   } else {
-    float p0[32], p1[32];
-    int32_t pi[32];
-    if constexpr (EPI == Epi::F32_AB) {
-      lds32(P.a, p0);
-      lds32(P.b, p1);
-      if (ep.img_sa) {
-        // alpha = sa*ws, beta = bias - (alpha*128)*Sw: k_int8_colparams's expressions
-        lds32(P.c, pi);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float a = __fmul_rn(img_sa, p0[i]);
-          p1[i] = __fsub_rn(p1[i], __fmul_rn(__fmul_rn(a, 128.0f), (float)pi[i]));
-          p0[i] = a;
-        }
-      }
-    } else if constexpr (EPI == Epi::F32_BIAS) {
-      lds32(P.a, p0);
-    } else {  // I8_WINO
-      lds32(P.a, p0);
-      lds32(P.b, p1);
-      lds32(P.c, pi);
-      if (ep.img_sa) {
-        // wso = (sa*0.25)*ws (winograd_int8.cpp:155)
-        const float q = __fmul_rn(img_sa, 0.25f);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) p0[i] = __fmul_rn(q, p0[i]);
-      }
-    }
     float v[32];
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      float x;
-      if constexpr (EPI == Epi::F32_AB) {
-        x = __fadd_rn(__fmul_rn(__int2float_rn((int32_t)r[i]), p0[i]), p1[i]);
-      } else if constexpr (EPI == Epi::F32_BIAS) {
-        x = __fadd_rn(__uint_as_float(r[i]), p0[i]);
-      } else {  // I8_WINO
-        const int32_t c = (int32_t)r[i] - 128 * pi[i];
-        x = __fmaf_rn(__fmul_rn(4.0f, __int2float_rn(c)), p0[i], p1[i]);
-      }
-      if (ep.act) x = relu_max(x);
-      v[i] = zero ? 0.0f : x;
-    }
-    if (ep.img_absmax) {
-#pragma unroll
-      for (int i = 0; i < 32; ++i)
-        if (j0 + i < N) amax_acc(am, v[i]);
-    }
+    epi_values32<EPI>(ep, j0, N, r, P, zero, img_sa, am, v);
     if constexpr (EPI == Epi::F32_BIAS) {
       if (ep.split_out) {
         // hi = bf16(v), lo = bf16(v - hi): the split k_pad_split4 makes of an fp32 input
