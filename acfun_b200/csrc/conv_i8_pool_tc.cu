@@ -87,6 +87,7 @@ __device__ __forceinline__ uint8_t i8p_quant(float xv, float inv_s) {
   return (uint8_t)(v < 0 ? 0 : (v > 255 ? 255 : v));
 }
 
+template <bool ACT, bool POST>
 __global__ void __launch_bounds__(i8p::THREADS, 1)
     k_conv_i8_pool_tc(const __grid_constant__ CUtensorMap tmX, I8PoolArgs a, unsigned* err) {
   using namespace i8p;
@@ -346,6 +347,10 @@ __global__ void __launch_bounds__(i8p::THREADS, 1)
     };
     const int m = q * 32 + lane;
     const int pi = m / TPC, pj = m % TPC;
+    // per image: the all-zero flag and whether any of this warp's channels has a dequantisation
+    // that is not increasing (alpha <= 0 with beta == +-0 and no ReLU: the zeros' signs follow
+    // the sums', so such a channel pools its four dequantised values one by one)
+    bool zero = false, slow_any = false;
     uint32_t local = 0;
     for (int t = t_begin; t < t_end; ++t, ++local) {
       const uint32_t buf = local % NBUF, use = local / NBUF;
@@ -353,15 +358,19 @@ __global__ void __launch_bounds__(i8p::THREADS, 1)
       dev::tc_fence_after();
       if (!ok || *abort_flag) break;
       const int n = t / tiles_img, rem = t - n * tiles_img;
+      const float* abn = a.ab + (size_t)n * 2 * a.Cout;
       if (n != n_run) {  // warp-uniform
         flush();
         n_run = n;
+        zero = a.img_zero[n] != 0;
+        bool sl = false;
+        if (!ACT && 32 * h + lane < a.Cout)
+          sl = !(abn[32 * h + lane] > 0.0f) && abn[a.Cout + 32 * h + lane] == 0.0f;
+        slow_any = __any_sync(0xffffffffu, sl);
       }
       const int pr = rem / a.segs, sg = rem - pr * a.segs;
       const int ph = TPR * pr + pi, pw = TPC * sg + pj;
       const bool store = ph < a.PH && pw < a.PW;
-      const float* abn = a.ab + (size_t)n * 2 * a.Cout;
-      const bool zero = a.img_zero[n] != 0;
       float* dst = a.out + (((size_t)n * a.PH + ph) * a.PW + pw) * a.Cout;
       const uint32_t tl = tmem + buf * 256 + ((uint32_t)(q * 32) << 16);
 #pragma unroll 1
@@ -373,59 +382,54 @@ __global__ void __launch_bounds__(i8p::THREADS, 1)
         dev::tmem_ld8(tl + 128 + c0, v2);
         dev::tmem_ld8(tl + 192 + c0, v3);
         dev::tmem_ld_wait();
-        float al[8], be[8];
-        {
-          const float4 a0 = __ldg(reinterpret_cast<const float4*>(abn + c0));
-          const float4 a1 = __ldg(reinterpret_cast<const float4*>(abn + c0 + 4));
-          const float4 b0 = __ldg(reinterpret_cast<const float4*>(abn + a.Cout + c0));
-          const float4 b1 = __ldg(reinterpret_cast<const float4*>(abn + a.Cout + c0 + 4));
-          al[0] = a0.x; al[1] = a0.y; al[2] = a0.z; al[3] = a0.w;
-          al[4] = a1.x; al[5] = a1.y; al[6] = a1.z; al[7] = a1.w;
-          be[0] = b0.x; be[1] = b0.y; be[2] = b0.z; be[3] = b0.w;
-          be[4] = b1.x; be[5] = b1.y; be[6] = b1.z; be[7] = b1.w;
-        }
-        // (float)acc*alpha + beta is non-decreasing in acc unless alpha <= 0 with beta == +-0
-        // and no ReLU (the zeros' signs then follow the sums'): such a chunk pools the four
-        // dequantised values one by one in the window order
-        bool slow = false;
-        if (!a.act) {
-#pragma unroll
-          for (int j = 0; j < 8; ++j) slow |= !(al[j] > 0.0f) && be[j] == 0.0f;
-        }
         float y[8];
-        if (!slow) {
+        if (zero) {
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const int mx = max(max((int)v0[j], (int)v1[j]), max((int)v2[j], (int)v3[j]));
-            float r = __fadd_rn(__fmul_rn(__int2float_rn(mx), al[j]), be[j]);
-            if (a.act) r = r > 0.0f ? r : 0.0f;
-            y[j] = r;
-          }
+          for (int j = 0; j < 8; ++j) y[j] = 0.0f;
         } else {
+          float al[8], be[8];
+          {
+            const float4 a0 = __ldg(reinterpret_cast<const float4*>(abn + c0));
+            const float4 a1 = __ldg(reinterpret_cast<const float4*>(abn + c0 + 4));
+            const float4 b0 = __ldg(reinterpret_cast<const float4*>(abn + a.Cout + c0));
+            const float4 b1 = __ldg(reinterpret_cast<const float4*>(abn + a.Cout + c0 + 4));
+            al[0] = a0.x; al[1] = a0.y; al[2] = a0.z; al[3] = a0.w;
+            al[4] = a1.x; al[5] = a1.y; al[6] = a1.z; al[7] = a1.w;
+            be[0] = b0.x; be[1] = b0.y; be[2] = b0.z; be[3] = b0.w;
+            be[4] = b1.x; be[5] = b1.y; be[6] = b1.z; be[7] = b1.w;
+          }
+          if (!slow_any) {
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            float r;
-            if (a.act || al[j] > 0.0f || be[j] != 0.0f) {
+            for (int j = 0; j < 8; ++j) {
               const int mx = max(max((int)v0[j], (int)v1[j]), max((int)v2[j], (int)v3[j]));
-              r = __fadd_rn(__fmul_rn(__int2float_rn(mx), al[j]), be[j]);
-              if (a.act) r = r > 0.0f ? r : 0.0f;
-            } else {
-              const int vv[4] = {(int)v0[j], (int)v1[j], (int)v2[j], (int)v3[j]};
-              r = -1e30f;
-#pragma unroll
-              for (int pp = 0; pp < 4; ++pp) {
-                const float uu = __fadd_rn(__fmul_rn(__int2float_rn(vv[pp]), al[j]), be[j]);
-                r = r > uu ? r : uu;
-              }
+              float r = __fadd_rn(__fmul_rn(__int2float_rn(mx), al[j]), be[j]);
+              if (ACT) r = r > 0.0f ? r : 0.0f;
+              y[j] = r;
             }
-            y[j] = r;
+          } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              float r;
+              if (ACT || al[j] > 0.0f || be[j] != 0.0f) {
+                const int mx = max(max((int)v0[j], (int)v1[j]), max((int)v2[j], (int)v3[j]));
+                r = __fadd_rn(__fmul_rn(__int2float_rn(mx), al[j]), be[j]);
+                if (ACT) r = r > 0.0f ? r : 0.0f;
+              } else {
+                const int vv[4] = {(int)v0[j], (int)v1[j], (int)v2[j], (int)v3[j]};
+                r = -1e30f;
+#pragma unroll
+                for (int pp = 0; pp < 4; ++pp) {
+                  const float uu = __fadd_rn(__fmul_rn(__int2float_rn(vv[pp]), al[j]), be[j]);
+                  r = r > uu ? r : uu;
+                }
+              }
+              y[j] = r;
+            }
           }
         }
+        if (POST) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          float r = zero ? 0.0f : y[j];
-          if (a.post_relu) r = r > 0.0f ? r : 0.0f;
-          y[j] = r;
+          for (int j = 0; j < 8; ++j) y[j] = y[j] > 0.0f ? y[j] : 0.0f;
         }
         if (store) {
 #pragma unroll
@@ -501,19 +505,20 @@ bool conv_i8_pool_tc_dev(Call& c, const float* x, int N, int H, int W, int Cin, 
       return false;
     }
   }
-  static bool attr_done[64] = {};
-  const int dv = current_device();
-  if (dv >= 0 && dv < 64 && !attr_done[dv]) {
-    if (!ACF_CUDA_OK(cudaFuncSetAttribute(k_conv_i8_pool_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          i8p::SMEM))) {
+  auto kern = act ? (post_relu ? k_conv_i8_pool_tc<true, true> : k_conv_i8_pool_tc<true, false>)
+                 : (post_relu ? k_conv_i8_pool_tc<false, true> : k_conv_i8_pool_tc<false, false>);
+  static bool attr_done[4][64] = {};
+  const int dv = current_device(), kv = (act ? 2 : 0) + (post_relu ? 1 : 0);
+  if (dv >= 0 && dv < 64 && !attr_done[kv][dv]) {
+    if (!ACF_CUDA_OK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, i8p::SMEM))) {
       c.fail();
       return false;
     }
-    attr_done[dv] = true;
+    attr_done[kv][dv] = true;
   }
   const int grid = (int)std::min<long long>(tiles, c.sm_count());
-  if (!ACF_CUDA_OK(launch_pdl(k_conv_i8_pool_tc, dim3(grid), dim3(i8p::THREADS), (size_t)i8p::SMEM, c.stream(),
-                              tx, a, c.err()))) {
+  if (!ACF_CUDA_OK(launch_pdl(kern, dim3(grid), dim3(i8p::THREADS), (size_t)i8p::SMEM, c.stream(), tx, a,
+                              c.err()))) {
     c.fail();
     return false;
   }
