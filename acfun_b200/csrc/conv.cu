@@ -201,58 +201,72 @@ __global__ void __launch_bounds__(128) k_conv_simt(const float* __restrict__ x, 
   }
 }
 
-// 1x1 pad-0 convolution (any stride) with few output channels on CUDA cores, register-tiled over
-// pixels: a thread owns PX consecutive output pixels x NBT output channels (S threads share a
-// pixel group, NB = S*NBT columns), so each 16-byte weight broadcast feeds PX*4 FMAs; the next
-// 4 input channels of its PX pixels are loaded while the current ones are multiplied.  Per
-// output the arithmetic is k_conv_simt's: an fp32 fma chain from 0 over the input channels,
-// then + bias, then ReLU.  Weights [Cin][Cout] (row stride ldw) are staged as [Cin][NB] once per
-// block of a persistent grid.
-template <int NB, int S, int PX>
-__global__ void __launch_bounds__(256, 2) k_pw_simt(const float* __restrict__ x, int H, int W, int Cs,
+// 1x1 pad-0 convolution (any stride) with few output channels on CUDA cores, one warp per
+// (pixel run, output-channel group): a warp owns 32*PX output pixels (PX consecutive ones per
+// lane) and NBT = NB/S output channels, so every weight load of the warp reads one shared-memory
+// address (a single-wavefront broadcast), and the S warps of a 128-thread block that share a
+// pixel run read the same input bytes (L1 hits after the first).  A ring of the next D
+// 4-channel input steps stays in flight, and the first D are issued before the weights are
+// staged.  Per output the arithmetic is k_conv_simt's: an fp32
+// fma chain from 0 over the input channels, then + bias, then ReLU.
+template <int NB, int S, int PX, int D>
+__global__ void __launch_bounds__(128, 4) k_pw_warp(const float* __restrict__ x, int H, int W, int Cs,
                                                  int coff, int Cin, const float* __restrict__ w,
                                                  long long ldw, const float* __restrict__ bias,
                                                  int Cout, int stride, int OH, int OW, unsigned M,
                                                  float* __restrict__ out, long long ldc, int act) {
-  constexpr int NBT = NB / S;
-  static_assert(NBT % 4 == 0, "16-byte weight broadcasts");
+  constexpr int NBT = NB / S, SETS = 4 / S, TP = 32 * PX * SETS;
+  static_assert(NBT % 4 == 0 && 4 % S == 0, "16-byte weight broadcasts, S divides the 4 warps");
   extern __shared__ float4 pw_sm4[];
   float* ws = reinterpret_cast<float*>(pw_sm4);  // [Cin][NB]
   float* bs = ws + Cin * NB;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g0 = (warp % S) * NBT;
+  const unsigned tiles = (M + TP - 1) / TP;
+  const float* src[PX];
+  bool valid[PX];
+  float4 xr[D][PX];  // ring of the next D 4-channel steps of the PX pixels
+  auto locate = [&](unsigned t) {
+    const unsigned mb = t * TP + (unsigned)(warp / S) * (32 * PX) + lane * PX;
+#pragma unroll
+    for (int p = 0; p < PX; ++p) {
+      const unsigned m = mb + p;
+      valid[p] = m < M;
+      const unsigned mm = valid[p] ? m : 0;
+      const unsigned ow = mm % OW, tt = mm / OW, oh = tt % OH, n = tt / OH;
+      src[p] = x + (((size_t)n * H + oh * stride) * W + ow * stride) * Cs + coff;
+    }
+#pragma unroll
+    for (int d = 0; d < D; ++d)
+#pragma unroll
+      for (int p = 0; p < PX; ++p)
+        if (4 * d < Cin) xr[d][p] = __ldg(reinterpret_cast<const float4*>(src[p] + 4 * d));
+  };
+  if (blockIdx.x < tiles) locate(blockIdx.x);
   stage_block<16>(ws, Cin * NB, [&](int i) {
     const int k = i / NB, j = i - k * NB;
     return (j < Cout) ? __ldg(w + (long long)k * ldw + j) : 0.0f;
   });
   for (int j = threadIdx.x; j < NB; j += blockDim.x) bs[j] = (bias && j < Cout) ? bias[j] : 0.0f;
   __syncthreads();
-  const unsigned groups = (M + PX - 1) / PX;
-  for (unsigned q = blockIdx.x * blockDim.x + threadIdx.x; q < groups * S; q += gridDim.x * blockDim.x) {
-    const unsigned g = q / S, g0 = (q % S) * NBT;
-    const float* src[PX];
-    bool valid[PX];
-#pragma unroll
-    for (int p = 0; p < PX; ++p) {
-      const unsigned m = g * PX + p;
-      valid[p] = m < M;
-      const unsigned mm = valid[p] ? m : 0;
-      const unsigned ow = mm % OW, t = mm / OW, oh = t % OH, n = t / OH;
-      src[p] = x + (((size_t)n * H + oh * stride) * W + ow * stride) * Cs + coff;
-    }
+  for (unsigned t = blockIdx.x; t < tiles; t += gridDim.x) {
+    if (t != blockIdx.x) locate(t);
     float acc[PX][NBT];
 #pragma unroll
     for (int p = 0; p < PX; ++p)
 #pragma unroll
       for (int j = 0; j < NBT; ++j) acc[p][j] = 0.0f;
-    float4 xn[PX];
+    for (int k0 = 0; k0 < Cin; k0 += 4 * D) {
 #pragma unroll
-    for (int p = 0; p < PX; ++p) xn[p] = __ldg(reinterpret_cast<const float4*>(src[p]));
-    for (int k = 0; k < Cin; k += 4) {
+    for (int d = 0; d < D; ++d) {
+      const int k = k0 + 4 * d;
+      if (k >= Cin) break;
       float4 xc[PX];
 #pragma unroll
-      for (int p = 0; p < PX; ++p) xc[p] = xn[p];
-      if (k + 4 < Cin) {
+      for (int p = 0; p < PX; ++p) xc[p] = xr[d][p];
+      if (k + 4 * D < Cin) {
 #pragma unroll
-        for (int p = 0; p < PX; ++p) xn[p] = __ldg(reinterpret_cast<const float4*>(src[p] + k + 4));
+        for (int p = 0; p < PX; ++p) xr[d][p] = __ldg(reinterpret_cast<const float4*>(src[p] + k + 4 * D));
       }
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
@@ -274,10 +288,12 @@ __global__ void __launch_bounds__(256, 2) k_pw_simt(const float* __restrict__ x,
         }
       }
     }
+    }
+    const unsigned mb = t * TP + (unsigned)(warp / S) * (32 * PX) + lane * PX;
 #pragma unroll
     for (int p = 0; p < PX; ++p) {
       if (!valid[p]) continue;
-      float* dst = out + (size_t)(g * PX + p) * ldc + g0;
+      float* dst = out + (size_t)(mb + p) * ldc + g0;
 #pragma unroll
       for (int j = 0; j < NBT; j += 4) {
         float4 v;
@@ -291,7 +307,7 @@ __global__ void __launch_bounds__(256, 2) k_pw_simt(const float* __restrict__ x,
           v.z = v.z > 0.0f ? v.z : 0.0f;
           v.w = v.w > 0.0f ? v.w : 0.0f;
         }
-        if ((int)g0 + j < Cout) *reinterpret_cast<float4*>(dst + j) = v;
+        if (g0 + j < Cout) *reinterpret_cast<float4*>(dst + j) = v;
       }
     }
   }
@@ -789,16 +805,17 @@ static bool conv_simt(Call& c, const float* x, int N, int H, int W, int Cs, int 
     return conv_pw_tc_dev(c, x, M, Cg, w, ldw, bias, Cout, out, ldc, act);
   if (KH == 1 && KW == 1 && pad == 0 && vec_in && vec_out && Cg % 4 == 0 && Cout % 4 == 0 &&
       (NB == 24 || NB == 64)) {
-    // 1x1: pixel-tiled kernel (4 pixels per thread)
-    const long long work = (M + 3) / 4 * (NB == 24 ? 2 : 4);
-    const int grid = (int)std::min<long long>((work + 255) / 256, 2LL * c.sm_count());
+    // 1x1: one warp per (pixel run, output-channel group); 24 channels: 1 pixel per lane (2
+    // warps share a pixel run), 64 channels: 2 pixels per lane (4 warps share it)
+    const int run = NB == 24 ? 32 * 1 * 2 : 32 * 2 * 1;
+    const int grid = (int)std::min<long long>((M + run - 1) / run, 4LL * c.sm_count());
     if (NB == 24)
-      k_pw_simt<24, 2, 4><<<grid, 256, smem, c.stream()>>>(x, H, W, Cs, coff, Cg, w, ldw, bias, Cout,
-                                                            stride, OH, OW, (unsigned)M, out, ldc, act);
+      k_pw_warp<24, 2, 1, 4><<<grid, 128, smem, c.stream()>>>(x, H, W, Cs, coff, Cg, w, ldw, bias, Cout,
+                                                               stride, OH, OW, (unsigned)M, out, ldc, act);
     else
-      k_pw_simt<64, 4, 4><<<grid, 256, smem, c.stream()>>>(x, H, W, Cs, coff, Cg, w, ldw, bias, Cout,
-                                                            stride, OH, OW, (unsigned)M, out, ldc, act);
-    return c.launched("k_pw_simt");
+      k_pw_warp<64, 4, 2, 2><<<grid, 128, smem, c.stream()>>>(x, H, W, Cs, coff, Cg, w, ldw, bias, Cout,
+                                                               stride, OH, OW, (unsigned)M, out, ldc, act);
+    return c.launched("k_pw_warp");
   }
   // a few resident blocks per SM, each walking many pixels: the weight staging is paid once
   // per block
