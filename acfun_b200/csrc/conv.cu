@@ -201,76 +201,77 @@ __global__ void __launch_bounds__(128) k_conv_simt(const float* __restrict__ x, 
   }
 }
 
-// 1x1 pad-0 convolution (any stride) with few output channels on CUDA cores, one warp per
-// (pixel run, output-channel group): a warp owns 32*PX output pixels (PX consecutive ones per
-// lane) and NBT = NB/S output channels, so every weight load of the warp reads one shared-memory
-// address (a single-wavefront broadcast), and the S warps of a 128-thread block that share a
-// pixel run read the same input bytes (L1 hits after the first).  A ring of the next D
-// 4-channel input steps stays in flight, and the first D are issued before the weights are
-// staged.  Per output the arithmetic is k_conv_simt's: an fp32
-// fma chain from 0 over the input channels, then + bias, then ReLU.
-template <int NB, int S, int PX, int D>
-__global__ void __launch_bounds__(128, 4) k_pw_warp(const float* __restrict__ x, int H, int W, int Cs,
+static __device__ __forceinline__ void cp_async16(void* sdst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((unsigned)__cvta_generic_to_shared(sdst)),
+               "l"(gsrc)
+               : "memory");
+}
+
+// 1x1 pad-0 convolution (any stride) with few output channels on CUDA cores, through shared
+// memory.  A 128-thread block owns a run of TP = 32*PX*(4/S) output pixels per tile: its input
+// rows (Cin floats each) are copied into shared memory once with coalesced 16-byte cp.async
+// (rows padded to an odd number of 16-byte chunks, so lane-per-pixel reads are conflict-free),
+// each warp then computes NBT = NB/S output channels of 32*PX of those pixels (pixel p*32+lane
+// of its set) with every weight load a warp-uniform broadcast, and the finished tile goes out
+// through a padded shared-memory tile as coalesced 16-byte stores.  The next tile's input
+// copy overlaps this tile's epilogue.  Per output the arithmetic is k_conv_simt's: an fp32 fma
+// chain from 0 over the input channels, then + bias, then ReLU.
+template <int NB, int S, int PX, int NW>
+__global__ void __launch_bounds__(32 * NW, 16 / NW) k_pw_tile(const float* __restrict__ x, int H, int W, int Cs,
                                                  int coff, int Cin, const float* __restrict__ w,
                                                  long long ldw, const float* __restrict__ bias,
                                                  int Cout, int stride, int OH, int OW, unsigned M,
                                                  float* __restrict__ out, long long ldc, int act) {
-  constexpr int NBT = NB / S, SETS = 4 / S, TP = 32 * PX * SETS;
-  static_assert(NBT % 4 == 0 && 4 % S == 0, "16-byte weight broadcasts, S divides the 4 warps");
-  extern __shared__ float4 pw_sm4[];
-  float* ws = reinterpret_cast<float*>(pw_sm4);  // [Cin][NB]
-  float* bs = ws + Cin * NB;
+  constexpr int NBT = NB / S, SETS = NW / S, TP = 32 * PX * SETS, NB4 = NB / 4, RO = NB4 | 1;
+  static_assert(NBT * S == NB && NBT % 4 == 0 && SETS * S == NW, "16-byte weight broadcasts, S divides the warps");
+  extern __shared__ float4 pt_sm4[];
+  const int C4 = Cin >> 2, RS = C4 | 1, CO4 = Cout >> 2;
+  float4* ws4 = pt_sm4;                     // [Cin][NB4] weights
+  float4* bs4 = ws4 + Cin * NB4;            // [NB4] bias
+  float4* xs = bs4 + NB4;                   // [TP][RS] input rows
+  float4* os = xs + TP * RS;                // [TP][RO] output rows
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g0 = (warp % S) * NBT;
+  const int g0 = (warp % S) * NBT, row0 = (warp / S) * 32 * PX + lane;
   const unsigned tiles = (M + TP - 1) / TP;
-  const float* src[PX];
-  bool valid[PX];
-  float4 xr[D][PX];  // ring of the next D 4-channel steps of the PX pixels
-  auto locate = [&](unsigned t) {
-    const unsigned mb = t * TP + (unsigned)(warp / S) * (32 * PX) + lane * PX;
-#pragma unroll
-    for (int p = 0; p < PX; ++p) {
-      const unsigned m = mb + p;
-      valid[p] = m < M;
-      const unsigned mm = valid[p] ? m : 0;
-      const unsigned ow = mm % OW, tt = mm / OW, oh = tt % OH, n = tt / OH;
-      src[p] = x + (((size_t)n * H + oh * stride) * W + ow * stride) * Cs + coff;
+  // row copies: with at most 32 chunks a row, one warp pass moves 32 / chunks rows (lane ->
+  // row offset, chunk); wider rows are walked 32 chunks at a time
+  const int rpi = C4 <= 32 ? 32 / C4 : 1, isub = C4 <= 32 ? lane / C4 : 0;
+  const int ic = C4 <= 32 ? lane - isub * C4 : lane;
+  const int rpo = 32 / CO4, osub = lane / CO4, oc = lane - osub * CO4;
+  auto fill = [&](unsigned t) {
+    if (isub >= rpi) return;
+    for (int r = warp * rpi + isub; r < TP; r += NW * rpi) {
+      const unsigned m = t * TP + r;
+      if (m >= M) break;
+      const unsigned ow = m % OW, tt = m / OW, oh = tt % OH, n = tt / OH;
+      const float* src = x + (((size_t)n * H + oh * stride) * W + ow * stride) * Cs + coff;
+      for (int c = ic; c < C4; c += 32) cp_async16(xs + r * RS + c, src + 4 * c);
     }
-#pragma unroll
-    for (int d = 0; d < D; ++d)
-#pragma unroll
-      for (int p = 0; p < PX; ++p)
-        if (4 * d < Cin) xr[d][p] = __ldg(reinterpret_cast<const float4*>(src[p] + 4 * d));
+    asm volatile("cp.async.commit_group;" ::: "memory");
   };
-  if (blockIdx.x < tiles) locate(blockIdx.x);
-  stage_block<16>(ws, Cin * NB, [&](int i) {
+  if (blockIdx.x < tiles) fill(blockIdx.x);
+  stage_block<16>(reinterpret_cast<float*>(ws4), Cin * NB, [&](int i) {
     const int k = i / NB, j = i - k * NB;
     return (j < Cout) ? __ldg(w + (long long)k * ldw + j) : 0.0f;
   });
-  for (int j = threadIdx.x; j < NB; j += blockDim.x) bs[j] = (bias && j < Cout) ? bias[j] : 0.0f;
-  __syncthreads();
+  for (int j = threadIdx.x; j < NB; j += blockDim.x)
+    reinterpret_cast<float*>(bs4)[j] = (bias && j < Cout) ? bias[j] : 0.0f;
   for (unsigned t = blockIdx.x; t < tiles; t += gridDim.x) {
-    if (t != blockIdx.x) locate(t);
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
     float acc[PX][NBT];
 #pragma unroll
     for (int p = 0; p < PX; ++p)
 #pragma unroll
       for (int j = 0; j < NBT; ++j) acc[p][j] = 0.0f;
-    for (int k0 = 0; k0 < Cin; k0 += 4 * D) {
-#pragma unroll
-    for (int d = 0; d < D; ++d) {
-      const int k = k0 + 4 * d;
-      if (k >= Cin) break;
+#pragma unroll 2
+    for (int k4 = 0; k4 < C4; ++k4) {
       float4 xc[PX];
 #pragma unroll
-      for (int p = 0; p < PX; ++p) xc[p] = xr[d][p];
-      if (k + 4 * D < Cin) {
-#pragma unroll
-        for (int p = 0; p < PX; ++p) xr[d][p] = __ldg(reinterpret_cast<const float4*>(src[p] + k + 4 * D));
-      }
+      for (int p = 0; p < PX; ++p) xc[p] = xs[(row0 + 32 * p) * RS + k4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        const float4* wr4 = reinterpret_cast<const float4*>(ws + (k + u) * NB + g0);
+        const float4* wr4 = ws4 + (4 * k4 + u) * NB4 + g0 / 4;
 #pragma unroll
         for (int j = 0; j < NBT; j += 4) {
           const float4 w4 = wr4[j / 4];
@@ -288,29 +289,37 @@ __global__ void __launch_bounds__(128, 4) k_pw_warp(const float* __restrict__ x,
         }
       }
     }
-    }
-    const unsigned mb = t * TP + (unsigned)(warp / S) * (32 * PX) + lane * PX;
+    __syncthreads();  // every warp is done with xs
+    if (t + gridDim.x < tiles) fill(t + gridDim.x);
 #pragma unroll
     for (int p = 0; p < PX; ++p) {
-      if (!valid[p]) continue;
-      float* dst = out + (size_t)(mb + p) * ldc + g0;
 #pragma unroll
       for (int j = 0; j < NBT; j += 4) {
+        const float4 b4 = bs4[(g0 + j) / 4];
         float4 v;
-        v.x = __fadd_rn(acc[p][j], bs[g0 + j]);
-        v.y = __fadd_rn(acc[p][j + 1], bs[g0 + j + 1]);
-        v.z = __fadd_rn(acc[p][j + 2], bs[g0 + j + 2]);
-        v.w = __fadd_rn(acc[p][j + 3], bs[g0 + j + 3]);
+        v.x = __fadd_rn(acc[p][j], b4.x);
+        v.y = __fadd_rn(acc[p][j + 1], b4.y);
+        v.z = __fadd_rn(acc[p][j + 2], b4.z);
+        v.w = __fadd_rn(acc[p][j + 3], b4.w);
         if (act) {
           v.x = v.x > 0.0f ? v.x : 0.0f;
           v.y = v.y > 0.0f ? v.y : 0.0f;
           v.z = v.z > 0.0f ? v.z : 0.0f;
           v.w = v.w > 0.0f ? v.w : 0.0f;
         }
-        if (g0 + j < Cout) *reinterpret_cast<float4*>(dst + j) = v;
+        os[(row0 + 32 * p) * RO + (g0 + j) / 4] = v;
+      }
+    }
+    __syncthreads();  // the tile's outputs are in os
+    if (osub < rpo) {
+      for (int r = warp * rpo + osub; r < TP; r += NW * rpo) {
+        const unsigned m = t * TP + r;
+        if (m >= M) break;
+        *reinterpret_cast<float4*>(out + (size_t)m * ldc + 4 * oc) = os[r * RO + oc];
       }
     }
   }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
 // Small-K convolution fused with the 2x2 / stride-2 / pad-0 max-pool that follows it (an ACFUN0
@@ -805,17 +814,27 @@ static bool conv_simt(Call& c, const float* x, int N, int H, int W, int Cs, int 
     return conv_pw_tc_dev(c, x, M, Cg, w, ldw, bias, Cout, out, ldc, act);
   if (KH == 1 && KW == 1 && pad == 0 && vec_in && vec_out && Cg % 4 == 0 && Cout % 4 == 0 &&
       (NB == 24 || NB == 64)) {
-    // 1x1: one warp per (pixel run, output-channel group); 24 channels: 1 pixel per lane (2
-    // warps share a pixel run), 64 channels: 2 pixels per lane (4 warps share it)
-    const int run = NB == 24 ? 32 * 1 * 2 : 32 * 2 * 1;
-    const int grid = (int)std::min<long long>((M + run - 1) / run, 4LL * c.sm_count());
-    if (NB == 24)
-      k_pw_warp<24, 2, 1, 4><<<grid, 128, smem, c.stream()>>>(x, H, W, Cs, coff, Cg, w, ldw, bias, Cout,
-                                                               stride, OH, OW, (unsigned)M, out, ldc, act);
-    else
-      k_pw_warp<64, 4, 2, 2><<<grid, 128, smem, c.stream()>>>(x, H, W, Cs, coff, Cg, w, ldw, bias, Cout,
-                                                               stride, OH, OW, (unsigned)M, out, ldc, act);
-    return c.launched("k_pw_warp");
+    // 1x1: blocks of NW warps over shared-memory tiles of 32*PX*(NW/S) output pixels
+    constexpr int S64 = 4, PX64 = 2, NW64 = 4, S24 = 2, PX24 = 1, NW24 = 4;
+    const int TP = NB == 24 ? 32 * PX24 * (NW24 / S24) : 32 * PX64 * (NW64 / S64);
+    const int NWv = NB == 24 ? NW24 : NW64;
+    const size_t tsmem = smem + (size_t)TP * ((Cg / 4) | 1) * 16 + (size_t)TP * ((NB / 4) | 1) * 16;
+    auto kern = NB == 24 ? k_pw_tile<24, S24, PX24, NW24> : k_pw_tile<64, S64, PX64, NW64>;
+    static bool attr_done[64][2] = {};
+    const int dv = current_device(), ki = NB == 24;
+    if (tsmem > 48 * 1024 && dv >= 0 && dv < 64 && !attr_done[dv][ki]) {
+      if (!ACF_CUDA_OK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024))) {
+        c.fail();
+        return false;
+      }
+      attr_done[dv][ki] = true;
+    }
+    const long long per_sm =
+        std::max<long long>(1, std::min<long long>(16 / NWv, (227 * 1024) / (long long)(tsmem + 1024)));
+    const int grid = (int)std::min<long long>((M + TP - 1) / TP, per_sm * c.sm_count());
+    kern<<<grid, 32 * NWv, tsmem, c.stream()>>>(x, H, W, Cs, coff, Cg, w, ldw, bias, Cout, stride, OH, OW,
+                                               (unsigned)M, out, ldc, act);
+    return c.launched("k_pw_tile");
   }
   // a few resident blocks per SM, each walking many pixels: the weight staging is paid once
   // per block
