@@ -271,7 +271,12 @@ __global__ void __launch_bounds__(halo::THREADS, 1)
             if (a.act) y = relu_max(y);
             o[i] = y;
           }
-          if (c0 + 32 <= a.Cout && (reinterpret_cast<uintptr_t>(dst + c0) & 15) == 0) {
+          if (c0 + 32 <= a.Cout && (reinterpret_cast<uintptr_t>(dst + c0) & 31) == 0) {
+            // 32-byte stores: a whole sector per lane
+#pragma unroll
+            for (int i = 0; i < 32; i += 8)
+              dev::st_global_v8(dst + c0 + i, reinterpret_cast<const uint32_t*>(o + i));
+          } else if (c0 + 32 <= a.Cout && (reinterpret_cast<uintptr_t>(dst + c0) & 15) == 0) {
 #pragma unroll
             for (int i = 0; i < 32; i += 4)
               *reinterpret_cast<float4*>(dst + c0 + i) = make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);

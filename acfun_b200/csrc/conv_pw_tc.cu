@@ -249,13 +249,18 @@ __global__ void __launch_bounds__(pw::THREADS, 1)
           if (a.act) y = relu_max(y);
           o[i] = y;
         }
-        if (c0 + 16 <= a.Cout && (reinterpret_cast<uintptr_t>(dst + c0) & 15) == 0) {
 #pragma unroll
-          for (int i = 0; i < 16; i += 4)
-            *reinterpret_cast<float4*>(dst + c0 + i) = make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
-        } else {
-          for (int i = 0; i < 16; ++i)
-            if (c0 + i < a.Cout) dst[c0 + i] = o[i];
+        for (int i = 0; i < 16; i += 8) {  // 8 columns at a time: one 32-byte store when whole
+          float* d = dst + c0 + i;
+          if (c0 + i + 8 <= a.Cout && (reinterpret_cast<uintptr_t>(d) & 31) == 0) {
+            dev::st_global_v8(d, reinterpret_cast<const uint32_t*>(o + i));
+          } else if (c0 + i + 8 <= a.Cout && (reinterpret_cast<uintptr_t>(d) & 15) == 0) {
+            *reinterpret_cast<float4*>(d) = make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
+            *reinterpret_cast<float4*>(d + 4) = make_float4(o[i + 4], o[i + 5], o[i + 6], o[i + 7]);
+          } else {
+            for (int e = 0; e < 8; ++e)
+              if (c0 + i + e < a.Cout) d[e] = o[i + e];
+          }
         }
       }
       dev::tc_fence_before();

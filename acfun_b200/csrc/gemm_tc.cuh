@@ -311,7 +311,10 @@ __device__ __forceinline__ void epi_store32(const EpiParams& ep, long long orow,
   const bool full = (j0 + 32 <= N);
   if constexpr (EPI == Epi::S32) {
     int32_t* dst = reinterpret_cast<int32_t*>(ep.C) + orow * ep.ldc + j0;
-    if (full && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+    if (full && ((reinterpret_cast<uintptr_t>(dst) & 31) == 0)) {
+#pragma unroll
+      for (int i = 0; i < 32; i += 8) dev::st_global_v8(dst + i, r + i);
+    } else if (full && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
 #pragma unroll
       for (int i = 0; i < 32; i += 4)
         *reinterpret_cast<uint4*>(dst + i) = make_uint4(r[i], r[i + 1], r[i + 2], r[i + 3]);
@@ -358,7 +361,13 @@ __device__ __forceinline__ void epi_store32(const EpiParams& ep, long long orow,
         uint32_t ph[16], pl[16];
 #pragma unroll
         for (int i = 0; i < 32; i += 2) nx_split_bf16x2(v[i], v[i + 1], ph[i / 2], pl[i / 2]);
-        if (full) {
+        if (full && ((reinterpret_cast<uintptr_t>(hi) | reinterpret_cast<uintptr_t>(lo)) & 31) == 0) {
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            dev::st_global_v8(hi + 16 * q, ph + 8 * q);
+            dev::st_global_v8(lo + 16 * q, pl + 8 * q);
+          }
+        } else if (full) {
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             reinterpret_cast<uint4*>(hi)[q] = make_uint4(ph[4 * q], ph[4 * q + 1], ph[4 * q + 2], ph[4 * q + 3]);
@@ -375,7 +384,11 @@ __device__ __forceinline__ void epi_store32(const EpiParams& ep, long long orow,
       }
     }
     float* dst = reinterpret_cast<float*>(ep.C) + orow * ep.ldc + j0;
-    if (full && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+    if (full && ((reinterpret_cast<uintptr_t>(dst) & 31) == 0)) {
+      // 32-byte stores: a whole sector per lane
+#pragma unroll
+      for (int i = 0; i < 32; i += 8) dev::st_global_v8(dst + i, reinterpret_cast<const uint32_t*>(v + i));
+    } else if (full && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
 #pragma unroll
       for (int i = 0; i < 32; i += 4)
         *reinterpret_cast<float4*>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
