@@ -434,8 +434,12 @@ __global__ void __launch_bounds__(i8p::THREADS, 1)
         if (store) {
 #pragma unroll
           for (int j = 0; j < 8; ++j) amax_acc(am, y[j]);
-          *reinterpret_cast<float4*>(dst + c0) = make_float4(y[0], y[1], y[2], y[3]);
-          *reinterpret_cast<float4*>(dst + c0 + 4) = make_float4(y[4], y[5], y[6], y[7]);
+          if ((reinterpret_cast<uintptr_t>(dst + c0) & 31) == 0) {
+            dev::st_global_v8(dst + c0, reinterpret_cast<const uint32_t*>(y));  // a whole sector
+          } else {
+            *reinterpret_cast<float4*>(dst + c0) = make_float4(y[0], y[1], y[2], y[3]);
+            *reinterpret_cast<float4*>(dst + c0 + 4) = make_float4(y[4], y[5], y[6], y[7]);
+          }
         }
       }
       dev::tc_fence_before();

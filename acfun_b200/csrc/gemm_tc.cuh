@@ -343,7 +343,9 @@ __device__ __forceinline__ void epi_store32(const EpiParams& ep, long long orow,
       packed[i / 4] = w;
     }
     int8_t* dst = reinterpret_cast<int8_t*>(ep.C) + orow * ep.ldc + j0;
-    if (full && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+    if (full && ((reinterpret_cast<uintptr_t>(dst) & 31) == 0)) {
+      dev::st_global_v8(dst, packed);  // one 32-byte store: a whole sector per lane
+    } else if (full && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
       *reinterpret_cast<uint4*>(dst) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
       *reinterpret_cast<uint4*>(dst + 16) = make_uint4(packed[4], packed[5], packed[6], packed[7]);
     } else {
@@ -452,7 +454,13 @@ __device__ __forceinline__ void epi_store_pool(const EpiParams& ep, long long or
       uint32_t ph[NC / 2], pl[NC / 2];
 #pragma unroll
       for (int i = 0; i < NC; i += 2) nx_split_bf16x2(v[i], v[i + 1], ph[i / 2], pl[i / 2]);
-      if (full && ((reinterpret_cast<uintptr_t>(hi) | reinterpret_cast<uintptr_t>(lo)) & 15) == 0) {
+      if (NC % 16 == 0 && full && ((reinterpret_cast<uintptr_t>(hi) | reinterpret_cast<uintptr_t>(lo)) & 31) == 0) {
+#pragma unroll
+        for (int q = 0; q < NC / 16; ++q) {
+          dev::st_global_v8(hi + 16 * q, ph + 8 * q);
+          dev::st_global_v8(lo + 16 * q, pl + 8 * q);
+        }
+      } else if (full && ((reinterpret_cast<uintptr_t>(hi) | reinterpret_cast<uintptr_t>(lo)) & 15) == 0) {
 #pragma unroll
         for (int q = 0; q < NC / 8; ++q) {
           reinterpret_cast<uint4*>(hi)[q] = make_uint4(ph[4 * q], ph[4 * q + 1], ph[4 * q + 2], ph[4 * q + 3]);
@@ -469,7 +477,10 @@ __device__ __forceinline__ void epi_store_pool(const EpiParams& ep, long long or
     }
   }
   float* dst = reinterpret_cast<float*>(ep.C) + orow * ep.ldc + j0;
-  if (full && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+  if (NC % 8 == 0 && full && (reinterpret_cast<uintptr_t>(dst) & 31) == 0) {
+#pragma unroll
+    for (int q = 0; q < NC / 8; ++q) dev::st_global_v8(dst + 8 * q, reinterpret_cast<const uint32_t*>(v + 8 * q));
+  } else if (full && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
 #pragma unroll
     for (int q = 0; q < NC / 4; ++q)
       reinterpret_cast<float4*>(dst)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
