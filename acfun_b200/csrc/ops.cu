@@ -608,6 +608,12 @@ bool dw_dev(Call& c, const float* in, int N, int H, int W, int C, const float* w
   const size_t smem = ((size_t)KH * KW * C + C) * 4;
   const bool rowk = C % 4 == 0 && aligned16(in) && aligned16(out) && smem <= 48 * 1024 &&
                     (long long)N * OH < (1LL << 31) && (long long)H * W * C < (1LL << 31);
+  static const bool dw_tma_on = [] {
+    const char* e = getenv("ACFUN_DW_TMA");
+    return !(e && !strcmp(e, "0"));
+  }();
+  if (dw_tma_on && dw3_tma_ok(in, out, bias, N, H, W, C, KH, KW, stride, pad, c.sm_count()))
+    return dw3_tma_dev(c, in, N, H, W, C, w, bias, out, act);
   if (rowk && KH == 3 && KW == 3 && stride == 1 && (!bias || aligned16(bias))) {
     // rows per item: 8 for tall maps (1.25 row reads per output row), fewer for short ones
     const long long per8 = (long long)N * ((OH + 7) / 8) * ((OW + 3) / 4) * (C / 4);

@@ -17,6 +17,12 @@ bool quantize_u8_dev(Call& c, const float* in, uint8_t* out, long long n, float 
 bool fill_u32_dev(Call& c, unsigned* d, unsigned v, long long n);
 bool dw_dev(Call& c, const float* in, int N, int H, int W, int C, const float* w,
             const float* bias, int KH, int KW, int stride, int pad, float* out, int act);
+// depthwise 3x3 / stride 1 / pad 1 fed by TMA halo boxes (dw_tma.cu); dw3_tma_ok says whether
+// the shape and pointers take it
+bool dw3_tma_ok(const float* in, const float* out, const float* bias, int N, int H, int W, int C,
+                int KH, int KW, int stride, int pad, int sm_count);
+bool dw3_tma_dev(Call& c, const float* in, int N, int H, int W, int C, const float* w, const float* bias,
+                 float* out, int act);
 bool group_dev(Call& c, const float* in, int N, int H, int W, int Cin, const float* w,
                const float* bias, int KH, int KW, int Cout, int stride, int pad, int groups,
                float* out, int act);

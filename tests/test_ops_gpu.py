@@ -103,6 +103,29 @@ def test_depthwise_cfg4_size(acf, orc):
     assert_bits_equal(got, ref, "cfg4 depthwise")
 
 
+@pytest.mark.parametrize("N,H,W,C,bias,act", [
+    (4, 112, 112, 32, True, 1),   # 128 tiles of 7 rows x 56 columns: the TMA-fed kernel
+    (2, 17, 13, 12, True, 1),     # odd width narrower than a column strip, ragged last row strip
+    (1, 30, 33, 40, False, 0),    # no bias, no ReLU
+    (3, 16, 250, 8, True, 1),     # a 250-column strip (box row of 252 pixels)
+    (2, 6, 9, 512, True, 1),      # C > 256: channel groups, fewer rows than a strip
+    (1, 9, 10, 144, True, 0),
+    (32, 56, 56, 8, True, 1),     # more tiles than SMs: the register-window kernel
+])
+def test_depthwise_tma_route_exact(acf, orc, N, H, W, C, bias, act):
+    """3x3 s1 p1 depthwise maps whose tiles fit one wave of CTAs run k_dw3_tma (TMA halo boxes
+    into shared memory, dw_tma.cu), the others k_dw3_roll; both keep the reference's per-output
+    fma chain, so every element equals the oracle bit for bit, borders and ragged strips included."""
+    g = np.random.default_rng(N * 1000 + H * 10 + W + C)
+    x = g.uniform(-1, 1, (N, H, W, C)).astype(np.float32)
+    w = g.uniform(-0.8, 0.8, (C, 3, 3)).astype(np.float32)
+    b = g.uniform(-0.1, 0.1, C).astype(np.float32) if bias else None
+    got = acf.conv2d_dw(x, w, b, 3, 3, 1, 1, act)
+    ref = np.empty_like(x)
+    orc.oracle().orc_conv2d(x, N, H, W, C, w, b.ctypes.data if bias else None, 3, 3, C, 1, 1, C, ref, act)
+    assert_bits_equal(got, ref, f"depthwise {N}x{H}x{W}x{C}")
+
+
 @pytest.mark.parametrize("st", [1, 2])
 def test_grouped_cfg4_size_exact(acf, orc, st):
     """BASELINE cfg4 grouped conv at its own shape: N=32, 14x14, 24 -> 48, groups 6, 3x3 pad 1,
