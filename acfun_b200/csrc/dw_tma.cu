@@ -21,16 +21,12 @@
 #include "numerics.cuh"
 #include "ops.cuh"
 
-#ifndef DWT_QW
-#define DWT_QW 2
-#endif
-
 namespace acf {
 namespace dwt {
 constexpr int R = 7;         // output rows per tile
 constexpr int MAX_SMEM = 227 * 1024;
 constexpr int MAX_THREADS = 384;  // producer warp + compute warps
-constexpr int QW = DWT_QW;        // output columns per compute thread
+constexpr int QW = 2;             // output columns per compute thread (4 measured slower)
 }  // namespace dwt
 
 struct DwtArgs {
@@ -38,9 +34,9 @@ struct DwtArgs {
   int ngrp, nstrip, ncs, tiles;  // C / CG, ceil(H / R), ceil(W / WT), N * nstrip * ncs * ngrp
   int ncomp;                     // compute threads: (CG / 4) * (WT / QW)
   uint32_t box_bytes;
-  const float* w;              // [C][9]
-  const float* bias;           // [C] or null
-  float* out;                  // NHWC, H x W
+  const float* w;                // [C][9]
+  const float* bias;             // [C] or null
+  float* out;                    // NHWC, H x W
 };
 
 // One input row of the rolling window: loads the thread's QW + 2 columns (only in-image ones, so
@@ -53,8 +49,7 @@ __device__ __forceinline__ void dwt_row(const float* boxrow, int CG, unsigned co
   float4 xr[QW + 2];
 #pragma unroll
   for (int j = 0; j < QW + 2; ++j)
-    xr[j] = ((cok >> j) & 1u) ? *reinterpret_cast<const float4*>(boxrow + j * CG)
-                                        : make_float4(0.f, 0.f, 0.f, 0.f);
+    xr[j] = ((cok >> j) & 1u) ? *reinterpret_cast<const float4*>(boxrow + j * CG) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
   for (int q = 0; q < QW; ++q) a2[q] = b4;
   if (!row_in) return;  // out-of-image rows contribute nothing
