@@ -276,6 +276,15 @@ Fp32Math fp32_math(Fp32Use use) {
 
 // Column split of the persistent walk's last wave (ConvGeom::nsplit): on unless
 // ACFUN_TAIL_SPLIT=0.
+// ACFUN_GEMM_2SM=0: plain GEMMs stay on one SM per tile instead of the SM-pair kernel
+static bool two_sm_on() {
+  static const bool on = [] {
+    const char* e = getenv("ACFUN_GEMM_2SM");
+    return !(e && !strcmp(e, "0"));
+  }();
+  return on;
+}
+
 static bool tail_split_on() {
   static const bool on = [] {
     const char* e = getenv("ACFUN_TAIL_SPLIT");
@@ -566,11 +575,7 @@ bool gemm_launch(Call& c, GemmKind kind, Epi epi, const Operand& A, const Operan
       const int v = pick(TuneFamily::I8);
       const bool wide = v >= 0 ? v == 1 : (N > 128 && tiles(M, N, 256) >= sms);
       // plain requantising GEMMs that fill the GPU with 256 x 256 tiles: the 2-SM MMA
-      static const bool two_sm = [] {
-        const char* e = getenv("ACFUN_GEMM_2SM");
-        return !(e && !strcmp(e, "0"));
-      }();
-      if (epi == Epi::S8_REQ && plain && two_sm && v < 0 && M >= 256 && N >= 256 &&
+      if (epi == Epi::S8_REQ && plain && two_sm_on() && v < 0 && M >= 256 && N >= 256 &&
           tiles(M, N, 256, 256) * 2 >= sms)
         return gemm_s8req_2sm(c, A, B, M, N, K, ep);
       if (epi == Epi::S8_REQ)
@@ -581,6 +586,10 @@ bool gemm_launch(Call& c, GemmKind kind, Epi epi, const Operand& A, const Operan
     case GemmKind::BF16: {
       if (epi != Epi::F32_BIAS) break;
       const int v = pick(TuneFamily::BF16);
+      // plain GEMMs with two or more waves of 256 x 256 tiles and a long K: the 2-SM MMA
+      // (4096^3: 136 against 147 us per call; at K = 333 and 1.2 waves the 1-SM kernel wins)
+      if (plain && two_sm_on() && v < 0 && M >= 256 && N >= 256 && K >= 1024 && tiles(M, N, 256, 256) >= sms)
+        return gemm_bf16_2sm(c, A, B, M, N, K, ep);
       if (v == 2 || (v < 0 && N > 128 && tiles(M, N, 256) >= sms))
         return launch_one<MK::F16, 256, 4, 1, Epi::F32_BIAS, false>(c, A, B, M, N, K, ep, cg);
       if (v == 1 || (v < 0 && N > 64 && tiles(M, N, 128) >= sms))

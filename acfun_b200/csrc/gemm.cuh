@@ -53,6 +53,9 @@ int gemm_bke(GemmKind kind);  // K elements per pipeline block (128 bytes)
 // s8 x s8 -> requantised s8 on CTA pairs (tcgen05.mma.cta_group::2, 256 x 256 tiles, gemm_2sm.cu)
 bool gemm_s8req_2sm(Call& c, const Operand& A, const Operand& B, int M, int N, int K,
                     const EpiParams& ep);
+// the same 2-SM kernel for bf16 A [M][K] x bf16 B [K][N] with the fp32 bias / ReLU epilogue
+bool gemm_bf16_2sm(Call& c, const Operand& A, const Operand& B, int M, int N, int K,
+                   const EpiParams& ep);
 
 // ---- tile table (acfun_autotune, tune.cu) ----
 // Plain GEMMs (no implicit convolution, no remap / split / pool / maximum epilogue) of three

@@ -1,8 +1,12 @@
-// gemm_2sm.cu — the s8 x s8 requantising GEMM (C[s8] = sat(rne(relu((acc + bias) * scale))))
-// with the 2-SM tensor-core MMA: a cluster of two CTAs on two SMs computes one 256 x 256 tile
-// (tcgen05.mma.cta_group::2, M = 256, N = 256), each CTA staging its 128 rows of A and its 128
-// columns of B, so a pipeline stage is 32 KB per CTA instead of the 48 KB a 128 x 256 tile on
-// one SM needs: six stages in flight instead of four, and half the B bytes per SM per MAC.
+// gemm_2sm.cu — GEMMs on the 2-SM tensor-core MMA: a cluster of two CTAs on two SMs computes one
+// 256 x 256 tile (tcgen05.mma.cta_group::2, M = 256, N = 256), each CTA staging its 128 rows of
+// A and its 128 columns of B, so a pipeline stage is 32 KB per CTA instead of the 48 KB a 128 x
+// 256 tile on one SM needs: six stages in flight instead of four, and half the B bytes per SM
+// per MAC.  Two instances: s8 x s8 with the requantising epilogue
+// (C[s8] = sat(rne(relu((acc + bias) * scale))), the bench headline) and bf16 x bf16 with the
+// fp32 bias / ReLU epilogue (acfun_gemm_bf16).  A stage holds 128 bytes of K either way (128
+// int8 or 64 bf16 elements); a CTA's 128 columns of B are one 128-byte swizzle atom wide for
+// int8 and two for bf16.
 //   warp 0      both CTAs: TMA producer for its own A rows / B columns; the copies complete
 //               on the leader CTA's (rank 0) full barrier (cp.async.bulk.tensor.cta_group::2),
 //               whose expect-tx covers both CTAs' bytes
@@ -10,7 +14,7 @@
 //               leader lane 0: the MMA issuer; its commits arrive on the barrier of that name
 //               in both CTAs (multicast), freeing both CTAs' stages / accumulators
 //   warps 2..9  both CTAs: epilogue over the CTA's own 128 accumulator rows x 256 columns, the
-//               S8_REQ arithmetic of gemm_tc_kernel; each warp arrives on the leader's
+//               arithmetic of gemm_tc_kernel's epilogue; each warp arrives on the leader's
 //               accumulator-empty barrier when it has drained a buffer
 // The pair walks 256 x 256 tiles persistently (grid = 2 x the number of SM pairs used).
 // No load uses cluster multicast: each CTA fetches its own operand halves.  Every wait is
@@ -27,7 +31,7 @@ constexpr int BN = 256;                 // accumulator columns (128 of B staged 
 constexpr int BK = 128;                 // K bytes per stage
 constexpr int STAGES = 6;
 constexpr int A_STAGE = BM * BK;        // 16 KB
-constexpr int B_STAGE = BK * (BN / 2);  // 16 KB: 128 K rows x 128 columns, MN-major
+constexpr int B_STAGE = BK * (BN / 2);  // 16 KB: this CTA's 128 columns x 128 bytes of K
 constexpr int STAGE = A_STAGE + B_STAGE;
 constexpr int NBUF = 2;
 constexpr int TMEM_COLS = NBUF * BN;    // 512
@@ -42,6 +46,21 @@ static_assert(SMEM <= 232448, "shared memory");
 // shared::cta address of a barrier with this bit cleared = the leader CTA's barrier at the same
 // offset (the CTA-pair addressing of sm_100 clusters)
 constexpr uint32_t kPeerBitMask = 0xFEFFFFFFu;
+
+// Per-kind stage geometry: K elements per stage, 128-byte B column chunks per CTA (MN-major
+// B, one TMA box and one swizzle atom each) and the B descriptor advance per 32-byte K-step.
+template <dev::MmaKind KIND>
+struct Kind2 {
+  static constexpr int ELEM = KIND == dev::MmaKind::I8 ? 1 : 2;
+  static constexpr int KE = BK / ELEM;
+  static constexpr int B_CHUNKS = (BN / 2) * ELEM / 128;
+  static constexpr int B_CHUNK = KE * 128;
+  static constexpr int CHUNK_COLS = 128 / ELEM;
+  static constexpr int KSTEP_B = (32 / ELEM) * 128;
+  static constexpr uint32_t C_FMT = KIND == dev::MmaKind::I8 ? 2u : 1u;  // s32 / f32 accumulator
+  static constexpr uint32_t AB_FMT = 1u;                                  // s8 / bf16 operands
+  static_assert(B_CHUNKS * B_CHUNK == B_STAGE, "stage layout");
+};
 }  // namespace g2
 
 namespace dev2 {
@@ -75,13 +94,21 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* m
       "l"(reinterpret_cast<uint64_t>(m)), "r"(dev::smem_u32(bar) & g2::kPeerBitMask), "r"(x), "r"(y)
       : "memory");
 }
-__device__ __forceinline__ void umma2_i8(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
-                                         uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
-      : "memory");
+template <dev::MmaKind KIND>
+__device__ __forceinline__ void umma2(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                      uint32_t accumulate) {
+  if constexpr (KIND == dev::MmaKind::I8)
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+        : "memory");
+  else
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+        : "memory");
 }
 // arrive (once) on `bar` in both CTAs of the pair when the issued MMAs are done
 __device__ __forceinline__ void umma2_commit_both(uint64_t* bar) {
@@ -104,10 +131,12 @@ __device__ __forceinline__ void mbar_arrive_leader(uint64_t* bar) {
 }
 }  // namespace dev2
 
+template <dev::MmaKind KIND, Epi EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(g2::THREADS, 1)
-    gemm_s8req_2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                          EpiParams ep, int M, int N, int K, unsigned* err) {
+    gemm_2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    EpiParams ep, int M, int N, int K, unsigned* err) {
   using namespace g2;
+  using KT = Kind2<KIND>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -125,7 +154,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(g2::THREADS, 1)
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   const int tiles_m = (M + 2 * BM - 1) / (2 * BM), tiles_n = (N + BN - 1) / BN;
   const int num_tiles = tiles_m * tiles_n;
-  const int nkb = (K + BK - 1) / BK;
+  const int nkb = (K + KT::KE - 1) / KT::KE;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -165,8 +194,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(g2::THREADS, 1)
         }
         uint8_t* st = smem + s * STAGE;
         if (rank == 0) dev::mbar_arrive_expect_tx(&full_bar[s], (uint32_t)(2 * STAGE));
-        dev2::tma_load_2d_pair(st, &tmA, &full_bar[s], kb * BK, m0);
-        dev2::tma_load_2d_pair(st + A_STAGE, &tmB, &full_bar[s], n0, kb * BK);
+        dev2::tma_load_2d_pair(st, &tmA, &full_bar[s], kb * KT::KE, m0);
+#pragma unroll
+        for (int ch = 0; ch < KT::B_CHUNKS; ++ch)
+          dev2::tma_load_2d_pair(st + A_STAGE + ch * KT::B_CHUNK, &tmB, &full_bar[s], n0 + ch * KT::CHUNK_COLS,
+                                 kb * KT::KE);
         ++it;
         if (++s == STAGES) {
           s = 0;
@@ -176,10 +208,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(g2::THREADS, 1)
     }
   } else if (warp == 1 && lane == 0 && rank == 0) {
     // ---------------- MMA issuer (leader only): M = 256 (128 rows from each CTA), N = 256
-    constexpr uint32_t idesc = dev::umma_idesc(2u, 1u, 1u, 0u, 1u, 256u, (uint32_t)BN);
+    constexpr uint32_t idesc = dev::umma_idesc(KT::C_FMT, KT::AB_FMT, KT::AB_FMT, 0u, 1u, 256u, (uint32_t)BN);
     const uint32_t base = dev::smem_u32(smem);
     const uint64_t a_desc0 = dev::umma_sdesc(base, 16, 8 * BK, dev::UMMA_SW128);
-    const uint64_t b_desc0 = dev::umma_sdesc(base + A_STAGE, B_STAGE, 1024, dev::UMMA_SW128);
+    // MN-major B: LBO = the stride between 128-byte column chunks, SBO = 8 K rows
+    const uint64_t b_desc0 = dev::umma_sdesc(base + A_STAGE, KT::B_CHUNK, 1024, dev::UMMA_SW128);
     bool ok = true;
     uint32_t s = 0, ph = 0, local = 0;
     for (int t = pair; t < num_tiles && ok; t += npairs, ++local) {
@@ -199,8 +232,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(g2::THREADS, 1)
         const uint64_t soff = (uint64_t)((s * (uint32_t)STAGE) >> 4);
 #pragma unroll
         for (int ks = 0; ks < BK / 32; ++ks)
-          dev2::umma2_i8(d_tmem, a_desc0 + soff + (uint64_t)((ks * 32) >> 4),
-                         b_desc0 + soff + (uint64_t)((ks * 32 * 128) >> 4), idesc, (kb | ks) != 0);
+          dev2::umma2<KIND>(d_tmem, a_desc0 + soff + (uint64_t)((ks * 32) >> 4),
+                            b_desc0 + soff + (uint64_t)((ks * KT::KSTEP_B) >> 4), idesc, (kb | ks) != 0);
         dev2::umma2_commit_both(&empty_bar[s]);
         if (++s == STAGES) {
           s = 0;
@@ -228,7 +261,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(g2::THREADS, 1)
         __syncwarp();
 #pragma unroll
         for (int k = 0; k < CHUNKS_PER_WARP; ++k)
-          epi_stage_cols<Epi::S8_REQ>(ep, n0 + h * 32 + 64 * k + lane, N, lane, my[k]);
+          epi_stage_cols<EPI>(ep, n0 + h * 32 + 64 * k + lane, N, lane, my[k]);
         __syncwarp();
         staged_n0 = n0;
       }
@@ -246,7 +279,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(g2::THREADS, 1)
         uint32_t v[32];
         dev::tmem_ld32(tmem + buf * BN + (uint32_t)c0 + ((uint32_t)(q * 32) << 16), v);
         dev::tmem_ld_wait();
-        if (r < M) epi_store32<Epi::S8_REQ>(ep, r, n0 + c0, N, v, my[k], false, 0.0f, am);
+        if (r < M) epi_store32<EPI>(ep, r, n0 + c0, N, v, my[k], false, 0.0f, am);
       }
       dev::tc_fence_before();
       __syncwarp();
@@ -262,24 +295,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(g2::THREADS, 1)
   }
 }
 
-// Launches the 2-SM kernel for S8_REQ on s8 A [M][lda] and s8 B [K][ldb] (device, TMA-aligned).
-bool gemm_s8req_2sm(Call& c, const Operand& A, const Operand& B, int M, int N, int K,
-                    const EpiParams& ep) {
+// Launches the 2-SM kernel on A [M][lda] (K-major) and B [K][ldb] (MN-major), device and
+// TMA-aligned: s8 operands with the requantising epilogue, or bf16 with the fp32 one.
+template <dev::MmaKind KIND, Epi EPI>
+static bool gemm_2sm_launch(Call& c, const Operand& A, const Operand& B, int M, int N, int K,
+                            const EpiParams& ep) {
   using namespace g2;
+  using KT = Kind2<KIND>;
+  const CUtensorMapDataType dt =
+      KIND == dev::MmaKind::I8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const uint64_t E = KT::ELEM;
   CUtensorMap ta, tb;
-  const uint64_t dA[2] = {(uint64_t)K, (uint64_t)M}, sA[1] = {(uint64_t)A.ld};
-  const uint32_t bA[2] = {(uint32_t)BK, (uint32_t)BM};
-  const uint64_t dB[2] = {(uint64_t)N, (uint64_t)K}, sB[1] = {(uint64_t)B.ld};
-  const uint32_t bB[2] = {(uint32_t)(BN / 2), (uint32_t)BK};
-  if (!encode_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, A.p, dA, sA, bA, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !encode_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, B.p, dB, sB, bB, CU_TENSOR_MAP_SWIZZLE_128B)) {
+  const uint64_t dA[2] = {(uint64_t)K, (uint64_t)M}, sA[1] = {(uint64_t)A.ld * E};
+  const uint32_t bA[2] = {(uint32_t)KT::KE, (uint32_t)BM};
+  const uint64_t dB[2] = {(uint64_t)N, (uint64_t)K}, sB[1] = {(uint64_t)B.ld * E};
+  const uint32_t bB[2] = {(uint32_t)KT::CHUNK_COLS, (uint32_t)KT::KE};
+  if (!encode_tmap(&ta, dt, 2, A.p, dA, sA, bA, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_tmap(&tb, dt, 2, B.p, dB, sB, bB, CU_TENSOR_MAP_SWIZZLE_128B)) {
     c.fail();
     return false;
   }
   static bool attr_done[64] = {false};
   const int dv = current_device();
   if (dv >= 0 && dv < 64 && !attr_done[dv]) {
-    if (!ACF_CUDA_OK(cudaFuncSetAttribute(gemm_s8req_2sm_kernel,
+    if (!ACF_CUDA_OK(cudaFuncSetAttribute(gemm_2sm_kernel<KIND, EPI>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM))) {
       c.fail();
       return false;
@@ -288,8 +327,18 @@ bool gemm_s8req_2sm(Call& c, const Operand& A, const Operand& B, int M, int N, i
   }
   const long long tiles = (long long)((M + 2 * BM - 1) / (2 * BM)) * ((N + BN - 1) / BN);
   const int pairs = (int)std::min<long long>(tiles, c.sm_count() / 2);
-  gemm_s8req_2sm_kernel<<<2 * pairs, THREADS, SMEM, c.stream()>>>(ta, tb, ep, M, N, K, c.err());
-  return c.launched("gemm_s8req_2sm_kernel");
+  gemm_2sm_kernel<KIND, EPI><<<2 * pairs, THREADS, SMEM, c.stream()>>>(ta, tb, ep, M, N, K, c.err());
+  return c.launched("gemm_2sm_kernel");
+}
+
+bool gemm_s8req_2sm(Call& c, const Operand& A, const Operand& B, int M, int N, int K,
+                    const EpiParams& ep) {
+  return gemm_2sm_launch<dev::MmaKind::I8, Epi::S8_REQ>(c, A, B, M, N, K, ep);
+}
+
+bool gemm_bf16_2sm(Call& c, const Operand& A, const Operand& B, int M, int N, int K,
+                   const EpiParams& ep) {
+  return gemm_2sm_launch<dev::MmaKind::F16, Epi::F32_BIAS>(c, A, B, M, N, K, ep);
 }
 
 }  // namespace acf

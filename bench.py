@@ -744,8 +744,8 @@ def main():
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak_tops, 1),
                          "unit": "TOPS", "frac": round(achieved / peak_tops, 4),
                          "peak_source": f"2 x bf16_tflops ({peak_src}, MEASURED_PEAKS.json): dense int8 = 2x bf16",
-                         "kernel": "gemm_s8req_2sm_kernel (256x256 tiles on SM pairs, tcgen05.mma.cta_group::2, "
-                                   "6 stages, S8_REQ)" if os.environ.get("ACFUN_GEMM_2SM", "1") != "0"
+                         "kernel": "gemm_2sm_kernel<I8, S8_REQ> (256x256 tiles on SM pairs, tcgen05.mma.cta_group::2, "
+                                   "6 stages)" if os.environ.get("ACFUN_GEMM_2SM", "1") != "0"
                                    else "gemm_tc_kernel<I8, BN=256, 4 stages, S8_REQ>",
                          "traffic": traffic},
             # our kernels in the two timed loops: one GEMM per device-resident call; the host-

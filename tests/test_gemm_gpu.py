@@ -118,7 +118,8 @@ def test_gemm_f32_tolerance(acf, orc, M, N, K):
 
 
 @pytest.mark.parametrize("M,N,K", [(64, 64, 64), (33, 47, 129), (1024, 1024, 1024), (200, 520, 300),
-                                   (2560, 2048, 256)])   # 160 tiles: a second, partial wave
+                                   (2560, 2048, 256),    # 160 tiles: a second, partial wave
+                                   (2200, 2450, 333)])   # ragged M / N / K
 def test_gemm_bf16_tolerance(acf, orc, M, N, K):
     g = np.random.default_rng(M * N + K)
     A = g.uniform(-1, 1, (M, K)).astype(np.float32)
@@ -130,6 +131,22 @@ def test_gemm_bf16_tolerance(acf, orc, M, N, K):
     assert max_rel(got, ref) < 1e-4
     exact = A.astype(np.float64) @ B.astype(np.float64)
     assert max_rel(got, exact) < TOL_BF16
+
+
+@pytest.mark.parametrize("M,N,K", [(4096, 4096, 4096),   # BASELINE cfg2 bf16 shape
+                                   (3100, 3300, 1100)])  # ragged M / N / K
+def test_gemm_bf16_2sm_sampled(acf, orc, M, N, K):
+    """bf16 GEMMs with two or more waves of 256 x 256 tiles and K >= 1024 run on the 2-SM kernel:
+    sampled rows (the first / last of a 256-row pair tile and the last row among them) against
+    the oracle's bf16 GEMM."""
+    g = np.random.default_rng(M + N + K)
+    A = g.uniform(-1, 1, (M, K)).astype(np.float32)
+    B = g.uniform(-1, 1, (K, N)).astype(np.float32)
+    got = acf.gemm_bf16(A, B)
+    rows = np.unique(np.concatenate([[0, 127, 128, 255, 256, M - 1], g.choice(M, 10, replace=False)]))
+    ref = np.empty((rows.size, N), np.float32)
+    orc.oracle().orc_gemm_bf16(rows.size, N, K, np.ascontiguousarray(A[rows]), B, ref)
+    assert max_rel(got[rows], ref) < 1e-4
 
 
 @pytest.mark.parametrize("name", sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLD, "gemm_f32_*.npz"))))
