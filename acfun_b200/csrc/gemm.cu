@@ -57,6 +57,7 @@ __device__ __forceinline__ float tf32_rne(float x) {
 
 __global__ void k_to_tf32x2(const float* __restrict__ src, long long lds, int rows, int cols,
                             float* __restrict__ dst, long long ldp, long long op_stride) {
+  dev::grid_dep_launch();  // the GEMM after it may start its prologue
   const long long groups = ldp / 4;
   const long long total = (long long)rows * groups;
   for (long long g = blockIdx.x * (long long)blockDim.x + threadIdx.x; g < total;
@@ -104,6 +105,7 @@ struct Bf16Job {
   long long ldp;
 };
 __global__ void k_to_bf16(Bf16Job j0, Bf16Job j1, long long g0, long long gt) {
+  dev::grid_dep_launch();  // the GEMM after it may start its prologue
   for (long long g = blockIdx.x * (long long)blockDim.x + threadIdx.x; g < gt;
        g += (long long)gridDim.x * blockDim.x) {
     const bool sec = g >= g0;
@@ -181,6 +183,7 @@ struct Bf16x2Job {
   long long ldp, op_stride;
 };
 __global__ void k_to_bf16x2(Bf16x2Job j0, Bf16x2Job j1, long long g0, long long gt) {
+  dev::grid_dep_launch();  // the GEMM after it may start its prologue
   for (long long g = blockIdx.x * (long long)blockDim.x + threadIdx.x; g < gt;
        g += (long long)gridDim.x * blockDim.x) {
     const bool sec = g >= g0;
@@ -406,7 +409,11 @@ static bool launch_one(Call& c, const Operand& A, const Operand& B, int M, int N
   }
   // persistent: one CTA per SM (1 CTA/SM by shared memory), tiles strided over the grid
   const dim3 grid((unsigned)(tiles < sms ? tiles : sms));
-  kern<<<grid, S::THREADS, S::SMEM, c.stream()>>>(ta, tb, ep, g, M, N, K, c.err());
+  if (!ACF_CUDA_OK(launch_pdl(kern, dim3(grid), dim3(S::THREADS), (size_t)S::SMEM, c.stream(), ta, tb, ep, g,
+                              M, N, K, c.err()))) {
+    c.fail();
+    return false;
+  }
   return c.launched("gemm_tc_kernel");
 }
 

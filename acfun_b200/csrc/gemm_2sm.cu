@@ -175,6 +175,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(g2::THREADS, 1)
     dev2::tmem_alloc2(tmem_slot, TMEM_COLS);
     dev2::tmem_relinquish2();
   }
+  // launched as a programmatic dependent: nothing the previous kernel produced is read, and
+  // nothing is written, before this
+  dev::grid_dep_wait();
   dev::tc_fence_before();
   dev2::cluster_sync();  // both CTAs' barriers initialised before any cross-CTA arrive
   dev::tc_fence_after();
@@ -327,7 +330,11 @@ static bool gemm_2sm_launch(Call& c, const Operand& A, const Operand& B, int M, 
   }
   const long long tiles = (long long)((M + 2 * BM - 1) / (2 * BM)) * ((N + BN - 1) / BN);
   const int pairs = (int)std::min<long long>(tiles, c.sm_count() / 2);
-  gemm_2sm_kernel<KIND, EPI><<<2 * pairs, THREADS, SMEM, c.stream()>>>(ta, tb, ep, M, N, K, c.err());
+  if (!ACF_CUDA_OK(launch_pdl(gemm_2sm_kernel<KIND, EPI>, dim3(2 * pairs), dim3(THREADS), (size_t)SMEM,
+                              c.stream(), ta, tb, ep, M, N, K, c.err()))) {
+    c.fail();
+    return false;
+  }
   return c.launched("gemm_2sm_kernel");
 }
 

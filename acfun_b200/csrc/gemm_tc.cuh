@@ -544,6 +544,9 @@ __global__ void __launch_bounds__(320, 1)
     dev::tmem_alloc(tmem_slot, S::TMEM_COLS);
     dev::tmem_relinquish();
   }
+  // launched as a programmatic dependent: the prologue above (barriers, tensor memory) may
+  // overlap the previous kernel; nothing it produced is read, and nothing is written, before this
+  dev::grid_dep_wait();
   dev::tc_fence_before();
   __syncthreads();
   dev::tc_fence_after();
