@@ -208,7 +208,8 @@ static __device__ __forceinline__ void cp_async16(void* sdst, const void* gsrc) 
 }
 
 // 1x1 pad-0 convolution (any stride) with few output channels on CUDA cores, through shared
-// memory.  A 128-thread block owns a run of TP = 32*PX*(4/S) output pixels per tile: its input
+// memory.  A block of NW warps (4 in the dispatch: 6 and 8 measured slower) owns a run of
+// TP = 32*PX*(NW/S) output pixels per tile: its input
 // rows (Cin floats each) are copied into shared memory once with coalesced 16-byte cp.async
 // (rows padded to an odd number of 16-byte chunks, so lane-per-pixel reads are conflict-free),
 // each warp then computes NBT = NB/S output channels of 32*PX of those pixels (pixel p*32+lane
